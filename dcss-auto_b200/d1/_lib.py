@@ -1,0 +1,49 @@
+"""ctypes loader for libd1.so with argument types for every exported entry point."""
+import ctypes as C
+import pathlib
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / 'libd1.so'
+ERR_NO_HOST_PATH = 9001
+ERR_BAD_ARGUMENT = 9002
+
+_P, _I, _U64, _F = C.c_void_p, C.c_int, C.c_uint64, C.c_float
+# name -> argtypes; every export returns int.
+SIGNATURES = {
+    'learn_state_bytes': [], 'learn_obs_size': [], 'learn_action_size': [], 'learn_out_size': [],
+    'learn_config_bytes': [],
+    'learn_init': [_P, _I, _P, _P, _U64, _P, _P, _P, _I],
+    'learn_step': [_P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _I],
+    'learn_step_active': [_P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I],
+    'learn_heuristic': [_P, _I, _P, _P, _P, _P, _I],
+    'learn_semantic_test': [_P, _P],
+    'learn_compact_state': [_P, _I, _P, _P],
+    'learn_distance_table': [_P, _P, _I, _P, _P],
+}
+
+_LIB = None
+
+
+class D1Error(RuntimeError):
+    pass
+
+
+def library():
+    """Load libd1.so once; raise (never fall back) when it is missing."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise D1Error(f'{LIB_PATH} is missing: build it with `make -C dcss-auto_b200/csrc` '
+                          '(or __graft_entry__.build()); there is no CPU fallback')
+        lib = C.CDLL(str(LIB_PATH))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = C.c_int
+        _LIB = lib
+    return _LIB
+
+
+def check(code, what='libd1 call'):
+    if code:
+        raise D1Error(f'{what} failed with error {code}')
+    return code

@@ -1,0 +1,96 @@
+/* libd1.so -- B200-native (sm_100a) batched D:1 environment step and PPO hot path.
+ *
+ * Plain C ABI: pointers and sizes only. Every buffer argument is DEVICE memory
+ * owned by the caller (allocated once, reused every step); the library never
+ * allocates on the hot path, never synchronises, and launches on the caller's
+ * stream. Every entry point returns 0 on success or a nonzero code: a CUDA error
+ * number from the launch, or one of the D1_ERR_* codes below.
+ *
+ * There is no host execution path: a call that asks for one (gpu == 0) returns
+ * D1_ERR_NO_HOST_PATH instead of silently running on the CPU.
+ */
+#ifndef D1_H
+#define D1_H
+#include <stddef.h>
+#include <stdint.h>
+#include <stdbool.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define D1_ERR_NO_HOST_PATH 9001 /* gpu == 0: this library has no CPU path */
+#define D1_ERR_BAD_ARGUMENT 9002 /* size, count or pointer outside the supported range */
+
+/* Monster kind and run configuration, byte-identical to the reference structs
+ * (gpu-d1/src/sim.h:61-67): 11 ints + 6 kinds of 4 ints = 140 bytes. */
+typedef struct { int speed, damage, tohit, bypass; } D1Kind;
+typedef struct {
+    int count, player, hp, ac100, ev100, sh100, shield_limit, regen, repair, gdr[2];
+    D1Kind kinds[6];
+} D1Config;
+
+/* Static map tables for the single fixture map, byte-identical to the reference
+ * (gpu-d1/src/learn.cu:130-139, single-map build). All pointers are device memory:
+ * floor u8[5600], cells i16[ncells] (reachable floor), index i16[5600],
+ * distance u16[ncells * 5600] (row i = BFS distance from cells[i]). */
+typedef struct {
+    const uint8_t *floor;
+    const int16_t *cells, *index;
+    const uint16_t *distance;
+    int ncells;
+} D1Tables;
+
+/* ======================================================================
+ * Reference-compatible task ("v1"): the reference's default learn.cu build,
+ * 9 actions (8 compass moves/attacks + wait), up to 8 monsters, 206 float
+ * observations, 9 mask floats and 8 outcome floats per env.
+ * Same names, argument meaning and error behaviour as the reference exports.
+ * ====================================================================== */
+
+/* Bytes of one env's opaque state row (reference: gpu-d1/src/learn.cu:644). */
+int learn_state_bytes(void);
+/* 206 (learn.cu:645). */
+int learn_obs_size(void);
+/* 9 (learn.cu:646). */
+int learn_action_size(void);
+/* 8 (learn.cu:647). */
+int learn_out_size(void);
+/* sizeof(D1Config) == 140 (learn.cu:648). */
+int learn_config_bytes(void);
+/* Seed env i with PCG32(mix(seed + i), i + 1), reset it and write its first
+ * observation and mask (reference: learn.cu:649-660). state: u8[n, state_bytes];
+ * obs f32[n, 206]; mask f32[n, 9]. `c` and `t` are host pointers to structs whose
+ * table pointers are device memory. */
+int learn_init(void *state, int n, const D1Config *c, const D1Tables *t, uint64_t seed, float *obs, float *mask,
+               void *stream, int gpu);
+/* One decision for every env: transition + auto-reset + observation
+ * (reference: learn.cu:661-665). actions i64[n]; out f32[n, 8]. */
+int learn_step(void *state, int n, const D1Config *c, const D1Tables *t, const int64_t *actions, int limit, float *obs,
+               float *mask, float *out, void *stream, int gpu);
+/* As learn_step, but envs with active[i] == false are left byte-for-byte untouched
+ * (reference: learn.cu:666-670). */
+int learn_step_active(void *state, int n, const D1Config *c, const D1Tables *t, const int64_t *actions, int limit,
+                      float *obs, float *mask, float *out, const bool *active, void *stream, int gpu);
+/* Pursuit baseline action per env (reference: learn.cu:671-675). */
+int learn_heuristic(void *state, int n, const D1Config *c, const D1Tables *t, int64_t *actions, void *stream, int gpu);
+/* Deterministic rule checks (move, last kill without retaliation, timeout,
+ * death reset), run on the device (reference: learn.cu:677-707, which ran them on
+ * the host). Returns 0 when all pass, else the number of the failed check. Blocks
+ * until the check kernel finishes. */
+int learn_semantic_test(const D1Config *c, const D1Tables *t);
+
+/* Extras with no reference counterpart, used by the Python wrapper and tests. */
+/* Canonical compact view of each env (33 x i64: rng.state, rng.inc, episode, hp,
+ * regen, blocks, player, ticks, killed, pos[8], energy[8], hp[8]) -- the fields of
+ * the reference State that determine every future step. rows: device i64[n, 33]. */
+int learn_compact_state(const void *state, int n, int64_t *rows, void *stream);
+/* All-pairs BFS distance table over 8-neighbour floor, one warp per source cell
+ * (replaces the Python BFS of gpu-d1/scripts/learn_env.py:25-39).
+ * floor u8[5600], cells i16[ncells] -> distance u16[ncells, 5600] (65535 = unreachable). */
+int learn_distance_table(const uint8_t *floor, const int16_t *cells, int ncells, uint16_t *distance, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* D1_H */

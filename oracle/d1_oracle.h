@@ -1,0 +1,58 @@
+/* TEST INFRASTRUCTURE ONLY -- the CPU oracle for the D:1 env-step hot path.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg load this
+ * library, and only as the checker. The product (libd1.so) never links it.
+ *
+ * Two task modes are restated here in plain C:
+ *   v1    the reference's default learn.cu build (gpu-d1/src/learn.cu with no -D
+ *         flags: 9 actions, 8 enemies, 206 observations, 8 outcome values), over
+ *         the rules of gpu-d1/src/sim.h. Pinned against the reference itself
+ *         compiled for the host (oracle/_ref/learn_v1.so) by tests/test_oracle.py.
+ *   spec  the BASELINE task (generated rooms+corridors maps, Philox4x32-10, 12
+ *         semantic actions, one-hot 15x15x8 + 32 observation). The reference has
+ *         no code for the map generator, Philox stream, action set or encoding,
+ *         so those parts are parity-unpinned; the combat, scheduler, pursuit,
+ *         LOS, wake, REST and attack-nearest rules reuse the v1-pinned helpers
+ *         and the reference's native LOS ray fan (pinned against native LOS).
+ */
+#pragma once
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Reference ABI structs (gpu-d1/src/sim.h:61-67, gpu-d1/src/learn.cu:130-139). */
+typedef struct { int speed, damage, tohit, bypass; } D1Kind;
+typedef struct {
+    int count, player, hp, ac100, ev100, sh100, shield_limit, regen, repair, gdr[2];
+    D1Kind kinds[6];
+} D1Config;
+typedef struct {
+    const uint8_t *floor;
+    const int16_t *cells, *index;
+    const uint16_t *distance;
+    int ncells;
+} D1Tables;
+
+/* ---- v1 (reference default build) ---- */
+enum { OV1_ENEMIES = 8, OV1_OBS = 206, OV1_ACTIONS = 9, OV1_OUT = 8, OV1_COMPACT = 33 };
+int oracle_v1_state_bytes(void);
+int oracle_v1_init(void *states, int n, const D1Config *c, const D1Tables *t, uint64_t seed,
+                   float *obs, float *mask);
+int oracle_v1_step(void *states, int n, const D1Config *c, const D1Tables *t, const int64_t *actions,
+                   int limit, float *obs, float *mask, float *out, const uint8_t *active);
+int oracle_v1_heuristic(void *states, int n, const D1Config *c, const D1Tables *t, int64_t *actions);
+/* Compact canonical view: rng.state, rng.inc, episode, hp, regen, blocks, player,
+ * ticks, killed, pos[8], energy[8], hp[8]  (33 x int64 per env). */
+int oracle_v1_compact(const void *states, int n, int64_t *rows);
+/* Same compact view read from the reference's own State bytes (learn.cu:106-129). */
+int oracle_v1_compact_from_reference(const void *ref_states, int n, int state_bytes, int64_t *rows);
+int oracle_v1_semantic_test(const D1Config *c, const D1Tables *t);
+/* Host all-pairs BFS distance table, the restatement of gpu-d1/scripts/learn_env.py:25-39. */
+int oracle_distance_table(const uint8_t *floor, const int16_t *cells, int ncells, uint16_t *distance);
+
+#ifdef __cplusplus
+}
+#endif

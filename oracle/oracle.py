@@ -1,0 +1,203 @@
+"""TEST INFRASTRUCTURE ONLY -- Python handles on the CPU oracle and on the reference build.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference leg
+import this module, and only as the checker. It wraps:
+
+* liboracle.so      -- the plain-C restatement in oracle/d1_oracle.c;
+* _ref/learn_v1.so  -- the reference's own gpu-d1/src/learn.cu default build,
+                       compiled for the host from the reference sources by
+                       `make -C oracle ref` (present only where the reference
+                       tree was available when it was built).
+
+The fixture tables are assembled the way gpu-d1/scripts/learn_env.py:15-40 and
+:66-75 assemble them.
+"""
+import ctypes as C
+import pathlib
+import subprocess
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+REPO = HERE.parent
+DATA = REPO / 'dcss-auto_b200' / 'd1' / 'data'
+
+V1_OBS, V1_ACTIONS, V1_OUT, V1_COMPACT = 206, 9, 8, 33
+
+
+class Tables(C.Structure):
+    _fields_ = [(k, C.c_void_p) for k in ('floor', 'cells', 'index', 'distance')] + [('ncells', C.c_int)]
+
+
+def build(ref=False):
+    """Compile the oracle (and, when asked and possible, the reference build)."""
+    subprocess.run(['make', '-s', '-C', str(HERE), 'liboracle.so'], check=True)
+    if ref:
+        subprocess.run(['make', '-s', '-C', str(HERE), 'ref'], check=True)
+
+
+_LIB = None
+
+
+def library():
+    global _LIB
+    if _LIB is None:
+        path = HERE / 'liboracle.so'
+        if not path.exists():
+            build()
+        lib = C.CDLL(str(path))
+        p, i = C.c_void_p, C.c_int
+        lib.oracle_v1_init.argtypes = [p, i, p, p, C.c_uint64, p, p]
+        lib.oracle_v1_step.argtypes = [p, i, p, p, p, i, p, p, p, p]
+        lib.oracle_v1_heuristic.argtypes = [p, i, p, p, p]
+        lib.oracle_v1_compact.argtypes = [p, i, p]
+        lib.oracle_v1_compact_from_reference.argtypes = [p, i, i, p]
+        lib.oracle_v1_semantic_test.argtypes = [p, p]
+        lib.oracle_distance_table.argtypes = [p, p, i, p]
+        _LIB = lib
+    return _LIB
+
+
+def reference_library():
+    """The reference's own host build, or None when it was not built here."""
+    path = HERE / '_ref' / 'learn_v1.so'
+    if not path.exists():
+        return None
+    lib = C.CDLL(str(path))
+    p, i = C.c_void_p, C.c_int
+    lib.learn_init.argtypes = [p, i, p, p, C.c_uint64, p, p, p, i]
+    lib.learn_step.argtypes = [p, i, p, p, p, i, p, p, p, p, i]
+    lib.learn_step_active.argtypes = [p, i, p, p, p, i, p, p, p, p, p, i]
+    lib.learn_heuristic.argtypes = [p, i, p, p, p, p, i]
+    lib.learn_semantic_test.argtypes = [p, p]
+    return lib
+
+
+_FIXTURE = None
+
+
+def fixture():
+    """(header, kinds, floor, cells, index, distance) for the reference map."""
+    global _FIXTURE
+    if _FIXTURE is None:
+        z = np.load(DATA / 'fixture_1057.npz')
+        header, kinds, floor, native = z['header'], z['kinds'], z['floor'], z['native_dist']
+        cells = np.flatnonzero((floor != 0) & (native < 65535)).astype(np.int16)
+        index = np.full(5600, -1, np.int16)
+        index[cells] = np.arange(len(cells))
+        distance = np.empty((len(cells), 5600), np.uint16)
+        code = library().oracle_distance_table(floor.ctypes.data, cells.ctypes.data, len(cells),
+                                               distance.ctypes.data)
+        assert code == 0
+        _FIXTURE = (header, kinds, floor, cells, index, distance)
+    return _FIXTURE
+
+
+def config_values(enemies):
+    """learn_env.py:67-70: [enemies, *header[:7], repair=1, *gdr, *kinds]."""
+    header, kinds = fixture()[:2]
+    ac = int(header[2]) // 100
+    gdr = [int((65536 * (ac + j)) ** 0.25) for j in range(2)]
+    return [enemies, *map(int, header[:7]), 1, *gdr, *map(int, kinds.reshape(-1))]
+
+
+class _Host:
+    """Host-memory env driven through a learn_*-shaped C entry table."""
+
+    def __init__(self, batch, enemies, seed, limit):
+        if not 1 <= enemies <= 8 or limit != 256:
+            raise ValueError('Supported: 1..8 enemies, fixed 256-decision deadline')
+        _, _, floor, cells, index, distance = fixture()
+        self.batch, self.enemies, self.limit = batch, enemies, limit
+        values = config_values(enemies)
+        self.config = (C.c_int * len(values))(*values)
+        self.arrays = [floor, cells, index, distance]
+        self.tables = Tables(floor.ctypes.data, cells.ctypes.data, index.ctypes.data, distance.ctypes.data,
+                             len(cells))
+        self.obs = np.zeros((batch, V1_OBS), np.float32)
+        self.mask = np.zeros((batch, V1_ACTIONS), np.float32)
+        self.out = np.zeros((batch, V1_OUT), np.float32)
+        self.actions = np.zeros(batch, np.int64)
+
+
+class OracleV1(_Host):
+    """The plain-C restatement of the reference default build."""
+
+    def __init__(self, batch=512, enemies=6, seed=0, limit=256):
+        super().__init__(batch, enemies, seed, limit)
+        self.lib = library()
+        self.state = np.zeros((batch, self.lib.oracle_v1_state_bytes()), np.uint8)
+        self.reset(seed)
+
+    def reset(self, seed):
+        code = self.lib.oracle_v1_init(self.state.ctypes.data, self.batch, C.byref(self.config),
+                                       C.byref(self.tables), seed, self.obs.ctypes.data, self.mask.ctypes.data)
+        assert code == 0
+        return self.obs
+
+    def step(self, actions, active=None):
+        actions = np.ascontiguousarray(actions, np.int64)
+        act = None if active is None else np.ascontiguousarray(active, np.uint8)
+        self.lib.oracle_v1_step(self.state.ctypes.data, self.batch, C.byref(self.config), C.byref(self.tables),
+                                actions.ctypes.data, self.limit, self.obs.ctypes.data, self.mask.ctypes.data,
+                                self.out.ctypes.data, None if act is None else act.ctypes.data)
+        return self.obs, self.out
+
+    def heuristic(self):
+        self.lib.oracle_v1_heuristic(self.state.ctypes.data, self.batch, C.byref(self.config),
+                                     C.byref(self.tables), self.actions.ctypes.data)
+        return self.actions
+
+    def compact(self):
+        rows = np.zeros((self.batch, V1_COMPACT), np.int64)
+        self.lib.oracle_v1_compact(self.state.ctypes.data, self.batch, rows.ctypes.data)
+        return rows
+
+    def semantic_test(self):
+        return self.lib.oracle_v1_semantic_test(C.byref(self.config), C.byref(self.tables))
+
+
+class ReferenceV1(_Host):
+    """The reference's own learn.cu host path (gpu=0), when built."""
+
+    def __init__(self, batch=512, enemies=6, seed=0, limit=256):
+        super().__init__(batch, enemies, seed, limit)
+        self.lib = reference_library()
+        if self.lib is None:
+            raise FileNotFoundError('oracle/_ref/learn_v1.so was not built')
+        self.state = np.zeros((batch, self.lib.learn_state_bytes()), np.uint8)
+        self.reset(seed)
+
+    def reset(self, seed):
+        code = self.lib.learn_init(self.state.ctypes.data, self.batch, C.byref(self.config), C.byref(self.tables),
+                                   seed, self.obs.ctypes.data, self.mask.ctypes.data, None, 0)
+        assert code == 0
+        return self.obs
+
+    def step(self, actions, active=None):
+        actions = np.ascontiguousarray(actions, np.int64)
+        if active is None:
+            self.lib.learn_step(self.state.ctypes.data, self.batch, C.byref(self.config), C.byref(self.tables),
+                                actions.ctypes.data, self.limit, self.obs.ctypes.data, self.mask.ctypes.data,
+                                self.out.ctypes.data, None, 0)
+        else:
+            act = np.ascontiguousarray(active, np.bool_)
+            self.lib.learn_step_active(self.state.ctypes.data, self.batch, C.byref(self.config),
+                                       C.byref(self.tables), actions.ctypes.data, self.limit, self.obs.ctypes.data,
+                                       self.mask.ctypes.data, self.out.ctypes.data, act.ctypes.data, None, 0)
+        return self.obs, self.out
+
+    def heuristic(self):
+        self.lib.learn_heuristic(self.state.ctypes.data, self.batch, C.byref(self.config), C.byref(self.tables),
+                                 self.actions.ctypes.data, None, 0)
+        return self.actions
+
+    def compact(self):
+        rows = np.zeros((self.batch, V1_COMPACT), np.int64)
+        code = library().oracle_v1_compact_from_reference(self.state.ctypes.data, self.batch,
+                                                          self.state.shape[1], rows.ctypes.data)
+        assert code == 0
+        return rows
+
+    def semantic_test(self):
+        return self.lib.learn_semantic_test(C.byref(self.config), C.byref(self.tables))
