@@ -44,13 +44,15 @@ __device__ __forceinline__ void load(const uint8_t *row, int lane, State &s) {
     s.rng.state = q[0];
     s.rng.inc = q[1];
     s.episode = q[2];
-    const int4 a = *reinterpret_cast<const int4 *>(row + 24 + 8);  // regen, blocks, player, ticks
-    s.hp = *reinterpret_cast<const int *>(row + 24);
-    s.regen = a.x;
-    s.blocks = a.y;
-    s.player = a.z;
-    s.ticks = a.w;
-    s.killed = *reinterpret_cast<const int *>(row + 44);
+    const int2 a = *reinterpret_cast<const int2 *>(row + 24);  // hp, regen
+    const int2 b = *reinterpret_cast<const int2 *>(row + 32);  // blocks, player
+    const int2 e = *reinterpret_cast<const int2 *>(row + 40);  // ticks, killed
+    s.hp = a.x;
+    s.regen = a.y;
+    s.blocks = b.x;
+    s.player = b.y;
+    s.ticks = e.x;
+    s.killed = e.y;
     const int16_t *m = reinterpret_cast<const int16_t *>(row + 48);
     int l = lane & 7;
     s.m_pos = m[l];
@@ -63,9 +65,9 @@ __device__ __forceinline__ void store(uint8_t *row, int lane, const State &s) {
         q[0] = s.rng.state;
         q[1] = s.rng.inc;
         q[2] = s.episode;
-        *reinterpret_cast<int *>(row + 24) = s.hp;
-        *reinterpret_cast<int4 *>(row + 32) = make_int4(s.regen, s.blocks, s.player, s.ticks);
-        *reinterpret_cast<int *>(row + 44) = s.killed;
+        *reinterpret_cast<int2 *>(row + 24) = make_int2(s.hp, s.regen);
+        *reinterpret_cast<int2 *>(row + 32) = make_int2(s.blocks, s.player);
+        *reinterpret_cast<int2 *>(row + 40) = make_int2(s.ticks, s.killed);
     }
     if (lane < ENEMIES) {
         int16_t *m = reinterpret_cast<int16_t *>(row + 48);

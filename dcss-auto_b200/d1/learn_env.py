@@ -88,7 +88,7 @@ class Env:
         self.state = torch.empty((batch, self.lib.learn_state_bytes()), dtype=torch.uint8, device=self.device)
         self.obs = torch.empty((batch, self.lib.learn_obs_size()), device=self.device)
         self.mask = torch.empty((batch, self.lib.learn_action_size()), device=self.device)
-        self.out = torch.empty((batch, self.lib.learn_out_size()), device=self.device)
+        self.out = torch.zeros((batch, self.lib.learn_out_size()), device=self.device)
         self.actions = torch.empty(batch, dtype=torch.int64, device=self.device)
         self.reset(seed)
 
