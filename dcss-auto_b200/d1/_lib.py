@@ -18,6 +18,13 @@ SIGNATURES = {
     'learn_semantic_test': [_P, _P],
     'learn_compact_state': [_P, _I, _P, _P],
     'learn_distance_table': [_P, _P, _I, _P, _P],
+    'd1_spec_state_bytes': [], 'd1_spec_obs_size': [], 'd1_spec_action_size': [], 'd1_spec_out_size': [],
+    'd1_spec_config_bytes': [],
+    'd1_spec_set_rays': [_P, _P, _P, _I],
+    'd1_spec_init': [_P, _I, _P, _U64, _I, _P, _P, _P],
+    'd1_spec_step': [_P, _I, _P, _P, _P, _P, _P, _P, _P],
+    'd1_spec_compact': [_P, _I, _P, _P],
+    'd1_spec_planes': [_P, _I, _P, _P, _P],
 }
 
 _LIB = None

@@ -1,0 +1,143 @@
+"""The BASELINE D:1 task on the B200 kernels (configs 0, 1 and 4).
+
+`SpecEnv` keeps the reference Env's shape -- `reset(seed)`, `step(actions,
+active=None) -> (obs, out)` and resident tensors -- with the spec task's
+buffers: obs bf16 [n, 1832] (one-hot 15x15 window x 8 channels + 32 scalars),
+legal u16 [n] (bit a set when action a is legal), out f32 [n, 10]. The
+observation can be written straight into a caller-provided buffer (a rollout
+slot) via `step(actions, obs_out=...)`.
+
+Env ids are global (`first_env + i`), so a shard of a multi-GPU run produces
+exactly the trajectories the same ids would produce on one GPU.
+"""
+import ctypes as C
+import pathlib
+
+import numpy as np
+import torch
+
+from ._lib import check, library
+
+DATA = pathlib.Path(__file__).resolve().parent / 'data'
+
+OBS, ACTIONS, OUT, COMPACT = 1832, 12, 10, 56
+ACTION_NAMES = ['N', 'E', 'S', 'W', 'NE', 'SE', 'SW', 'NW', 'wait', 'rest', 'attack', 'descend']
+
+
+class Kind(C.Structure):
+    _fields_ = [(k, C.c_int) for k in ('speed', 'damage', 'tohit', 'bypass')]
+
+
+class SpecConfig(C.Structure):
+    _fields_ = ([(k, C.c_int) for k in ('hp', 'ac100', 'ev100', 'sh100', 'shield_limit', 'regen')]
+                + [('gdr', C.c_int * 2)]
+                + [(k, C.c_int) for k in ('min_monsters', 'max_monsters', 'min_mhp', 'max_mhp', 'ogre', 'ogre_hp',
+                                          'ogre_min_damage', 'limit', 'explore_milli', 'kill_milli',
+                                          'descend_milli', 'death_milli')]
+                + [('kinds', Kind * 5)])
+
+
+def gdr_for(ac100):
+    """Cached GDR pair for AC = ac100 // 100 and +1 (gpu-d1/scripts/learn_env.py:67-68)."""
+    ac = ac100 // 100
+    return tuple(int((65536 * (ac + j)) ** 0.25) for j in range(2))
+
+
+# BASELINE config 0/1: player HP 15 AC 2 (EV, SH, shield limit and regeneration
+# from the reference fixture header), 3-10 monsters with HP 2-8 drawn from rat,
+# jackal, goblin and kobold; config 4 adds one sleeping ogre (HP 30, damage 2-17).
+# Kind rows are (speed, max damage, to-hit, bypass); rat, jackal and goblin are
+# the reference fixture's roster entries, kobold and ogre are added here.
+DEFAULT = dict(hp=15, ac100=200, ev100=794, sh100=906, shield_limit=2, regen=23, gdr=gdr_for(200),
+               min_monsters=3, max_monsters=10, min_mhp=2, max_mhp=8, ogre=0, ogre_hp=30, ogre_min_damage=2,
+               limit=512, explore_milli=2, kill_milli=1000, descend_milli=3000, death_milli=1000,
+               kinds=[(10, 3, 19, 15), (14, 3, 19, 15), (10, 1, 19, 15), (10, 4, 19, 15), (5, 17, 30, 25)])
+OGRE = dict(DEFAULT, ogre=1)
+
+
+def make_config(values=None):
+    values = dict(DEFAULT if values is None else values)
+    c = SpecConfig()
+    for k, v in values.items():
+        if k == 'gdr':
+            c.gdr[0], c.gdr[1] = v
+        elif k == 'kinds':
+            for i, kind in enumerate(v):
+                c.kinds[i] = Kind(*kind)
+        else:
+            setattr(c, k, int(v))
+    return c
+
+
+_RAYS = {}
+
+
+def device_rays(device):
+    """Register the native LOS ray fan with the library (once per device)."""
+    key = str(device)
+    if key not in _RAYS:
+        z = np.load(DATA / 'los_rays.npz')
+        blk = torch.from_numpy(z['blockers'].astype(np.uint64).view(np.int64)).to(device)
+        ex = torch.from_numpy(z['end_x'].astype(np.uint8)).to(device)
+        ey = torch.from_numpy(z['end_y'].astype(np.uint8)).to(device)
+        _RAYS[key] = (blk, ex, ey)
+    blk, ex, ey = _RAYS[key]
+    check(library().d1_spec_set_rays(blk.data_ptr(), ex.data_ptr(), ey.data_ptr(), blk.numel()), 'd1_spec_set_rays')
+    return _RAYS[key]
+
+
+class SpecEnv:
+    def __init__(self, batch, config=None, seed=0, first_env=0, device='cuda'):
+        self.device = torch.device('cuda:0' if device == 'cuda' else device)
+        if self.device.type != 'cuda':
+            raise ValueError('libd1 runs on CUDA devices only; use the oracle for CPU reference runs')
+        self.lib = library()
+        self.batch, self.first_env = batch, first_env
+        self.values = dict(DEFAULT if config is None else config)
+        self.config = make_config(self.values)
+        assert C.sizeof(self.config) == self.lib.d1_spec_config_bytes()
+        with torch.cuda.device(self.device):
+            self.rays = device_rays(self.device)
+        self.state = torch.empty((batch, self.lib.d1_spec_state_bytes()), dtype=torch.uint8, device=self.device)
+        self.obs = torch.empty((batch, OBS), dtype=torch.bfloat16, device=self.device)
+        self.legal = torch.empty(batch, dtype=torch.int16, device=self.device)  # u16 bits
+        self.out = torch.zeros((batch, OUT), device=self.device)
+        self.reset(seed)
+
+    @property
+    def stream(self):
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def reset(self, seed, obs_out=None):
+        obs = self.obs if obs_out is None else obs_out
+        check(self.lib.d1_spec_init(self.state.data_ptr(), self.batch, C.byref(self.config), seed, self.first_env,
+                                    obs.data_ptr(), self.legal.data_ptr(), self.stream), 'd1_spec_init')
+        return obs
+
+    def step(self, actions, active=None, obs_out=None):
+        assert actions.device == self.device and actions.dtype == torch.int64 and actions.is_contiguous()
+        act = 0
+        if active is not None:
+            assert active.device == self.device and active.dtype == torch.bool and active.shape == (self.batch,)
+            act = active.data_ptr()
+        obs = self.obs if obs_out is None else obs_out
+        check(self.lib.d1_spec_step(self.state.data_ptr(), self.batch, C.byref(self.config), actions.data_ptr(),
+                                    obs.data_ptr(), self.legal.data_ptr(), self.out.data_ptr(), act or None,
+                                    self.stream), 'd1_spec_step')
+        return obs, self.out
+
+    def legal_mask(self):
+        """Legal actions as a float [n, 12] mask (the reference's mask layout)."""
+        bits = self.legal.to(torch.int32) & 0xffff
+        return ((bits[:, None] >> torch.arange(ACTIONS, device=self.device)) & 1).float()
+
+    def compact(self):
+        rows = torch.empty((self.batch, COMPACT), dtype=torch.int64, device=self.device)
+        check(self.lib.d1_spec_compact(self.state.data_ptr(), self.batch, rows.data_ptr(), self.stream))
+        return rows
+
+    def planes(self):
+        f = torch.empty((self.batch, 210), dtype=torch.int32, device=self.device)
+        v = torch.empty((self.batch, 210), dtype=torch.int32, device=self.device)
+        check(self.lib.d1_spec_planes(self.state.data_ptr(), self.batch, f.data_ptr(), v.data_ptr(), self.stream))
+        return f, v

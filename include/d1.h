@@ -90,6 +90,55 @@ int learn_compact_state(const void *state, int n, int64_t *rows, void *stream);
  * floor u8[5600], cells i16[ncells] -> distance u16[ncells, 5600] (65535 = unreachable). */
 int learn_distance_table(const uint8_t *floor, const int16_t *cells, int ncells, uint16_t *distance, void *stream);
 
+
+/* ======================================================================
+ * BASELINE task ("spec"): generated 80x70 rooms+corridors maps, a per-env
+ * Philox4x32-10 stream keyed by the global env id, 12 semantic actions
+ * (0-7 move/attack N,E,S,W,NE,SE,SW,NW; 8 wait; 9 rest; 10 attack the weakest
+ * visible adjacent monster; 11 descend), 1832 bf16 observations (one-hot 15x15
+ * LOS window x 8 channels + 32 scalars), a u16 legal-action bit mask and 10
+ * outcome floats per env. No reference entry point exists for this task; its
+ * rules reuse the reference's (see each kernel's comments).
+ * ====================================================================== */
+typedef struct {
+    int hp, ac100, ev100, sh100, shield_limit, regen, gdr[2]; /* player */
+    int min_monsters, max_monsters, min_mhp, max_mhp;        /* regular monsters per episode, <= 10 */
+    int ogre, ogre_hp, ogre_min_damage;                       /* one sleeping ogre when ogre != 0 */
+    int limit;                                                /* physical-turn deadline */
+    int explore_milli, kill_milli, descend_milli, death_milli;
+    D1Kind kinds[5];                                          /* rat, jackal, goblin, kobold, ogre */
+} D1SpecConfig;
+
+/* 2048 */
+int d1_spec_state_bytes(void);
+/* 1832 */
+int d1_spec_obs_size(void);
+/* 12 */
+int d1_spec_action_size(void);
+/* 10: reward, done, descended, killed, hp, turns, death, timeout, elapsed turns, invalid */
+int d1_spec_out_size(void);
+/* sizeof(D1SpecConfig) */
+int d1_spec_config_bytes(void);
+/* Register the LOS ray fan (device arrays, kept by the caller for the library's
+ * lifetime): per ray a 64-bit blocker mask over the 8x8 quadrant and its end
+ * cell. Must be called before any other d1_spec_* compute call. */
+int d1_spec_set_rays(const unsigned long long *blockers, const uint8_t *end_x, const uint8_t *end_y, int n);
+/* Generate env i's first map from Philox(key = {first_env + i, lo32(seed)}),
+ * reset it and write its observation. state u8[n, 2048]; obs bf16[n, 1832];
+ * legal u16[n]. */
+int d1_spec_init(void *state, int n, const D1SpecConfig *c, uint64_t seed, int first_env, void *obs_bf16,
+                 uint16_t *legal, void *stream);
+/* One semantic decision per env with auto-reset; envs with active[i] == false
+ * (when active is not NULL) are left untouched. actions i64[n]; out f32[n, 10]. */
+int d1_spec_step(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, uint16_t *legal,
+                 float *out, const bool *active, void *stream);
+/* Canonical compact view, 56 x i64 per env: Philox draw count, env id, episode,
+ * hp, regen, blocks, player, turns, killed, stairs, monster count, floor seen,
+ * then pos[11], energy[11], hp[11], kind*2+awake[11]. */
+int d1_spec_compact(const void *state, int n, int64_t *rows, void *stream);
+/* Floor and remembered-cell bit planes, u32[n, 210] each (row y = words 3y..3y+2). */
+int d1_spec_planes(const void *state, int n, uint32_t *floor, uint32_t *viewed, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

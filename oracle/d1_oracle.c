@@ -511,3 +511,670 @@ int oracle_distance_table(const uint8_t *floor, const int16_t *cells, int ncells
     free(queue);
     return 0;
 }
+
+/* ================================================================== */
+/* spec task: the BASELINE configuration (generated maps, Philox,      */
+/* 12 semantic actions, one-hot 15x15x8 + 32 observation).             */
+/* Rules reused from the reference: sim.h:130-269 (melee, scheduler,   */
+/* pursuit, repair search), learn.cu:505-598 (player move/attack,      */
+/* regeneration, reward accounting), semantic-actions-v1 learn.cu      */
+/* :190-216 (15x15 LOS view, LOS+6-tile wake), :296-331 (reveal),      */
+/* :418-450 (attack-nearest, REST gating), :554-563 (sleep energy),    */
+/* d1-stairs-v2 learn.cu:732 (descend ends the episode with a clear).  */
+/* The generator, stream, action set and encoding have no reference:  */
+/* parity for those parts is against this restatement only.            */
+/* ================================================================== */
+#define PLANE 210
+#define MAXM OSPEC_MAXM
+
+static struct {
+    int n;
+    int ex[512], ey[512];
+    uint64_t blk[512];
+} RAYS;
+
+int oracle_set_rays(const int32_t *ex, const int32_t *ey, const uint64_t *blockers, int n) {
+    if (n < 0 || n > 512) return 1;
+    RAYS.n = n;
+    for (int i = 0; i < n; i++) {
+        RAYS.ex[i] = ex[i];
+        RAYS.ey[i] = ey[i];
+        RAYS.blk[i] = blockers[i];
+    }
+    return 0;
+}
+
+/* Philox4x32-10: ten rounds of the two 32x32->64 multiplies with the Weyl key
+ * schedule (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy as
+ * 1, 2, 3", SC'11). */
+void oracle_philox(const uint32_t in[4], const uint32_t key[2], uint32_t out[4]) {
+    uint32_t c0 = in[0], c1 = in[1], c2 = in[2], c3 = in[3], k0 = key[0], k1 = key[1];
+    for (int r = 0; r < 10; r++) {
+        if (r) {
+            k0 += 0x9E3779B9u;
+            k1 += 0xBB67AE85u;
+        }
+        uint64_t p0 = (uint64_t)0xD2511F53u * c0, p1 = (uint64_t)0xCD9E8D57u * c2;
+        uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0, n1 = (uint32_t)p1;
+        uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1, n3 = (uint32_t)p0;
+        c0 = n0;
+        c1 = n1;
+        c2 = n2;
+        c3 = n3;
+    }
+    out[0] = c0;
+    out[1] = c1;
+    out[2] = c2;
+    out[3] = c3;
+}
+
+typedef struct {
+    uint64_t ctr;              /* draws consumed from this env's stream */
+    uint32_t env, seed_lo, seed_hi, episode;
+    int hp, regen, blocks, player, ticks, killed, stairs, nmon, floor_seen;
+    int16_t pos[MAXM], energy[MAXM], mhp[MAXM];
+    uint8_t kind[MAXM], awake[MAXM];
+    uint32_t floor[PLANE], viewed[PLANE];
+    uint32_t vis[15];          /* derived: LOS window from the player, row dy+7, bit dx+7 */
+} Spec;
+
+int oracle_spec_state_bytes(void) { return (int)sizeof(Spec); }
+
+/* Draw n of env e under run seed s: word (n & 3) of
+ * Philox4x32-10(ctr = {lo(n>>2), hi(n>>2), hi(s), 0}, key = {e, lo(s)}). */
+static uint32_t spec_next(void *g) {
+    Spec *s = (Spec *)g;
+    uint64_t b = s->ctr >> 2;
+    uint32_t ctr[4] = {(uint32_t)b, (uint32_t)(b >> 32), s->seed_hi, 0}, key[2] = {s->env, s->seed_lo}, o[4];
+    oracle_philox(ctr, key, o);
+    uint32_t v = o[s->ctr & 3];
+    s->ctr++;
+    return v;
+}
+static int sr(Spec *s, int bound) { return rng_r(spec_next, s, bound); }
+
+static int bit_at(const uint32_t *plane, int p) {
+    int x = p % W, y = p / W;
+    return (plane[y * 3 + x / 32] >> (x % 32)) & 1;
+}
+static void bit_set(uint32_t *plane, int p) {
+    int x = p % W, y = p / W;
+    plane[y * 3 + x / 32] |= 1u << (x % 32);
+}
+static int sfloor(const Spec *s, int p) { return p >= 0 && p < N && bit_at(s->floor, p); }
+
+static void carve(Spec *s, int x0, int y0, int x1, int y1) {
+    if (x0 > x1) { int t = x0; x0 = x1; x1 = t; }
+    if (y0 > y1) { int t = y0; y0 = y1; y1 = t; }
+    for (int y = y0; y <= y1; y++)
+        for (int x = x0; x <= x1; x++) bit_set(s->floor, y * W + x);
+}
+
+/* 4-9 rooms with sides 4-12 inside the one-cell wall border; room k is joined to
+ * room k-1 by an L corridor between their centres, horizontal-first or
+ * vertical-first by a coin flip. */
+static void spec_gen_map(Spec *s) {
+    memset(s->floor, 0, sizeof s->floor);
+    int rooms = 4 + sr(s, 6), pcx = 0, pcy = 0;
+    for (int k = 0; k < rooms; k++) {
+        int w = 4 + sr(s, 9), h = 4 + sr(s, 9);
+        int x0 = 1 + sr(s, W - w - 1), y0 = 1 + sr(s, H - h - 1);
+        carve(s, x0, y0, x0 + w - 1, y0 + h - 1);
+        int cx = x0 + w / 2, cy = y0 + h / 2;
+        if (k > 0) {
+            if (sr(s, 2) == 0) {
+                carve(s, pcx, pcy, cx, pcy);
+                carve(s, cx, pcy, cx, cy);
+            } else {
+                carve(s, pcx, pcy, pcx, cy);
+                carve(s, pcx, cy, cx, cy);
+            }
+        }
+        pcx = cx;
+        pcy = cy;
+    }
+}
+
+static int popc32(uint32_t v) { return __builtin_popcount(v); }
+static int floor_count(const Spec *s) {
+    int n = 0;
+    for (int w = 0; w < PLANE; w++) n += popc32(s->floor[w]);
+    return n;
+}
+/* The k-th floor cell in row-major order. */
+static int kth_floor(const Spec *s, int k) {
+    for (int w = 0; w < PLANE; w++) {
+        int c = popc32(s->floor[w]);
+        if (k < c) {
+            uint32_t v = s->floor[w];
+            for (int b = 0; b < 32; b++)
+                if ((v >> b) & 1) {
+                    if (k == 0) return (w / 3) * W + (w % 3) * 32 + b;
+                    k--;
+                }
+        }
+        k -= c;
+    }
+    return -1;
+}
+
+static int s_occupant(const Spec *s, int p) {
+    for (int i = 0; i < s->nmon; i++)
+        if (s->mhp[i] > 0 && s->pos[i] == p) return i;
+    return -1;
+}
+
+/* Native ray-fan LOS (gpu-d1/scripts/compile_corpus.py:67-81): per quadrant, a
+ * ray dies when any in-map wall lies on it; live rays reveal their end cell when
+ * that cell is on the map. The origin is always seen. */
+static void los_core(const uint8_t *floor_u8, const uint32_t *floor_bits, int origin, uint32_t vis[15]) {
+    static const int SX[4] = {1, -1, -1, 1}, SY[4] = {1, 1, -1, -1};
+    int px = origin % W, py = origin / W;
+    memset(vis, 0, 15 * sizeof(uint32_t));
+    vis[7] |= 1u << 7;
+    for (int q = 0; q < 4; q++) {
+        uint64_t opq = 0;
+        for (int y = 0; y < 8; y++)
+            for (int x = 0; x < 8; x++) {
+                int cx = px + SX[q] * x, cy = py + SY[q] * y;
+                if (cx < 0 || cx >= W || cy < 0 || cy >= H) continue;
+                int p = cy * W + cx;
+                int fl = floor_u8 ? floor_u8[p] != 0 : bit_at(floor_bits, p);
+                if (!fl) opq |= 1ull << (y * 8 + x);
+            }
+        for (int r = 0; r < RAYS.n; r++) {
+            if (RAYS.blk[r] & opq) continue;
+            int cx = px + SX[q] * RAYS.ex[r], cy = py + SY[q] * RAYS.ey[r];
+            if (cx < 0 || cx >= W || cy < 0 || cy >= H) continue;
+            vis[SY[q] * RAYS.ey[r] + 7] |= 1u << (SX[q] * RAYS.ex[r] + 7);
+        }
+    }
+}
+
+int oracle_los_mask(const uint8_t *floor, int origin, uint32_t *mask10) {
+    uint32_t vis[15];
+    if (RAYS.n == 0) return 1;
+    los_core(floor, NULL, origin, vis);
+    memset(mask10, 0, 10 * sizeof(uint32_t));
+    for (int dy = -7; dy <= 7; dy++)
+        for (int dx = -7; dx <= 7; dx++)
+            if ((vis[dy + 7] >> (dx + 7)) & 1) {
+                int bit = (dy + 8) * 17 + dx + 8;
+                mask10[bit / 32] |= 1u << (bit % 32);
+            }
+    return 0;
+}
+
+static void spec_los(Spec *s) { los_core(NULL, s->floor, s->player, s->vis); }
+static int s_visible(const Spec *s, int p) {
+    int dx = p % W - s->player % W, dy = p / W - s->player / W;
+    if (dx < -7 || dx > 7 || dy < -7 || dy > 7) return 0;
+    return (s->vis[dy + 7] >> (dx + 7)) & 1;
+}
+/* Mark every visible cell remembered; count newly seen floor (semantic-actions-v1
+ * learn.cu:296-331 with MARK_WALLS: `seen` is `viewed` restricted to floor). */
+static int spec_reveal(Spec *s) {
+    int newly = 0;
+    for (int dy = -7; dy <= 7; dy++)
+        for (int dx = -7; dx <= 7; dx++) {
+            if (!((s->vis[dy + 7] >> (dx + 7)) & 1)) continue;
+            int p = (s->player / W + dy) * W + s->player % W + dx;
+            if (bit_at(s->viewed, p)) continue;
+            bit_set(s->viewed, p);
+            if (bit_at(s->floor, p)) newly++;
+        }
+    s->floor_seen += newly;
+    return newly;
+}
+static int s_visible_awake(const Spec *s) {
+    for (int i = 0; i < s->nmon; i++)
+        if (s->mhp[i] > 0 && s->awake[i] && s_visible(s, s->pos[i])) return 1;
+    return 0;
+}
+/* semantic-actions-v1 learn.cu:423-428: weakest visible adjacent monster, first
+ * compass direction on ties. */
+static int s_adjacent_attack(const Spec *s) {
+    int best = -1, hp = 100000;
+    for (int d = 0; d < 8; d++) {
+        int p = neighbor(s->player, d);
+        if (p < 0) continue;
+        int id = s_occupant(s, p);
+        if (id >= 0 && s->mhp[id] > 0 && s_visible(s, p) && s->mhp[id] < hp) {
+            hp = s->mhp[id];
+            best = d;
+        }
+    }
+    return best;
+}
+
+static void spec_reset(Spec *s, const D1SpecConfig *c) {
+    spec_gen_map(s);
+    int nf = floor_count(s);
+    s->stairs = kth_floor(s, sr(s, nf));
+    int tries = 0;
+    do { s->player = kth_floor(s, sr(s, nf)); } while (s->player == s->stairs && ++tries < 4096);
+    for (int i = 0; i < MAXM; i++) {
+        s->pos[i] = 0;
+        s->energy[i] = 0;
+        s->mhp[i] = 0;
+        s->kind[i] = 0;
+        s->awake[i] = 0;
+    }
+    s->nmon = 0;
+    int target = c->min_monsters + sr(s, c->max_monsters - c->min_monsters + 1);
+    for (int i = 0; i < target; i++) {
+        int kind = sr(s, 4), hp = c->min_mhp + sr(s, c->max_mhp - c->min_mhp + 1), p, bad;
+        tries = 0;
+        do {
+            p = kth_floor(s, sr(s, nf));
+            bad = p == s->player || p == s->stairs || s_occupant(s, p) >= 0;
+        } while (bad && ++tries < 4096);
+        if (bad) break;
+        s->pos[i] = (int16_t)p;
+        s->mhp[i] = (int16_t)hp;
+        s->kind[i] = (uint8_t)kind;
+        s->energy[i] = (int16_t)(70 + sr(s, 10));
+        s->awake[i] = 0;
+        s->nmon = i + 1;
+    }
+    if (c->ogre) {
+        for (int t = 0; t < 64; t++) {
+            int p = kth_floor(s, sr(s, nf));
+            if (cheb(p, s->player) >= 12 && p != s->stairs && s_occupant(s, p) < 0) {
+                int i = s->nmon++;
+                s->pos[i] = (int16_t)p;
+                s->mhp[i] = (int16_t)c->ogre_hp;
+                s->kind[i] = 4;
+                s->energy[i] = (int16_t)(70 + sr(s, 10));
+                s->awake[i] = 0;
+                break;
+            }
+        }
+    }
+    s->hp = c->hp;
+    s->regen = 0;
+    s->blocks = 0;
+    s->ticks = 0;
+    s->killed = 0;
+    s->floor_seen = 0;
+    memset(s->viewed, 0, sizeof s->viewed);
+    spec_los(s);
+    spec_reveal(s); /* the first view earns no reward */
+}
+
+/* Full FIFO BFS from the player over 8-neighbour floor (the distance field the
+ * reference precomputes per player cell, learn.cu:168-176). */
+static void spec_bfs(const Spec *s, uint16_t *ds) {
+    static int queue[N];
+    for (int p = 0; p < N; p++) ds[p] = 65535;
+    int head = 0, tail = 0;
+    ds[s->player] = 0;
+    queue[tail++] = s->player;
+    while (head < tail) {
+        int p = queue[head++];
+        for (int d = 0; d < 8; d++) {
+            int q = neighbor(p, d);
+            if (q >= 0 && bit_at(s->floor, q) && ds[q] == 65535) {
+                ds[q] = (uint16_t)(ds[p] + 1);
+                queue[tail++] = q;
+            }
+        }
+    }
+}
+
+/* sim.h:207-253 on the generated map. */
+static int spec_choose_move(Spec *s, const uint16_t *dist, int id) {
+    int p = s->pos[id], best = -1, bd = dist[p], ties = 0, rotation = sr(s, 4);
+    for (int z = 0; z < 8; z++) {
+        int d = z < 4 ? (z + rotation) % 4 : 4 + (z + rotation) % 4;
+        int q = neighbor(p, d);
+        if (q < 0 || !bit_at(s->floor, q) || q == s->player || s_occupant(s, q) >= 0) continue;
+        int dq = dist[q];
+        if (dq < bd) {
+            bd = dq;
+            best = q;
+            ties = 1;
+        } else if (dq == bd && best >= 0 && sr(s, ++ties) == 0)
+            best = q;
+    }
+    if (best >= 0) return best;
+    int cells[24], first[24], len = 1;
+    cells[0] = p;
+    first[0] = -1;
+    for (int head = 0; head < len; head++)
+        for (int d = 0; d < 8; d++) {
+            int q = neighbor(cells[head], d);
+            if (q < 0 || !bit_at(s->floor, q) || q == s->player || s_occupant(s, q) >= 0) continue;
+            int seen = 0;
+            for (int j = 0; j < len; j++)
+                if (cells[j] == q) { seen = 1; break; }
+            if (seen) continue;
+            int step = head == 0 ? q : first[head];
+            if (dist[q] < dist[p]) return step;
+            if (len < 24) {
+                cells[len] = q;
+                first[len] = step;
+                len++;
+            }
+        }
+    return -1;
+}
+
+static void spec_act(Spec *s, const D1SpecConfig *c, const uint16_t *dist, int id) {
+    s->energy[id] -= 10;
+    if (cheb(s->pos[id], s->player) == 1) {
+        const D1Kind *k = &c->kinds[s->kind[id]];
+        int dmin = s->kind[id] == 4 ? c->ogre_min_damage : 1;
+        D1Config pc;
+        memset(&pc, 0, sizeof pc);
+        pc.ev100 = c->ev100;
+        pc.sh100 = c->sh100;
+        pc.ac100 = c->ac100;
+        pc.shield_limit = c->shield_limit;
+        pc.gdr[0] = c->gdr[0];
+        pc.gdr[1] = c->gdr[1];
+        D1Kind kk = *k;
+        /* incoming_attack rolls 1 + r(damage); the ogre's range starts at dmin. */
+        if (dmin == 1) {
+            incoming_attack(spec_next, s, &pc, &kk, &s->hp, &s->blocks);
+        } else {
+            /* sim.h:130-163 with damage = dmin + r(damage - dmin + 1). */
+            Next32 nx = spec_next;
+            int hit = rng_r(nx, s, kk.tohit + 1);
+            int ev = rng_round(nx, s, pc.ev100, 100);
+            ev = rng_avg(nx, s, 2 * ev);
+            int margin = hit - ev;
+            if (rng_r(nx, s, 100) < 5) margin = (rng_r(nx, s, 2) ? 1 : -1) * 1000;
+            int bypass = rng_r(nx, s, kk.bypass);
+            int sh = rng_round(nx, s, pc.sh100, 100);
+            int block = rng_avg(nx, s, sh * 2) / 3 - 1;
+            if (block >= bypass && s->blocks < pc.shield_limit) {
+                s->blocks++;
+                return;
+            }
+            if (margin < 0) return;
+            int damage = dmin + rng_r(nx, s, kk.damage - dmin + 1);
+            int ac = rng_round(nx, s, pc.ac100, 100);
+            int gac = rng_round(nx, s, pc.ac100, 100);
+            int gdr = pc.gdr[gac - pc.ac100 / 100];
+            int saved = rng_r(nx, s, ac + 1);
+            int half = rng_round(nx, s, ac, 2);
+            saved = mx(saved, mn(gdr * kk.damage / 100, half));
+            damage = mx(0, damage - saved);
+            s->hp -= damage;
+        }
+        return;
+    }
+    int q = spec_choose_move(s, dist, id);
+    if (q >= 0) s->pos[id] = (int16_t)q;
+}
+
+static int spec_scan(const Spec *s) {
+    int best = -1;
+    for (int i = 0; i < s->nmon; i++)
+        if (s->energy[i] >= 80 &&
+            (best < 0 || s->energy[i] > s->energy[best] || (s->energy[i] == s->energy[best] && i < best)))
+            best = i;
+    return best;
+}
+
+enum { PRIM_WAIT = 8, PRIM_DESCEND = 9 };
+typedef struct { float reward; int done, descended, death, timeout; } Prim;
+
+/* One physical turn: learn.cu:505-598 with the sleep/exploration variants of
+ * semantic-actions-v1 learn.cu:638-730 and the stairs clear of d1-stairs-v2. */
+static Prim spec_primitive(Spec *s, const D1SpecConfig *c, int d) {
+    static uint16_t dist[N];
+    Prim r = {0};
+    int reward_milli = -1;
+    s->blocks = 0;
+    s->regen += c->regen;
+    while (s->regen >= 100) {
+        s->hp = mn(c->hp, s->hp + 1);
+        s->regen -= 100;
+    }
+    if (d >= 0 && d < 8) {
+        int p = neighbor(s->player, d);
+        if (sfloor(s, p)) {
+            int id = s_occupant(s, p);
+            if (id >= 0) {
+                if (sr(s, 5) != 0) {
+                    s->mhp[id] = (int16_t)(s->mhp[id] - (1 + sr(s, 4)));
+                    if (s->mhp[id] <= 0) {
+                        s->mhp[id] = 0;
+                        s->energy[id] = -30000;
+                        s->killed++;
+                        reward_milli += c->kill_milli;
+                    }
+                }
+            } else {
+                s->player = p;
+                spec_los(s);
+            }
+        }
+    }
+    int descended = d == PRIM_DESCEND && s->player == s->stairs && s->hp > 0;
+    reward_milli += c->explore_milli * spec_reveal(s);
+    if (!descended) {
+        for (int i = 0; i < s->nmon; i++)
+            if (s->mhp[i] > 0 && !s->awake[i] && cheb(s->pos[i], s->player) <= 6 && s_visible(s, s->pos[i])) {
+                s->awake[i] = 1;
+                s->energy[i] = 70;
+            }
+        for (int i = 0; i < s->nmon; i++)
+            if (s->mhp[i] > 0 && !s->awake[i]) s->energy[i] = -30000;
+        for (int i = 0; i < s->nmon; i++)
+            if (s->mhp[i] > 0) s->energy[i] = (int16_t)(s->energy[i] + c->kinds[s->kind[i]].speed);
+        spec_bfs(s, dist);
+        while (s->hp > 0) {
+            int id = spec_scan(s);
+            if (id < 0) break;
+            spec_act(s, c, dist, id);
+        }
+    }
+    s->ticks++;
+    int death = s->hp <= 0, timeout = !descended && !death && s->ticks >= c->limit;
+    if (descended) reward_milli += c->descend_milli;
+    if (death) reward_milli -= c->death_milli;
+    r.reward = 0.001f * (float)reward_milli;
+    r.done = descended || death || timeout;
+    r.descended = descended;
+    r.death = death;
+    r.timeout = timeout;
+    return r;
+}
+
+/* Actions: 0-7 move/attack N,E,S,W,NE,SE,SW,NW; 8 wait; 9 rest; 10 attack the
+ * weakest visible adjacent monster; 11 descend. An action that is not legal
+ * becomes one wait turn and is flagged invalid. REST repeats wait turns until HP
+ * is full, an awake monster is in view, or the episode ends. */
+static void spec_decision(Spec *s, const D1SpecConfig *c, int a, float *out) {
+    float total = 0.f;
+    int elapsed = 0, invalid = 0;
+    Prim r;
+    for (;;) {
+        int d = PRIM_WAIT;
+        if (a >= 0 && a < 8) d = a;
+        else if (a == 8) d = PRIM_WAIT;
+        else if (a == 9) invalid = s->hp >= c->hp || s_visible_awake(s) || c->regen <= 0;
+        else if (a == 10) {
+            d = s_adjacent_attack(s);
+            if (d < 0) {
+                d = PRIM_WAIT;
+                invalid = 1;
+            }
+        } else if (a == 11) {
+            if (s->player == s->stairs) d = PRIM_DESCEND;
+            else invalid = 1;
+        } else
+            invalid = 1;
+        r = spec_primitive(s, c, d);
+        elapsed++;
+        total += r.reward;
+        if (r.done || invalid || a != 9) break;
+        if (s->hp >= c->hp || s_visible_awake(s)) break;
+    }
+    out[0] = total;
+    out[1] = (float)r.done;
+    out[2] = (float)r.descended;
+    out[3] = (float)s->killed;
+    out[4] = (float)mx(0, s->hp);
+    out[5] = (float)s->ticks;
+    out[6] = (float)r.death;
+    out[7] = (float)r.timeout;
+    out[8] = (float)elapsed;
+    out[9] = (float)invalid;
+    if (r.done) {
+        s->episode++;
+        spec_reset(s, c);
+    }
+}
+
+/* One-hot channel per 15x15 window cell: 0 unknown/off-map, 1 remembered wall,
+ * 2 remembered floor out of view, 3 visible floor, 4 stairs, 5 visible sleeping
+ * monster, 6 visible awake monster, 7 visible ogre. Then 32 scalars. */
+static void spec_observe(const Spec *s, const D1SpecConfig *c, float *o, uint16_t *legal) {
+    const int px = s->player % W, py = s->player / W;
+    for (int j = 0; j < OSPEC_OBS; j++) o[j] = 0;
+    for (int wy = 0; wy < 15; wy++)
+        for (int wx = 0; wx < 15; wx++) {
+            int cx = px + wx - 7, cy = py + wy - 7, ch = 0;
+            if (cx >= 0 && cx < W && cy >= 0 && cy < H) {
+                int p = cy * W + cx;
+                if (bit_at(s->viewed, p)) {
+                    if (!bit_at(s->floor, p)) ch = 1;
+                    else {
+                        int vis = (s->vis[wy] >> wx) & 1, id = vis ? s_occupant(s, p) : -1;
+                        if (id >= 0) ch = s->kind[id] == 4 ? 7 : s->awake[id] ? 6 : 5;
+                        else if (p == s->stairs) ch = 4;
+                        else ch = vis ? 3 : 2;
+                    }
+                }
+            }
+            o[(wy * 15 + wx) * 8 + ch] = 1.f;
+        }
+    float *f = o + 1800;
+    int nvis = 0, nvis_awake = 0, near = -1, neard = 1000, nadj = 0, weakest = 0, ogre = -1;
+    for (int i = 0; i < s->nmon; i++) {
+        if (s->mhp[i] <= 0 || !s_visible(s, s->pos[i])) continue;
+        nvis++;
+        nvis_awake += s->awake[i];
+        int d = cheb(s->pos[i], s->player);
+        if (d < neard) {
+            neard = d;
+            near = i;
+        }
+        if (d == 1) {
+            nadj++;
+            if (weakest == 0 || s->mhp[i] < weakest) weakest = s->mhp[i];
+        }
+        if (s->kind[i] == 4) ogre = i;
+    }
+    int rest_ok = s->hp < c->hp && c->regen > 0 && !s_visible_awake(s);
+    int attack_ok = s_adjacent_attack(s) >= 0;
+    int known = bit_at(s->viewed, s->stairs);
+    f[0] = s->hp / (float)c->hp;
+    f[1] = s->regen / 100.f;
+    f[2] = s->ticks / (float)c->limit;
+    f[3] = s->killed / 10.f;
+    f[4] = px / 80.f;
+    f[5] = py / 70.f;
+    f[6] = nvis / 10.f;
+    f[7] = nvis_awake / 10.f;
+    if (near >= 0) {
+        f[8] = 1.f;
+        f[9] = (s->pos[near] % W - px) / 7.f;
+        f[10] = (s->pos[near] / W - py) / 7.f;
+        f[11] = s->mhp[near] / 16.f;
+        f[12] = (float)s->awake[near];
+        f[13] = s->kind[near] / 4.f;
+    }
+    f[14] = (float)known;
+    if (known) {
+        f[15] = (s->stairs % W - px) / 80.f;
+        f[16] = (s->stairs / W - py) / 70.f;
+    }
+    f[17] = (float)(s->player == s->stairs);
+    f[18] = nadj / 8.f;
+    f[19] = weakest / 16.f;
+    f[20] = (float)rest_ok;
+    f[21] = (float)attack_ok;
+    f[22] = s->floor_seen / 1024.f;
+    f[23] = s->blocks / 2.f;
+    f[24] = 1.f;
+    if (ogre >= 0) {
+        f[25] = 1.f;
+        f[26] = (s->pos[ogre] % W - px) / 7.f;
+        f[27] = (s->pos[ogre] / W - py) / 7.f;
+        f[28] = (float)s->awake[ogre];
+        f[29] = s->mhp[ogre] / 30.f;
+    }
+    uint16_t bits = 1u << 8;
+    for (int d = 0; d < 8; d++)
+        if (sfloor(s, neighbor(s->player, d))) bits |= (uint16_t)(1u << d);
+    if (rest_ok) bits |= 1u << 9;
+    if (attack_ok) bits |= 1u << 10;
+    if (s->player == s->stairs) bits |= 1u << 11;
+    *legal = bits;
+}
+
+int oracle_spec_init(void *states, int n, const D1SpecConfig *c, uint64_t seed, int first_env, float *obs,
+                     uint16_t *legal) {
+    Spec *s = (Spec *)states;
+    if (RAYS.n == 0 || c->max_monsters > 10 || c->min_monsters < 0 || c->min_monsters > c->max_monsters) return 1;
+    for (int i = 0; i < n; i++) {
+        memset(&s[i], 0, sizeof(Spec));
+        s[i].env = (uint32_t)(first_env + i);
+        s[i].seed_lo = (uint32_t)seed;
+        s[i].seed_hi = (uint32_t)(seed >> 32);
+        spec_reset(&s[i], c);
+        spec_observe(&s[i], c, obs + (size_t)i * OSPEC_OBS, legal + i);
+    }
+    return 0;
+}
+
+int oracle_spec_step(void *states, int n, const D1SpecConfig *c, const int64_t *actions, float *obs, uint16_t *legal,
+                     float *out) {
+    Spec *s = (Spec *)states;
+    for (int i = 0; i < n; i++) {
+        spec_decision(&s[i], c, (int)actions[i], out + (size_t)i * OSPEC_OUT);
+        spec_observe(&s[i], c, obs + (size_t)i * OSPEC_OBS, legal + i);
+    }
+    return 0;
+}
+
+int oracle_spec_compact(const void *states, int n, int64_t *rows) {
+    const Spec *s = (const Spec *)states;
+    for (int i = 0; i < n; i++) {
+        int64_t *r = rows + (size_t)i * OSPEC_COMPACT;
+        const Spec *e = &s[i];
+        r[0] = (int64_t)e->ctr;
+        r[1] = e->env;
+        r[2] = e->episode;
+        r[3] = e->hp;
+        r[4] = e->regen;
+        r[5] = e->blocks;
+        r[6] = e->player;
+        r[7] = e->ticks;
+        r[8] = e->killed;
+        r[9] = e->stairs;
+        r[10] = e->nmon;
+        r[11] = e->floor_seen;
+        for (int k = 0; k < MAXM; k++) {
+            r[12 + k] = e->pos[k];
+            r[23 + k] = e->energy[k];
+            r[34 + k] = e->mhp[k];
+            r[45 + k] = e->kind[k] * 2 + e->awake[k];
+        }
+    }
+    return 0;
+}
+
+int oracle_spec_planes(const void *states, int n, uint32_t *floor, uint32_t *viewed) {
+    const Spec *s = (const Spec *)states;
+    for (int i = 0; i < n; i++) {
+        memcpy(floor + (size_t)i * PLANE, s[i].floor, sizeof s[i].floor);
+        memcpy(viewed + (size_t)i * PLANE, s[i].viewed, sizeof s[i].viewed);
+    }
+    return 0;
+}

@@ -53,6 +53,38 @@ int oracle_v1_semantic_test(const D1Config *c, const D1Tables *t);
 /* Host all-pairs BFS distance table, the restatement of gpu-d1/scripts/learn_env.py:25-39. */
 int oracle_distance_table(const uint8_t *floor, const int16_t *cells, int ncells, uint16_t *distance);
 
+
+/* ---- spec (BASELINE task) ---- */
+typedef struct {
+    int hp, ac100, ev100, sh100, shield_limit, regen, gdr[2]; /* player */
+    int min_monsters, max_monsters, min_mhp, max_mhp;        /* regular monsters per episode */
+    int ogre, ogre_hp, ogre_min_damage;                       /* one sleeping ogre when ogre != 0 */
+    int limit;                                                /* physical-turn deadline */
+    int explore_milli, kill_milli, descend_milli, death_milli;
+    D1Kind kinds[5];                                          /* rat, jackal, goblin, kobold, ogre */
+} D1SpecConfig;
+enum { OSPEC_MAXM = 11, OSPEC_OBS = 1832, OSPEC_ACTIONS = 12, OSPEC_OUT = 10, OSPEC_COMPACT = 56 };
+/* The native LOS ray fan: n rays ending at (ex, ey) in the 8x8 quadrant, blocked
+ * by any opaque cell in `blockers` (bit y*8+x). Must be set before any spec call. */
+int oracle_set_rays(const int32_t *ex, const int32_t *ey, const uint64_t *blockers, int n);
+/* LOS from `origin` on a u8[5600] floor map, in the reference's 17x17 mask format
+ * (bit (dy+8)*17 + dx+8, 10 x u32), for pinning against native LOS tables. */
+int oracle_los_mask(const uint8_t *floor, int origin, uint32_t *mask10);
+/* Philox4x32-10 block (Salmon et al., SC'11): out = philox(ctr, key). */
+void oracle_philox(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
+int oracle_spec_state_bytes(void);
+/* env ids are `first_env + i`; obs is float [n, 1832]; legal is u16 [n] bits. */
+int oracle_spec_init(void *states, int n, const D1SpecConfig *c, uint64_t seed, int first_env, float *obs,
+                     uint16_t *legal);
+int oracle_spec_step(void *states, int n, const D1SpecConfig *c, const int64_t *actions, float *obs, uint16_t *legal,
+                     float *out);
+/* 56 x int64 per env: ctr, env, episode, hp, regen, blocks, player, ticks, killed,
+ * stairs, nmon, floor_seen, then pos[11], energy[11], hp[11], kind*2+awake [11].
+ */
+int oracle_spec_compact(const void *states, int n, int64_t *rows);
+/* Copies the floor and remembered (viewed) bit planes, u32[n, 210] each. */
+int oracle_spec_planes(const void *states, int n, uint32_t *floor, uint32_t *viewed);
+
 #ifdef __cplusplus
 }
 #endif

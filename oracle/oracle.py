@@ -201,3 +201,111 @@ class ReferenceV1(_Host):
 
     def semantic_test(self):
         return self.lib.learn_semantic_test(C.byref(self.config), C.byref(self.tables))
+
+
+# ---------------------------------------------------------------------------
+# spec task: generated maps, Philox, 12 semantic actions
+# ---------------------------------------------------------------------------
+SPEC_OBS, SPEC_ACTIONS, SPEC_OUT, SPEC_COMPACT, SPEC_MAXM = 1832, 12, 10, 56, 11
+
+
+class Kind(C.Structure):
+    _fields_ = [(k, C.c_int) for k in ('speed', 'damage', 'tohit', 'bypass')]
+
+
+class SpecConfig(C.Structure):
+    _fields_ = ([(k, C.c_int) for k in ('hp', 'ac100', 'ev100', 'sh100', 'shield_limit', 'regen')]
+                + [('gdr', C.c_int * 2)]
+                + [(k, C.c_int) for k in ('min_monsters', 'max_monsters', 'min_mhp', 'max_mhp', 'ogre', 'ogre_hp',
+                                          'ogre_min_damage', 'limit', 'explore_milli', 'kill_milli',
+                                          'descend_milli', 'death_milli')]
+                + [('kinds', Kind * 5)])
+
+
+def spec_config(values):
+    """Build the C struct from a dict with the SpecConfig field names."""
+    c = SpecConfig()
+    for k, v in values.items():
+        if k == 'gdr':
+            c.gdr[0], c.gdr[1] = v
+        elif k == 'kinds':
+            for i, kind in enumerate(v):
+                c.kinds[i] = Kind(*kind)
+        else:
+            setattr(c, k, int(v))
+    return c
+
+
+_RAYS_SET = False
+
+
+def rays():
+    z = np.load(DATA / 'los_rays.npz')
+    return z['end_x'].astype(np.int32), z['end_y'].astype(np.int32), z['blockers'].astype(np.uint64)
+
+
+def spec_library():
+    global _RAYS_SET
+    lib = library()
+    if not _RAYS_SET:
+        p, i = C.c_void_p, C.c_int
+        lib.oracle_set_rays.argtypes = [p, p, p, i]
+        lib.oracle_los_mask.argtypes = [p, i, p]
+        lib.oracle_philox.argtypes = [p, p, p]
+        lib.oracle_philox.restype = None
+        lib.oracle_spec_init.argtypes = [p, i, p, C.c_uint64, i, p, p]
+        lib.oracle_spec_step.argtypes = [p, i, p, p, p, p, p]
+        lib.oracle_spec_compact.argtypes = [p, i, p]
+        lib.oracle_spec_planes.argtypes = [p, i, p, p]
+        ex, ey, blk = rays()
+        lib._rays_keep = (ex, ey, blk)
+        assert lib.oracle_set_rays(ex.ctypes.data, ey.ctypes.data, blk.ctypes.data, len(ex)) == 0
+        _RAYS_SET = True
+    return lib
+
+
+def los_mask(floor_u8, origin):
+    out = np.zeros(10, np.uint32)
+    assert spec_library().oracle_los_mask(np.ascontiguousarray(floor_u8, np.uint8).ctypes.data, origin,
+                                          out.ctypes.data) == 0
+    return out
+
+
+def philox(ctr, key):
+    ctr = np.ascontiguousarray(ctr, np.uint32)
+    key = np.ascontiguousarray(key, np.uint32)
+    out = np.zeros(4, np.uint32)
+    spec_library().oracle_philox(ctr.ctypes.data, key.ctypes.data, out.ctypes.data)
+    return out
+
+
+class OracleSpec:
+    """CPU restatement of the spec task; float obs [n, 1832], u16 legal bits [n]."""
+
+    def __init__(self, batch, config, seed=0, first_env=0):
+        self.lib = spec_library()
+        self.batch = batch
+        self.config = spec_config(config)
+        self.state = np.zeros((batch, self.lib.oracle_spec_state_bytes()), np.uint8)
+        self.obs = np.zeros((batch, SPEC_OBS), np.float32)
+        self.legal = np.zeros(batch, np.uint16)
+        self.out = np.zeros((batch, SPEC_OUT), np.float32)
+        assert self.lib.oracle_spec_init(self.state.ctypes.data, batch, C.byref(self.config), seed, first_env,
+                                         self.obs.ctypes.data, self.legal.ctypes.data) == 0
+
+    def step(self, actions):
+        actions = np.ascontiguousarray(actions, np.int64)
+        self.lib.oracle_spec_step(self.state.ctypes.data, self.batch, C.byref(self.config), actions.ctypes.data,
+                                  self.obs.ctypes.data, self.legal.ctypes.data, self.out.ctypes.data)
+        return self.obs, self.out
+
+    def compact(self):
+        rows = np.zeros((self.batch, SPEC_COMPACT), np.int64)
+        self.lib.oracle_spec_compact(self.state.ctypes.data, self.batch, rows.ctypes.data)
+        return rows
+
+    def planes(self):
+        f = np.zeros((self.batch, 210), np.uint32)
+        v = np.zeros((self.batch, 210), np.uint32)
+        self.lib.oracle_spec_planes(self.state.ctypes.data, self.batch, f.ctypes.data, v.ctypes.data)
+        return f, v
