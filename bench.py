@@ -1,0 +1,314 @@
+#!/usr/bin/env python3
+"""Throughput of the batched D:1 env step feeding the policy.
+
+A step is one decision for every env of the job: MLP policy forward and masked
+sampling on observation slot t, then the env step that writes slot t+1 (the
+rollout loop of gpu-d1/scripts/run_ring_ablations.py:346-352). Weak scaling:
+each rank owns 65,536 envs (global env ids rank*65536 + i). Data is synthetic:
+every env plays its own seeded generated map.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Prints one JSON line on rank 0.
+"""
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / 'dcss-auto_b200'))
+
+METRIC = 'env decisions/sec (sim+policy, device-timed)'
+UNIT = 'decisions/s'
+ENVS, HORIZON = 65536, 128
+# Algorithmic bytes per decision of the env step (sim + bf16 observation write):
+# 2*128 B compact state + 700 B bit-packed map + 8 B action + 5 B reward/done
+# + 3,664 B observation.
+ENV_BYTES_PER_DECISION = 969 + 3664
+POLICY_FLOPS_PER_DECISION = 2 * (1832 * 256 + 256 * 256 + 256 * 13)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=128)
+    ap.add_argument('--warmup', type=int, default=8)
+    ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    ap.add_argument('--envs', type=int, default=ENVS, help='envs per GPU')
+    ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-cpu', action='store_true')
+    return ap.parse_args()
+
+
+class Clocks:
+    """Sample SM clocks and throttle reasons with nvidia-smi during the timed region."""
+    Q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+         'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+         'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.Q}',
+                                          '--format=csv,noheader,nounits', '-lms', '100'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(',')])
+
+    def stop(self):
+        if self.proc is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace('.', '').isdigit()]
+        smax = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace('.', '').isdigit()]
+        reasons = set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for r in self.rows:
+            if len(r) > 8:
+                for name, v in zip(names, r[5:9]):
+                    if v.strip().lower() == 'active':
+                        reasons.add(name)
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': max(smax) if smax else None,
+                'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def peaks():
+    try:
+        return json.loads((REPO / 'MEASURED_PEAKS.json').read_text()), 'measured'
+    except Exception:
+        return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'bf16_tflops_sustained': 1400.0}, 'fallback'
+
+
+# ---------------------------------------------------------------- CPU legs
+def cpu_rollout(n_envs, steps, threads):
+    """The oracle's spec env (C, one slice per thread) + a CPU torch policy of the
+    same architecture. Returns decisions/s."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, str(REPO / 'oracle'))
+    import oracle
+    from d1.spec_env import DEFAULT
+    oracle.build()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    w1 = torch.randn(256, 1832, generator=g) / 1832 ** 0.5
+    w2 = torch.randn(256, 256, generator=g) / 16.0
+    wh = torch.randn(13, 256, generator=g) / 16.0
+    per = (n_envs + threads - 1) // threads
+    envs = [oracle.OracleSpec(min(per, n_envs - i * per), DEFAULT, seed=0, first_env=i * per)
+            for i in range(threads) if i * per < n_envs]
+    from concurrent.futures import ThreadPoolExecutor
+    pool = ThreadPoolExecutor(len(envs))
+    actions = [np.zeros(e.batch, np.int64) for e in envs]
+
+    def one_step(step):
+        obs = torch.from_numpy(np.concatenate([e.obs for e in envs]))
+        legal = np.concatenate([e.legal for e in envs])
+        h = torch.relu(torch.relu(obs @ w1.T) @ w2.T) @ wh.T
+        a, _ = oracle.sample_actions(h[:, :12].numpy(), legal, 0, step)
+        off = 0
+        for i, e in enumerate(envs):
+            actions[i][:] = a[off:off + e.batch]
+            off += e.batch
+        list(pool.map(lambda i: envs[i].step(actions[i]), range(len(envs))))
+
+    one_step(0)
+    t0 = time.perf_counter()
+    for s in range(steps):
+        one_step(s + 1)
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    return n_envs * steps / dt, dt
+
+
+def run_reference(args, rank, world):
+    """`--impl reference`: the CPU implementation of this path timed on the host
+    cores. The reference has no code for the BASELINE task, so this is the oracle
+    port of it (the reference's own learn.cu host path covers only the fixture
+    task); every host thread is used."""
+    if rank != 0:
+        return
+    cores = len(os.sched_getaffinity(0))
+    n = min(args.envs, 8192)
+    rate, dt = cpu_rollout(n, max(args.steps // 16, 2), cores)
+    line = {'impl': 'reference', 'metric': METRIC, 'value': rate, 'unit': UNIT, 'n_gpus': args.gpus,
+            'steps': args.steps, 'warmup': args.warmup, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+            'config': {'workload': 'config1 rollout: generated D:1 maps, MLP 1832-256-256-13, host CPU',
+                       'envs_sampled': n},
+            'cpu_baseline': {'value': rate, 'unit': UNIT, 'cores': cores, 'kind': 'port',
+                             'sample': f'{n} envs x {max(args.steps // 16, 2)} decisions ({dt:.1f} s)'},
+            'e2e': {'value': rate, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU leg
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from d1.policy import Policy
+    from d1.rollout import Rollout
+    from d1.spec_env import SpecEnv
+
+    dev = torch.device('cuda', local_rank)
+    torch.cuda.set_device(dev)
+    B, T = args.envs, HORIZON
+    env = SpecEnv(B, seed=1, first_env=rank * B, device=dev)
+    policy = Policy(device=dev, seed=0)
+    roll = Rollout(env, policy, T, seed=1)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(k):
+        t = k % T
+        if t == 0 and k > 0:
+            roll.roll()
+        roll.step(t)
+
+    for k in range(args.warmup):
+        step(k)
+    # Kernel-level timing of the env step (events on its launching stream).
+    ev_env = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    orig_env_step = env.step
+
+    def timed_env_step(*a, **kw):
+        i = timed_env_step.i
+        ev_env[i][0].record(stream)
+        r = orig_env_step(*a, **kw)
+        ev_env[i][1].record(stream)
+        timed_env_step.i += 1
+        return r
+    timed_env_step.i = 0
+    clocks = Clocks(local_rank)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    env.step = timed_env_step
+    start.record(stream)
+    for k in range(args.warmup, args.warmup + args.steps):
+        step(k)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    env.step = orig_env_step
+    clk = clocks.stop()
+    ms = start.elapsed_time(stop)
+    env_ms = sum(a.elapsed_time(b) for a, b in ev_env) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    ms = t.item()
+    value = B * world * args.steps / (ms / 1e3)
+
+    # End to end through the public API with host buffers: actions come from
+    # pinned host memory, the outcome rows and next actions go back every step.
+    e2e = None
+    if not args.no_e2e:
+        h_act = torch.zeros(B, dtype=torch.int64).pin_memory()
+        h_out = torch.empty((B, env.out.shape[1])).pin_memory()
+        h_next = torch.empty(B, dtype=torch.int64).pin_memory()
+        d_act = torch.empty(B, dtype=torch.int64, device=dev)
+        obs, legal = env.obs, env.legal
+        logp = torch.empty(B, device=dev)
+        val = torch.empty(B, device=dev)
+        nxt = torch.empty(B, dtype=torch.int64, device=dev)
+        env.reset(2)
+        e2e_steps = max(8, args.steps // 4)
+        for k in range(3):
+            d_act.copy_(h_act, non_blocking=True)
+            env.step(d_act)
+            policy.act(obs, legal, 3, k, rank * B, action=nxt, logp=logp, value=val)
+            h_out.copy_(env.out, non_blocking=True)
+            h_next.copy_(nxt, non_blocking=True)
+            torch.cuda.synchronize()
+            h_act.copy_(h_next)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for k in range(e2e_steps):
+            d_act.copy_(h_act, non_blocking=True)
+            env.step(d_act)
+            policy.act(obs, legal, 3, 100 + k, rank * B, action=nxt, logp=logp, value=val)
+            h_out.copy_(env.out, non_blocking=True)
+            h_next.copy_(nxt, non_blocking=True)
+            torch.cuda.synchronize()
+            h_act.copy_(h_next)
+        e2e_s = torch.tensor([time.perf_counter() - t0], device=dev)
+        if world > 1:
+            dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+        e2e = {'value': B * world * e2e_steps / e2e_s.item(), 'unit': UNIT,
+               'h2d_bytes_per_step': B * 8, 'd2h_bytes_per_step': B * (env.out.shape[1] * 4 + 8),
+               'steps': e2e_steps}
+
+    if rank != 0:
+        return
+    pk, pk_kind = peaks()
+    achieved = ENV_BYTES_PER_DECISION * B / (env_ms / 1e3) / 1e9
+    line = {
+        'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+        'config': {'workload': 'config1 rollout: 65,536 envs/GPU on seeded generated 80x70 D:1 maps, '
+                               'obs 1832 bf16, MLP 1832-256-256-13 (random N(0,1/fan_in)), masked sampling',
+                   'envs_per_gpu': B, 'horizon': T, 'parallelism': f'dp{world} (env shards)',
+                   'l2': 'inputs larger than L2 (240 MB obs slot + 134 MB env state per step)'},
+        'roofline': {'kernel': 'd1::spec::step_kernel', 'bound': 'hbm', 'achieved': achieved,
+                     'peak': pk['hbm_gbs'], 'unit': 'GB/s', 'frac': achieved / pk['hbm_gbs'],
+                     'traffic': None, 'peak_kind': pk_kind,
+                     'algorithmic_bytes_per_decision': ENV_BYTES_PER_DECISION,
+                     'kernel_ms_per_step': env_ms},
+        'clocks': clk,
+        'e2e': e2e,
+        'gpu_launches': args.steps * 2,
+    }
+    if not args.no_cpu:
+        cores = len(os.sched_getaffinity(0))
+        rate, dt = cpu_rollout(4096, 6, cores)
+        line['cpu_baseline'] = {'value': rate, 'unit': UNIT, 'cores': cores, 'kind': 'port',
+                                'sample': f'4096 envs x 6 decisions of the same workload ({dt:.1f} s)'}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local_rank = int(os.environ.get('LOCAL_RANK', '0'))
+    if args.impl == 'reference':
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

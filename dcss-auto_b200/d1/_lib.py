@@ -25,6 +25,7 @@ SIGNATURES = {
     'd1_spec_step': [_P, _I, _P, _P, _P, _P, _P, _P, _P],
     'd1_spec_compact': [_P, _I, _P, _P],
     'd1_spec_planes': [_P, _I, _P, _P, _P],
+    'd1_policy_head_sample': [_P, _I, _I, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],
 }
 
 _LIB = None

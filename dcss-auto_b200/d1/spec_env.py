@@ -108,23 +108,28 @@ class SpecEnv:
     def stream(self):
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def reset(self, seed, obs_out=None):
+    def reset(self, seed, obs_out=None, legal_out=None):
         obs = self.obs if obs_out is None else obs_out
+        legal = self.legal if legal_out is None else legal_out
         check(self.lib.d1_spec_init(self.state.data_ptr(), self.batch, C.byref(self.config), seed, self.first_env,
-                                    obs.data_ptr(), self.legal.data_ptr(), self.stream), 'd1_spec_init')
+                                    obs.data_ptr(), legal.data_ptr(), self.stream), 'd1_spec_init')
         return obs
 
-    def step(self, actions, active=None, obs_out=None):
+    def step(self, actions, active=None, obs_out=None, legal_out=None, out_out=None):
+        """One semantic decision per env. `obs_out`/`legal_out`/`out_out` let the
+        caller point the writes at rollout-buffer slots (no extra copies)."""
         assert actions.device == self.device and actions.dtype == torch.int64 and actions.is_contiguous()
         act = 0
         if active is not None:
             assert active.device == self.device and active.dtype == torch.bool and active.shape == (self.batch,)
             act = active.data_ptr()
         obs = self.obs if obs_out is None else obs_out
+        legal = self.legal if legal_out is None else legal_out
+        out = self.out if out_out is None else out_out
         check(self.lib.d1_spec_step(self.state.data_ptr(), self.batch, C.byref(self.config), actions.data_ptr(),
-                                    obs.data_ptr(), self.legal.data_ptr(), self.out.data_ptr(), act or None,
-                                    self.stream), 'd1_spec_step')
-        return obs, self.out
+                                    obs.data_ptr(), legal.data_ptr(), out.data_ptr(), act or None, self.stream),
+              'd1_spec_step')
+        return obs, out
 
     def legal_mask(self):
         """Legal actions as a float [n, 12] mask (the reference's mask layout)."""

@@ -139,6 +139,21 @@ int d1_spec_compact(const void *state, int n, int64_t *rows, void *stream);
 /* Floor and remembered-cell bit planes, u32[n, 210] each (row y = words 3y..3y+2). */
 int d1_spec_planes(const void *state, int n, uint32_t *floor, uint32_t *viewed, void *stream);
 
+/* ======================================================================
+ * Policy and PPO kernels (no reference counterpart as kernels: the reference
+ * runs these as PyTorch ops, gpu-d1/scripts/run_ring_ablations.py:209-223 and
+ * :346-372).
+ * ====================================================================== */
+/* Head and sampler: for each row of h bf16[n, hidden] (hidden == 256) computes
+ * logits = h . wh[0:12]^T + bh[0:12] and value = h . wh[12] + bh[12]
+ * (wh bf16[13, hidden], bh f32[13]); when `action` is not NULL draws
+ * action ~ softmax(logits over the legal bits of legal[row]) with one Philox
+ * uniform keyed by (first_env + row, seed, step) and writes log p(action).
+ * Any of action/logp/value/logits may be NULL. */
+int d1_policy_head_sample(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
+                          const uint16_t *legal, uint64_t seed, uint64_t step, int first_env, int64_t *action,
+                          float *logp, float *value, float *logits, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,6 +9,7 @@
 
 #include <stdlib.h>
 #include <string.h>
+#include <math.h>
 
 #define W 80
 #define H 70
@@ -1175,6 +1176,73 @@ int oracle_spec_planes(const void *states, int n, uint32_t *floor, uint32_t *vie
     for (int i = 0; i < n; i++) {
         memcpy(floor + (size_t)i * PLANE, s[i].floor, sizeof s[i].floor);
         memcpy(viewed + (size_t)i * PLANE, s[i].viewed, sizeof s[i].viewed);
+    }
+    return 0;
+}
+
+/* ================================================================== */
+/* Action sampling: masked categorical over 12 logits                  */
+/* (gpu-d1/scripts/run_ring_ablations.py:221-223 masks illegal logits  */
+/* to -1e9 and samples torch.distributions.Categorical; torch's        */
+/* multinomial stream is not a stable specification, so the draw is    */
+/* defined here: inverse CDF over exp(l - max) in action order with one */
+/* Philox uniform per (env, step)).                                    */
+/* ================================================================== */
+static float o_bits_float(uint32_t u) {
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+/* e^x for x <= 0: Cody-Waite reduction with the Cephes ln2 split, degree-7
+ * Taylor polynomial, exponent-field scaling (every op separately rounded). */
+static float o_exp_nonpos(float x) {
+    if (x < -87.0f) return 0.0f;
+    const float k = __builtin_rintf(x * 1.44269504088896341f);
+    float r = x + -(k * 0.693359375f);
+    r = r + -(k * -2.12194440e-4f);
+    float p = 1.0f / 5040.0f;
+    p = p * r + 1.0f / 720.0f;
+    p = p * r + 1.0f / 120.0f;
+    p = p * r + 1.0f / 24.0f;
+    p = p * r + 1.0f / 6.0f;
+    p = p * r + 0.5f;
+    p = p * r + 1.0f;
+    p = p * r + 1.0f;
+    return p * o_bits_float((uint32_t)((int)k + 127) << 23);
+}
+
+int oracle_exp_nonpos(const float *x, int n, float *y) {
+    for (int i = 0; i < n; i++) y[i] = o_exp_nonpos(x[i]);
+    return 0;
+}
+
+int oracle_sample_actions(const float *logits, const uint16_t *legal, int n, uint64_t seed, uint64_t step,
+                          int first_env, int64_t *action, float *logp) {
+    for (int i = 0; i < n; i++) {
+        const float *l = logits + (size_t)i * 12;
+        uint32_t bits = legal ? legal[i] : 0xfffu;
+        float m = -3.402823466e38f, z[12], total = 0.f;
+        for (int j = 0; j < 12; j++)
+            if ((bits >> j) & 1u) m = l[j] > m ? l[j] : m;
+        for (int j = 0; j < 12; j++) {
+            z[j] = ((bits >> j) & 1u) ? o_exp_nonpos(l[j] + -m) : 0.f;
+            total = total + z[j];
+        }
+        uint32_t ctr[4] = {(uint32_t)step, (uint32_t)(step >> 32), (uint32_t)(seed >> 32), 1u};
+        uint32_t key[2] = {(uint32_t)(first_env + i), (uint32_t)seed}, o[4];
+        oracle_philox(ctr, key, o);
+        const float t = ((float)(o[0] >> 8) * (1.0f / 16777216.0f)) * total;
+        int a = -1, last = 0;
+        float run = 0.f;
+        for (int j = 0; j < 12; j++) {
+            if (!((bits >> j) & 1u)) continue;
+            last = j;
+            run = run + z[j];
+            if (a < 0 && t < run) a = j;
+        }
+        if (a < 0) a = last;
+        action[i] = a;
+        logp[i] = (l[a] - m) - logf(total);
     }
     return 0;
 }

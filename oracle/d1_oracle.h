@@ -84,6 +84,10 @@ int oracle_spec_step(void *states, int n, const D1SpecConfig *c, const int64_t *
 int oracle_spec_compact(const void *states, int n, int64_t *rows);
 /* Copies the floor and remembered (viewed) bit planes, u32[n, 210] each. */
 int oracle_spec_planes(const void *states, int n, uint32_t *floor, uint32_t *viewed);
+/* Masked categorical sampling over 12 logits (see d1_oracle.c). */
+int oracle_exp_nonpos(const float *x, int n, float *y);
+int oracle_sample_actions(const float *logits, const uint16_t *legal, int n, uint64_t seed, uint64_t step,
+                          int first_env, int64_t *action, float *logp);
 
 #ifdef __cplusplus
 }

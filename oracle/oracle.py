@@ -309,3 +309,27 @@ class OracleSpec:
         v = np.zeros((self.batch, 210), np.uint32)
         self.lib.oracle_spec_planes(self.state.ctypes.data, self.batch, f.ctypes.data, v.ctypes.data)
         return f, v
+
+
+def exp_nonpos(x):
+    lib = library()
+    lib.oracle_exp_nonpos.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib.oracle_exp_nonpos(x.ctypes.data, x.size, y.ctypes.data)
+    return y
+
+
+def sample_actions(logits, legal, seed, step, first_env=0):
+    """Oracle of the policy sampler: (actions int64, logp float32)."""
+    lib = spec_library()
+    lib.oracle_sample_actions.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_uint64, C.c_uint64, C.c_int,
+                                          C.c_void_p, C.c_void_p]
+    logits = np.ascontiguousarray(logits, np.float32)
+    legal = np.ascontiguousarray(legal, np.uint16)
+    n = logits.shape[0]
+    a = np.empty(n, np.int64)
+    lp = np.empty(n, np.float32)
+    lib.oracle_sample_actions(logits.ctypes.data, legal.ctypes.data, n, seed, step, first_env, a.ctypes.data,
+                              lp.ctypes.data)
+    return a, lp

@@ -1,0 +1,68 @@
+"""Policy head + sampler on the GPU: logits/value against a PyTorch fp32
+restatement (tolerance), actions given logits against the CPU oracle (exact)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def lib():
+    from d1._lib import library
+    oracle.build()
+    return library()
+
+
+def run_head(lib, h, wh, bh, legal, seed, step, first_env=0):
+    n = h.shape[0]
+    a = torch.empty(n, dtype=torch.int64, device='cuda')
+    lp = torch.empty(n, device='cuda')
+    v = torch.empty(n, device='cuda')
+    lg = torch.empty((n, 12), device='cuda')
+    code = lib.d1_policy_head_sample(h.data_ptr(), n, 256, wh.data_ptr(), bh.data_ptr(),
+                                     None if legal is None else legal.data_ptr(), seed, step, first_env,
+                                     a.data_ptr(), lp.data_ptr(), v.data_ptr(), lg.data_ptr(), 0)
+    assert code == 0
+    torch.cuda.synchronize()
+    return a, lp, v, lg
+
+
+def test_head_matches_fp32_reference_and_sampler_matches_oracle(lib):
+    g = torch.Generator().manual_seed(0)
+    n = 65536
+    h = torch.relu(torch.randn(n, 256, generator=g)).to(torch.bfloat16).cuda()
+    wh = (torch.randn(13, 256, generator=g) / 16).to(torch.bfloat16).cuda()
+    bh = torch.randn(13, generator=g).cuda()
+    legal = torch.randint(0, 1 << 12, (n,), generator=g).to(torch.int32)
+    legal = (legal | (1 << 8)).to(torch.int16).cuda()
+    a, lp, v, lg = run_head(lib, h, wh, bh, legal, seed=1234, step=77, first_env=5)
+    ref = h.float() @ wh.float().T + bh
+    assert torch.allclose(lg, ref[:, :12], rtol=1e-4, atol=1e-4)
+    assert torch.allclose(v, ref[:, 12], rtol=1e-4, atol=1e-4)
+    ora, olp = oracle.sample_actions(lg.cpu().numpy(), legal.cpu().numpy().view(np.uint16), 1234, 77, 5)
+    assert np.array_equal(a.cpu().numpy(), ora)
+    assert np.allclose(lp.cpu().numpy(), olp, rtol=1e-5, atol=1e-5)
+    bits = legal.cpu().numpy().view(np.uint16).astype(np.int64)
+    assert ((bits >> a.cpu().numpy()) & 1).all(), 'sampled an illegal action'
+    # log-prob agrees with torch's masked log-softmax
+    masked = lg.masked_fill(((legal.to(torch.int32)[:, None] >> torch.arange(12, device='cuda')) & 1) == 0, -1e9)
+    ref_lp = torch.log_softmax(masked, -1).gather(1, a[:, None])[:, 0]
+    assert torch.allclose(lp, ref_lp, rtol=1e-5, atol=1e-5)
+
+
+def test_sampling_frequencies_follow_the_softmax(lib):
+    n = 1 << 18
+    g = torch.Generator().manual_seed(1)
+    wh = torch.zeros(13, 256, dtype=torch.bfloat16, device='cuda')
+    bh = torch.tensor([0.0, 1.0, -1.0, 2.0, 0.5, -3.0, 0.0, 1.5, 0.2, -0.5, 1.0, 0.0, 0.0], device='cuda')
+    h = torch.zeros(n, 256, dtype=torch.bfloat16, device='cuda')
+    legal = torch.full((n,), 0b101111111011, dtype=torch.int16, device='cuda')  # action 2 and 10 illegal
+    a, _, _, _ = run_head(lib, h, wh, bh, legal, seed=9, step=3)
+    counts = torch.bincount(a, minlength=12).double().cpu() / n
+    p = torch.softmax(bh[:12].masked_fill(torch.tensor([(0b101111111011 >> j) & 1 == 0 for j in range(12)],
+                                                          device='cuda'), -1e9), -1).double().cpu()
+    assert counts[2] == 0 and counts[10] == 0
+    assert torch.allclose(counts, p, atol=4e-3)
