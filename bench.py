@@ -41,6 +41,7 @@ def parse():
     ap.add_argument('--warmup', type=int, default=8)
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--envs', type=int, default=ENVS, help='envs per GPU')
+    ap.add_argument('--horizon', type=int, default=HORIZON, help='rollout slots (profiling runs shrink it)')
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
     return ap.parse_args()
@@ -146,14 +147,14 @@ def run_reference(args, rank, world):
         return
     cores = len(os.sched_getaffinity(0))
     n = min(args.envs, 8192)
-    rate, dt = cpu_rollout(n, max(args.steps // 16, 2), cores)
+    rate, dt = cpu_rollout(n, max(args.steps // 2, 16), cores)
     line = {'impl': 'reference', 'metric': METRIC, 'value': rate, 'unit': UNIT, 'n_gpus': args.gpus,
             'steps': args.steps, 'warmup': args.warmup, 'higher_is_better': True, 'scaling': 'weak',
             'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
             'config': {'workload': 'config1 rollout: generated D:1 maps, MLP 1832-256-256-13, host CPU',
                        'envs_sampled': n},
             'cpu_baseline': {'value': rate, 'unit': UNIT, 'cores': cores, 'kind': 'port',
-                             'sample': f'{n} envs x {max(args.steps // 16, 2)} decisions ({dt:.1f} s)'},
+                             'sample': f'{n} envs x {max(args.steps // 2, 16)} decisions ({dt:.1f} s)'},
             'e2e': {'value': rate, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
     print(json.dumps(line), flush=True)
 
@@ -168,7 +169,7 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device('cuda', local_rank)
     torch.cuda.set_device(dev)
-    B, T = args.envs, HORIZON
+    B, T = args.envs, args.horizon
     env = SpecEnv(B, seed=1, first_env=rank * B, device=dev)
     policy = Policy(device=dev, seed=0)
     roll = Rollout(env, policy, T, seed=1)
@@ -282,9 +283,9 @@ def run_ours(args, rank, world, local_rank):
     }
     if not args.no_cpu:
         cores = len(os.sched_getaffinity(0))
-        rate, dt = cpu_rollout(4096, 6, cores)
+        rate, dt = cpu_rollout(8192, 100, cores)
         line['cpu_baseline'] = {'value': rate, 'unit': UNIT, 'cores': cores, 'kind': 'port',
-                                'sample': f'4096 envs x 6 decisions of the same workload ({dt:.1f} s)'}
+                                'sample': f'8192 envs x 100 decisions of the same workload ({dt:.1f} s)'}
     print(json.dumps(line), flush=True)
 
 
