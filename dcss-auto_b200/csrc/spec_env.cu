@@ -12,7 +12,8 @@
 // State row (2048 B per env):
 //   0    u64 ctr (Philox draws consumed)   8 u32 env, seed_lo, seed_hi, episode
 //   24   i32 hp, regen, blocks, player     40 i32 ticks, killed, stairs, nmon
-//   56   i32 floor_seen                    60..127 unused
+//   56   i32 floor_seen                    64 u16 vis[16] (LOS window rows, dy+7 -> bit dx+7)
+//   96..127 unused
 //   128  i16 pos[16]  160 i16 energy[16]  192 i16 hp[16]  224 u8 kind[16]  240 u8 awake[16]
 //   256  u32 floor[210]  (row y = words 3y..3y+2, bit x%32 of word x/32)
 //   1096 u32 viewed[210] (cells ever in view: remembered terrain)
@@ -24,7 +25,7 @@ namespace d1 {
 namespace spec {
 
 constexpr int MAXM = 11, OBS = 1832, CELLS = 225, ACTIONS = 12, OUT = 10, COMPACT = 56;
-constexpr int ROW = 2048, PL = 210, OFF_MON = 128, OFF_FLOOR = 256, OFF_VIEWED = 256 + 4 * PL;
+constexpr int ROW = 2048, PL = 210, OFF_VIS = 64, OFF_MON = 128, OFF_FLOOR = 256, OFF_VIEWED = 256 + 4 * PL;
 constexpr int WARPS = 4, MAX_RAYS = 320;
 constexpr int PRIM_WAIT = 8, PRIM_DESCEND = 9;
 
@@ -44,6 +45,11 @@ __device__ __forceinline__ uint4 philox(uint4 c, uint32_t k0, uint32_t k1) {
     }
     return c;
 }
+// One out-of-line copy of the ten rounds: every draw site of the rules shares it,
+// which keeps the hot loop small enough for the instruction cache.
+__device__ __noinline__ uint4 philox_block(uint64_t b, uint32_t c2, uint32_t k0, uint32_t k1) {
+    return philox(make_uint4((uint32_t)b, (uint32_t)(b >> 32), c2, 0u), k0, k1);
+}
 // Warp-cooperative stream: lane j holds block (base + j), so one refill (one
 // Philox evaluation per lane) serves the next 128 draws of the env; a draw is a
 // select plus one shuffle. Only ever called from warp-uniform code.
@@ -54,8 +60,7 @@ struct WarpPhilox {
     int lane;
     __device__ __forceinline__ void refill() {
         base = n >> 2;
-        const uint64_t b = base + (uint64_t)lane;
-        blk = philox(make_uint4((uint32_t)b, (uint32_t)(b >> 32), c2, 0u), k0, k1);
+        blk = philox_block(base + (uint64_t)lane, c2, k0, k1);
     }
     __device__ __forceinline__ uint32_t next() {
         const uint64_t b = n >> 2;
@@ -70,8 +75,10 @@ struct WarpPhilox {
 
 // ------------------------------------------------------------------ state
 struct Smem {
-    uint32_t floor[PL], viewed[PL], seen[PL], cur[PL], nxt[PL];
+    uint32_t floor[PL], viewed[PL], seen[PL], cur[PL];
+    uint32_t occ[PL];  // live monster positions during the monster phase
     uint32_t vis[16];  // LOS window rows: vis[dy+7] bit dx+7
+    uint16_t vmask[16], fmask[16];  // remembered / floor bits of the window rows
     uint8_t dist8[N];  // BFS distance mod 256 (valid where `seen`)
     uint8_t opqb[32];
     uint8_t occ_ch[CELLS + 7];
@@ -179,13 +186,15 @@ __device__ void compute_los(Env &e, const Rays &rays, int nrays) {
         const int sh = (ay & 3) * 8;
         const int hiw = ay >> 2;
         uint32_t pos = 0, neg = 0;  // x >= 0 side, x <= 0 side (before reversal)
+        const uint32_t q0 = hiw ? w[1] : w[0], q1 = hiw ? w[3] : w[2];
+        const uint32_t q2 = hiw ? w[5] : w[4], q3 = hiw ? w[7] : w[6];
         if (dy >= 0) {
-            pos |= (w[0 + hiw] >> sh) & 0xffu;  // q0 (+,+)
-            neg |= (w[2 + hiw] >> sh) & 0xffu;  // q1 (-,+)
+            pos |= (q0 >> sh) & 0xffu;  // q0 (+,+)
+            neg |= (q1 >> sh) & 0xffu;  // q1 (-,+)
         }
         if (dy <= 0) {
-            pos |= (w[6 + hiw] >> sh) & 0xffu;  // q3 (+,-)
-            neg |= (w[4 + hiw] >> sh) & 0xffu;  // q2 (-,-)
+            pos |= (q3 >> sh) & 0xffu;  // q3 (+,-)
+            neg |= (q2 >> sh) & 0xffu;  // q2 (-,-)
         }
         uint32_t row = (pos << 7) | (__brev(neg) >> 24);
         if (dy == 0) row |= 1u << 7;
@@ -198,6 +207,7 @@ __device__ void compute_los(Env &e, const Rays &rays, int nrays) {
         if (hi < 14) row &= (1u << (hi + 1)) - 1u;
         s.vis[lane] = row;
     }
+    if (lane == 15) s.vis[15] = 0;
     __syncwarp();
 }
 
@@ -415,16 +425,19 @@ __device__ void reset(Env &e, const D1SpecConfig &c, const Rays &rays, int nrays
 }
 
 // ------------------------------------------------------------------ pursuit field
-// Layered BFS from the player over floor, stopped one layer past the farthest
-// awake monster (monsters act at most twice per turn and every cell a move can
-// reach or compare against then has an exact distance; farther cells read as
-// unreached, which every comparison of sim.h:207-253 treats like any value
-// larger than the mover's own). Distances are stored mod 256 and recovered
-// relative to the mover's exact distance (all compared cells lie within 24
-// steps of it). Sets m_dist (65535 = unreached) on each monster lane.
+// Layered BFS from the player over floor. Only monsters that will move this
+// turn (awake, energy >= 80, not adjacent) read the field, and they act at most
+// `1 + extra_layers` times, each move raising their distance by at most one; the
+// search therefore stops `extra_layers` layers past the farthest of them, where
+// every cell a move compares against has its exact distance and every farther
+// cell reads as unreached -- which all comparisons of sim.h:207-253 treat like
+// any value larger than the mover's own. Layer k only touches rows within k of
+// the player. Distances are stored mod 256 and recovered relative to the
+// mover's exact distance (every compared cell lies within 24 steps of it).
+// Sets m_dist (65535 = unreached) on each mover lane.
 __device__ void pursuit_bfs(Env &e, int extra_layers) {
     Smem &s = *e.sm;
-    const bool need = e.lane < e.nmon && e.m_hp > 0 && e.m_awake;
+    const bool need = e.lane < e.nmon && e.m_hp > 0 && e.m_awake && e.m_energy >= 80 && cheb(e.m_pos, e.player) > 1;
     e.m_dist = 65535;
     if (!__any_sync(FULL, need)) return;
     for (int r = e.lane; r < PL; r += 32) {
@@ -440,36 +453,47 @@ __device__ void pursuit_bfs(Env &e, int extra_layers) {
         s.dist8[e.player] = 0;
     }
     __syncwarp();
+    const int py = e.player / W;
     int stop_after = 0x7fffffff;
     for (int k = 1;; k++) {
+        const int ylo = imax(0, py - k), yhi = imin(H - 1, py + k);
+        uint32_t nw[3][3];
         bool any = false;
-        for (int y = e.lane; y < H; y += 32) {
-            const uint32_t *c0 = s.cur + y * 3;
-            uint32_t a0 = c0[0], a1 = c0[1], a2 = c0[2];
-            if (y > 0) { a0 |= c0[-3]; a1 |= c0[-2]; a2 |= c0[-1]; }
-            if (y < H - 1) { a0 |= c0[3]; a1 |= c0[4]; a2 |= c0[5]; }
-            const uint32_t d0 = a0 | (a0 << 1) | (a0 >> 1) | (a1 << 31);
-            const uint32_t d1 = a1 | (a1 << 1) | (a0 >> 31) | (a1 >> 1) | (a2 << 31);
-            const uint32_t d2 = a2 | (a2 << 1) | (a1 >> 31) | (a2 >> 1);
-            const int r = y * 3;
-            const uint32_t n0 = d0 & s.floor[r] & ~s.seen[r];
-            const uint32_t n1 = d1 & s.floor[r + 1] & ~s.seen[r + 1];
-            const uint32_t n2 = d2 & s.floor[r + 2] & ~s.seen[r + 2];
-            s.nxt[r] = n0; s.nxt[r + 1] = n1; s.nxt[r + 2] = n2;
-            any |= (n0 | n1 | n2) != 0;
+#pragma unroll
+        for (int i = 0; i < 3; i++) {
+            const int y = ylo + e.lane + 32 * i;
+            nw[i][0] = nw[i][1] = nw[i][2] = 0;
+            if (y <= yhi) {
+                const uint32_t *c0 = s.cur + y * 3;
+                uint32_t a0 = c0[0], a1 = c0[1], a2 = c0[2];
+                if (y > 0) { a0 |= c0[-3]; a1 |= c0[-2]; a2 |= c0[-1]; }
+                if (y < H - 1) { a0 |= c0[3]; a1 |= c0[4]; a2 |= c0[5]; }
+                const uint32_t d0 = a0 | (a0 << 1) | (a0 >> 1) | (a1 << 31);
+                const uint32_t d1 = a1 | (a1 << 1) | (a0 >> 31) | (a1 >> 1) | (a2 << 31);
+                const uint32_t d2 = a2 | (a2 << 1) | (a1 >> 31) | (a2 >> 1);
+                const int r = y * 3;
+                nw[i][0] = d0 & s.floor[r] & ~s.seen[r];
+                nw[i][1] = d1 & s.floor[r + 1] & ~s.seen[r + 1];
+                nw[i][2] = d2 & s.floor[r + 2] & ~s.seen[r + 2];
+                any |= (nw[i][0] | nw[i][1] | nw[i][2]) != 0;
+            }
         }
         __syncwarp();
-        for (int y = e.lane; y < H; y += 32) {
 #pragma unroll
-            for (int i = 0; i < 3; i++) {
-                const int r = y * 3 + i;
-                uint32_t w = s.nxt[r];
-                s.seen[r] |= w;
-                s.cur[r] = w;
-                while (w) {
-                    const int b = __ffs(w) - 1;
-                    s.dist8[y * W + i * 32 + b] = (uint8_t)k;
-                    w &= w - 1;
+        for (int i = 0; i < 3; i++) {
+            const int y = ylo + e.lane + 32 * i;
+            if (y <= yhi) {
+#pragma unroll
+                for (int j = 0; j < 3; j++) {
+                    const int r = y * 3 + j;
+                    uint32_t w = nw[i][j];
+                    s.seen[r] |= w;
+                    s.cur[r] = w;
+                    while (w) {
+                        const int b = __ffs(w) - 1;
+                        s.dist8[y * W + j * 32 + b] = (uint8_t)k;
+                        w &= w - 1;
+                    }
                 }
             }
         }
@@ -501,14 +525,7 @@ __device__ int choose_move(Env &e, int p, int D, int &dq_out) {
     if (D == 65535) return -1;  // unreachable component: every comparison fails
     const int d = lane & 7;
     const int q = neighbor(p, d);
-    bool okq = q >= 0 && floor_at(e, q) && q != e.player;
-    {
-        // occupancy of this lane's neighbour: every monster lane tests it
-        for (int k = 0; k < e.nmon; k++) {
-            const int pk = __shfl_sync(FULL, e.m_pos, k), hk = __shfl_sync(FULL, e.m_hp, k);
-            if (hk > 0 && pk == q) okq = false;
-        }
-    }
+    const bool okq = q >= 0 && floor_at(e, q) && q != e.player && !bitp(e.sm->occ, q);
     const int dq = okq ? dist_rel(e, q, D) : 0;
     int best = -1, bd = D, bdist = D, ties = 0;
     for (int z = 0; z < 8; z++) {
@@ -534,11 +551,7 @@ __device__ int choose_move(Env &e, int p, int D, int &dq_out) {
     for (int head = 0; head < len; head++) {
         const int ch = __shfl_sync(FULL, cell, head), fh = __shfl_sync(FULL, first, head);
         const int qn = neighbor(ch, d);
-        bool okn = qn >= 0 && floor_at(e, qn) && qn != e.player;
-        for (int k = 0; k < e.nmon; k++) {
-            const int pk = __shfl_sync(FULL, e.m_pos, k), hk = __shfl_sync(FULL, e.m_hp, k);
-            if (hk > 0 && pk == qn) okn = false;
-        }
+        const bool okn = qn >= 0 && floor_at(e, qn) && qn != e.player && !bitp(e.sm->occ, qn);
         const int dqn = okn ? dist_rel(e, qn, D) : 65535;
         for (int dd = 0; dd < 8; dd++) {
             const int qz = __shfl_sync(FULL, qn, dd), dz = __shfl_sync(FULL, dqn, dd);
@@ -582,9 +595,13 @@ __device__ void act(Env &e, const D1SpecConfig &c, int id) {
     int dq = 65535;
     const int q = choose_move(e, mp, D, dq);
     if (q >= 0 && e.lane == id) {
+        uint32_t *occ = e.sm->occ;
+        occ[(mp / W) * 3 + (mp % W) / 32] &= ~(1u << ((mp % W) & 31));
+        occ[(q / W) * 3 + (q % W) / 32] |= 1u << ((q % W) & 31);
         e.m_pos = q;
         e.m_dist = dq;
     }
+    __syncwarp();
 }
 
 __device__ __forceinline__ bool visible_awake(const Env &e) {
@@ -653,6 +670,12 @@ __device__ Prim primitive(Env &e, const D1SpecConfig &c, const Rays &rays, int n
         }
         if (alive && !e.m_awake) e.m_energy = -30000;
         if (alive) e.m_energy = (int16_t)(e.m_energy + kind_of(c, e.m_kind).speed);
+        if (__any_sync(FULL, alive && e.m_energy >= 80)) {
+            for (int r = e.lane; r < PL; r += 32) e.sm->occ[r] = 0;
+            __syncwarp();
+            if (alive) atomicOr(&e.sm->occ[(e.m_pos / W) * 3 + (e.m_pos % W) / 32], 1u << ((e.m_pos % W) & 31));
+            __syncwarp();
+        }
         pursuit_bfs(e, extra_layers);
         while (e.hp > 0) {
             const int id = scan_ready(e.m_energy, e.lane, e.nmon);
@@ -740,21 +763,30 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
         s.occ_ch[(dy + 7) * 15 + dx + 7] = (uint8_t)(e.m_kind == 4 ? 7 : e.m_awake ? 6 : 5);
     }
     __syncwarp();
+    if (lane < 15) {
+        const int cy = py + lane - 7;
+        uint32_t vm = 0, fm = 0;
+        if (cy >= 0 && cy < H) {
+            vm = row15(s.viewed + cy * 3, px - 7);
+            fm = row15(s.floor + cy * 3, px - 7);
+        }
+        s.vmask[lane] = (uint16_t)vm;
+        s.fmask[lane] = (uint16_t)fm;
+    }
+    __syncwarp();
+    const int sdx = e.stairs % W - px, sdy = e.stairs / W - py;
+    const int sj = (sdx >= -7 && sdx <= 7 && sdy >= -7 && sdy <= 7) ? (sdy + 7) * 15 + sdx + 7 : -1;
     uint4 *dst = reinterpret_cast<uint4 *>(obs);
     for (int j = lane; j < CELLS; j += 32) {
-        const int wy = j / 15, wx = j % 15, cx = px + wx - 7, cy = py + wy - 7;
+        const int wy = j / 15, wx = j - wy * 15;
         int ch = 0;
-        if (cx >= 0 && cx < W && cy >= 0 && cy < H) {
-            const int p = cy * W + cx;
-            if (bitp(s.viewed, p)) {
-                if (!bitp(s.floor, p)) ch = 1;
-                else {
-                    const bool vis = (s.vis[wy] >> wx) & 1u;
-                    const int m = s.occ_ch[j];
-                    if (m != 0xff) ch = m;
-                    else if (p == e.stairs) ch = 4;
-                    else ch = vis ? 3 : 2;
-                }
+        if ((s.vmask[wy] >> wx) & 1u) {
+            if (!((s.fmask[wy] >> wx) & 1u)) ch = 1;
+            else {
+                const int m = s.occ_ch[j];
+                if (m != 0xff) ch = m;
+                else if (j == sj) ch = 4;
+                else ch = ((s.vis[wy] >> wx) & 1u) ? 3 : 2;
             }
         }
         // bf16 1.0 = 0x3f80 in half-word `ch`
@@ -859,6 +891,7 @@ __device__ void load(Env &e, const uint8_t *row) {
         e.sm->floor[r] = fp[r];
         e.sm->viewed[r] = vp[r];
     }
+    if (e.lane < 16) e.sm->vis[e.lane] = reinterpret_cast<const uint16_t *>(row + OFF_VIS)[e.lane];
     __syncwarp();
     e.rng.refill();
     e.dirty_lo = H;
@@ -877,6 +910,7 @@ __device__ void store(const Env &e, uint8_t *row) {
         i32[14] = e.floor_seen;
     }
     if (e.lane < 16) {
+        reinterpret_cast<uint16_t *>(row + OFF_VIS)[e.lane] = (uint16_t)e.sm->vis[e.lane];
         int16_t *m = reinterpret_cast<int16_t *>(row + OFF_MON);
         m[e.lane] = (int16_t)e.m_pos;
         m[16 + e.lane] = (int16_t)e.m_energy;
@@ -953,7 +987,6 @@ __global__ void __launch_bounds__(WARPS * 32)
     e.sm = &sms[w];
     uint8_t *row = state + (size_t)env * ROW;
     load(e, row);
-    compute_los(e, rays, nrays);
     const float o = decision(e, c, rays, nrays, extra_layers, (int)actions[env]);
     if (e.lane < OUT) out[(size_t)env * OUT + e.lane] = o;
     observe(e, c, obs + (size_t)env * OBS, legal + env);
