@@ -1,0 +1,357 @@
+// Dense layers on the 5th-generation tensor cores (sm_100a tcgen05 + TMA).
+//
+//   C[M, N] = act(A[M, K] . B[N, K]^T + bias[N])      (bf16 operands, fp32 accumulate)
+//
+// Both operands are K-major (row-major with K contiguous), as the policy's
+// activations and nn.Linear-style weights are. One CTA computes a 128 x 256
+// tile; K advances in 64-element blocks through a 4-stage ring of shared-memory
+// buffers filled by TMA (128-byte swizzle, zero fill past the tensor edges).
+//
+// Warp roles (192 threads): warp 0 lane 0 issues TMA loads; warp 1 owns the
+// tensor-memory allocation and one lane issues tcgen05.mma (M=128, N=256, K=16
+// per instruction, accumulator in 256 TMEM columns); warps 2-5 are the epilogue,
+// each reading its 32 TMEM lanes (= 32 tile rows) with tcgen05.ld.
+//
+// Outputs (any subset): bf16 C (row-major), bf16 C^T (feature-major, for the
+// weight-gradient GEMMs of the backward pass), and fp32 C (row-major, one slab
+// per K split for deterministic split-K reduction).
+//
+// Every wait on an mbarrier is bounded: on expiry the kernel records an error
+// code in d1_gemm_error and runs its teardown (TMEM is always freed).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/d1.h"
+
+namespace d1 {
+namespace tc {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+
+__device__ int g_error;
+
+struct Params {
+    int M, N, K;
+    int k_tiles_per_split, k_tiles_total;
+    const float *bias;   // may be null
+    int relu;
+    __nv_bfloat16 *c;    // row-major [M, ldc] (may be null)
+    int ldc;
+    __nv_bfloat16 *ct;   // feature-major [N, ldct] (may be null)
+    int ldct;
+    float *cf;           // fp32 row-major [splits][M, ldcf] (may be null)
+    int ldcf;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Bounded parity wait: true when the phase completed, false after WAIT_LIMIT polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major tile stored with the 128-byte
+// swizzle (rows of 128 B, 8-row groups 1024 B apart): start address >> 4,
+// stride byte offset 1024 >> 4, fixed version bits 46-48 = 0b001, swizzle mode 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)(16u >> 4) << 16;      // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024u >> 4) << 32;    // stride byte offset
+    d |= (uint64_t)1 << 46;               // version
+    d |= (uint64_t)2 << 61;               // 128-byte swizzle
+    return d;
+}
+// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, both
+// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(IDESC), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+#define D1_TMEM_LD32(taddr, v)                                                                                      \
+    asm volatile(                                                                                                   \
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18," \
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                                             \
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),          \
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),    \
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),  \
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])   \
+        : "r"(taddr))
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 1);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), accum = smem_u32(bars + 2 * STAGES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN, split = blockIdx.z;
+    const int kt0 = split * p.k_tiles_per_split;
+    const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
+    const int nkt = kt1 - kt0;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        mbar_init(accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0 && lane == 0) {
+        // TMA producer
+        int issued = 0;
+        for (int i = 0; i < nkt && ok; i++) {
+            const int s = i % STAGES;
+            const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+            if (i >= STAGES && !mbar_wait(empty0 + 8 * s, ph ^ 1u)) {
+                ok = false;
+                break;
+            }
+            const uint32_t a_dst = smem_u32(smem + s * STAGE_BYTES), b_dst = a_dst + A_BYTES;
+            mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
+            const int kx = (kt0 + i) * BK;
+            tma_load_2d(a_dst, &map_a, full0 + 8 * s, kx, m0);
+            tma_load_2d(b_dst, &map_b, full0 + 8 * s, kx, n0);
+            issued = i + 1;
+        }
+        if (!ok) {
+            atomicExch(&g_error, 1);
+            // Drain copies already in flight before the CTA may exit.
+            for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
+                mbar_wait(full0 + 8 * (i % STAGES), (uint32_t)(i / STAGES) & 1u);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer
+        for (int i = 0; i < nkt; i++) {
+            const int s = i % STAGES;
+            if (!mbar_wait(full0 + 8 * s, (uint32_t)(i / STAGES) & 1u)) {
+                atomicExch(&g_error, 2);
+                ok = false;
+                break;
+            }
+            fence_after();
+            const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES), b_base = a_base + A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; kk++)
+                mma(tmem, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), (i > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(empty0 + 8 * s);
+        }
+        mma_commit(accum);
+    } else if (warp >= 2) {
+        // Epilogue: warp w reads TMEM lanes 32*(w % 4) .. +31 = tile rows.
+        const int q = warp & 3;
+        const int row = m0 + q * 32 + lane;
+        if (!mbar_wait(accum, 0)) {
+            atomicExch(&g_error, 3);
+            ok = false;
+        }
+        fence_after();
+        if (ok) {
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; cc++) {
+                uint32_t v[32];
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32);
+                __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the row/column guards
+                D1_TMEM_LD32(taddr, v);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                const int col0 = n0 + cc * 32;
+                if (row >= p.M || col0 >= p.N) continue;
+                float f[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    float x = __uint_as_float(v[j]);
+                    if (p.bias && col0 + j < p.N) x += p.bias[col0 + j];
+                    if (p.relu) x = fmaxf(x, 0.f);
+                    f[j] = x;
+                }
+                const bool full_cols = col0 + 32 <= p.N;
+                if (p.cf) {
+                    float *dst = p.cf + (size_t)split * p.M * p.ldcf + (size_t)row * p.ldcf + col0;
+                    if (full_cols) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4 *>(dst + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j < p.N) dst[j] = f[j];
+                    }
+                }
+                if (p.c) {
+                    __nv_bfloat16 *dst = p.c + (size_t)row * p.ldc + col0;
+                    if (full_cols) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            uint4 w;
+                            __nv_bfloat162 h0 = __floats2bfloat162_rn(f[j], f[j + 1]);
+                            __nv_bfloat162 h1 = __floats2bfloat162_rn(f[j + 2], f[j + 3]);
+                            __nv_bfloat162 h2 = __floats2bfloat162_rn(f[j + 4], f[j + 5]);
+                            __nv_bfloat162 h3 = __floats2bfloat162_rn(f[j + 6], f[j + 7]);
+                            w.x = *reinterpret_cast<uint32_t *>(&h0);
+                            w.y = *reinterpret_cast<uint32_t *>(&h1);
+                            w.z = *reinterpret_cast<uint32_t *>(&h2);
+                            w.w = *reinterpret_cast<uint32_t *>(&h3);
+                            *reinterpret_cast<uint4 *>(dst + j) = w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j < p.N) dst[j] = __float2bfloat16_rn(f[j]);
+                    }
+                }
+                if (p.ct) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (col0 + j < p.N) p.ct[(size_t)(col0 + j) * p.ldct + row] = __float2bfloat16_rn(f[j]);
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    }
+    return fn;
+}
+
+// 2-D bf16 tensor [rows, cols] with row pitch `ld` elements; box BK x box_rows.
+static bool make_map(CUtensorMap *m, const void *base, int rows, int cols, int ld, int box_rows) {
+    EncodeTiled enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace tc
+}  // namespace d1
+
+using namespace d1::tc;
+
+extern "C" {
+
+int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
+            void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits, void *stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || !a || !b || (!c && !ct && !cf) || splits < 1) return D1_ERR_BAD_ARGUMENT;
+    // TMA rules: 16-byte aligned bases and row pitches.
+    if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) || (lda * 2) % 16 ||
+        (ldb * 2) % 16 || lda < K || ldb < K)
+        return D1_ERR_BAD_ARGUMENT;
+    if (c && ((reinterpret_cast<uintptr_t>(c) & 15) || ldc % 8 || ldc < N)) return D1_ERR_BAD_ARGUMENT;
+    if (cf && ((reinterpret_cast<uintptr_t>(cf) & 15) || ldcf % 4 || ldcf < N)) return D1_ERR_BAD_ARGUMENT;
+    if (ct && ldct < M) return D1_ERR_BAD_ARGUMENT;
+    if (splits > 1 && (c || ct)) return D1_ERR_BAD_ARGUMENT;  // split-K writes fp32 partial slabs only
+    const int kt = (K + BK - 1) / BK;
+    if (splits > kt) splits = kt;
+    const int per = (kt + splits - 1) / splits;
+    splits = (kt + per - 1) / per;  // every split gets at least one K block
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, a, M, K, lda, BM) || !make_map(&mb, b, N, K, ldb, BN)) return D1_ERR_BAD_ARGUMENT;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return (int)e;
+        attr = true;
+    }
+    Params p{M, N, K, per, kt, bias, relu, (__nv_bfloat16 *)c, ldc, (__nv_bfloat16 *)ct, ldct, cf, ldcf};
+    dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, splits);
+    gemm_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
+    return (int)cudaGetLastError();
+}
+
+// Splits actually used for (K, requested splits): callers size fp32 slabs with it.
+int d1_gemm_splits(int K, int splits) {
+    const int kt = (K + BK - 1) / BK;
+    if (splits < 1) splits = 1;
+    if (splits > kt) splits = kt;
+    const int per = (kt + splits - 1) / splits;
+    return (kt + per - 1) / per;
+}
+
+// Last error recorded by a GEMM wait that expired (0 = none); clears it.
+int d1_gemm_error(void) {
+    int h = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&h, g_error, sizeof(int)) != cudaSuccess) return -1;
+    if (h) cudaMemcpyToSymbol(g_error, &z, sizeof(int));
+    return h;
+}
+
+}  // extern "C"

@@ -26,6 +26,9 @@ SIGNATURES = {
     'd1_spec_compact': [_P, _I, _P, _P],
     'd1_spec_planes': [_P, _I, _P, _P, _P],
     'd1_policy_head_sample': [_P, _I, _I, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],
+    'd1_gemm': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
+    'd1_gemm_splits': [_I, _I],
+    'd1_gemm_error': [],
 }
 
 _LIB = None

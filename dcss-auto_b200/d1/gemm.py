@@ -1,6 +1,39 @@
-"""Dense layers of the policy: y = relu(x @ w^T + b), bf16 in/out, fp32 accumulate."""
+"""Dense layers of the policy on the tcgen05 GEMM (d1_gemm): bf16 in/out, fp32 accumulate."""
 import torch
 
+from ._lib import check, library
 
-def linear_relu(x, w, b):
-    return torch.nn.functional.linear(x, w, b.to(torch.bfloat16)).relu_()
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def gemm(a, b, bias=None, relu=False, out=None, out_t=None, out_f32=None, splits=1):
+    """act(a @ b.T + bias). a: bf16 [M, K], b: bf16 [N, K] (row pitches may exceed K).
+    Any of out (bf16 [M, N]), out_t (bf16 [N, M]) and out_f32 (fp32 [splits, M, N])."""
+    M, K = a.shape
+    N = b.shape[0]
+    assert b.shape[1] == K and a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16
+    assert a.stride(1) == 1 and b.stride(1) == 1
+    if out is None and out_t is None and out_f32 is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    lib = library()
+    check(lib.d1_gemm(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), M, N, K,
+                      None if bias is None else bias.data_ptr(), int(relu),
+                      None if out is None else out.data_ptr(), 0 if out is None else out.stride(0),
+                      None if out_t is None else out_t.data_ptr(), 0 if out_t is None else out_t.stride(0),
+                      None if out_f32 is None else out_f32.data_ptr(), 0 if out_f32 is None else out_f32.stride(-2),
+                      splits, _stream(a)), 'd1_gemm')
+    return out if out is not None else (out_t if out_t is not None else out_f32)
+
+
+def splits_for(K, splits):
+    return library().d1_gemm_splits(K, splits)
+
+
+def linear_relu(x, w, b, out=None):
+    return gemm(x, w, bias=b, relu=True, out=out)
+
+
+def gemm_error():
+    return library().d1_gemm_error()

@@ -153,6 +153,19 @@ int d1_spec_planes(const void *state, int n, uint32_t *floor, uint32_t *viewed, 
 int d1_policy_head_sample(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
                           const uint16_t *legal, uint64_t seed, uint64_t step, int first_env, int64_t *action,
                           float *logp, float *value, float *logits, void *stream);
+/* Tensor-core dense layer (tcgen05 + TMA): C = act(A . B^T + bias) with
+ * A bf16[M, K] (row pitch lda), B bf16[N, K] (row pitch ldb), fp32 accumulation,
+ * act = ReLU when relu != 0. Writes any of: c bf16[M, ldc] row-major, ct
+ * bf16[N, ldct] (C transposed), cf fp32 (row-major, pitch ldcf, one [M, ldcf]
+ * slab per K split). splits > 1 splits K across CTAs and requires c == ct ==
+ * NULL; the number of slabs written is d1_gemm_splits(K, splits). Bases and
+ * pitches must be 16-byte aligned (TMA). */
+int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
+            void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits, void *stream);
+int d1_gemm_splits(int K, int splits);
+/* Nonzero when a GEMM pipeline wait expired (the kernel then skipped its work
+ * and freed its tensor memory); reading clears it. Synchronises the device. */
+int d1_gemm_error(void);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,61 @@
+"""tcgen05 GEMM against a PyTorch fp32 restatement of the same op (bf16 inputs,
+fp32 accumulation): relative error bound 2e-3 on bf16 outputs, 1e-4 on fp32."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def G():
+    from d1 import gemm
+    return gemm
+
+
+def ref(a, b, bias=None, relu=False):
+    y = a.float() @ b.float().T
+    if bias is not None:
+        y = y + bias
+    return y.relu() if relu else y
+
+
+@pytest.mark.parametrize('M,N,K', [(128, 256, 64), (65536, 256, 1832), (4096, 256, 256), (1000, 256, 1832),
+                                   (16384, 13, 256), (300, 1832, 256)])
+def test_bf16_out_with_bias_relu(G, M, N, K):
+    g = torch.Generator(device='cuda').manual_seed(M + N + K)
+    a = torch.randn(M, K, device='cuda', generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, device='cuda', generator=g) / K ** 0.5).to(torch.bfloat16)
+    bias = torch.randn(N, device='cuda', generator=g)
+    ldc = (N + 7) // 8 * 8
+    out = torch.empty((M, ldc), dtype=torch.bfloat16, device='cuda')[:, :N]
+    G.gemm(a, b, bias=bias, relu=True, out=out)
+    torch.cuda.synchronize()
+    assert G.gemm_error() == 0
+    r = ref(a, b, bias, True)
+    err = (out.float() - r).abs().max().item()
+    assert err <= 2e-3 * r.abs().max().item() + 1e-2, err
+
+
+def test_transposed_and_fp32_outputs(G):
+    M, N, K = 2048, 256, 512
+    a = torch.randn(M, K, device='cuda').to(torch.bfloat16)
+    b = torch.randn(N, K, device='cuda').to(torch.bfloat16)
+    ct = torch.empty((N, M), dtype=torch.bfloat16, device='cuda')
+    cf = torch.empty((1, M, N), device='cuda')
+    G.gemm(a, b, out_t=ct, out_f32=cf)
+    r = ref(a, b)
+    assert torch.allclose(cf[0], r, rtol=1e-4, atol=1e-3)
+    assert torch.allclose(ct.float(), r.T, rtol=1e-2, atol=1e-1)
+
+
+def test_split_k_partials_sum_to_the_product(G):
+    M, N, K = 256, 1832, 16384
+    a = torch.randn(M, K, device='cuda').to(torch.bfloat16)
+    b = torch.randn(N, K, device='cuda').to(torch.bfloat16)
+    s = G.splits_for(K, 16)
+    ld = (N + 3) // 4 * 4
+    cf = torch.empty((s, M, ld), device='cuda')
+    G.gemm(a, b, out_f32=cf[:, :, :N], splits=16)
+    r = ref(a, b)
+    got = cf[:, :, :N].sum(0)
+    assert torch.allclose(got, r, rtol=1e-4, atol=1e-2)
