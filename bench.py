@@ -260,6 +260,23 @@ def run_ours(args, rank, world, local_rank):
                'h2d_bytes_per_step': B * 8, 'd2h_bytes_per_step': B * (env.out.shape[1] * 4 + 8),
                'steps': e2e_steps}
 
+    # Tensor-core layer alone (policy layer 1, M = envs, N = 256, K = 1832), timed
+    # with events on its launching stream after the rollout measurement.
+    from d1 import gemm as G
+    x = roll.obs[0]
+    w1, b1 = policy.bf16['w1'], policy.params['b1']
+    h1 = torch.empty((B, 256), dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        G.gemm(x, w1, bias=b1, relu=True, out=h1)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    g0.record(stream)
+    for i in range(reps):
+        G.gemm(roll.obs[i % T], w1, bias=b1, relu=True, out=h1)
+    g1.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = g0.elapsed_time(g1) / reps
+    gemm_tflops = 2.0 * B * 1832 * 256 / (gemm_ms / 1e3) / 1e12
     if rank != 0:
         return
     pk, pk_kind = peaks()
@@ -277,9 +294,13 @@ def run_ours(args, rank, world, local_rank):
                      'traffic': None, 'peak_kind': pk_kind,
                      'algorithmic_bytes_per_decision': ENV_BYTES_PER_DECISION,
                      'kernel_ms_per_step': env_ms},
+        'roofline_policy_gemm': {'kernel': 'd1::tc::gemm_kernel (layer 1: M=%d, N=256, K=1832)' % B,
+                                 'bound': 'tensor', 'achieved': gemm_tflops, 'peak': pk['bf16_tflops'],
+                                 'unit': 'TFLOP/s', 'frac': gemm_tflops / pk['bf16_tflops'],
+                                 'ms_per_launch': gemm_ms, 'peak_kind': pk_kind + ' burst'},
         'clocks': clk,
         'e2e': e2e,
-        'gpu_launches': args.steps * 2,
+        'gpu_launches': args.steps * 4,
     }
     if not args.no_cpu:
         cores = len(os.sched_getaffinity(0))

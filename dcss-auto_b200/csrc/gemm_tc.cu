@@ -7,10 +7,11 @@
 // tile; K advances in 64-element blocks through a 4-stage ring of shared-memory
 // buffers filled by TMA (128-byte swizzle, zero fill past the tensor edges).
 //
-// Warp roles (192 threads): warp 0 lane 0 issues TMA loads; warp 1 owns the
+// Warp roles (320 threads): warp 0 lane 0 issues TMA loads; warp 1 owns the
 // tensor-memory allocation and one lane issues tcgen05.mma (M=128, N=256, K=16
-// per instruction, accumulator in 256 TMEM columns); warps 2-5 are the epilogue,
-// each reading its 32 TMEM lanes (= 32 tile rows) with tcgen05.ld.
+// per instruction, accumulators in 2 x 256 TMEM columns); warps 2-9 are the
+// epilogue, warp w reading TMEM lanes 32*(w%4).. (= 32 tile rows) of one
+// 128-column half with tcgen05.ld.
 //
 // Outputs (any subset): bf16 C (row-major), bf16 C^T (feature-major, for the
 // weight-gradient GEMMs of the backward pass), and fp32 C (row-major, one slab
@@ -25,12 +26,15 @@
 
 #include "../../include/d1.h"
 
+
 namespace d1 {
 namespace tc {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int BIAS_BYTES = EPI_WARPS * (BN / 2) * 4;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + BIAS_BYTES;
+constexpr int SM_COUNT = 148;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 
@@ -121,30 +125,36 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
           "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])   \
         : "r"(taddr))
 
+// Persistent: one CTA per SM walks tiles t = blockIdx.x, blockIdx.x + gridDim.x,
+// ... (tile -> (m block, n block, K split)). The TMA ring runs continuously
+// across tile boundaries and the accumulator is double-buffered in TMEM
+// (2 x 256 columns), so the epilogue of one tile overlaps the MMAs of the next.
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p,
+                int tiles_m, int tiles_n, int tiles_total) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 1);
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), accum = smem_u32(bars + 2 * STAGES);
+    // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2]; then the TMEM slot
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+    const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN, split = blockIdx.z;
-    const int kt0 = split * p.k_tiles_per_split;
-    const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
-    const int nkt = kt1 - kt0;
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
-        mbar_init(accum, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(accf0 + 8 * b, 1);
+            mbar_init(acce0 + 8 * b, EPI_WARPS);  // one arrival per epilogue warp
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS)
+                     "r"(2 * TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -152,81 +162,119 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
-    bool ok = true;
 
     if (warp == 0 && lane == 0) {
-        // TMA producer
-        int issued = 0;
-        for (int i = 0; i < nkt && ok; i++) {
-            const int s = i % STAGES;
-            const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-            if (i >= STAGES && !mbar_wait(empty0 + 8 * s, ph ^ 1u)) {
-                ok = false;
-                break;
+        // ---- TMA producer: k blocks of every tile of this CTA, one ring
+        int it = 0, inflight_lo = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles_total && ok; t += gridDim.x) {
+            const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
+            const int kt0 = split * p.k_tiles_per_split;
+            const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
+            for (int kt = kt0; kt < kt1; kt++, it++) {
+                const int s = it % STAGES;
+                if (it >= STAGES && !mbar_wait(empty0 + 8 * s, ((uint32_t)(it / STAGES) & 1u) ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                if (it >= STAGES) inflight_lo = it - STAGES + 1;
+                const uint32_t a_dst = smem_u32(smem + s * STAGE_BYTES), b_dst = a_dst + A_BYTES;
+                mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
+                tma_load_2d(a_dst, &map_a, full0 + 8 * s, kt * BK, mt * BM);
+                tma_load_2d(b_dst, &map_b, full0 + 8 * s, kt * BK, nt * BN);
             }
-            const uint32_t a_dst = smem_u32(smem + s * STAGE_BYTES), b_dst = a_dst + A_BYTES;
-            mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
-            const int kx = (kt0 + i) * BK;
-            tma_load_2d(a_dst, &map_a, full0 + 8 * s, kx, m0);
-            tma_load_2d(b_dst, &map_b, full0 + 8 * s, kx, n0);
-            issued = i + 1;
         }
         if (!ok) {
             atomicExch(&g_error, 1);
-            // Drain copies already in flight before the CTA may exit.
-            for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
-                mbar_wait(full0 + 8 * (i % STAGES), (uint32_t)(i / STAGES) & 1u);
+            for (int i = inflight_lo; i < it; i++) mbar_wait(full0 + 8 * (i % STAGES), (uint32_t)(i / STAGES) & 1u);
         }
     } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        for (int i = 0; i < nkt; i++) {
-            const int s = i % STAGES;
-            if (!mbar_wait(full0 + 8 * s, (uint32_t)(i / STAGES) & 1u)) {
-                atomicExch(&g_error, 2);
+        // ---- MMA issuer
+        int it = 0, local = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles_total && ok; t += gridDim.x, local++) {
+            const int split = t / (tiles_m * tiles_n);
+            const int kt0 = split * p.k_tiles_per_split;
+            const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
+            const int b = local & 1;
+            const uint32_t acc = tmem + (uint32_t)(b * TMEM_COLS);
+            if (local >= 2 && !mbar_wait(acce0 + 8 * b, ((uint32_t)(local >> 1) & 1u) ^ 1u)) {
+                atomicExch(&g_error, 4);
                 ok = false;
                 break;
             }
             fence_after();
-            const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES), b_base = a_base + A_BYTES;
+            for (int kt = kt0; kt < kt1; kt++, it++) {
+                const int s = it % STAGES;
+                if (!mbar_wait(full0 + 8 * s, (uint32_t)(it / STAGES) & 1u)) {
+                    atomicExch(&g_error, 2);
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES), b_base = a_base + A_BYTES;
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; kk++)
-                mma(tmem, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), (i > 0 || kk > 0) ? 1u : 0u);
-            mma_commit(empty0 + 8 * s);
+                for (int kk = 0; kk < BK / 16; kk++)
+                    mma(acc, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32),
+                        (kt > kt0 || kk > 0) ? 1u : 0u);
+                mma_commit(empty0 + 8 * s);
+            }
+            mma_commit(accf0 + 8 * b);
         }
-        mma_commit(accum);
     } else if (warp >= 2) {
-        // Epilogue: warp w reads TMEM lanes 32*(w % 4) .. +31 = tile rows.
-        const int q = warp & 3;
-        const int row = m0 + q * 32 + lane;
-        if (!mbar_wait(accum, 0)) {
-            atomicExch(&g_error, 3);
-            ok = false;
-        }
-        fence_after();
-        if (ok) {
+        // ---- epilogue: warp w reads TMEM lanes 32*(w % 4) .. +31 (= tile rows)
+        // and column half (w - 2) / 4 of the accumulator.
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        float *bias_s = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES + 256) + (warp - 2) * (BN / 2);
+        int local = 0;
+        for (int t = blockIdx.x; t < tiles_total; t += gridDim.x, local++) {
+            const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
+            const int b = local & 1;
+            const int row = mt * BM + q * 32 + lane;
+            const int c0 = nt * BN + half * (BN / 2);
+            // this warp's 128 bias values (zero past N or without bias)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int col = c0 + lane * 4 + j;
+                bias_s[lane * 4 + j] = (p.bias && col < p.N) ? __ldg(p.bias + col) : 0.f;
+            }
+            __syncwarp();
+            if (!mbar_wait(accf0 + 8 * b, (uint32_t)(local >> 1) & 1u)) {
+                atomicExch(&g_error, 3);
+                break;
+            }
+            fence_after();
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 32; cc++) {
+            for (int cc = 0; cc < BN / 64; cc++) {
                 uint32_t v[32];
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32);
+                const uint32_t taddr = tmem + (uint32_t)(b * TMEM_COLS) + ((uint32_t)(q * 32) << 16) +
+                                       (uint32_t)(half * (BN / 2) + cc * 32);
                 __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the row/column guards
                 D1_TMEM_LD32(taddr, v);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                const int col0 = n0 + cc * 32;
+                const int col0 = c0 + cc * 32;
                 if (row >= p.M || col0 >= p.N) continue;
                 float f[32];
+                const float4 *bs = reinterpret_cast<const float4 *>(bias_s + cc * 32);
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    float x = __uint_as_float(v[j]);
-                    if (p.bias && col0 + j < p.N) x += p.bias[col0 + j];
-                    if (p.relu) x = fmaxf(x, 0.f);
-                    f[j] = x;
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 bb = bs[j / 4];
+                    f[j] = __uint_as_float(v[j]) + bb.x;
+                    f[j + 1] = __uint_as_float(v[j + 1]) + bb.y;
+                    f[j + 2] = __uint_as_float(v[j + 2]) + bb.z;
+                    f[j + 3] = __uint_as_float(v[j + 3]) + bb.w;
+                }
+                if (p.relu) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) f[j] = fmaxf(f[j], 0.f);
                 }
                 const bool full_cols = col0 + 32 <= p.N;
                 if (p.cf) {
                     float *dst = p.cf + (size_t)split * p.M * p.ldcf + (size_t)row * p.ldcf + col0;
                     if (full_cols) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4 *>(dst + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4 *>(dst + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 32; j++)
@@ -261,13 +309,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                         if (col0 + j < p.N) p.ct[(size_t)(col0 + j) * p.ldct + row] = __float2bfloat16_rn(f[j]);
                 }
             }
+            // Release this accumulator buffer to the MMA issuer.
+            fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce0 + 8 * b) : "memory");
         }
     }
     fence_before();
     __syncthreads();
     if (warp == 1) {
         fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TMEM_COLS)
+                     : "memory");
     }
 }
 
@@ -332,8 +385,16 @@ int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K,
         attr = true;
     }
     Params p{M, N, K, per, kt, bias, relu, (__nv_bfloat16 *)c, ldc, (__nv_bfloat16 *)ct, ldct, cf, ldcf};
-    dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, splits);
-    gemm_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
+    const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+    const int tiles = tiles_m * tiles_n * splits;
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = SM_COUNT;
+    }
+    const int grid = tiles < sms ? tiles : sms;
+    gemm_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, p, tiles_m, tiles_n, tiles);
     return (int)cudaGetLastError();
 }
 
