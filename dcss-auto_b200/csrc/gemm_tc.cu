@@ -45,6 +45,8 @@ struct Params {
     int k_tiles_per_split, k_tiles_total;
     const float *bias;   // may be null
     int relu;
+    const __nv_bfloat16 *mask;  // row-major [M, ldm]: zero where mask <= 0 (may be null)
+    int ldm;
     __nv_bfloat16 *c;    // row-major [M, ldc] (may be null)
     int ldc;
     __nv_bfloat16 *ct;   // feature-major [N, ldct] (may be null)
@@ -84,6 +86,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
+__device__ __forceinline__ bool full_cols_m(int col0, int n) { return col0 + 32 <= n; }
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -268,6 +271,23 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; j++) f[j] = fmaxf(f[j], 0.f);
                 }
+                if (p.mask) {
+                    const __nv_bfloat16 *mk = p.mask + (size_t)row * p.ldm + col0;
+                    if (full_cols_m(col0, p.N)) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            const uint4 raw = *reinterpret_cast<const uint4 *>(mk + j);
+                            const __nv_bfloat16 *h = reinterpret_cast<const __nv_bfloat16 *>(&raw);
+#pragma unroll
+                            for (int i = 0; i < 8; i++)
+                                if (!(__bfloat162float(h[i]) > 0.f)) f[j + i] = 0.f;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j >= p.N || !(__bfloat162float(mk[j]) > 0.f)) f[j] = 0.f;
+                    }
+                }
                 const bool full_cols = col0 + 32 <= p.N;
                 if (p.cf) {
                     float *dst = p.cf + (size_t)split * p.M * p.ldcf + (size_t)row * p.ldcf + col0;
@@ -362,7 +382,8 @@ using namespace d1::tc;
 extern "C" {
 
 int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
-            void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits, void *stream) {
+            const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits,
+            void *stream) {
     if (M <= 0 || N <= 0 || K <= 0 || !a || !b || (!c && !ct && !cf) || splits < 1) return D1_ERR_BAD_ARGUMENT;
     // TMA rules: 16-byte aligned bases and row pitches.
     if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) || (lda * 2) % 16 ||
@@ -371,6 +392,7 @@ int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K,
     if (c && ((reinterpret_cast<uintptr_t>(c) & 15) || ldc % 8 || ldc < N)) return D1_ERR_BAD_ARGUMENT;
     if (cf && ((reinterpret_cast<uintptr_t>(cf) & 15) || ldcf % 4 || ldcf < N)) return D1_ERR_BAD_ARGUMENT;
     if (ct && ldct < M) return D1_ERR_BAD_ARGUMENT;
+    if (mask && ((reinterpret_cast<uintptr_t>(mask) & 15) || ldm % 8 || ldm < N)) return D1_ERR_BAD_ARGUMENT;
     if (splits > 1 && (c || ct)) return D1_ERR_BAD_ARGUMENT;  // split-K writes fp32 partial slabs only
     const int kt = (K + BK - 1) / BK;
     if (splits > kt) splits = kt;
@@ -384,7 +406,8 @@ int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K,
         if (e != cudaSuccess) return (int)e;
         attr = true;
     }
-    Params p{M, N, K, per, kt, bias, relu, (__nv_bfloat16 *)c, ldc, (__nv_bfloat16 *)ct, ldct, cf, ldcf};
+    Params p{M, N, K, per, kt, bias, relu, (const __nv_bfloat16 *)mask, ldm, (__nv_bfloat16 *)c, ldc,
+             (__nv_bfloat16 *)ct, ldct, cf, ldcf};
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n * splits;
     static int sms = 0;

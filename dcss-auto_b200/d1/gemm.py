@@ -8,7 +8,7 @@ def _stream(t):
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
-def gemm(a, b, bias=None, relu=False, out=None, out_t=None, out_f32=None, splits=1):
+def gemm(a, b, bias=None, relu=False, out=None, out_t=None, out_f32=None, splits=1, mask=None):
     """act(a @ b.T + bias). a: bf16 [M, K], b: bf16 [N, K] (row pitches may exceed K).
     Any of out (bf16 [M, N]), out_t (bf16 [N, M]) and out_f32 (fp32 [splits, M, N])."""
     M, K = a.shape
@@ -20,6 +20,7 @@ def gemm(a, b, bias=None, relu=False, out=None, out_t=None, out_f32=None, splits
     lib = library()
     check(lib.d1_gemm(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), M, N, K,
                       None if bias is None else bias.data_ptr(), int(relu),
+                      None if mask is None else mask.data_ptr(), 0 if mask is None else mask.stride(0),
                       None if out is None else out.data_ptr(), 0 if out is None else out.stride(0),
                       None if out_t is None else out_t.data_ptr(), 0 if out_t is None else out_t.stride(0),
                       None if out_f32 is None else out_f32.data_ptr(), 0 if out_f32 is None else out_f32.stride(-2),

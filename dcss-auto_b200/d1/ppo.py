@@ -1,0 +1,168 @@
+"""GAE and the PPO update of gpu-d1/scripts/run_ring_ablations.py:354-372 on the
+B200 kernels, with BASELINE config 2's loss (value clipping, vf/entropy
+coefficients) and a switch for the reference loss (0.25 * MSE, no value clip).
+
+Per minibatch (all device work is libd1 kernels, launched on the current stream):
+
+  gather     X = obs[idx], X^T                    d1_ppo_gather
+  layer 1    h1 = relu(X W1^T + b1), h1^T          d1_gemm (tcgen05)
+  layer 2    h2 = relu(h1 W2^T + b2)               d1_gemm
+  loss       head, PPO loss, dlogits/dvalue,       d1_ppo_loss (fused)
+             dh2 = dhead Wh * relu'(h2), dh2^T, partials of dWh, dbh, db2
+  dW2        dh2^T h1 (split-K fp32 slabs)         d1_gemm + d1_reduce_slabs
+  dh1^T      (dh2 W2) * relu'(h1), transposed      d1_gemm (mask epilogue)
+  dW1        dh1^T X (split-K fp32 slabs)          d1_gemm + d1_reduce_slabs
+  db1        row sums of dh1^T                     d1_row_sum_bf16
+  all-reduce flat fp32 gradient (NCCL, multi-GPU)  torch.distributed
+  optimizer  grad-norm clip + Adam + bf16 copies   d1_sumsq + d1_adam
+
+The gradient of every minibatch is a mean over that rank's minibatch; with R
+ranks the all-reduced gradient is divided by R, so it equals the gradient of the
+union minibatch (every rank uses equal-size minibatches).
+"""
+import ctypes as C
+
+import torch
+
+from ._lib import check, library
+from . import gemm as G
+from .policy import HID, NOUT, OBS
+
+LOSS_TERMS = ('pg', 'vf', 'entropy', 'clip_count', 'approx_kl')
+
+
+class AdamSegment(C.Structure):
+    _fields_ = [('offset', C.c_int64), ('count', C.c_int64), ('rows', C.c_int), ('cols', C.c_int),
+                ('bf16', C.c_void_p), ('bf16_t', C.c_void_p)]
+
+
+class PPO:
+    def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
+                 ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
+                 gae_mode=1, splits=8, group=None):
+        self.policy, self.rollout = policy, rollout
+        self.mb, self.epochs = minibatch, epochs
+        self.lr, self.clip, self.vclip, self.vf_coef, self.ent_coef = lr, clip, vclip, vf_coef, ent_coef
+        self.max_grad_norm, self.gamma, self.lam, self.eps, self.betas = max_grad_norm, gamma, lam, adam_eps, betas
+        self.gae_mode, self.group = gae_mode, group
+        self.lib = library()
+        dev = policy.device
+        T, B = rollout.T, rollout.env.batch
+        self.total = T * B
+        if self.total % minibatch:
+            raise ValueError('rollout size must be a multiple of the minibatch')
+        f32, bf = dict(device=dev), dict(device=dev, dtype=torch.bfloat16)
+        self.adv = torch.empty((T, B), **f32)
+        self.ret = torch.empty((T, B), **f32)
+        self.stats = torch.zeros(2, dtype=torch.float64, device=dev)
+        self.grad = torch.zeros(policy.size, **f32)
+        self.m = torch.zeros(policy.size, **f32)
+        self.v = torch.zeros(policy.size, **f32)
+        self.sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
+        self.step_count = 0
+        mb = minibatch
+        self.x = torch.empty((mb, OBS), **bf)
+        self.xt = torch.empty((OBS, mb), **bf)
+        self.h1 = torch.empty((mb, HID), **bf)
+        self.h1t = torch.empty((HID, mb), **bf)
+        self.h2 = torch.empty((mb, HID), **bf)
+        self.dh2 = torch.empty((mb, HID), **bf)
+        self.dh2t = torch.empty((HID, mb), **bf)
+        self.dh1t = torch.empty((HID, mb), **bf)
+        self.s1 = G.splits_for(mb, splits)
+        self.slab1 = torch.empty((self.s1, HID, OBS), **f32)
+        self.s2 = G.splits_for(mb, splits)
+        self.slab2 = torch.empty((self.s2, HID, HID), **f32)
+        self.part_len = self.lib.d1_ppo_loss_part_len()
+        self.loss_blocks = 128
+        self.part = torch.empty((self.loss_blocks, self.part_len), **f32)
+        self.terms = torch.zeros(8, **f32)
+        self.history = []
+        lay = policy.layout
+        self.off = {k: lay[k][0] for k in lay}
+        head_len = NOUT * HID + NOUT + HID
+        assert self.off['bh'] == self.off['wh'] + NOUT * HID and self.off['b2'] == self.off['bh'] + NOUT
+        self.head_len = head_len
+        bfc = policy.bf16
+        segs = [AdamSegment(self.off['w1'], HID * OBS, HID, OBS, bfc['w1'].data_ptr(), None),
+                AdamSegment(self.off['w2'], HID * HID, HID, HID, bfc['w2'].data_ptr(), bfc['w2t'].data_ptr()),
+                AdamSegment(self.off['wh'], NOUT * HID, NOUT, HID, bfc['wh'].data_ptr(), None)]
+        self.segs = (AdamSegment * len(segs))(*segs)
+
+    @property
+    def stream(self):
+        return torch.cuda.current_stream(self.policy.device).cuda_stream
+
+    # ------------------------------------------------------------------ GAE
+    def advantages(self):
+        r = self.rollout
+        out = r.out  # [T, B, OUT]: reward at column 0, done at column 1
+        self.stats.zero_()
+        check(self.lib.d1_gae(out.data_ptr(), out[:, :, 1].data_ptr(), out.stride(0), out.stride(1),
+                              r.values.data_ptr(), r.T, r.env.batch, self.gamma, self.lam, self.adv.data_ptr(),
+                              self.ret.data_ptr(), self.stats.data_ptr(), self.gae_mode, self.stream), 'd1_gae')
+        count = float(self.total)
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.all_reduce(self.stats, group=self.group)
+            count *= dist.get_world_size(self.group)
+        self.adv_count = count
+        return self.adv, self.ret
+
+    # ------------------------------------------------------------------ update
+    def minibatch(self, idx):
+        """One gradient step on the rollout samples `idx` (int64, length mb)."""
+        p, r, lib, s = self.policy, self.rollout, self.lib, self.stream
+        mb = self.mb
+        obs = r.obs[:r.T].reshape(self.total, OBS)
+        check(lib.d1_ppo_gather(obs.data_ptr(), OBS, idx.data_ptr(), mb, self.x.data_ptr(), self.xt.data_ptr(),
+                                mb, s), 'd1_ppo_gather')
+        p.hidden_layers(self.x, h1=self.h1, h1t=self.h1t, h2=self.h2)
+        g = self.grad
+        check(lib.d1_ppo_loss(self.h2.data_ptr(), p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(),
+                              idx.data_ptr(), r.legal.data_ptr(), r.actions.data_ptr(), r.logp.data_ptr(),
+                              self.adv.data_ptr(), self.ret.data_ptr(), r.values.data_ptr(), self.stats.data_ptr(),
+                              self.adv_count, mb, self.clip, self.vclip, self.vf_coef, self.ent_coef,
+                              self.dh2.data_ptr(), self.dh2t.data_ptr(), mb, self.part.data_ptr(), self.loss_blocks,
+                              s), 'd1_ppo_loss')
+        # dWh, dbh, db2 straight into the flat gradient; loss terms aside
+        check(lib.d1_sum_rows(self.part.data_ptr(), self.loss_blocks, self.part_len, self.head_len,
+                              g[self.off['wh']:].data_ptr(), s), 'd1_sum_rows')
+        check(lib.d1_sum_rows(self.part[:, self.head_len:].data_ptr(), self.loss_blocks, self.part_len, 8,
+                              self.terms.data_ptr(), s), 'd1_sum_rows')
+        # dW2 = dh2^T h1
+        G.gemm(self.dh2t, self.h1t, out_f32=self.slab2, splits=self.s2)
+        check(lib.d1_reduce_slabs(self.slab2.data_ptr(), self.s2, HID * HID, g[self.off['w2']:].data_ptr(), s))
+        # dh1^T = ((dh2 W2) * relu'(h1))^T
+        G.gemm(self.dh2, p.bf16['w2t'], mask=self.h1, out_t=self.dh1t)
+        # dW1 = dh1^T X, db1 = row sums of dh1^T
+        G.gemm(self.dh1t, self.xt, out_f32=self.slab1, splits=self.s1)
+        check(lib.d1_reduce_slabs(self.slab1.data_ptr(), self.s1, HID * OBS, g[self.off['w1']:].data_ptr(), s))
+        check(lib.d1_row_sum_bf16(self.dh1t.data_ptr(), HID, mb, mb, g[self.off['b1']:].data_ptr(), s))
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.all_reduce(g, group=self.group)
+            g.div_(dist.get_world_size(self.group))
+        self.sumsq.zero_()
+        check(lib.d1_sumsq(g.data_ptr(), g.numel(), self.sumsq.data_ptr(), s))
+        self.step_count += 1
+        check(lib.d1_adam(p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
+                          self.sumsq.data_ptr(), g.numel(), self.lr, self.betas[0], self.betas[1], self.eps,
+                          self.max_grad_norm, self.step_count, self.segs, len(self.segs), s), 'd1_adam')
+        return self.terms
+
+    def update(self, generator=None):
+        """epochs x (total / mb) minibatch steps over a fresh permutation each epoch."""
+        dev = self.policy.device
+        for _ in range(self.epochs):
+            perm = torch.randperm(self.total, device=dev, generator=generator)
+            for i in range(0, self.total, self.mb):
+                self.minibatch(perm[i:i + self.mb])
+
+    def iteration(self, generator=None):
+        """Collect a rollout, compute advantages, update: one PPO iteration."""
+        r = self.rollout
+        r.collect()
+        self.advantages()
+        self.update(generator)
+        r.roll()

