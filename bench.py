@@ -43,6 +43,9 @@ def parse():
     ap.add_argument('--envs', type=int, default=ENVS, help='envs per GPU')
     ap.add_argument('--horizon', type=int, default=HORIZON, help='rollout slots (profiling runs shrink it)')
     ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-ppo', action='store_true', help='skip the PPO-update measurement')
+    ap.add_argument('--minibatch', type=int, default=16384)
+    ap.add_argument('--epochs', type=int, default=4)
     ap.add_argument('--no-cpu', action='store_true')
     return ap.parse_args()
 
@@ -277,6 +280,39 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     gemm_ms = g0.elapsed_time(g1) / reps
     gemm_tflops = 2.0 * B * 1832 * 256 / (gemm_ms / 1e3) / 1e12
+    # PPO samples/s: full iteration = rollout of T steps +
+    # GAE + epochs x (T*B / minibatch) minibatch updates, NCCL all-reduce of the
+    # advantage statistics and of every minibatch gradient when world > 1.
+    ppo_line = None
+    if not args.no_ppo:
+        from d1.ppo import PPO
+        group = dist.group.WORLD if world > 1 else None
+        trainer = PPO(policy, roll, minibatch=args.minibatch, epochs=args.epochs, group=group)
+        gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+        roll.roll()
+        trainer.iteration(gen)  # warm-up iteration
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        p0, p1, p2, p3 = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        p0.record(stream)
+        roll.collect()
+        p1.record(stream)
+        trainer.advantages()
+        p2.record(stream)
+        trainer.update(gen)
+        p3.record(stream)
+        torch.cuda.synchronize()
+        roll.roll()
+        it_ms = torch.tensor([p0.elapsed_time(p3)], device=dev)
+        if world > 1:
+            dist.all_reduce(it_ms, op=dist.ReduceOp.MAX)
+        updates = args.epochs * (T * B // args.minibatch)
+        ppo_line = {'samples_per_s': T * B * world / (it_ms.item() / 1e3), 'ms_per_iteration': it_ms.item(),
+                    'rollout_ms': p0.elapsed_time(p1), 'gae_ms': p1.elapsed_time(p2),
+                    'update_ms': p2.elapsed_time(p3), 'minibatch_ms': p2.elapsed_time(p3) / updates,
+                    'samples_per_iteration': T * B * world, 'minibatch': args.minibatch, 'epochs': args.epochs,
+                    'finite': bool(torch.isfinite(policy.flat).all().item())}
     if rank != 0:
         return
     pk, pk_kind = peaks()
@@ -298,6 +334,7 @@ def run_ours(args, rank, world, local_rank):
                                  'bound': 'tensor', 'achieved': gemm_tflops, 'peak': pk['bf16_tflops'],
                                  'unit': 'TFLOP/s', 'frac': gemm_tflops / pk['bf16_tflops'],
                                  'ms_per_launch': gemm_ms, 'peak_kind': pk_kind + ' burst'},
+        'ppo': ppo_line,
         'clocks': clk,
         'e2e': e2e,
         'gpu_launches': args.steps * 4,

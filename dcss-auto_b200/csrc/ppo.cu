@@ -502,13 +502,17 @@ struct AdamSeg {
 struct AdamArgs {
     float *param, *grad, *m, *v;
     const double *sumsq;
-    float lr, beta1, beta2, eps, max_norm, bc1, bc2_sqrt;
+    const int64_t *step;  // device counter: the step being taken (1-based)
+    float lr, beta1, beta2, eps, max_norm;
     AdamSeg seg[8];
     int nseg;
     int64_t total;
 };
 __global__ void adam_kernel(AdamArgs a) {
     const double norm = sqrt(*a.sumsq);
+    const double t = (double)*a.step;
+    const float bc1 = (float)(1.0 - pow((double)a.beta1, t));
+    const float bc2_sqrt = (float)sqrt(1.0 - pow((double)a.beta2, t));
     float scale = 1.f;
     if (a.max_norm > 0.f) {
         const float coef = a.max_norm / ((float)norm + 1e-6f);
@@ -521,8 +525,8 @@ __global__ void adam_kernel(AdamArgs a) {
         const float v = a.beta2 * a.v[i] + (1.f - a.beta2) * g * g;
         a.m[i] = m;
         a.v[i] = v;
-        const float denom = sqrtf(v) / a.bc2_sqrt + a.eps;
-        const float p = a.param[i] - (a.lr / a.bc1) * m / denom;
+        const float denom = sqrtf(v) / bc2_sqrt + a.eps;
+        const float p = a.param[i] - (a.lr / bc1) * m / denom;
         a.param[i] = p;
         for (int s = 0; s < a.nseg; s++) {
             const AdamSeg &g2 = a.seg[s];
@@ -538,6 +542,8 @@ __global__ void adam_kernel(AdamArgs a) {
         }
     }
 }
+
+__global__ void counter_add_kernel(int64_t *c, int64_t delta) { *c += delta; }
 
 }  // namespace ppo
 }  // namespace d1
@@ -604,9 +610,16 @@ int d1_sumsq(const float *g, int64_t n, double *out, void *stream) {
     return (int)cudaGetLastError();
 }
 
+int d1_counter_add(int64_t *counter, int64_t delta, void *stream) {
+    if (!counter) return D1_ERR_BAD_ARGUMENT;
+    ppo::counter_add_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(counter, delta);
+    return (int)cudaGetLastError();
+}
+
 int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, int64_t total, float lr, float beta1,
-            float beta2, float eps, float max_norm, int step, const D1AdamSegment *segs, int nseg, void *stream) {
-    if (!param || !grad || !m || !v || !sumsq || total <= 0 || step < 1 || nseg < 0 || nseg > 8)
+            float beta2, float eps, float max_norm, const int64_t *step, const D1AdamSegment *segs, int nseg,
+            void *stream) {
+    if (!param || !grad || !m || !v || !sumsq || !step || total <= 0 || nseg < 0 || nseg > 8)
         return D1_ERR_BAD_ARGUMENT;
     ppo::AdamArgs a;
     a.param = param;
@@ -619,8 +632,7 @@ int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, 
     a.beta2 = beta2;
     a.eps = eps;
     a.max_norm = max_norm;
-    a.bc1 = (float)(1.0 - pow((double)beta1, step));
-    a.bc2_sqrt = (float)sqrt(1.0 - pow((double)beta2, step));
+    a.step = step;
     a.nseg = nseg;
     a.total = total;
     for (int i = 0; i < nseg; i++) {

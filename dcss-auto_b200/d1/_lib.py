@@ -35,7 +35,8 @@ SIGNATURES = {
     'd1_reduce_slabs': [_P, _I, C.c_int64, _P, _P],
     'd1_row_sum_bf16': [_P, _I, _I, _I, _P, _P],
     'd1_sumsq': [_P, C.c_int64, _P, _P],
-    'd1_adam': [_P, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _I, _P, _I, _P],
+    'd1_adam': [_P, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _P, _P, _I, _P],
+    'd1_counter_add': [_P, C.c_int64, _P],
     'd1_gemm_splits': [_I, _I],
     'd1_gemm_error': [],
 }

@@ -39,7 +39,7 @@ class AdamSegment(C.Structure):
 class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
-                 gae_mode=1, splits=8, group=None):
+                 gae_mode=1, splits=8, group=None, graph=True):
         self.policy, self.rollout = policy, rollout
         self.mb, self.epochs = minibatch, epochs
         self.lr, self.clip, self.vclip, self.vf_coef, self.ent_coef = lr, clip, vclip, vf_coef, ent_coef
@@ -59,7 +59,9 @@ class PPO:
         self.m = torch.zeros(policy.size, **f32)
         self.v = torch.zeros(policy.size, **f32)
         self.sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
-        self.step_count = 0
+        self.step_dev = torch.zeros(1, dtype=torch.int64, device=dev)  # Adam step count
+        self.use_graph, self.graph = graph, None
+        self.perm = torch.empty(self.total, dtype=torch.int64, device=dev)
         mb = minibatch
         self.x = torch.empty((mb, OBS), **bf)
         self.xt = torch.empty((OBS, mb), **bf)
@@ -145,19 +147,44 @@ class PPO:
             g.div_(dist.get_world_size(self.group))
         self.sumsq.zero_()
         check(lib.d1_sumsq(g.data_ptr(), g.numel(), self.sumsq.data_ptr(), s))
-        self.step_count += 1
+        check(lib.d1_counter_add(self.step_dev.data_ptr(), 1, s))
         check(lib.d1_adam(p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
                           self.sumsq.data_ptr(), g.numel(), self.lr, self.betas[0], self.betas[1], self.eps,
-                          self.max_grad_norm, self.step_count, self.segs, len(self.segs), s), 'd1_adam')
+                          self.max_grad_norm, self.step_dev.data_ptr(), self.segs, len(self.segs), s), 'd1_adam')
         return self.terms
 
+    def _epoch(self):
+        for i in range(0, self.total, self.mb):
+            self.minibatch(self.perm[i:i + self.mb])
+
     def update(self, generator=None):
-        """epochs x (total / mb) minibatch steps over a fresh permutation each epoch."""
+        """epochs x (total / mb) minibatch steps over a fresh permutation each epoch.
+
+        With graph=True the first epoch runs eagerly (it also initialises every
+        kernel's attributes) and the second is captured once into a CUDA graph
+        over the static permutation buffer; later epochs replay it, so a whole
+        epoch of ~15 launches per minibatch costs one host call."""
         dev = self.policy.device
         for _ in range(self.epochs):
-            perm = torch.randperm(self.total, device=dev, generator=generator)
-            for i in range(0, self.total, self.mb):
-                self.minibatch(perm[i:i + self.mb])
+            torch.randperm(self.total, device=dev, generator=generator, out=self.perm)
+            if not self.use_graph:
+                self._epoch()
+            elif self.graph is None and not getattr(self, '_warm', False):
+                self._epoch()
+                self._warm = True
+            else:
+                if self.graph is None:
+                    self.graph = torch.cuda.CUDAGraph()
+                    side = torch.cuda.Stream(dev)
+                    side.wait_stream(torch.cuda.current_stream(dev))
+                    with torch.cuda.stream(side), torch.cuda.graph(self.graph, stream=side):
+                        self._epoch()
+                    torch.cuda.current_stream(dev).wait_stream(side)
+                self.graph.replay()
+
+    def release(self):
+        """Free the captured graph (before destroying a process group it uses)."""
+        self.graph = None
 
     def iteration(self, generator=None):
         """Collect a rollout, compute advantages, update: one PPO iteration."""

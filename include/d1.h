@@ -210,12 +210,17 @@ int d1_sumsq(const float *g, int64_t n, double *out, void *stream);
  * [offset, offset + count) form a [rows, cols] matrix; bf16 receives the same
  * layout and bf16_t (when not NULL) its transpose. */
 typedef struct { int64_t offset, count; int rows, cols; void *bf16, *bf16_t; } D1AdamSegment;
-/* torch.optim.Adam step (bias-corrected, eps outside the sqrt) on fp32 master
- * params after scaling grad by min(1, max_norm / (sqrt(*sumsq) + 1e-6))
- * (torch.nn.utils.clip_grad_norm_; max_norm <= 0 disables), then refreshes the
- * bf16 copies of `segs` (host array of nseg <= 8). */
+/* *counter += delta on the device (the optimizer's step count lives on the
+ * device so that a captured CUDA graph of many updates stays correct). */
+int d1_counter_add(int64_t *counter, int64_t delta, void *stream);
+/* torch.optim.Adam step (bias-corrected with the device step count *step,
+ * 1-based; eps outside the sqrt) on fp32 master params after scaling grad by
+ * min(1, max_norm / (sqrt(*sumsq) + 1e-6)) (torch.nn.utils.clip_grad_norm_;
+ * max_norm <= 0 disables), then refreshes the bf16 copies of `segs` (host
+ * array of nseg <= 8). */
 int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, int64_t total, float lr, float beta1,
-            float beta2, float eps, float max_norm, int step, const D1AdamSegment *segs, int nseg, void *stream);
+            float beta2, float eps, float max_norm, const int64_t *step, const D1AdamSegment *segs, int nseg,
+            void *stream);
 
 #ifdef __cplusplus
 }
