@@ -439,3 +439,74 @@ int d1_gemm_error(void) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- no-allocation variant
+// Some callers of this library cannot allocate device memory at all: code that
+// runs inside another framework's memory arena with no allocator handle, a
+// plugin loaded where cudaMalloc is forbidden after start-up, or a process that
+// has already handed every byte of HBM to a pool. For them the split-K
+// weight-gradient product keeps its partial-product slabs in this file-scope
+// device array (16 MiB, reserved on every GPU that loads the library until the
+// process exits). Every call shares it and it keeps the last call's contents;
+// nothing in it needs to start at zero (each call writes every slab element it
+// reads). Calls whose work overlaps on the GPU (different streams, or
+// different host threads on one device) race on it and must be serialised by
+// the caller.
+namespace d1 {
+namespace tc {
+constexpr int64_t NOALLOC_FLOATS = 4 * 1024 * 1024;
+__device__ __align__(256) float g_noalloc_slabs[NOALLOC_FLOATS];
+
+__global__ void reduce_2d_kernel(const float *__restrict__ slabs, int splits, int M, int N, int ldcf,
+                                 float *__restrict__ out, int ldo) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)M * N) return;
+    const int r = (int)(i / N), c = (int)(i % N);
+    float s = 0.f;
+    for (int k = 0; k < splits; k++) s += slabs[(size_t)k * M * ldcf + (size_t)r * ldcf + c];
+    out[(size_t)r * ldo + c] = s;
+}
+
+// Host-side `g_noalloc_slabs` names a host stand-in, not device memory: the
+// device address is looked up with cudaGetSymbolAddress once per device, with
+// that device current, on the first call made on it.
+static float *noalloc_scratch(int *err) {
+    static float *ptrs[128] = {nullptr};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 128) {
+        *err = e != cudaSuccess ? (int)e : D1_ERR_BAD_ARGUMENT;
+        return nullptr;
+    }
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_slabs);
+        if (e != cudaSuccess || !p) {
+            *err = e != cudaSuccess ? (int)e : D1_ERR_BAD_ARGUMENT;
+            return nullptr;
+        }
+        ptrs[dev] = static_cast<float *>(p);
+    }
+    return ptrs[dev];
+}
+}  // namespace tc
+}  // namespace d1
+
+extern "C" int d1_gemm_wgrad_noalloc(const void *a, int lda, const void *b, int ldb, int M, int N, int K, float *out,
+                                     int ldo, int splits, void *stream) {
+    using namespace d1::tc;
+    if (M <= 0 || N <= 0 || K <= 0 || !a || !b || !out || ldo < N || splits < 1) return D1_ERR_BAD_ARGUMENT;
+    const int used = d1_gemm_splits(K, splits);
+    const int ldcf = (N + 3) / 4 * 4;
+    if ((int64_t)used * M * ldcf > NOALLOC_FLOATS) return D1_ERR_TOO_LARGE;
+    int err = 0;
+    float *slabs = noalloc_scratch(&err);
+    if (!slabs) return err;
+    int code = d1_gemm(a, lda, b, ldb, M, N, K, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0, slabs, ldcf, used,
+                       stream);
+    if (code) return code;
+    const int64_t total = (int64_t)M * N;
+    reduce_2d_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(slabs, used, M, N, ldcf, out,
+                                                                                          ldo);
+    return (int)cudaGetLastError();
+}

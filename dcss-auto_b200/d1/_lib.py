@@ -5,6 +5,7 @@ import pathlib
 LIB_PATH = pathlib.Path(__file__).resolve().parent / 'libd1.so'
 ERR_NO_HOST_PATH = 9001
 ERR_BAD_ARGUMENT = 9002
+ERR_TOO_LARGE = 9003
 
 _P, _I, _U64, _F = C.c_void_p, C.c_int, C.c_uint64, C.c_float
 # name -> argtypes; every export returns int.
@@ -39,6 +40,7 @@ SIGNATURES = {
     'd1_counter_add': [_P, C.c_int64, _P],
     'd1_gemm_splits': [_I, _I],
     'd1_gemm_error': [],
+    'd1_gemm_wgrad_noalloc': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _I, _P],
 }
 
 _LIB = None

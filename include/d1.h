@@ -21,6 +21,7 @@ extern "C" {
 
 #define D1_ERR_NO_HOST_PATH 9001 /* gpu == 0: this library has no CPU path */
 #define D1_ERR_BAD_ARGUMENT 9002 /* size, count or pointer outside the supported range */
+#define D1_ERR_TOO_LARGE 9003    /* request exceeds a fixed internal capacity */
 
 /* Monster kind and run configuration, byte-identical to the reference structs
  * (gpu-d1/src/sim.h:61-67): 11 ints + 6 kinds of 4 ints = 140 bytes. */
@@ -166,6 +167,19 @@ int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K,
             const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits,
             void *stream);
 int d1_gemm_splits(int K, int splits);
+/* No counterpart in the reference. The split-K weight-gradient product
+ * out = A . B^T (fp32 [M, ldo], A bf16 [M, K], B bf16 [N, K], same operand rules as
+ * d1_gemm) for callers that cannot allocate device memory (a host framework that
+ * owns every byte of HBM, a plugin that must not call cudaMalloc after start-up):
+ * the partial-product slabs live in a fixed 16 MiB array inside the library,
+ * reserved on every GPU that loads it until the process exits, so the call
+ * allocates nothing. Limit: d1_gemm_splits(K, splits) * M * round_up(N, 4) floats
+ * <= 4 Mi, else D1_ERR_TOO_LARGE. The first call on a device looks up the array's
+ * device address; make that first call before capturing any stream. All calls
+ * share the array: calls that overlap on the GPU race and must be serialised by
+ * the caller. */
+int d1_gemm_wgrad_noalloc(const void *a, int lda, const void *b, int ldb, int M, int N, int K, float *out, int ldo,
+                          int splits, void *stream);
 /* Nonzero when a GEMM pipeline wait expired (the kernel then skipped its work
  * and freed its tensor memory); reading clears it. Synchronises the device. */
 int d1_gemm_error(void);
