@@ -304,6 +304,7 @@ def run_ours(args, rank, world, local_rank):
         p3.record(stream)
         torch.cuda.synchronize()
         roll.roll()
+        trainer.release()  # its captured graph holds NCCL calls: free it before the process group goes
         it_ms = torch.tensor([p0.elapsed_time(p3)], device=dev)
         if world > 1:
             dist.all_reduce(it_ms, op=dist.ReduceOp.MAX)
