@@ -26,7 +26,16 @@ namespace spec {
 
 constexpr int MAXM = 11, OBS = 1832, CELLS = 225, ACTIONS = 12, OUT = 10, COMPACT = 56;
 constexpr int ROW = 2048, PL = 210, OFF_VIS = 64, OFF_MON = 128, OFF_FLOOR = 256, OFF_VIEWED = 256 + 4 * PL;
-constexpr int WARPS = 4, MAX_RAYS = 320;
+#ifndef D1_SPEC_WARPS
+#define D1_SPEC_WARPS 1
+#endif
+#ifndef D1_SPEC_MIN_WARPS
+#define D1_SPEC_MIN_WARPS 24
+#endif
+// Warps (envs) per block, and the resident warps per SM the register budget is
+// sized for (a launch-bounds hint).
+constexpr int WARPS = D1_SPEC_WARPS, MIN_BLOCKS = (D1_SPEC_MIN_WARPS + D1_SPEC_WARPS - 1) / D1_SPEC_WARPS;
+constexpr int MAX_RAYS = 320;
 constexpr int PRIM_WAIT = 8, PRIM_DESCEND = 9;
 
 // ------------------------------------------------------------------ RNG
@@ -83,10 +92,13 @@ struct Smem {
     uint8_t opqb[32];
     uint8_t occ_ch[CELLS + 7];
 };
-struct Rays {
-    unsigned long long blk[MAX_RAYS];
-    uint8_t ex[MAX_RAYS], ey[MAX_RAYS];
+// The LOS ray fan in global memory (2.2 KB, L1-resident): per ray a 64-bit
+// blocker mask over the 8x8 quadrant and its end cell.
+struct RayArgs {
+    const uint4 *ray;  // {blocker mask lo, hi, end bit index ey*8+ex, 0}
+    int n;
 };
+constexpr int RAY_ITERS = MAX_RAYS / 32;
 
 struct Env {
     WarpPhilox rng;
@@ -143,20 +155,26 @@ __device__ __forceinline__ void or_row15(uint32_t *r, int s, uint32_t m) {
 // Native ray fan (gpu-d1/scripts/compile_corpus.py:67-81) for the 15x15 view:
 // in each quadrant a ray dies on any in-map wall it crosses; live rays light
 // their end cell if it is on the map; the origin is always lit.
-__device__ void compute_los(Env &e, const Rays &rays, int nrays) {
+__device__ void compute_los(Env &e, const RayArgs &ra) {
     Smem &s = *e.sm;
     const int lane = e.lane, px = e.player % W, py = e.player / W;
     {
+        // lane = quadrant q * 8 + row y: the 8 cells x = 0..7 outward from the
+        // player in that quadrant row; opaque = on the map and not floor.
         const int q = lane >> 3, y = lane & 7;
-        const int sx = (q == 0 || q == 3) ? 1 : -1, sy = (q < 2) ? 1 : -1;
+        const bool east = (q == 0 || q == 3);
+        const int sy = (q < 2) ? 1 : -1;
         const int cy = py + sy * y;
         uint32_t b = 0;
         if (cy >= 0 && cy < H) {
-#pragma unroll
-            for (int x = 0; x < 8; x++) {
-                const int cx = px + sx * x;
-                if (cx >= 0 && cx < W && !bitp(s.floor, cy * W + cx)) b |= 1u << x;
-            }
+            const uint32_t *row = s.floor + cy * 3;
+            // 15 columns px-7 .. px+7 and which of them are on the map
+            const uint32_t fl = row15(row, px - 7);
+            uint32_t on = 0x7fffu;
+            if (px - 7 < 0) on &= 0x7fffu << (7 - px);
+            if (px + 7 > W - 1) on &= 0x7fffu >> (px + 7 - (W - 1));
+            const uint32_t opq15 = on & ~fl;
+            b = east ? (opq15 >> 7) & 0xffu : (__brev(opq15) >> 24) & 0xffu;  // west: bit x = column px - x
         }
         s.opqb[lane] = (uint8_t)b;
     }
@@ -166,9 +184,16 @@ __device__ void compute_los(Env &e, const Rays &rays, int nrays) {
     const unsigned long long o2 = *reinterpret_cast<const unsigned long long *>(s.opqb + 16);
     const unsigned long long o3 = *reinterpret_cast<const unsigned long long *>(s.opqb + 24);
     unsigned long long v0 = 0, v1 = 0, v2 = 0, v3 = 0;
-    for (int r = lane; r < nrays; r += 32) {
-        const unsigned long long blk = rays.blk[r];
-        const unsigned long long endb = 1ull << (rays.ey[r] * 8 + rays.ex[r]);
+    uint4 rr[RAY_ITERS];
+#pragma unroll
+    for (int i = 0; i < RAY_ITERS; i++) {
+        const int r = lane + 32 * i;
+        rr[i] = r < ra.n ? __ldg(ra.ray + r) : make_uint4(0xffffffffu, 0xffffffffu, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < RAY_ITERS; i++) {
+        const unsigned long long blk = (unsigned long long)rr[i].x | ((unsigned long long)rr[i].y << 32);
+        const unsigned long long endb = 1ull << rr[i].z;
         if (!(blk & o0)) v0 |= endb;
         if (!(blk & o1)) v1 |= endb;
         if (!(blk & o2)) v2 |= endb;
@@ -357,7 +382,7 @@ __device__ int kth_floor(const Env &e, int k) {
 
 __device__ __forceinline__ int occupant(const Env &e, int p) { return d1::occupant(e.m_pos, e.m_hp, p); }
 
-__device__ void reset(Env &e, const D1SpecConfig &c, const Rays &rays, int nrays) {
+__device__ void reset(Env &e, const D1SpecConfig &c, const RayArgs &ra) {
     gen_map(e);
     const int nf = floor_count(e);
     e.stairs = kth_floor(e, rng_r(e.rng, nf));
@@ -420,7 +445,7 @@ __device__ void reset(Env &e, const D1SpecConfig &c, const Rays &rays, int nrays
     e.floor_dirty = true;
     e.dirty_lo = 0;
     e.dirty_hi = H - 1;
-    compute_los(e, rays, nrays);
+    compute_los(e, ra);
     reveal(e);
 }
 
@@ -628,7 +653,7 @@ struct Prim {
 };
 
 // One physical turn (learn.cu:505-598 with the sleep/explore/stairs variants).
-__device__ Prim primitive(Env &e, const D1SpecConfig &c, const Rays &rays, int nrays, int extra_layers, int d) {
+__device__ Prim primitive(Env &e, const D1SpecConfig &c, const RayArgs &ra, int extra_layers, int d) {
     Prim r;
     int reward_milli = -1;
     e.blocks = 0;
@@ -656,7 +681,7 @@ __device__ Prim primitive(Env &e, const D1SpecConfig &c, const Rays &rays, int n
                 }
             } else {
                 e.player = p;
-                compute_los(e, rays, nrays);
+                compute_los(e, ra);
             }
         }
     }
@@ -699,7 +724,7 @@ __device__ Prim primitive(Env &e, const D1SpecConfig &c, const Rays &rays, int n
 // HP, an awake monster in view, or the end), 10 attack the weakest visible
 // adjacent monster, 11 descend. Illegal actions cost one wait turn.
 // Returns out[lane] for lane < OUT.
-__device__ float decision(Env &e, const D1SpecConfig &c, const Rays &rays, int nrays, int extra_layers, int a) {
+__device__ float decision(Env &e, const D1SpecConfig &c, const RayArgs &ra, int extra_layers, int a) {
     float total = 0.f;
     int elapsed = 0;
     bool invalid = false;
@@ -720,7 +745,7 @@ __device__ float decision(Env &e, const D1SpecConfig &c, const Rays &rays, int n
             else invalid = true;
         } else
             invalid = true;
-        r = primitive(e, c, rays, nrays, extra_layers, d);
+        r = primitive(e, c, ra, extra_layers, d);
         elapsed++;
         total += r.reward;
         if (r.done || invalid || a != 9) break;
@@ -741,7 +766,7 @@ __device__ float decision(Env &e, const D1SpecConfig &c, const Rays &rays, int n
     }
     if (r.done) {
         e.episode++;
-        reset(e, c, rays, nrays);
+        reset(e, c, ra);
     }
     return o;
 }
@@ -777,26 +802,20 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
     const int sdx = e.stairs % W - px, sdy = e.stairs / W - py;
     const int sj = (sdx >= -7 && sdx <= 7 && sdy >= -7 && sdy <= 7) ? (sdy + 7) * 15 + sdx + 7 : -1;
     uint4 *dst = reinterpret_cast<uint4 *>(obs);
-    for (int j = lane; j < CELLS; j += 32) {
-        const int wy = j / 15, wx = j - wy * 15;
-        int ch = 0;
-        if ((s.vmask[wy] >> wx) & 1u) {
-            if (!((s.fmask[wy] >> wx) & 1u)) ch = 1;
-            else {
-                const int m = s.occ_ch[j];
-                if (m != 0xff) ch = m;
-                else if (j == sj) ch = 4;
-                else ch = ((s.vis[wy] >> wx) & 1u) ? 3 : 2;
-            }
-        }
+#pragma unroll
+    for (int k = 0; k < (CELLS + 31) / 32; k++) {
+        const int j = lane + 32 * k;
+        const int jc = j < CELLS ? j : CELLS - 1;
+        const int wy = jc / 15, wx = jc - wy * 15;
+        const uint32_t vm = s.vmask[wy], fm = s.fmask[wy], vr = s.vis[wy];
+        const int m = s.occ_ch[jc];
+        const int floor_ch = m != 0xff ? m : (jc == sj ? 4 : (((vr >> wx) & 1u) ? 3 : 2));
+        const int ch = ((vm >> wx) & 1u) ? (((fm >> wx) & 1u) ? floor_ch : 1) : 0;
         // bf16 1.0 = 0x3f80 in half-word `ch`
         const uint32_t one = 0x3f80u << (16 * (ch & 1));
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if ((ch >> 1) == 0) v.x = one;
-        else if ((ch >> 1) == 1) v.y = one;
-        else if ((ch >> 1) == 2) v.z = one;
-        else v.w = one;
-        dst[j] = v;
+        const int w = ch >> 1;
+        const uint4 v = make_uint4(w == 0 ? one : 0u, w == 1 ? one : 0u, w == 2 ? one : 0u, w == 3 ? one : 0u);
+        if (j < CELLS) dst[j] = v;
     }
     // scalars
     const int nvis = __popc(__ballot_sync(FULL, mvis));
@@ -816,40 +835,23 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
     const int na = __shfl_sync(FULL, e.m_awake, near < 0 ? 0 : near), nk = __shfl_sync(FULL, e.m_kind, near < 0 ? 0 : near);
     const int op = __shfl_sync(FULL, e.m_pos, ogre < 0 ? 0 : ogre), oh = __shfl_sync(FULL, e.m_hp, ogre < 0 ? 0 : ogre);
     const int oa = __shfl_sync(FULL, e.m_awake, ogre < 0 ? 0 : ogre);
-    float f = 0.f;
-    switch (lane) {
-        case 0: f = e.hp / (float)c.hp; break;
-        case 1: f = e.regen / 100.f; break;
-        case 2: f = e.ticks / (float)c.limit; break;
-        case 3: f = e.killed / 10.f; break;
-        case 4: f = px / 80.f; break;
-        case 5: f = py / 70.f; break;
-        case 6: f = nvis / 10.f; break;
-        case 7: f = nvis_awake / 10.f; break;
-        case 8: f = near >= 0 ? 1.f : 0.f; break;
-        case 9: f = near >= 0 ? (np % W - px) / 7.f : 0.f; break;
-        case 10: f = near >= 0 ? (np / W - py) / 7.f : 0.f; break;
-        case 11: f = near >= 0 ? nh / 16.f : 0.f; break;
-        case 12: f = near >= 0 ? (float)na : 0.f; break;
-        case 13: f = near >= 0 ? nk / 4.f : 0.f; break;
-        case 14: f = known ? 1.f : 0.f; break;
-        case 15: f = known ? (e.stairs % W - px) / 80.f : 0.f; break;
-        case 16: f = known ? (e.stairs / W - py) / 70.f : 0.f; break;
-        case 17: f = e.player == e.stairs ? 1.f : 0.f; break;
-        case 18: f = nadj / 8.f; break;
-        case 19: f = weakest / 16.f; break;
-        case 20: f = rest_ok ? 1.f : 0.f; break;
-        case 21: f = attack_ok ? 1.f : 0.f; break;
-        case 22: f = e.floor_seen / 1024.f; break;
-        case 23: f = e.blocks / 2.f; break;
-        case 24: f = 1.f; break;
-        case 25: f = ogre >= 0 ? 1.f : 0.f; break;
-        case 26: f = ogre >= 0 ? (op % W - px) / 7.f : 0.f; break;
-        case 27: f = ogre >= 0 ? (op / W - py) / 7.f : 0.f; break;
-        case 28: f = ogre >= 0 ? (float)oa : 0.f; break;
-        case 29: f = ogre >= 0 ? oh / 30.f : 0.f; break;
-        default: break;
-    }
+    // Feature `lane` = num[lane] / den[lane] with the same operands as the
+    // oracle's expressions (every value is an int or a 0/1 flag over a float
+    // constant), so one correctly rounded division per lane reproduces it.
+    const int npx = near >= 0 ? np % W - px : 0, npy = near >= 0 ? np / W - py : 0;
+    const int opx = ogre >= 0 ? op % W - px : 0, opy = ogre >= 0 ? op / W - py : 0;
+    const float num[32] = {(float)e.hp, (float)e.regen, (float)e.ticks, (float)e.killed, (float)px, (float)py,
+                           (float)nvis, (float)nvis_awake, near >= 0 ? 1.f : 0.f, (float)npx, (float)npy,
+                           near >= 0 ? (float)nh : 0.f, near >= 0 ? (float)na : 0.f, near >= 0 ? (float)nk : 0.f,
+                           known ? 1.f : 0.f, known ? (float)(e.stairs % W - px) : 0.f,
+                           known ? (float)(e.stairs / W - py) : 0.f, e.player == e.stairs ? 1.f : 0.f, (float)nadj,
+                           (float)weakest, rest_ok ? 1.f : 0.f, attack_ok ? 1.f : 0.f, (float)e.floor_seen,
+                           (float)e.blocks, 1.f, ogre >= 0 ? 1.f : 0.f, (float)opx, (float)opy,
+                           ogre >= 0 ? (float)oa : 0.f, ogre >= 0 ? (float)oh : 0.f, 0.f, 0.f};
+    const float den[32] = {(float)c.hp, 100.f, (float)c.limit, 10.f, 80.f, 70.f, 10.f, 10.f, 1.f, 7.f, 7.f, 16.f,
+                           1.f, 4.f, 1.f, 80.f, 70.f, 1.f, 8.f, 16.f, 1.f, 1.f, 1024.f, 2.f, 1.f, 1.f, 7.f, 7.f,
+                           1.f, 30.f, 1.f, 1.f};
+    const float f = num[lane] / den[lane];
     obs[1800 + lane] = __float2bfloat16_rn(f);
     if (lane < 8) {
         const bool ok = floor_at(e, neighbor(e.player, lane));
@@ -885,13 +887,28 @@ __device__ void load(Env &e, const uint8_t *row) {
     e.m_hp = e.lane < MAXM ? m[32 + l] : 0;
     e.m_kind = row[OFF_MON + 96 + l];
     e.m_awake = row[OFF_MON + 112 + l];
+    // All plane words are loaded into registers before any shared-memory store:
+    // the compiler cannot prove the generic shared pointer does not alias the
+    // row, so interleaving would serialise the DRAM round trips.
     const uint32_t *fp = reinterpret_cast<const uint32_t *>(row + OFF_FLOOR);
     const uint32_t *vp = reinterpret_cast<const uint32_t *>(row + OFF_VIEWED);
-    for (int r = e.lane; r < PL; r += 32) {
-        e.sm->floor[r] = fp[r];
-        e.sm->viewed[r] = vp[r];
+    uint32_t fw[7], vw[7];
+#pragma unroll
+    for (int i = 0; i < 7; i++) {
+        const int r = e.lane + 32 * i;
+        fw[i] = r < PL ? __ldg(fp + r) : 0u;
+        vw[i] = r < PL ? __ldg(vp + r) : 0u;
     }
-    if (e.lane < 16) e.sm->vis[e.lane] = reinterpret_cast<const uint16_t *>(row + OFF_VIS)[e.lane];
+    const uint32_t vis16 = e.lane < 16 ? reinterpret_cast<const uint16_t *>(row + OFF_VIS)[e.lane] : 0u;
+#pragma unroll
+    for (int i = 0; i < 7; i++) {
+        const int r = e.lane + 32 * i;
+        if (r < PL) {
+            e.sm->floor[r] = fw[i];
+            e.sm->viewed[r] = vw[i];
+        }
+    }
+    if (e.lane < 16) e.sm->vis[e.lane] = vis16;
     __syncwarp();
     e.rng.refill();
     e.dirty_lo = H;
@@ -926,29 +943,10 @@ __device__ void store(const Env &e, uint8_t *row) {
         for (int r = e.dirty_lo * 3 + e.lane; r < (e.dirty_hi + 1) * 3; r += 32) vp[r] = e.sm->viewed[r];
 }
 
-__device__ __forceinline__ int load_rays(Rays &rays, const unsigned long long *blk, const uint8_t *ex,
-                                         const uint8_t *ey, int nrays) {
-    for (int i = threadIdx.x; i < nrays; i += blockDim.x) {
-        rays.blk[i] = blk[i];
-        rays.ex[i] = ex[i];
-        rays.ey[i] = ey[i];
-    }
-    __syncthreads();
-    return nrays;
-}
-
-struct RayArgs {
-    const unsigned long long *blk;
-    const uint8_t *ex, *ey;
-    int n;
-};
-
-__global__ void __launch_bounds__(WARPS * 32)
+__global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     init_kernel(uint8_t *state, int n, D1SpecConfig c, RayArgs ra, uint64_t seed, int first_env,
                 __nv_bfloat16 *obs, uint16_t *legal) {
-    __shared__ Rays rays;
     __shared__ Smem sms[WARPS];
-    const int nrays = load_rays(rays, ra.blk, ra.ex, ra.ey, ra.n);
     const int w = threadIdx.x >> 5, env = blockIdx.x * WARPS + w;
     if (env >= n) return;
     Env e;
@@ -964,7 +962,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     e.rng.refill();
     e.dirty_lo = H;
     e.dirty_hi = -1;
-    reset(e, c, rays, nrays);
+    reset(e, c, ra);
     observe(e, c, obs + (size_t)env * OBS, legal + env);
     uint8_t *row = state + (size_t)env * ROW;
     for (int i = e.lane; i < OFF_FLOOR / 4; i += 32) reinterpret_cast<uint32_t *>(row)[i] = 0;
@@ -972,12 +970,10 @@ __global__ void __launch_bounds__(WARPS * 32)
     store(e, row);
 }
 
-__global__ void __launch_bounds__(WARPS * 32)
+__global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     step_kernel(uint8_t *state, int n, D1SpecConfig c, RayArgs ra, int extra_layers, const int64_t *actions,
                 __nv_bfloat16 *obs, uint16_t *legal, float *out, const bool *active) {
-    __shared__ Rays rays;
     __shared__ Smem sms[WARPS];
-    const int nrays = load_rays(rays, ra.blk, ra.ex, ra.ey, ra.n);
     const int w = threadIdx.x >> 5, env = blockIdx.x * WARPS + w;
     if (env >= n) return;
     if (active && !active[env]) return;
@@ -987,7 +983,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     e.sm = &sms[w];
     uint8_t *row = state + (size_t)env * ROW;
     load(e, row);
-    const float o = decision(e, c, rays, nrays, extra_layers, (int)actions[env]);
+    const float o = decision(e, c, ra, extra_layers, (int)actions[env]);
     if (e.lane < OUT) out[(size_t)env * OUT + e.lane] = o;
     observe(e, c, obs + (size_t)env * OBS, legal + env);
     store(e, row);
@@ -1028,7 +1024,7 @@ __global__ void planes_kernel(const uint8_t *state, int n, uint32_t *floor, uint
 
 using namespace d1;
 
-static spec::RayArgs g_rays = {nullptr, nullptr, nullptr, 0};
+static spec::RayArgs g_rays = {nullptr, 0};
 
 extern "C" {
 
@@ -1038,11 +1034,9 @@ int d1_spec_action_size(void) { return spec::ACTIONS; }
 int d1_spec_out_size(void) { return spec::OUT; }
 int d1_spec_config_bytes(void) { return (int)sizeof(D1SpecConfig); }
 
-int d1_spec_set_rays(const unsigned long long *blockers, const uint8_t *end_x, const uint8_t *end_y, int n) {
-    if (n <= 0 || n > spec::MAX_RAYS || !blockers || !end_x || !end_y) return D1_ERR_BAD_ARGUMENT;
-    g_rays.blk = blockers;
-    g_rays.ex = end_x;
-    g_rays.ey = end_y;
+int d1_spec_set_rays(const void *rays, int n) {
+    if (n <= 0 || n > spec::MAX_RAYS || !rays || (reinterpret_cast<uintptr_t>(rays) & 15)) return D1_ERR_BAD_ARGUMENT;
+    g_rays.ray = static_cast<const uint4 *>(rays);
     g_rays.n = n;
     return 0;
 }

@@ -21,7 +21,7 @@ SIGNATURES = {
     'learn_distance_table': [_P, _P, _I, _P, _P],
     'd1_spec_state_bytes': [], 'd1_spec_obs_size': [], 'd1_spec_action_size': [], 'd1_spec_out_size': [],
     'd1_spec_config_bytes': [],
-    'd1_spec_set_rays': [_P, _P, _P, _I],
+    'd1_spec_set_rays': [_P, _I],
     'd1_spec_init': [_P, _I, _P, _U64, _I, _P, _P, _P],
     'd1_spec_step': [_P, _I, _P, _P, _P, _P, _P, _P, _P],
     'd1_spec_compact': [_P, _I, _P, _P],

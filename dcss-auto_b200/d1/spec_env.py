@@ -73,17 +73,20 @@ _RAYS = {}
 
 
 def device_rays(device):
-    """Register the native LOS ray fan with the library (once per device)."""
+    """Register the native LOS ray fan with the library (packed once per device:
+    4 x u32 per ray = blocker mask lo, hi, end bit index, 0)."""
     key = str(device)
     if key not in _RAYS:
         z = np.load(DATA / 'los_rays.npz')
-        blk = torch.from_numpy(z['blockers'].astype(np.uint64).view(np.int64)).to(device)
-        ex = torch.from_numpy(z['end_x'].astype(np.uint8)).to(device)
-        ey = torch.from_numpy(z['end_y'].astype(np.uint8)).to(device)
-        _RAYS[key] = (blk, ex, ey)
-    blk, ex, ey = _RAYS[key]
-    check(library().d1_spec_set_rays(blk.data_ptr(), ex.data_ptr(), ey.data_ptr(), blk.numel()), 'd1_spec_set_rays')
-    return _RAYS[key]
+        blk = z['blockers'].astype(np.uint64)
+        packed = np.zeros((len(blk), 4), np.uint32)
+        packed[:, 0] = (blk & np.uint64(0xffffffff)).astype(np.uint32)
+        packed[:, 1] = (blk >> np.uint64(32)).astype(np.uint32)
+        packed[:, 2] = (z['end_y'] * 8 + z['end_x']).astype(np.uint32)
+        _RAYS[key] = torch.from_numpy(packed.view(np.int32)).to(device)
+    rays = _RAYS[key]
+    check(library().d1_spec_set_rays(rays.data_ptr(), rays.shape[0]), 'd1_spec_set_rays')
+    return rays
 
 
 class SpecEnv:

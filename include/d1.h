@@ -120,10 +120,11 @@ int d1_spec_action_size(void);
 int d1_spec_out_size(void);
 /* sizeof(D1SpecConfig) */
 int d1_spec_config_bytes(void);
-/* Register the LOS ray fan (device arrays, kept by the caller for the library's
- * lifetime): per ray a 64-bit blocker mask over the 8x8 quadrant and its end
- * cell. Must be called before any other d1_spec_* compute call. */
-int d1_spec_set_rays(const unsigned long long *blockers, const uint8_t *end_x, const uint8_t *end_y, int n);
+/* Register the LOS ray fan (a device array kept by the caller for the library's
+ * lifetime, 16-byte aligned): n records of 4 x u32 {blocker mask bits 0-31,
+ * bits 32-63 (bit y*8+x of the 8x8 quadrant), end-cell bit index ey*8+ex, 0}.
+ * n <= 320. Must be called before any other d1_spec_* compute call. */
+int d1_spec_set_rays(const void *rays, int n);
 /* Generate env i's first map from Philox(key = {first_env + i, lo32(seed)}),
  * reset it and write its observation. state u8[n, 2048]; obs bf16[n, 1832];
  * legal u16[n]. */
