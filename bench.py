@@ -34,6 +34,14 @@ ENV_BYTES_PER_DECISION = 969 + 3664
 POLICY_FLOPS_PER_DECISION = 2 * (1832 * 256 + 256 * 256 + 256 * 13)
 
 
+_T0 = time.perf_counter()
+
+
+def progress(msg):
+    """One line per phase on stderr (stdout carries only the JSON result)."""
+    print(f'[bench {time.perf_counter() - _T0:7.1f}s] {msg}', file=sys.stderr, flush=True)
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -78,7 +86,14 @@ class Clocks:
             return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
         time.sleep(0.25)
         self.proc.terminate()
-        self.proc.wait()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:  # a sampler stuck in the driver must not hold the bench
+            self.proc.kill()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                pass
         sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace('.', '').isdigit()]
         smax = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace('.', '').isdigit()]
         reasons = set()
@@ -184,6 +199,7 @@ def run_ours(args, rank, world, local_rank):
             roll.roll()
         roll.step(t)
 
+    progress('env + policy built; warm-up')
     for k in range(args.warmup):
         step(k)
     # Kernel-level timing of the env step (events on its launching stream).
@@ -224,6 +240,7 @@ def run_ours(args, rank, world, local_rank):
 
     # End to end through the public API with host buffers: actions come from
     # pinned host memory, the outcome rows and next actions go back every step.
+    progress(f'rollout timed: {value / 1e6:.1f} M decisions/s')
     e2e = None
     if not args.no_e2e:
         h_act = torch.zeros(B, dtype=torch.int64).pin_memory()
@@ -265,6 +282,7 @@ def run_ours(args, rank, world, local_rank):
 
     # Tensor-core layer alone (policy layer 1, M = envs, N = 256, K = 1832), timed
     # with events on its launching stream after the rollout measurement.
+    progress('e2e done')
     from d1 import gemm as G
     x = roll.obs[0]
     w1, b1 = policy.bf16['w1'], policy.params['b1']
@@ -290,7 +308,9 @@ def run_ours(args, rank, world, local_rank):
         trainer = PPO(policy, roll, minibatch=args.minibatch, epochs=args.epochs, group=group)
         gen = torch.Generator(device=dev).manual_seed(1234 + rank)
         roll.roll()
+        progress('PPO warm-up iteration')
         trainer.iteration(gen)  # warm-up iteration
+        progress('PPO timed iteration')
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -341,6 +361,7 @@ def run_ours(args, rank, world, local_rank):
         'gpu_launches': args.steps * 4,
     }
     if not args.no_cpu:
+        progress('CPU baseline')
         cores = len(os.sched_getaffinity(0))
         rate, dt = cpu_rollout(8192, 100, cores)
         line['cpu_baseline'] = {'value': rate, 'unit': UNIT, 'cores': cores, 'kind': 'port',

@@ -145,43 +145,93 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32) gae_scan_kernel(GaeArgs a) {
 
 // ------------------------------------------------------------------ minibatch gather
 // X[i] = obs[idx[i]] (bf16 rows of F features) and X^T (feature-major, the
-// B operand of the first-layer weight-gradient GEMM). A block moves 32 samples
-// x 64 features per pass through a shared-memory tile so both writes coalesce.
-constexpr int G_SAMPLES = 32, G_FEAT = 64;
+// B operand of the first-layer weight-gradient GEMM). Block (x, y) owns 64
+// samples and G_GROUP 64-feature chunks of their rows, which it walks through a
+// G_STAGES-deep cp.async ring in shared memory: five chunks (40 KB) are in
+// flight while the sixth is written out. Row writes are 128-byte sample
+// segments, transposed writes 128-byte feature segments. Splitting the features
+// over blockIdx.y gives ~7 blocks per SM at minibatch 16,384, so the samples
+// spread evenly over the 148 SMs. F must be a multiple of 8.
+constexpr int G_SAMPLES = 64, G_FEAT = 64, G_STAGES = 6, G_PITCH = G_FEAT, G_GROUP = 8;
+// A stage holds 64 sample rows of 128 B. The 16-byte unit u of row r sits at
+// unit u ^ ((r >> 3) & 7), so the transposed reads (8 threads on rows 8 apart,
+// same feature) land in 8 different banks instead of one.
+__device__ __forceinline__ int g_swz(int row, int unit) { return row * G_PITCH + ((unit ^ ((row >> 3) & 7)) << 3); }
+constexpr int G_SMEM = G_STAGES * G_SAMPLES * G_PITCH * 2;
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__restrict__ obs, int F,
                                                      const int64_t *__restrict__ idx, int n, __nv_bfloat16 *x,
                                                      __nv_bfloat16 *xt, int ldt) {
-    __shared__ __align__(16) __nv_bfloat16 tile[G_SAMPLES][G_FEAT + 8];
+    extern __shared__ __align__(16) __nv_bfloat16 gbuf[];  // [G_STAGES][G_SAMPLES][G_PITCH]
     const int s0 = blockIdx.x * G_SAMPLES;
-    const int t = threadIdx.x;
-    const int ls = t / 8, part = t % 8;  // load: sample, 8-feature part
-    const int gs = s0 + ls;
-    const int64_t src = gs < n ? idx[gs] : 0;
-    for (int f0 = 0; f0 < F; f0 += G_FEAT) {
-        const int f = f0 + part * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (gs < n && f < F) {
-            v = *reinterpret_cast<const uint4 *>(obs + (size_t)src * F + f);
-            if (x) *reinterpret_cast<uint4 *>(x + (size_t)gs * F + f) = v;
-        }
-        *reinterpret_cast<uint4 *>(&tile[ls][part * 8]) = v;
-        __syncthreads();
-        if (xt) {
-            const int feat = t / 4, q = t % 4;  // store: feature, 8-sample part
-            const int ff = f0 + feat;
-            if (ff < F && s0 + q * 8 < n) {
-                __align__(16) __nv_bfloat16 o[8];
+    const int t = threadIdx.x, part = t & 7;
+    const int c_begin = blockIdx.y * G_GROUP;
+    const int nchunks = min((F + G_FEAT - 1) / G_FEAT - c_begin, G_GROUP);
+    const __nv_bfloat16 *src[2];
+    bool live[2];
 #pragma unroll
-                for (int i = 0; i < 8; i++) o[i] = tile[q * 8 + i][feat];
-                if (s0 + q * 8 + 8 <= n) {
-                    *reinterpret_cast<uint4 *>(xt + (size_t)ff * ldt + s0 + q * 8) = *reinterpret_cast<uint4 *>(o);
-                } else {
-                    for (int i = 0; i < 8 && s0 + q * 8 + i < n; i++) xt[(size_t)ff * ldt + s0 + q * 8 + i] = o[i];
+    for (int h = 0; h < 2; h++) {
+        const int gs = s0 + (t >> 3) + 32 * h;
+        live[h] = gs < n;
+        src[h] = obs + (live[h] ? (size_t)idx[gs] * F : 0);
+    }
+    auto issue = [&](int c) {
+        if (c < nchunks) {
+            __nv_bfloat16 *buf = gbuf + (c % G_STAGES) * (G_SAMPLES * G_PITCH);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int ls = (t >> 3) + 32 * h, f = (c_begin + c) * G_FEAT + part * 8;
+                const bool ok = live[h] && f < F;
+                cp_async16(buf + g_swz(ls, part), ok ? src[h] + f : obs, ok ? 16 : 0);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int c = 0; c < G_STAGES - 1; c++) issue(c);
+    for (int c = 0; c < nchunks; c++) {
+        issue(c + G_STAGES - 1);
+        cp_async_wait<G_STAGES - 1>();
+        __syncthreads();
+        const __nv_bfloat16 *buf = gbuf + (c % G_STAGES) * (G_SAMPLES * G_PITCH);
+        const int f0 = (c_begin + c) * G_FEAT;
+        if (x) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int ls = (t >> 3) + 32 * h, f = f0 + part * 8;
+                if (live[h] && f < F)
+                    *reinterpret_cast<uint4 *>(x + (size_t)(s0 + ls) * F + f) =
+                        *reinterpret_cast<const uint4 *>(buf + g_swz(ls, part));
+            }
+        }
+        if (xt) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int feat = (t >> 3) + 32 * h;  // 8 threads = 64 samples of one feature
+                const int ff = f0 + feat, sb = s0 + part * 8;
+                if (ff < F && sb < n) {
+                    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) o[i] = buf[g_swz(part * 8 + i, feat >> 3) + (feat & 7)];
+                    if (sb + 8 <= n) {
+                        *reinterpret_cast<uint4 *>(xt + (size_t)ff * ldt + sb) = *reinterpret_cast<uint4 *>(o);
+                    } else {
+                        for (int i = 0; i < 8 && sb + i < n; i++) xt[(size_t)ff * ldt + sb + i] = o[i];
+                    }
                 }
             }
         }
         __syncthreads();
     }
+    cp_async_wait<0>();
 }
 
 // ------------------------------------------------------------------ fused head + loss + backward to h2
@@ -195,6 +245,10 @@ __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__rest
 // and its gradient with respect to logits/value, then dh2 = dhead . Wh masked by
 // ReLU'(h2) (bf16, row-major and transposed). Block partials of dWh, dbh, db2
 // and of the loss terms go to `part` for a deterministic reduction.
+//
+// A warp owns four rows at a time: lanes split the 256 hidden units for the 13
+// dot products and the dh2 row; lanes 0-11 then each own one action for the
+// softmax, entropy and logit gradient (warp shuffles do the reductions).
 struct LossArgs {
     const __nv_bfloat16 *h2;   // [n, 256]
     const __nv_bfloat16 *wh;   // [13, 256]
@@ -218,31 +272,55 @@ struct LossSmem {
     float w_s[L_NOUT][L_HID];
     float hs[L_ROWS][L_HID + 4];  // h2 rows (fp32)
     float gs[L_ROWS][L_HID + 4];  // dh2 rows (fp32, masked)
-    float dh_s[L_ROWS][L_NOUT];
+    float dh_s[L_ROWS][16];       // dlogits[12], dvalue, 0, 0, 0
+    float accw[L_NOUT][L_HID];    // dWh column accumulators between row batches
     float terms_s[8][8];
+    // the batch's per-row rollout values, fetched in one round of parallel loads
+    float r_olp[L_ROWS], r_adv[L_ROWS], r_ret[L_ROWS], r_vold[L_ROWS];
+    int r_bits[L_ROWS], r_act[L_ROWS];
 };
-__global__ void __launch_bounds__(256) loss_kernel(LossArgs a) {
+
+__device__ __forceinline__ float group16_max(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+    return v;
+}
+__device__ __forceinline__ float group16_sum(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+__global__ void __launch_bounds__(256, 2) loss_kernel(LossArgs a) {
     extern __shared__ __align__(16) uint8_t loss_raw[];
     LossSmem &S = *reinterpret_cast<LossSmem *>(loss_raw);
-    auto &w_s = S.w_s;
-    auto &hs = S.hs;
-    auto &gs = S.gs;
-    auto &dh_s = S.dh_s;
-    auto &terms_s = S.terms_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < L_NOUT * L_HID; i += 256) w_s[i / L_HID][i % L_HID] = __bfloat162float(a.wh[i]);
+    for (int i = tid; i < L_NOUT * L_HID; i += 256) S.w_s[i / L_HID][i % L_HID] = __bfloat162float(a.wh[i]);
     const double mean = a.adv_stats[0] / a.adv_count;
     const double var = (a.adv_stats[1] - a.adv_stats[0] * mean) / (a.adv_count - 1.0);
     const float amean = (float)mean, astd = (float)sqrt(var > 0 ? var : 0.0);
     const float inv_n = 1.f / (float)a.n;
-    float acc_w[L_NOUT] = {0};  // this thread's dWh column (k = tid), summed over rows
+    float bh_l = 0.f;  // this lane's action bias (lanes 0-11), value bias on all lanes
+    for (int j = 0; j < L_NACT; j++)
+        if (lane == j) bh_l = a.bh[j];
+    const float bh_v = a.bh[L_NACT];
+#pragma unroll
+    for (int j = 0; j < L_NOUT; j++) S.accw[j][tid] = 0.f;
     float acc_b2 = 0.f, acc_bh = 0.f;
     float t_pg = 0.f, t_vf = 0.f, t_ent = 0.f, t_clip = 0.f, t_kl = 0.f;
     __syncthreads();
     const int nb = (a.n + L_ROWS - 1) / L_ROWS;
     for (int blk = blockIdx.x; blk < nb; blk += gridDim.x) {
         const int r0 = blk * L_ROWS;
-        // stage h2 rows as fp32
+        if (tid < L_ROWS && r0 + tid < a.n) {
+            const int64_t sidx = a.idx[r0 + tid];
+            S.r_bits[tid] = a.legal[sidx];
+            S.r_act[tid] = (int)a.action[sidx];
+            S.r_olp[tid] = a.old_logp[sidx];
+            S.r_adv[tid] = a.adv[sidx];
+            S.r_ret[tid] = a.ret[sidx];
+            S.r_vold[tid] = a.old_value[sidx];
+        }
         for (int i = tid; i < L_ROWS * (L_HID / 8); i += 256) {
             const int r = i / (L_HID / 8), c = (i % (L_HID / 8)) * 8;
             float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -256,11 +334,10 @@ __global__ void __launch_bounds__(256) loss_kernel(LossArgs a) {
                     f[2 * j + 1] = ff.y;
                 }
             }
-#pragma unroll
-            for (int j = 0; j < 8; j++) hs[r][c + j] = f[j];
+            *reinterpret_cast<float4 *>(&S.hs[r][c]) = make_float4(f[0], f[1], f[2], f[3]);
+            *reinterpret_cast<float4 *>(&S.hs[r][c + 4]) = make_float4(f[4], f[5], f[6], f[7]);
         }
         __syncthreads();
-        // warp w handles rows w, w+8, w+16, w+24: each lane sums 8 of 256 elements
         for (int rr = warp; rr < L_ROWS; rr += 8) {
             const int row = r0 + rr;
             float acc[L_NOUT];
@@ -268,43 +345,34 @@ __global__ void __launch_bounds__(256) loss_kernel(LossArgs a) {
             for (int j = 0; j < L_NOUT; j++) {
                 float sum = 0.f;
 #pragma unroll
-                for (int i = 0; i < 8; i++) sum += hs[rr][lane + 32 * i] * w_s[j][lane + 32 * i];
+                for (int i = 0; i < 8; i++) sum += S.hs[rr][lane + 32 * i] * S.w_s[j][lane + 32 * i];
                 acc[j] = sum;
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
                 for (int j = 0; j < L_NOUT; j++) acc[j] += __shfl_xor_sync(FULL, acc[j], o);
-            float dl[L_NACT], dv = 0.f;
+            float dl = 0.f, dv = 0.f;  // this lane's dlogit (lanes 0-11) and the value gradient
+            if (row < a.n) {
+                const uint32_t bits = (uint32_t)S.r_bits[rr];
+                const int act = S.r_act[rr];
+                float l = acc[0];
 #pragma unroll
-            for (int j = 0; j < L_NACT; j++) dl[j] = 0.f;
-            if (row < a.n && lane == 0) {
-                const int64_t sidx = a.idx[row];
-                const uint32_t bits = a.legal[sidx];
-                const int act = (int)a.action[sidx];
-                float l[L_NACT], m = -3.402823466e38f;
-#pragma unroll
-                for (int j = 0; j < L_NACT; j++) {
-                    l[j] = acc[j] + a.bh[j];
-                    if ((bits >> j) & 1u) m = fmaxf(m, l[j]);
-                }
-                float z = 0.f;
-#pragma unroll
-                for (int j = 0; j < L_NACT; j++)
-                    if ((bits >> j) & 1u) z += expf(l[j] - m);
+                for (int j = 1; j < L_NACT; j++)
+                    if (lane == j) l = acc[j];
+                l += bh_l;
+                const bool ok = lane < L_NACT && ((bits >> lane) & 1u);
+                const float m = group16_max(ok ? l : -3.402823466e38f);
+                const float z = group16_sum(ok ? expf(l - m) : 0.f);
                 const float lz = logf(z);
-                float p[L_NACT], ent = 0.f, la = 0.f;
-#pragma unroll
-                for (int j = 0; j < L_NACT; j++) {
-                    const bool ok = (bits >> j) & 1u;
-                    const float lp = l[j] - m - lz;
-                    p[j] = ok ? expf(lp) : 0.f;
-                    if (ok) ent -= p[j] * lp;
-                    if (j == act) la = lp;
-                }
-                const float value = acc[L_NACT] + a.bh[L_NACT];
-                const float adv = (a.adv[sidx] - amean) / (astd + 1e-8f);
-                const float ratio = expf(la - a.old_logp[sidx]);
+                const float lp = l - m - lz;
+                const float p = ok ? expf(lp) : 0.f;
+                const float ent = -group16_sum(ok ? p * lp : 0.f);
+                const float la = __shfl_sync(FULL, lp, act & 15);
+                const float value = acc[L_NACT] + bh_v;
+                const float adv = (S.r_adv[rr] - amean) / (astd + 1e-8f);
+                const float olp = S.r_olp[rr];
+                const float ratio = expf(la - olp);
                 const float s1 = ratio * adv, rc = fminf(fmaxf(ratio, 1.f - a.clip), 1.f + a.clip), s2 = rc * adv;
                 const float pg = -fminf(s1, s2);
                 // d pg / d logp(a): only the selected branch carries gradient
@@ -313,8 +381,7 @@ __global__ void __launch_bounds__(256) loss_kernel(LossArgs a) {
                 if (s1 <= s2) dpg_dr = -adv;
                 else if (ratio > 1.f - a.clip && ratio < 1.f + a.clip) dpg_dr = -adv;
                 const float dlogp = dpg_dr * ratio * inv_n;
-                // value term
-                const float R = a.ret[sidx], vold = a.old_value[sidx];
+                const float R = S.r_ret[rr], vold = S.r_vold[rr];
                 float vf, dvf;
                 const float e1 = value - R;
                 if (a.vclip > 0.f) {
@@ -333,38 +400,27 @@ __global__ void __launch_bounds__(256) loss_kernel(LossArgs a) {
                 }
                 dv = a.vf_coef * dvf * inv_n;
                 // d(-ent_coef * H)/dl_j = ent_coef * p_j * (log p_j + H)
-#pragma unroll
-                for (int j = 0; j < L_NACT; j++) {
-                    if (!((bits >> j) & 1u)) continue;
-                    const float lp = l[j] - m - lz;
-                    float g = dlogp * ((j == act ? 1.f : 0.f) - p[j]);
-                    g += a.ent_coef * inv_n * p[j] * (lp + ent);
-                    dl[j] = g;
+                if (ok) dl = dlogp * ((lane == act ? 1.f : 0.f) - p) + a.ent_coef * inv_n * p * (lp + ent);
+                if (lane == 0) {
+                    t_pg += pg;
+                    t_vf += vf;
+                    t_ent += ent;
+                    t_clip += fabsf(ratio - 1.f) > a.clip ? 1.f : 0.f;
+                    t_kl += olp - la;
                 }
-                t_pg += pg;
-                t_vf += vf;
-                t_ent += ent;
-                t_clip += fabsf(ratio - 1.f) > a.clip ? 1.f : 0.f;
-                t_kl += a.old_logp[sidx] - la;
             }
+            if (lane < 16) S.dh_s[rr][lane] = lane < L_NACT ? dl : (lane == L_NACT ? dv : 0.f);
+            float dls[L_NACT];
 #pragma unroll
-            for (int j = 0; j < L_NACT; j++) dl[j] = __shfl_sync(FULL, dl[j], 0);
-            dv = __shfl_sync(FULL, dv, 0);
-            if (lane < L_NOUT) {
-                float mine = dv;
-#pragma unroll
-                for (int j = 0; j < L_NACT; j++)
-                    if (lane == j) mine = dl[j];
-                dh_s[rr][lane] = row < a.n ? mine : 0.f;
-            }
+            for (int j = 0; j < L_NACT; j++) dls[j] = __shfl_sync(FULL, dl, j);
             // dh2 = dhead . Wh, masked by ReLU'(h2)
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 const int k = lane + 32 * i;
-                float g = dv * w_s[L_NACT][k];
+                float g = dv * S.w_s[L_NACT][k];
 #pragma unroll
-                for (int j = 0; j < L_NACT; j++) g += dl[j] * w_s[j][k];
-                gs[rr][k] = (row < a.n && hs[rr][k] > 0.f) ? g : 0.f;
+                for (int j = 0; j < L_NACT; j++) g += dls[j] * S.w_s[j][k];
+                S.gs[rr][k] = (row < a.n && S.hs[rr][k] > 0.f) ? g : 0.f;
             }
         }
         __syncthreads();
@@ -372,26 +428,39 @@ __global__ void __launch_bounds__(256) loss_kernel(LossArgs a) {
         {
             const int k = tid;
             float b2 = 0.f;
+            float acc_w[L_NOUT];
+#pragma unroll
+            for (int j = 0; j < L_NOUT; j++) acc_w[j] = S.accw[j][k];
 #pragma unroll 4
             for (int r = 0; r < L_ROWS; r++) {
-                const float h = hs[r][k];
-#pragma unroll
-                for (int j = 0; j < L_NOUT; j++) acc_w[j] += dh_s[r][j] * h;
-                b2 += gs[r][k];
+                const float h = S.hs[r][k];
+                const float4 d0 = *reinterpret_cast<const float4 *>(&S.dh_s[r][0]);
+                const float4 d1 = *reinterpret_cast<const float4 *>(&S.dh_s[r][4]);
+                const float4 d2 = *reinterpret_cast<const float4 *>(&S.dh_s[r][8]);
+                const float d3 = S.dh_s[r][12];
+                acc_w[0] += d0.x * h; acc_w[1] += d0.y * h; acc_w[2] += d0.z * h; acc_w[3] += d0.w * h;
+                acc_w[4] += d1.x * h; acc_w[5] += d1.y * h; acc_w[6] += d1.z * h; acc_w[7] += d1.w * h;
+                acc_w[8] += d2.x * h; acc_w[9] += d2.y * h; acc_w[10] += d2.z * h; acc_w[11] += d2.w * h;
+                acc_w[12] += d3 * h;
+                b2 += S.gs[r][k];
             }
+#pragma unroll
+            for (int j = 0; j < L_NOUT; j++) S.accw[j][k] = acc_w[j];
             acc_b2 += b2;
             if (tid < L_NOUT)
-                for (int r = 0; r < L_ROWS; r++) acc_bh += dh_s[r][tid];
+                for (int r = 0; r < L_ROWS; r++) acc_bh += S.dh_s[r][tid];
         }
-        // dh2 row-major (coalesced: a row is 512 B) and transposed (a feature row of
-        // 32 consecutive samples is 64 B)
-        for (int i = tid; i < L_ROWS * (L_HID / 8); i += 256) {
-            const int r = i / (L_HID / 8), c = (i % (L_HID / 8)) * 8;
-            if (r0 + r < a.n && a.dh2) {
-                __align__(16) __nv_bfloat16 o[8];
+        // dh2 row-major (a row is 512 B) and transposed (a feature row of 32
+        // consecutive samples is 64 B)
+        if (a.dh2) {
+            for (int i = tid; i < L_ROWS * (L_HID / 8); i += 256) {
+                const int r = i / (L_HID / 8), c = (i % (L_HID / 8)) * 8;
+                if (r0 + r < a.n) {
+                    __align__(16) __nv_bfloat16 o[8];
 #pragma unroll
-                for (int j = 0; j < 8; j++) o[j] = __float2bfloat16_rn(gs[r][c + j]);
-                *reinterpret_cast<uint4 *>(a.dh2 + (size_t)(r0 + r) * L_HID + c) = *reinterpret_cast<uint4 *>(o);
+                    for (int j = 0; j < 8; j++) o[j] = __float2bfloat16_rn(S.gs[r][c + j]);
+                    *reinterpret_cast<uint4 *>(a.dh2 + (size_t)(r0 + r) * L_HID + c) = *reinterpret_cast<uint4 *>(o);
+                }
             }
         }
         if (a.dh2t) {
@@ -400,7 +469,7 @@ __global__ void __launch_bounds__(256) loss_kernel(LossArgs a) {
                 if (r0 + q < a.n) {
                     __align__(16) __nv_bfloat16 o[8];
 #pragma unroll
-                    for (int j = 0; j < 8; j++) o[j] = __float2bfloat16_rn(gs[q + j][k]);
+                    for (int j = 0; j < 8; j++) o[j] = __float2bfloat16_rn(S.gs[q + j][k]);
                     if (r0 + q + 8 <= a.n)
                         *reinterpret_cast<uint4 *>(a.dh2t + (size_t)k * a.ldt + r0 + q) = *reinterpret_cast<uint4 *>(o);
                     else
@@ -410,55 +479,87 @@ __global__ void __launch_bounds__(256) loss_kernel(LossArgs a) {
         }
         __syncthreads();
     }
-    // block partials
     float *out = a.part + (size_t)blockIdx.x * L_PART;
 #pragma unroll
-    for (int j = 0; j < L_NOUT; j++) out[j * L_HID + tid] = acc_w[j];
+    for (int j = 0; j < L_NOUT; j++) out[j * L_HID + tid] = S.accw[j][tid];
     if (tid < L_NOUT) out[L_NOUT * L_HID + tid] = acc_bh;
     out[L_NOUT * L_HID + L_NOUT + tid] = acc_b2;
-    // loss terms: reduce the lane-0 values of every warp
     if (lane == 0) {
-        terms_s[warp][0] = t_pg;
-        terms_s[warp][1] = t_vf;
-        terms_s[warp][2] = t_ent;
-        terms_s[warp][3] = t_clip;
-        terms_s[warp][4] = t_kl;
+        S.terms_s[warp][0] = t_pg;
+        S.terms_s[warp][1] = t_vf;
+        S.terms_s[warp][2] = t_ent;
+        S.terms_s[warp][3] = t_clip;
+        S.terms_s[warp][4] = t_kl;
     }
     __syncthreads();
     if (tid < 5) {
         float v = 0.f;
-        for (int w = 0; w < 8; w++) v += terms_s[w][tid];
+        for (int w = 0; w < 8; w++) v += S.terms_s[w][tid];
         out[L_NOUT * L_HID + L_NOUT + L_HID + tid] = v;
     }
     if (tid >= 5 && tid < 8) out[L_NOUT * L_HID + L_NOUT + L_HID + tid] = 0.f;
 }
 
 // out[i] = sum over p of parts[p * stride + i] (loss-kernel block partials).
-__global__ void sum_rows_kernel(const float *parts, int nparts, int stride, int len, float *out) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= len) return;
-    float s = 0.f;
-    for (int p = 0; p < nparts; p++) s += parts[(size_t)p * stride + i];
-    out[i] = s;
+// A block owns 32 consecutive i; its 8 warps sum interleaved part subsets
+// (p = warp, warp + 8, ...) and the per-warp sums are added in warp order, so
+// the result does not depend on scheduling.
+__global__ void __launch_bounds__(256) sum_rows_kernel(const float *parts, int nparts, int stride, int len,
+                                                       float *out) {
+    __shared__ float part_s[8][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int i = blockIdx.x * 32 + lane;
+    float s0 = 0.f, s1 = 0.f;
+    if (i < len) {
+        int p = warp;
+        for (; p + 8 < nparts; p += 16) {
+            s0 += parts[(size_t)p * stride + i];
+            s1 += parts[(size_t)(p + 8) * stride + i];
+        }
+        if (p < nparts) s0 += parts[(size_t)p * stride + i];
+    }
+    part_s[warp][lane] = s0 + s1;
+    __syncthreads();
+    if (warp == 0 && i < len) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) t += part_s[w][lane];
+        out[i] = t;
+    }
 }
 
-// out[i] = sum over splits of slabs[s][i] (split-K partial products), i < count.
+// out[i] = sum over splits of slabs[s][i] (split-K partial products), i < count;
+// four elements per thread when count is a multiple of 4.
 __global__ void reduce_slabs_kernel(const float *__restrict__ slabs, int splits, int64_t count, float *out) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= count) return;
-    float s = 0.f;
-    for (int k = 0; k < splits; k++) s += slabs[(size_t)k * count + i];
-    out[i] = s;
+    const int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if ((count & 3) == 0) {
+        if (i4 * 4 >= count) return;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < splits; k++) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(slabs + (size_t)k * count) + i4);
+            s.x += v.x;
+            s.y += v.y;
+            s.z += v.z;
+            s.w += v.w;
+        }
+        reinterpret_cast<float4 *>(out)[i4] = s;
+    } else {
+        if (i4 >= count) return;
+        float s = 0.f;
+        for (int k = 0; k < splits; k++) s += slabs[(size_t)k * count + i4];
+        out[i4] = s;
+    }
 }
 
-// out[r] = sum of row r of a bf16 [rows, cols] matrix (pitch ld); one warp per row.
-__global__ void row_sum_bf16_kernel(const __nv_bfloat16 *__restrict__ m, int rows, int cols, int ld, float *out) {
-    const int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (r >= rows) return;
+// out[r] = sum of row r of a bf16 [rows, cols] matrix (pitch ld); one block per row.
+__global__ void __launch_bounds__(256) row_sum_bf16_kernel(const __nv_bfloat16 *__restrict__ m, int rows, int cols,
+                                                           int ld, float *out) {
+    __shared__ float ws[8];
+    const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float s = 0.f;
-    for (int c = lane * 8; c < cols; c += 256) {
+    for (int c = threadIdx.x * 8; c < cols; c += 256 * 8) {
         if (c + 8 <= cols) {
-            const uint4 raw = *reinterpret_cast<const uint4 *>(m + (size_t)r * ld + c);
+            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(m + (size_t)r * ld + c));
             const __nv_bfloat162 *p2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -470,23 +571,34 @@ __global__ void row_sum_bf16_kernel(const __nv_bfloat16 *__restrict__ m, int row
         }
     }
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
-    if (lane == 0) out[r] = s;
+    if (lane == 0) ws[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < 8; w++) t += ws[w];
+        out[r] = t;
+    }
 }
 
 // ------------------------------------------------------------------ optimizer
 // sum of squares of g[0..n) into *out (double, accumulated)
-__global__ void sumsq_kernel(const float *__restrict__ g, int64_t n, double *out) {
+__global__ void __launch_bounds__(256) sumsq_kernel(const float *__restrict__ g, int64_t n, double *out) {
     double s = 0.0;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        s += (double)g[i] * g[i];
+    const int64_t n4 = n / 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(g) + i);
+        s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+    if (blockIdx.x == 0)
+        for (int64_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) s += (double)g[i] * g[i];
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
-    __shared__ double ws[32];
+    __shared__ double ws[8];
     if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        s = threadIdx.x < blockDim.x / 32 ? ws[threadIdx.x] : 0.0;
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
-        if (threadIdx.x == 0) atomicAdd(out, s);
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < 8; w++) t += ws[w];
+        atomicAdd(out, t);
     }
 }
 
@@ -545,6 +657,20 @@ __global__ void adam_kernel(AdamArgs a) {
 
 __global__ void counter_add_kernel(int64_t *c, int64_t delta) { *c += delta; }
 
+// Dynamic shared memory above 48 KB is opted into once per kernel and device;
+// `ready` is that kernel's bitmask of devices already set up.
+static int opt_in_smem(const void *fn, int bytes, uint64_t *ready) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 64 && (*ready >> dev) & 1) return 0;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 64) *ready |= 1ull << dev;
+    return 0;
+}
+
 }  // namespace ppo
 }  // namespace d1
 
@@ -555,7 +681,12 @@ extern "C" {
 
 int d1_ppo_gather(const void *obs, int F, const int64_t *idx, int n, void *x, void *xt, int ldt, void *stream) {
     if (!obs || !idx || n <= 0 || F <= 0 || F % 8 || (xt && (ldt < n || ldt % 8))) return D1_ERR_BAD_ARGUMENT;
-    ppo::gather_kernel<<<(n + ppo::G_SAMPLES - 1) / ppo::G_SAMPLES, 256, 0, (cudaStream_t)stream>>>(
+    static uint64_t ready = 0;
+    const int err = ppo::opt_in_smem((const void *)ppo::gather_kernel, ppo::G_SMEM, &ready);
+    if (err) return err;
+    const int groups = ((F + ppo::G_FEAT - 1) / ppo::G_FEAT + ppo::G_GROUP - 1) / ppo::G_GROUP;
+    const dim3 grid((n + ppo::G_SAMPLES - 1) / ppo::G_SAMPLES, groups);
+    ppo::gather_kernel<<<grid, 256, ppo::G_SMEM, (cudaStream_t)stream>>>(
         (const __nv_bfloat16 *)obs, F, idx, n, (__nv_bfloat16 *)x, (__nv_bfloat16 *)xt, ldt);
     return (int)cudaGetLastError();
 }
@@ -570,13 +701,9 @@ int d1_ppo_loss(const void *h2, const void *wh, const float *bh, const int64_t *
     if (n <= 0 || blocks <= 0 || !h2 || !wh || !bh || !idx || !legal || !action || !old_logp || !adv || !ret ||
         !old_value || !adv_stats || !part || adv_count < 2 || (dh2t && ldt < n))
         return D1_ERR_BAD_ARGUMENT;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(ppo::loss_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)sizeof(ppo::LossSmem));
-        if (e != cudaSuccess) return (int)e;
-        attr = true;
-    }
+    static uint64_t ready = 0;
+    const int err = ppo::opt_in_smem((const void *)ppo::loss_kernel, (int)sizeof(ppo::LossSmem), &ready);
+    if (err) return err;
     ppo::LossArgs a{(const __nv_bfloat16 *)h2, (const __nv_bfloat16 *)wh, bh, idx, legal, action, old_logp, adv,
                     ret, old_value, adv_stats, adv_count, n, clip, vclip, vf_coef, ent_coef,
                     (__nv_bfloat16 *)dh2, (__nv_bfloat16 *)dh2t, ldt, part};
@@ -586,27 +713,30 @@ int d1_ppo_loss(const void *h2, const void *wh, const float *bh, const int64_t *
 
 int d1_sum_rows(const float *parts, int nparts, int stride, int len, float *out, void *stream) {
     if (!parts || !out || nparts <= 0 || len <= 0 || stride < len) return D1_ERR_BAD_ARGUMENT;
-    ppo::sum_rows_kernel<<<(len + 255) / 256, 256, 0, (cudaStream_t)stream>>>(parts, nparts, stride, len, out);
+    ppo::sum_rows_kernel<<<(len + 31) / 32, 256, 0, (cudaStream_t)stream>>>(parts, nparts, stride, len, out);
     return (int)cudaGetLastError();
 }
 
 int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, void *stream) {
     if (!slabs || !out || splits <= 0 || count <= 0) return D1_ERR_BAD_ARGUMENT;
-    ppo::reduce_slabs_kernel<<<(unsigned)((count + 255) / 256), 256, 0, (cudaStream_t)stream>>>(slabs, splits, count,
-                                                                                                 out);
+    const int64_t threads = (count & 3) == 0 ? count / 4 : count;
+    if (((count & 3) == 0) && ((reinterpret_cast<uintptr_t>(slabs) | reinterpret_cast<uintptr_t>(out)) & 15))
+        return D1_ERR_BAD_ARGUMENT;
+    ppo::reduce_slabs_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(slabs, splits, count,
+                                                                                                    out);
     return (int)cudaGetLastError();
 }
 
 int d1_row_sum_bf16(const void *m, int rows, int cols, int ld, float *out, void *stream) {
     if (!m || !out || rows <= 0 || cols <= 0 || ld < cols || ld % 8) return D1_ERR_BAD_ARGUMENT;
-    ppo::row_sum_bf16_kernel<<<(rows + 7) / 8, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16 *)m, rows, cols,
-                                                                                 ld, out);
+    ppo::row_sum_bf16_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16 *)m, rows, cols, ld, out);
     return (int)cudaGetLastError();
 }
 
 int d1_sumsq(const float *g, int64_t n, double *out, void *stream) {
-    if (!g || !out || n <= 0) return D1_ERR_BAD_ARGUMENT;
-    ppo::sumsq_kernel<<<296, 256, 0, (cudaStream_t)stream>>>(g, n, out);
+    if (!g || !out || n <= 0 || (reinterpret_cast<uintptr_t>(g) & 15)) return D1_ERR_BAD_ARGUMENT;
+    const int64_t blocks = (n / 4 + 255) / 256;
+    ppo::sumsq_kernel<<<(unsigned)(blocks < 1 ? 1 : (blocks > 1184 ? 1184 : blocks)), 256, 0, (cudaStream_t)stream>>>(g, n, out);
     return (int)cudaGetLastError();
 }
 

@@ -76,7 +76,9 @@ class PPO:
         self.s2 = G.splits_for(mb, splits)
         self.slab2 = torch.empty((self.s2, HID, HID), **f32)
         self.part_len = self.lib.d1_ppo_loss_part_len()
-        self.loss_blocks = 128
+        batches = (mb + 31) // 32                     # the loss kernel takes 32 rows per pass
+        per = (batches + 295) // 296                  # passes per block with two blocks per SM
+        self.loss_blocks = (batches + per - 1) // per
         self.part = torch.empty((self.loss_blocks, self.part_len), **f32)
         self.terms = torch.zeros(8, **f32)
         self.history = []
