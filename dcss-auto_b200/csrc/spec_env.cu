@@ -815,7 +815,7 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
         const uint32_t one = 0x3f80u << (16 * (ch & 1));
         const int w = ch >> 1;
         const uint4 v = make_uint4(w == 0 ? one : 0u, w == 1 ? one : 0u, w == 2 ? one : 0u, w == 3 ? one : 0u);
-        if (j < CELLS) dst[j] = v;
+        if (obs && j < CELLS) dst[j] = v;
     }
     // scalars
     const int nvis = __popc(__ballot_sync(FULL, mvis));
@@ -852,7 +852,7 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
                            1.f, 4.f, 1.f, 80.f, 70.f, 1.f, 8.f, 16.f, 1.f, 1.f, 1024.f, 2.f, 1.f, 1.f, 7.f, 7.f,
                            1.f, 30.f, 1.f, 1.f};
     const float f = num[lane] / den[lane];
-    obs[1800 + lane] = __float2bfloat16_rn(f);
+    if (obs) obs[1800 + lane] = __float2bfloat16_rn(f);
     if (lane < 8) {
         const bool ok = floor_at(e, neighbor(e.player, lane));
         const unsigned b = __ballot_sync(0xffu, ok);
@@ -963,7 +963,7 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     e.dirty_lo = H;
     e.dirty_hi = -1;
     reset(e, c, ra);
-    observe(e, c, obs + (size_t)env * OBS, legal + env);
+    observe(e, c, obs ? obs + (size_t)env * OBS : nullptr, legal + env);
     uint8_t *row = state + (size_t)env * ROW;
     for (int i = e.lane; i < OFF_FLOOR / 4; i += 32) reinterpret_cast<uint32_t *>(row)[i] = 0;
     __syncwarp();
@@ -985,8 +985,87 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     load(e, row);
     const float o = decision(e, c, ra, extra_layers, (int)actions[env]);
     if (e.lane < OUT) out[(size_t)env * OUT + e.lane] = o;
-    observe(e, c, obs + (size_t)env * OBS, legal + env);
+    observe(e, c, obs ? obs + (size_t)env * OBS : nullptr, legal + env);
     store(e, row);
+}
+
+// ------------------------------------------------------------------ conv-policy crop
+// Egocentric 63 x 63 crop under D4 element g, one u16 code per pixel (rows of
+// pitch 64, column 63 zero): bits 0-2 the observation's one-hot class, bit 3
+// "on the map", bits 4-8 the hp of a visible monster there. Pixel (x, y) shows
+// the map cell at offset d4(g, x - 31, y - 31) from the player, with
+// d4 = rotation by g % 4 quarter turns ((dx, dy), (dy, -dx), (-dx, -dy), (-dy, dx))
+// followed by an x mirror when g >= 4, the sampling rule of the reference's
+// centered-map encoder (vision15-centered-map-v1/src/fast_maps.cu:7-9). One warp
+// per env: the planes and the 15 x 15 monster window are staged in shared
+// memory, then each lane codes two pixels of every crop row.
+constexpr int CROP = 63, CROP_PITCH = 64, CROP_WARPS = 8;
+struct CropSmem {
+    uint32_t floor[PL], viewed[PL], vis[16];
+    uint16_t occ[CELLS];  // code of the visible monster in the 15 x 15 window, 0 = none
+};
+__global__ void __launch_bounds__(CROP_WARPS * 32) crop_kernel(const uint8_t *state, int n, int g, uint16_t *out) {
+    __shared__ CropSmem sms[CROP_WARPS];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, env = blockIdx.x * CROP_WARPS + w;
+    if (env >= n) return;
+    CropSmem &s = sms[w];
+    const uint8_t *row = state + (size_t)env * ROW;
+    const int *i32 = reinterpret_cast<const int *>(row);
+    const int player = i32[9], stairs = i32[12], nmon = i32[13];
+    const int px = player % W, py = player / W;
+    const uint32_t *fp = reinterpret_cast<const uint32_t *>(row + OFF_FLOOR);
+    const uint32_t *vp = reinterpret_cast<const uint32_t *>(row + OFF_VIEWED);
+    for (int r = lane; r < PL; r += 32) {
+        s.floor[r] = fp[r];
+        s.viewed[r] = vp[r];
+    }
+    if (lane < 16) s.vis[lane] = reinterpret_cast<const uint16_t *>(row + OFF_VIS)[lane];
+    for (int j = lane; j < CELLS; j += 32) s.occ[j] = 0;
+    __syncwarp();
+    if (lane < MAXM && lane < nmon) {
+        const int16_t *m = reinterpret_cast<const int16_t *>(row + OFF_MON);
+        const int pos = m[lane], hp = m[32 + lane];
+        const int kind = row[OFF_MON + 96 + lane], awake = row[OFF_MON + 112 + lane];
+        const int dx = pos % W - px, dy = pos / W - py;
+        if (hp > 0 && dx >= -7 && dx <= 7 && dy >= -7 && dy <= 7 && ((s.vis[dy + 7] >> (dx + 7)) & 1u)) {
+            const int cls = kind == 4 ? 7 : awake ? 6 : 5;
+            s.occ[(dy + 7) * 15 + dx + 7] = (uint16_t)(cls | 8 | ((hp > 31 ? 31 : hp) << 4));
+        }
+    }
+    __syncwarp();
+    const int r = g & 3;
+    const bool mirror = g >= 4;
+    uint16_t *o = out + (size_t)env * (CROP * CROP_PITCH);
+    for (int y = 0; y < CROP; y++) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int x = lane + 32 * h;
+            uint32_t code = 0;
+            if (x < CROP) {
+                const int dx = x - 31, dy = y - 31;
+                int sx = r == 0 ? dx : r == 1 ? dy : r == 2 ? -dx : -dy;
+                const int sy = r == 0 ? dy : r == 1 ? -dx : r == 2 ? -dy : dx;
+                if (mirror) sx = -sx;
+                const int cx = px + sx, cy = py + sy;
+                if (cx >= 0 && cx < W && cy >= 0 && cy < H) {
+                    const int word = cy * 3 + (cx >> 5), bit = cx & 31;
+                    uint32_t cls = 0;
+                    if ((s.viewed[word] >> bit) & 1u) {
+                        if (!((s.floor[word] >> bit) & 1u)) {
+                            cls = 1;
+                        } else {
+                            const bool win = sx >= -7 && sx <= 7 && sy >= -7 && sy <= 7;
+                            const bool vis = win && ((s.vis[sy + 7] >> (sx + 7)) & 1u);
+                            const uint32_t occ = vis ? s.occ[(sy + 7) * 15 + sx + 7] : 0u;
+                            cls = occ ? occ : (cy * W + cx == stairs ? 4u : vis ? 3u : 2u);
+                        }
+                    }
+                    code = cls | 8u;
+                }
+            }
+            o[y * CROP_PITCH + x] = (uint16_t)code;
+        }
+    }
 }
 
 __global__ void compact_kernel(const uint8_t *state, int n, int64_t *rows) {
@@ -1070,6 +1149,14 @@ int d1_spec_init(void *state, int n, const D1SpecConfig *c, uint64_t seed, int f
     if (n == 0) return 0;
     spec::init_kernel<<<(n + spec::WARPS - 1) / spec::WARPS, spec::WARPS * 32, 0, (cudaStream_t)stream>>>(
         (uint8_t *)state, n, *c, g_rays, seed, first_env, (__nv_bfloat16 *)obs_bf16, legal);
+    return (int)cudaGetLastError();
+}
+
+int d1_spec_crop(const void *state, int n, int g, uint16_t *crop, void *stream) {
+    if (n < 0 || g < 0 || g > 7 || !state || !crop) return D1_ERR_BAD_ARGUMENT;
+    if (n == 0) return 0;
+    spec::crop_kernel<<<(n + spec::CROP_WARPS - 1) / spec::CROP_WARPS, spec::CROP_WARPS * 32, 0,
+                        (cudaStream_t)stream>>>((const uint8_t *)state, n, g, crop);
     return (int)cudaGetLastError();
 }
 

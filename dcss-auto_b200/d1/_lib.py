@@ -41,6 +41,13 @@ SIGNATURES = {
     'd1_gemm_splits': [_I, _I],
     'd1_gemm_error': [],
     'd1_gemm_wgrad_noalloc': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _I, _P],
+    'd1_spec_crop': [_P, _I, _I, _P, _P],
+    'd1_conv_in_bytes': [_I],
+    'd1_conv_weight_bytes': [_I],
+    'd1_conv_pack_weights': [_I, _P, _P, _P],
+    'd1_conv_layer': [_I, _P, _I, _P, _P, _P, _P],
+    'd1_conv_error': [],
+    'd1_ar_head_sample': [_P, _I, _P, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P, _P, _P, _P],
 }
 
 _LIB = None

@@ -90,7 +90,10 @@ def device_rays(device):
 
 
 class SpecEnv:
-    def __init__(self, batch, config=None, seed=0, first_env=0, device='cuda'):
+    def __init__(self, batch, config=None, seed=0, first_env=0, device='cuda', observe=True):
+        """observe=False skips the 1832-feature observation writes (the conv
+        policy reads the env state through d1_spec_crop instead); legal bits and
+        outcomes are still written."""
         self.device = torch.device('cuda:0' if device == 'cuda' else device)
         if self.device.type != 'cuda':
             raise ValueError('libd1 runs on CUDA devices only; use the oracle for CPU reference runs')
@@ -102,7 +105,7 @@ class SpecEnv:
         with torch.cuda.device(self.device):
             self.rays = device_rays(self.device)
         self.state = torch.empty((batch, self.lib.d1_spec_state_bytes()), dtype=torch.uint8, device=self.device)
-        self.obs = torch.empty((batch, OBS), dtype=torch.bfloat16, device=self.device)
+        self.obs = torch.empty((batch, OBS), dtype=torch.bfloat16, device=self.device) if observe else None
         self.legal = torch.empty(batch, dtype=torch.int16, device=self.device)  # u16 bits
         self.out = torch.zeros((batch, OUT), device=self.device)
         self.reset(seed)
@@ -115,7 +118,8 @@ class SpecEnv:
         obs = self.obs if obs_out is None else obs_out
         legal = self.legal if legal_out is None else legal_out
         check(self.lib.d1_spec_init(self.state.data_ptr(), self.batch, C.byref(self.config), seed, self.first_env,
-                                    obs.data_ptr(), legal.data_ptr(), self.stream), 'd1_spec_init')
+                                    None if obs is None else obs.data_ptr(), legal.data_ptr(), self.stream),
+              'd1_spec_init')
         return obs
 
     def step(self, actions, active=None, obs_out=None, legal_out=None, out_out=None):
@@ -130,7 +134,8 @@ class SpecEnv:
         legal = self.legal if legal_out is None else legal_out
         out = self.out if out_out is None else out_out
         check(self.lib.d1_spec_step(self.state.data_ptr(), self.batch, C.byref(self.config), actions.data_ptr(),
-                                    obs.data_ptr(), legal.data_ptr(), out.data_ptr(), act or None, self.stream),
+                                    None if obs is None else obs.data_ptr(), legal.data_ptr(), out.data_ptr(),
+                                    act or None, self.stream),
               'd1_spec_step')
         return obs, out
 

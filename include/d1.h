@@ -140,6 +140,17 @@ int d1_spec_step(void *state, int n, const D1SpecConfig *c, const int64_t *actio
 int d1_spec_compact(const void *state, int n, int64_t *rows, void *stream);
 /* Floor and remembered-cell bit planes, u32[n, 210] each (row y = words 3y..3y+2). */
 int d1_spec_planes(const void *state, int n, uint32_t *floor, uint32_t *viewed, void *stream);
+/* Conv-policy input: the egocentric 63x63 crop of each env
+ * under D4 element g (0-7), u16 [n, 63, 64] (column 63 zero). Pixel (x, y) shows
+ * the map cell at offset d4(g, x - 31, y - 31) from the player, d4 = rotation by
+ * g % 4 quarter turns ((dx, dy) -> (dy, -dx)), then an x mirror for g >= 4 (the
+ * sampling rule of gpu-d1/branches/vision15-centered-map-v1/src/fast_maps.cu:4-17).
+ * Code bits 0-2: the observation's one-hot class (0 unknown, 1 wall, 2 remembered
+ * floor, 3 visible floor, 4 stairs, 5 asleep, 6 awake, 7 ogre); bit 3: on the
+ * map; bits 4-8: hp of the visible monster there. The conv stack expands it to
+ * 10 channels (8 one-hot, hp / 32, on-map). d1_spec_step/init accept
+ * obs_bf16 == NULL when only the crop (and legal bits) are wanted. */
+int d1_spec_crop(const void *state, int n, int g, uint16_t *crop, void *stream);
 
 /* ======================================================================
  * Policy and PPO kernels (no reference counterpart as kernels: the reference
@@ -181,6 +192,37 @@ int d1_gemm_splits(int K, int splits);
  * the caller. */
 int d1_gemm_wgrad_noalloc(const void *a, int lda, const void *b, int ldb, int M, int N, int K, float *out, int ldo,
                           int splits, void *stream);
+/* Conv encoder of the centered-map policy on tcgen05 (the
+ * reference runs it as torch Conv2d layers, vision15-centered-map-v1/scripts/
+ * tactical_models.py:11-13): three 3x3 stride-2 convs with ReLU,
+ * 10 -> 32 -> 64 -> 64 channels, 63x63 -> 31x31 -> 15x15 -> 7x7.
+ * Layer 1 reads the u16 crops of d1_spec_crop; layers 2 and 3 read the previous
+ * layer's output, written by it in the layer's own input layout
+ * (d1_conv_in_bytes(layer) bytes per env); layer 3 writes the flattened NHWC
+ * FC input, bf16 [n, 3136] (feature (y*7 + x)*64 + channel). w_packed is the
+ * layer's weight in operand layout (d1_conv_weight_bytes(layer) bytes, made by
+ * d1_conv_pack_weights from torch's fp32 [Cout, Cin, 3, 3]); bias f32 [Cout].
+ * Buffers 16-byte aligned. d1_conv_in_bytes(4) is the FC input row (6272 B). */
+int d1_conv_in_bytes(int layer);
+int d1_conv_weight_bytes(int layer);
+int d1_conv_pack_weights(int layer, const float *w, void *packed, void *stream);
+int d1_conv_layer(int layer, const void *in, int n, const void *w_packed, const float *bias, void *out, void *stream);
+/* Nonzero when a conv pipeline wait expired; reading clears it. Synchronises. */
+int d1_conv_error(void);
+/* Autoregressive verb x target head (the reference's
+ * ActionDistribution, autoregressive-actions-v1/scripts/tactical_models.py:8-30,
+ * with 12 verbs and 9 targets). hb f32 [n, 80] = head GEMM rows [verb logits
+ * 0-11, value 12, direction pre-activation 13-76, pad]; cond f32 [2, 64] (the
+ * type embedding's first-layer term for MOVE and ATTACK); wt f32 [9, 64], bt f32
+ * [9]. Draws the verb, then the target of a directional verb, from Philox words
+ * 0 and 1 keyed by (first_env + row, seed, step), and writes the joint index
+ * (9*verb + target for MOVE/ATTACK, else 16 + verb), the env action, log p,
+ * value and, when given, the entropy and the verb [n, 12] / target [n, 2, 9]
+ * logits. Any output may be NULL. */
+int d1_ar_head_sample(const float *hb, int n, const float *cond, const float *wt, const float *bt,
+                      const uint16_t *legal, uint64_t seed, uint64_t step, int first_env, int64_t *joint,
+                      int64_t *env_action, float *logp, float *value, float *entropy, float *verb_logits,
+                      float *target_logits, void *stream);
 /* Nonzero when a GEMM pipeline wait expired (the kernel then skipped its work
  * and freed its tensor memory); reading clears it. Synchronises the device. */
 int d1_gemm_error(void);

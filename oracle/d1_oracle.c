@@ -1246,3 +1246,180 @@ int oracle_sample_actions(const float *logits, const uint16_t *legal, int n, uin
     }
     return 0;
 }
+
+/* ---- conv policy inputs and the autoregressive head ---- */
+
+/* D4 element g acting on a crop offset (dx, dy): rotation r = g % 4 gives
+ * (dx, dy), (dy, -dx), (-dx, -dy), (-dy, dx); g >= 4 then negates x. This is the
+ * sampling rule of gpu-d1/branches/vision15-centered-map-v1/src/fast_maps.cu:7-9. */
+static void d4_offset(int g, int dx, int dy, int *sx, int *sy) {
+    const int r = g & 3;
+    int a = r == 0 ? dx : r == 1 ? dy : r == 2 ? -dx : -dy;
+    int b = r == 0 ? dy : r == 1 ? -dx : r == 2 ? -dy : dx;
+    if (g >= 4) a = -a;
+    *sx = a;
+    *sy = b;
+}
+
+/* Egocentric 63x63 crop (rows of pitch 64, column 63 zero) of each env under D4
+ * element g. Pixel (x, y) shows map cell (px + sx, py + sy) with (sx, sy) =
+ * d4_offset(g, x - 31, y - 31), coded in a u16:
+ *   bits 0-2  the one-hot class of the 15x15 observation (0 unknown, 1 wall,
+ *             2 remembered floor, 3 visible floor, 4 stairs, 5 asleep, 6 awake,
+ *             7 ogre); visibility is the LOS window, monsters only when visible
+ *   bit 3     the cell is on the 80x70 map
+ *   bits 4-8  hp (<= 31) of the visible monster standing there. */
+int oracle_spec_crop(const void *states, int n, int g, uint16_t *out) {
+    if (g < 0 || g > 7) return 1;
+    const Spec *ss = (const Spec *)states;
+    for (int i = 0; i < n; i++) {
+        const Spec *s = &ss[i];
+        const int px = s->player % W, py = s->player / W;
+        uint16_t *o = out + (size_t)i * 63 * 64;
+        for (int y = 0; y < 63; y++) {
+            for (int x = 0; x < 64; x++) {
+                uint16_t code = 0;
+                if (x < 63) {
+                    int sx, sy;
+                    d4_offset(g, x - 31, y - 31, &sx, &sy);
+                    const int cx = px + sx, cy = py + sy;
+                    if (cx >= 0 && cx < W && cy >= 0 && cy < H) {
+                        const int p = cy * W + cx;
+                        int cls = 0, hp = 0;
+                        if (bit_at(s->viewed, p)) {
+                            if (!bit_at(s->floor, p)) cls = 1;
+                            else {
+                                const int vis = sx >= -7 && sx <= 7 && sy >= -7 && sy <= 7 &&
+                                                ((s->vis[sy + 7] >> (sx + 7)) & 1);
+                                const int id = vis ? s_occupant(s, p) : -1;
+                                if (id >= 0) {
+                                    cls = s->kind[id] == 4 ? 7 : s->awake[id] ? 6 : 5;
+                                    hp = s->mhp[id] > 31 ? 31 : s->mhp[id];
+                                } else if (p == s->stairs) cls = 4;
+                                else cls = vis ? 3 : 2;
+                            }
+                        }
+                        code = (uint16_t)(cls | 8 | (hp << 4));
+                    }
+                }
+                o[y * 64 + x] = code;
+            }
+        }
+    }
+    return 0;
+}
+
+/* Validity of the verbs and of the targets of the two directional verbs from
+ * the spec env's legal bits (0-7 passable neighbour, 8 wait, 9 rest allowed,
+ * 10 an adjacent visible monster, 11 on the stairs):
+ *   verb 0 MOVE     targets 0-7 = passable directions, target 8 never
+ *   verb 1 ATTACK   targets 0-7 = passable directions, 8 = nearest; all need bit 10
+ *   verb 2 WAIT, 3 REST, 4 DESCEND (bits 8, 9, 11); verbs 5-11 are not offered on D:1.
+ * A directional verb is valid when any of its targets is (type_mask of
+ * autoregressive-actions-v1/scripts/tactical_models.py:10-12). */
+static void ar_masks(uint32_t bits, int vvalid[12], int tvalid[2][9]) {
+    for (int t = 0; t < 9; t++) {
+        tvalid[0][t] = t < 8 ? (int)((bits >> t) & 1u) : 0;
+        tvalid[1][t] = ((bits >> 10) & 1u) ? (t < 8 ? (int)((bits >> t) & 1u) : 1) : 0;
+    }
+    for (int v = 0; v < 12; v++) vvalid[v] = 0;
+    for (int k = 0; k < 2; k++)
+        for (int t = 0; t < 9; t++) vvalid[k] |= tvalid[k][t];
+    vvalid[2] = (int)((bits >> 8) & 1u);
+    vvalid[3] = (int)((bits >> 9) & 1u);
+    vvalid[4] = (int)((bits >> 11) & 1u);
+}
+
+static const int AR_ENV_ACTION[28] = {0, 1, 2, 3, 4, 5, 6, 7, -1,        /* MOVE t */
+                                      0, 1, 2, 3, 4, 5, 6, 7, 10,        /* ATTACK t (bump), nearest */
+                                      8, 9, 11, -1, -1, -1, -1, -1, -1, -1};  /* WAIT REST DESCEND, D:1-absent */
+
+/* Inverse-CDF draw over the valid entries of l[0..k): returns the index and the
+ * max / normaliser used (the flat sampler's arithmetic). */
+static int ar_draw(const float *l, const int *ok, int k, float u, float *m_out, float *total_out) {
+    float m = -3.402823466e38f, z[12], total = 0.f;
+    for (int j = 0; j < k; j++)
+        if (ok[j]) m = l[j] > m ? l[j] : m;
+    for (int j = 0; j < k; j++) {
+        z[j] = ok[j] ? o_exp_nonpos(l[j] + -m) : 0.f;
+        total = total + z[j];
+    }
+    const float t = u * total;
+    int a = -1, last = 0;
+    float run = 0.f;
+    for (int j = 0; j < k; j++) {
+        if (!ok[j]) continue;
+        last = j;
+        run = run + z[j];
+        if (a < 0 && t < run) a = j;
+    }
+    *m_out = m;
+    *total_out = total;
+    return a < 0 ? last : a;
+}
+
+/* Entropy of the masked categorical over l[0..k) (masked entries carry no mass). */
+static float ar_entropy(const float *l, const int *ok, int k, float *p_out) {
+    float m = -3.402823466e38f, total = 0.f;
+    for (int j = 0; j < k; j++)
+        if (ok[j]) m = l[j] > m ? l[j] : m;
+    for (int j = 0; j < k; j++) total += ok[j] ? expf(l[j] - m) : 0.f;
+    const float lz = logf(total);
+    float h = 0.f;
+    for (int j = 0; j < k; j++) {
+        float p = 0.f;
+        if (ok[j]) {
+            const float lp = l[j] - m - lz;
+            p = expf(lp);
+            h -= p * lp;
+        }
+        if (p_out) p_out[j] = p;
+    }
+    return h;
+}
+
+/* Autoregressive verb x target sampling (type-first factorisation of
+ * autoregressive-actions-v1/scripts/tactical_models.py:8-30 with 12 verbs and 9
+ * targets). The verb is drawn with uniform word 0, the target of a directional
+ * verb with word 1 of Philox(ctr = {lo(step), hi(step), hi(seed), 2},
+ * key = {env, lo(seed)}); a directional verb with no valid target samples all
+ * nine (the reference's safe dummy conditional). joint = 9v + t for v < 2, else
+ * 16 + v. logp = log p(verb) + log p(target | verb); entropy = H(verb) +
+ * sum over directional verbs of p(verb) H(target | verb). */
+int oracle_sample_ar(const float *vl, const float *tl, const uint16_t *legal, int n, uint64_t seed, uint64_t step,
+                     int first_env, int64_t *joint, int64_t *env_action, float *logp, float *entropy) {
+    for (int i = 0; i < n; i++) {
+        const float *l = vl + (size_t)i * 12, *lt = tl + (size_t)i * 18;
+        int vvalid[12], tvalid[2][9], safe[2][9];
+        ar_masks(legal[i], vvalid, tvalid);
+        for (int k = 0; k < 2; k++) {
+            int any = 0;
+            for (int t = 0; t < 9; t++) any |= tvalid[k][t];
+            for (int t = 0; t < 9; t++) safe[k][t] = tvalid[k][t] || !any;
+        }
+        uint32_t ctr[4] = {(uint32_t)step, (uint32_t)(step >> 32), (uint32_t)(seed >> 32), 2u};
+        uint32_t key[2] = {(uint32_t)(first_env + i), (uint32_t)seed}, o[4];
+        oracle_philox(ctr, key, o);
+        const float uv = (float)(o[0] >> 8) * (1.0f / 16777216.0f), ut = (float)(o[1] >> 8) * (1.0f / 16777216.0f);
+        float mv, tv, mt = 0.f, tt = 1.f;
+        const int v = ar_draw(l, vvalid, 12, uv, &mv, &tv);
+        int t = 0;
+        float lp = (l[v] - mv) - logf(tv);
+        if (v < 2) {
+            t = ar_draw(lt + 9 * v, safe[v], 9, ut, &mt, &tt);
+            lp += (lt[9 * v + t] - mt) - logf(tt);
+        }
+        const int j = v < 2 ? 9 * v + t : 16 + v;
+        joint[i] = j;
+        if (env_action) env_action[i] = AR_ENV_ACTION[j];
+        logp[i] = lp;
+        if (entropy) {
+            float pv[12];
+            float h = ar_entropy(l, vvalid, 12, pv);
+            for (int k = 0; k < 2; k++)
+                if (pv[k] > 0.f) h += pv[k] * ar_entropy(lt + 9 * k, safe[k], 9, NULL);
+            entropy[i] = h;
+        }
+    }
+    return 0;
+}

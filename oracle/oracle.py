@@ -257,6 +257,8 @@ def spec_library():
         lib.oracle_spec_step.argtypes = [p, i, p, p, p, p, p]
         lib.oracle_spec_compact.argtypes = [p, i, p]
         lib.oracle_spec_planes.argtypes = [p, i, p, p]
+        lib.oracle_spec_crop.argtypes = [p, i, i, p]
+        lib.oracle_sample_ar.argtypes = [p, p, p, i, C.c_uint64, C.c_uint64, i, p, p, p, p]
         ex, ey, blk = rays()
         lib._rays_keep = (ex, ey, blk)
         assert lib.oracle_set_rays(ex.ctypes.data, ey.ctypes.data, blk.ctypes.data, len(ex)) == 0
@@ -304,6 +306,12 @@ class OracleSpec:
         self.lib.oracle_spec_compact(self.state.ctypes.data, self.batch, rows.ctypes.data)
         return rows
 
+    def crop(self, g=0):
+        """u16 [n, 63, 64] egocentric crops under D4 element g (conv policy input)."""
+        out = np.zeros((self.batch, 63, 64), np.uint16)
+        assert self.lib.oracle_spec_crop(self.state.ctypes.data, self.batch, g, out.ctypes.data) == 0
+        return out
+
     def planes(self):
         f = np.zeros((self.batch, 210), np.uint32)
         v = np.zeros((self.batch, 210), np.uint32)
@@ -333,3 +341,23 @@ def sample_actions(logits, legal, seed, step, first_env=0):
     lib.oracle_sample_actions(logits.ctypes.data, legal.ctypes.data, n, seed, step, first_env, a.ctypes.data,
                               lp.ctypes.data)
     return a, lp
+
+
+AR_ENV_ACTION = np.array([0, 1, 2, 3, 4, 5, 6, 7, -1, 0, 1, 2, 3, 4, 5, 6, 7, 10, 8, 9, 11, -1, -1, -1, -1, -1, -1, -1],
+                         np.int64)
+
+
+def sample_ar(verb_logits, target_logits, legal, seed, step, first_env=0):
+    """Oracle of the autoregressive verb x target sampler:
+    (joint int64, env action int64, logp float32, entropy float32)."""
+    lib = spec_library()
+    vl = np.ascontiguousarray(verb_logits, np.float32)
+    tl = np.ascontiguousarray(target_logits, np.float32)
+    legal = np.ascontiguousarray(legal, np.uint16)
+    n = vl.shape[0]
+    assert vl.shape == (n, 12) and tl.shape == (n, 2, 9)
+    j, a = np.empty(n, np.int64), np.empty(n, np.int64)
+    lp, ent = np.empty(n, np.float32), np.empty(n, np.float32)
+    lib.oracle_sample_ar(vl.ctypes.data, tl.ctypes.data, legal.ctypes.data, n, seed, step, first_env, j.ctypes.data,
+                         a.ctypes.data, lp.ctypes.data, ent.ctypes.data)
+    return j, a, lp, ent
