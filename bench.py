@@ -55,6 +55,9 @@ def parse():
     ap.add_argument('--minibatch', type=int, default=16384)
     ap.add_argument('--epochs', type=int, default=4)
     ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--no-conv', action='store_true', help='skip the config-3 conv-policy rollout line')
+    ap.add_argument('--conv-envs', type=int, default=131072, help='envs per GPU of the config-3 line')
+    ap.add_argument('--conv-steps', type=int, default=16)
     return ap.parse_args()
 
 
@@ -334,6 +337,55 @@ def run_ours(args, rank, world, local_rank):
                     'update_ms': p2.elapsed_time(p3), 'minibatch_ms': p2.elapsed_time(p3) / updates,
                     'samples_per_iteration': T * B * world, 'minibatch': args.minibatch, 'epochs': args.epochs,
                     'finite': bool(torch.isfinite(policy.flat).all().item())}
+    # centered-map conv policy with the autoregressive head,
+    # 131,072 envs per GPU; a step = crop + conv stack + FC + head + AR sampling
+    # + env step (no 1832-feature observation is written).
+    conv_line = None
+    if not args.no_conv:
+        from d1.conv_policy import ConvPolicy, conv_error
+        progress('config 3 conv rollout')
+        n3 = args.conv_envs
+        env3 = SpecEnv(n3, seed=3, first_env=rank * n3, device=dev, observe=False)
+        pol3 = ConvPolicy(device=dev, seed=0)
+        buf3 = pol3.buffers(n3)
+        out3 = None
+        for k in range(3):
+            out3 = pol3.act(env3.state, env3.legal, n3, buf3, 3, k, rank * n3, out=out3)
+            env3.step(out3['env_action'])
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        c0.record(stream)
+        for k in range(args.conv_steps):
+            last = k == args.conv_steps - 1
+            pol3.encode(env3.state, n3, buf3)
+            if last:
+                f0.record(stream)
+            pol3.features(buf3, n3)
+            if last:
+                f1.record(stream)
+            out3 = pol3.act_from_features(env3.legal, n3, buf3, 3, 100 + k, rank * n3, out=out3)
+            env3.step(out3['env_action'])
+        c1.record(stream)
+        torch.cuda.synchronize()
+        t3 = torch.tensor([c0.elapsed_time(c1)], device=dev)
+        if world > 1:
+            dist.all_reduce(t3, op=dist.ReduceOp.MAX)
+        feat_ms = f0.elapsed_time(f1)
+        conv_flop = (5535360 + 8294400 + 3612672 + 3211264) * n3
+        pk3, _ = peaks()
+        conv_line = {'metric': 'env decisions/sec, centered-map conv policy + autoregressive head (config 3)',
+                     'value': n3 * world * args.conv_steps / (t3.item() / 1e3), 'unit': UNIT,
+                     'ms_per_step': t3.item() / args.conv_steps, 'envs_per_gpu': n3, 'steps': args.conv_steps,
+                     'roofline': {'kernels': 'd1::conv::conv_kernel<1..3> + FC/head d1::tc::gemm_kernel',
+                                  'bound': 'tensor', 'achieved': conv_flop / (feat_ms / 1e3) / 1e12,
+                                  'peak': pk3['bf16_tflops'], 'unit': 'TFLOP/s',
+                                  'frac': conv_flop / (feat_ms / 1e3) / 1e12 / pk3['bf16_tflops'],
+                                  'flop_per_decision': conv_flop // n3, 'features_ms': feat_ms},
+                     'conv_error': conv_error()}
+        del env3, pol3, buf3, out3
     if rank != 0:
         return
     pk, pk_kind = peaks()
@@ -356,6 +408,7 @@ def run_ours(args, rank, world, local_rank):
                                  'unit': 'TFLOP/s', 'frac': gemm_tflops / pk['bf16_tflops'],
                                  'ms_per_launch': gemm_ms, 'peak_kind': pk_kind + ' burst'},
         'ppo': ppo_line,
+        'config3': conv_line,
         'clocks': clk,
         'e2e': e2e,
         'gpu_launches': args.steps * 4,

@@ -20,10 +20,12 @@
 // in TMEM. Output columns ox >= the valid width and rows past the output are
 // computed from neighbouring data and discarded by the epilogue.
 //
-// Each CTA (256 threads, two per SM so one CTA's MMAs overlap the other's
-// staging and epilogue) walks units: layer 1 = half an env (output rows 0-15 or
-// 16-30), expanded from the u16 crop codes into one-hot bf16 planes in shared
-// memory; layers 2 and 3 = one env, whose planes the previous layer's epilogue
+// Each CTA walks units, several CTAs per SM so one CTA's MMAs overlap the
+// others' staging and epilogues: layer 1 (four 128-thread CTAs per SM) = a
+// quarter env (8 output rows), expanded from the u16 crop codes into one-hot
+// bf16 planes in shared memory, the next quarter's crop rows prefetched into
+// registers while the MMAs run; layers 2 and 3 (two 256-thread CTAs per SM) =
+// one env, whose planes the previous layer's epilogue
 // wrote to global memory in exactly the shared-memory layout, so one bulk copy
 // stages them. The epilogue (TMEM -> bias, ReLU -> bf16) scatters every output
 // pixel into the next layer's phase planes (or the FC input). Weights stay in
@@ -38,28 +40,32 @@
 namespace d1 {
 namespace conv {
 
-constexpr int THREADS = 256, CROP_PITCH = 64, CROP_ROWS = 63;
+constexpr int CROP_PITCH = 64, CROP_ROWS = 63;
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 __device__ int g_error;
 
 template <int L>
 struct Geo;
-// layer 1: crop codes -> 31x31x32; unit = half an env (17 phase rows)
+// layer 1: crop codes -> 31x31x32; unit = a quarter env (8 output rows from 9
+// phase rows = 18 crop rows); four 128-thread CTAs per SM
 template <>
 struct Geo<1> {
-    static constexpr int CIN = 10, CHUNKS = 2, N = 32, PW = 32, PLANE = 17 * 32, MT = 4, UNITS = 2, TAIL = 64;
+    static constexpr int CIN = 10, CHUNKS = 2, N = 32, PW = 32, PLANE = 9 * 32, MT = 2, UNITS = 4, TAIL = 64;
+    static constexpr int THREADS = 128, CTAS_PER_SM = 4, ROWS_IN = 18;
     static constexpr int OUT_BYTES = 4 * 4 * 256 * 16;  // layer-2 planes
 };
 // layer 2: 31x31x32 -> 15x15x64
 template <>
 struct Geo<2> {
     static constexpr int CIN = 32, CHUNKS = 4, N = 64, PW = 16, PLANE = 256, MT = 2, UNITS = 1, TAIL = 32;
+    static constexpr int THREADS = 256, CTAS_PER_SM = 2;
     static constexpr int OUT_BYTES = 4 * 8 * 64 * 16;  // layer-3 planes
 };
 // layer 3: 15x15x64 -> 7x7x64 = FC input
 template <>
 struct Geo<3> {
     static constexpr int CIN = 64, CHUNKS = 8, N = 64, PW = 8, PLANE = 64, MT = 1, UNITS = 1, TAIL = 80;
+    static constexpr int THREADS = 256, CTAS_PER_SM = 2;
     static constexpr int OUT_BYTES = 49 * 64 * 2;
 };
 template <int L>
@@ -68,7 +74,7 @@ struct Lay {
     static constexpr int IN_BYTES = 4 * G::CHUNKS * G::PLANE * 16;     // planes of one unit
     static constexpr int IN_SMEM = IN_BYTES + G::TAIL * 16;            // + overrun pad
     static constexpr int W_BYTES = 9 * G::CHUNKS * G::N * 16;
-    static constexpr int STAGE_BYTES = L == 1 ? 34 * CROP_PITCH * 2 : 0;  // crop rows of a half
+    static constexpr int STAGE_BYTES = L == 1 ? 18 * CROP_PITCH * 2 : 0;  // crop rows of a quarter
     static constexpr int OFF_W = IN_SMEM, OFF_BIAS = OFF_W + W_BYTES, OFF_STAGE = OFF_BIAS + G::N * 4;
     static constexpr int OFF_BAR = (OFF_STAGE + STAGE_BYTES + 15) & ~15;
     static constexpr int SMEM = OFF_BAR + 64;
@@ -150,23 +156,37 @@ __device__ __forceinline__ void finish32(const uint32_t *v, const float *bias, u
     }
 }
 
-// Layer-1 staging of one half env: crop rows [32h, 32h + 34) (zero past row 62)
-// into shared memory, then every phase-plane pixel expanded to 16 channels:
+// Layer-1 staging of a quarter env: its 18 crop rows (zero past row 62) are
+// fetched into registers (the next unit's while the current unit's MMAs run),
+// stored to shared memory, and every phase-plane pixel expanded to 16 channels:
 // one-hot class (0-7), monster hp / 32 (8), on-the-map flag (9), zeros.
-__device__ void stage_crop(const uint16_t *__restrict__ crop, int env, int half, uint8_t *smem) {
+constexpr int STAGE_VECS = 18 * CROP_PITCH * 2 / 16;                    // uint4 per unit
+constexpr int STAGE_REGS = (STAGE_VECS + Geo<1>::THREADS - 1) / Geo<1>::THREADS;
+__device__ __forceinline__ void fetch_crop(const uint16_t *__restrict__ crop, int unit, int units, uint4 *r) {
+    const int env = unit >> 2, quarter = unit & 3;
+    const uint4 *src = reinterpret_cast<const uint4 *>(crop + (size_t)env * CROP_ROWS * CROP_PITCH);
+    constexpr int VPR = CROP_PITCH * 2 / 16;
+#pragma unroll
+    for (int k = 0; k < STAGE_REGS; k++) {
+        const int i = threadIdx.x + k * Geo<1>::THREADS;
+        const int y = 16 * quarter + i / VPR;
+        r[k] = (unit < units && i < STAGE_VECS && y < CROP_ROWS) ? __ldg(src + y * VPR + i % VPR)
+                                                                  : make_uint4(0, 0, 0, 0);
+    }
+}
+__device__ void expand_crop(const uint4 *r, uint8_t *smem) {
     using Y = Lay<1>;
     uint4 *st = reinterpret_cast<uint4 *>(smem + Y::OFF_STAGE);
-    const uint4 *src = reinterpret_cast<const uint4 *>(crop + (size_t)env * CROP_ROWS * CROP_PITCH);
-    constexpr int VPR = CROP_PITCH * 2 / 16;  // uint4 per crop row
-    for (int i = threadIdx.x; i < 34 * VPR; i += THREADS) {
-        const int y = 32 * half + i / VPR;
-        st[i] = y < CROP_ROWS ? __ldg(src + y * VPR + i % VPR) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < STAGE_REGS; k++) {
+        const int i = threadIdx.x + k * Geo<1>::THREADS;
+        if (i < STAGE_VECS) st[i] = r[k];
     }
     __syncthreads();
     const uint16_t *rows = reinterpret_cast<const uint16_t *>(st);
     uint4 *planes = reinterpret_cast<uint4 *>(smem);
     constexpr int PLANE = Geo<1>::PLANE;
-    for (int e = threadIdx.x; e < 4 * PLANE; e += THREADS) {
+    for (int e = threadIdx.x; e < 4 * PLANE; e += Geo<1>::THREADS) {
         const int phase = e / PLANE, pos = e - phase * PLANE;
         const int yl = pos >> 5, xp = pos & 31;
         const int y = 2 * yl + (phase >> 1), x = 2 * xp + (phase & 1);
@@ -183,11 +203,12 @@ __device__ void stage_crop(const uint16_t *__restrict__ crop, int env, int half,
 }
 
 template <int L>
-__global__ void __launch_bounds__(THREADS, 2)
+__global__ void __launch_bounds__(Geo<L>::THREADS, Geo<L>::CTAS_PER_SM)
     conv_kernel(const void *__restrict__ in, int n, const uint4 *__restrict__ w, const float *__restrict__ bias,
                 uint8_t *__restrict__ out) {
     using G = Geo<L>;
     using Y = Lay<L>;
+    constexpr int THREADS = G::THREADS, WGROUPS = THREADS / 128;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Y::OFF_BAR);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2);
@@ -222,29 +243,48 @@ __global__ void __launch_bounds__(THREADS, 2)
     const uint32_t in_base = smem_u32(smem), w_base = smem_u32(w_s);
     const int units = n * G::UNITS;
     uint32_t it = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, it++) {
-        const int env = u / G::UNITS, half = u % G::UNITS;
-        // ---- stage the unit's input planes
-        if constexpr (L == 1) {
-            stage_crop(static_cast<const uint16_t *>(in), env, half, smem);
-            fence_proxy_async();
-            __syncthreads();
-        } else {
-            if (tid == 0) {
+    uint4 pre[L == 1 ? STAGE_REGS : 1];
+    if constexpr (L == 1) fetch_crop(static_cast<const uint16_t *>(in), blockIdx.x, units, pre);
+    // Layers 2 and 3: one bulk copy of a unit's planes into the input buffer,
+    // completing on in_bar.
+    bool outstanding = false;  // thread 0: a requested copy not yet waited for
+    uint32_t out_parity = 0;
+    auto request = [&](int unit, uint32_t parity) {
+        if constexpr (L != 1) {
+            if (tid == 0 && unit < units) {
+                outstanding = true;
+                out_parity = parity;
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(in_bar),
                              "r"((uint32_t)Y::IN_BYTES)
                              : "memory");
-                const uint8_t *src = static_cast<const uint8_t *>(in) + (size_t)env * Y::IN_BYTES;
+                const uint8_t *src = static_cast<const uint8_t *>(in) + (size_t)unit * Y::IN_BYTES;
                 constexpr int PIECE = 16384;
 #pragma unroll 1
                 for (int off = 0; off < Y::IN_BYTES; off += PIECE)
                     bulk_load(in_base + off, src + off, (uint32_t)min(PIECE, Y::IN_BYTES - off), in_bar);
             }
         }
+    };
+    request(blockIdx.x, 0u);
+    for (int u = blockIdx.x; u < units; u += gridDim.x, it++) {
+        const int env = u / G::UNITS, part = u % G::UNITS;
+        // ---- stage the unit's input planes
+        if constexpr (L == 1) {
+            expand_crop(pre, smem);
+            fence_proxy_async();
+            __syncthreads();
+        } else {
+            // the unit's planes were requested when the previous unit's MMAs
+            // completed (or before the loop for the first unit)
+            (void)env;
+        }
         // ---- MMAs: M tiles x 9 taps x K steps
         if (tid == 0) {
             bool ok = true;
-            if constexpr (L != 1) ok = mbar_wait(in_bar, it & 1u);
+            if constexpr (L != 1) {
+                ok = mbar_wait(in_bar, it & 1u);
+                if (ok) outstanding = false;
+            }
             if (!ok) {
                 atomicExch(&g_error, 1);
                 *abort_s = 1;
@@ -271,6 +311,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
         __syncthreads();
         if (*abort_s) break;
+        // the next unit's crop rows load while the MMAs run
+        if constexpr (L == 1) fetch_crop(static_cast<const uint16_t *>(in), u + gridDim.x, units, pre);
         const bool done = mbar_wait(mma_bar, it & 1u);
         if (!done) {
             atomicExch(&g_error, 2);
@@ -279,15 +321,17 @@ __global__ void __launch_bounds__(THREADS, 2)
         fence_after();
         __syncthreads();
         if (*abort_s) break;
+        // the input buffer is free: the next unit's planes load during the epilogue
+        request(u + gridDim.x, (it + 1) & 1u);
         // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. of its tiles / column chunks
         const int q = warp & 3, wh = warp >> 2;
         if constexpr (L == 1) {
 #pragma unroll 1
-            for (int m = wh; m < G::MT; m += 2) {
+            for (int m = wh; m < G::MT; m += WGROUPS) {
                 uint32_t v[32];
                 D1_CONV_TMEM_LD32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(m * G::N), v);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                const int oy = 16 * half + m * 4 + q, ox = lane;
+                const int oy = 8 * part + m * 4 + q, ox = lane;
                 if (oy < 31 && ox < 31) {
                     uint4 o[4];
                     finish32(v, bias_s, o);
@@ -332,6 +376,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         fence_before();
         __syncthreads();
     }
+    // after an abort, let a copy still in flight land before the CTA exits
+    if (tid == 0 && outstanding) mbar_wait(in_bar, out_parity);
     fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -368,9 +414,9 @@ static int launch(const void *in, int n, const void *w, const float *bias, void 
         if (e != cudaSuccess) return (int)e;
         if (dev < 64) ready |= 1ull << dev;
     }
-    const int units = n * Geo<L>::UNITS;
-    const int grid = units < 2 * 148 ? units : 2 * 148;
-    conv_kernel<L><<<grid, THREADS, Y::SMEM, stream>>>(in, n, static_cast<const uint4 *>(w), bias,
+    const int units = n * Geo<L>::UNITS, slots = Geo<L>::CTAS_PER_SM * 148;
+    const int grid = units < slots ? units : slots;
+    conv_kernel<L><<<grid, Geo<L>::THREADS, Y::SMEM, stream>>>(in, n, static_cast<const uint4 *>(w), bias,
                                                          static_cast<uint8_t *>(out));
     return (int)cudaGetLastError();
 }

@@ -20,7 +20,8 @@ BASELINE config 3 (63x63x10 crop, 32-64-64 convs, FC 512, 12 verbs x 9 targets).
 Weights are fp32 masters initialised N(0, 1/fan_in) (biases N(0, 0.01^2) so the
 bias paths are exercised) from a torch CPU generator; bf16 copies in operand
 layout feed the kernels. Activations between conv layers go through buffers
-sized for `chunk` envs at a time, so at chunk <= 1024 they stay in L2.
+sized for `chunk` envs at a time (64 KB + 32 KB per env); 16,384 keeps each
+launch many waves deep, which measured faster than L2-sized chunks.
 """
 import torch
 
@@ -34,7 +35,7 @@ CONV = [(10, 32), (32, 64), (64, 64)]
 
 
 class ConvPolicy:
-    def __init__(self, device='cuda', seed=0, chunk=1024):
+    def __init__(self, device='cuda', seed=0, chunk=16384):
         self.device = torch.device(device)
         self.lib = library()
         self.chunk = chunk
@@ -114,6 +115,12 @@ class ConvPolicy:
         """Sample joint actions for n envs from their state rows: returns a dict of
         device tensors joint, env_action (int64), logp, value (fp32) and, with
         debug=True, entropy, verb_logits [n, 12], target_logits [n, 2, 9]."""
+        self.encode(state, n, buf, g)
+        self.features(buf, n)
+        return self.act_from_features(legal, n, buf, seed, step, first_env, out, debug)
+
+    def act_from_features(self, legal, n, buf, seed, step, first_env=0, out=None, debug=False):
+        """The autoregressive head on buf['hb'] (filled by features())."""
         dev = self.device
         if out is None:
             out = {k: torch.empty(n, dtype=torch.int64, device=dev) for k in ('joint', 'env_action')}
@@ -122,8 +129,6 @@ class ConvPolicy:
                 out['entropy'] = torch.empty(n, device=dev)
                 out['verb_logits'] = torch.empty((n, NV), device=dev)
                 out['target_logits'] = torch.empty((n, 2, NT), device=dev)
-        self.encode(state, n, buf, g)
-        self.features(buf, n)
         s = torch.cuda.current_stream(dev).cuda_stream
         ptr = lambda k: out[k].data_ptr() if k in out else None
         p = self.params
