@@ -28,26 +28,13 @@
 
 #include "d1_common.cuh"
 #include "d1_math.cuh"
+#include "d1_philox.cuh"
 
 namespace d1 {
 namespace ar {
 
 constexpr int HB = 80, PRE = 64, NV = 12, NT = 9, ROWS = 128;
 constexpr int HB_PITCH = HB + 1;
-
-__device__ __forceinline__ uint4 philox(uint4 c, uint32_t k0, uint32_t k1) {
-#pragma unroll
-    for (int r = 0; r < 10; r++) {
-        if (r) {
-            k0 += 0x9E3779B9u;
-            k1 += 0xBB67AE85u;
-        }
-        const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
-        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
-        c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
-    }
-    return c;
-}
 
 __constant__ int ENV_ACTION[28] = {0, 1, 2, 3, 4, 5, 6, 7, -1, 0, 1, 2, 3, 4,  5,  6,  7,  10,
                                    8, 9, 11, -1, -1, -1, -1, -1, -1, -1};
@@ -114,7 +101,26 @@ struct Args {
     int64_t *joint, *env_action;
     float *logp, *value, *entropy;
     float *verb_logits, *target_logits;  // optional debug copies [n, 12], [n, 2, 9]
+    int greedy;                          // argmax verb, then argmax target (ActionDistribution.greedy)
 };
+// First valid index of the maximal logit; `m` and `total` as draw<> computes them.
+template <int K>
+__device__ __forceinline__ int argmax(const float *l, uint32_t ok, float &m, float &total) {
+    m = -3.402823466e38f;
+#pragma unroll
+    for (int j = 0; j < K; j++)
+        if ((ok >> j) & 1u) m = fmaxf(m, l[j]);
+    total = 0.f;
+    int a = -1;
+#pragma unroll
+    for (int j = 0; j < K; j++) {
+        if ((ok >> j) & 1u) {
+            total = D1_ADD(total, d1_exp_nonpos(D1_ADD(l[j], -m)));
+            if (a < 0 && l[j] == m) a = j;
+        }
+    }
+    return a < 0 ? 0 : a;
+}
 
 // One thread per env; the block's 128 head rows are staged through shared
 // memory with coalesced loads (pitch 81 floats: conflict-free row reads).
@@ -161,11 +167,10 @@ __global__ void __launch_bounds__(ROWS) ar_kernel(Args a) {
         vok |= ((bits >> 11) & 1u) << 4;
         const uint32_t safe0 = t_move ? t_move : 0x1ffu, safe1 = t_att ? t_att : 0x1ffu;
         // draws
-        const uint4 o = philox(make_uint4((uint32_t)a.step, (uint32_t)(a.step >> 32), (uint32_t)(a.seed >> 32), 2u),
-                               (uint32_t)(a.first_env + row), (uint32_t)a.seed);
+        const uint4 o = policy_draw((uint32_t)(a.first_env + row), a.seed, a.step, 2u);
         const float uv = (float)(o.x >> 8) * (1.0f / 16777216.0f), ut = (float)(o.y >> 8) * (1.0f / 16777216.0f);
         float mv, sv;
-        const int v = draw<NV>(vl, vok, uv, mv, sv);
+        const int v = a.greedy ? argmax<NV>(vl, vok, mv, sv) : draw<NV>(vl, vok, uv, mv, sv);
         float lv = vl[0];
 #pragma unroll
         for (int j = 1; j < NV; j++)
@@ -177,7 +182,7 @@ __global__ void __launch_bounds__(ROWS) ar_kernel(Args a) {
 #pragma unroll
             for (int j = 0; j < NT; j++) lt[j] = v == 0 ? tl[0][j] : tl[1][j];
             float mt, st;
-            t = draw<NT>(lt, v == 0 ? safe0 : safe1, ut, mt, st);
+            t = a.greedy ? argmax<NT>(lt, v == 0 ? safe0 : safe1, mt, st) : draw<NT>(lt, v == 0 ? safe0 : safe1, ut, mt, st);
             float lsel = lt[0];
 #pragma unroll
             for (int j = 1; j < NT; j++)
@@ -215,7 +220,20 @@ extern "C" int d1_ar_head_sample(const float *hb, int n, const float *cond, cons
     if (n < 0 || !hb || !cond || !wt || !bt || !legal) return D1_ERR_BAD_ARGUMENT;
     if (n == 0) return 0;
     Args a{hb, cond, wt, bt, legal, n, first_env, seed, step, joint, env_action, logp, value, entropy, verb_logits,
-           target_logits};
+           target_logits, 0};
+    int blocks = (n + ROWS - 1) / ROWS;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    ar_kernel<<<blocks, ROWS, 0, (cudaStream_t)stream>>>(a);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int d1_ar_head_greedy(const float *hb, int n, const float *cond, const float *wt, const float *bt,
+                                 const uint16_t *legal, int64_t *joint, int64_t *env_action, float *logp, float *value,
+                                 void *stream) {
+    using namespace d1::ar;
+    if (n < 0 || !hb || !cond || !wt || !bt || !legal) return D1_ERR_BAD_ARGUMENT;
+    if (n == 0) return 0;
+    Args a{hb, cond, wt, bt, legal, n, 0, 0, 0, joint, env_action, logp, value, nullptr, nullptr, nullptr, 1};
     int blocks = (n + ROWS - 1) / ROWS;
     if (blocks > 148 * 8) blocks = 148 * 8;
     ar_kernel<<<blocks, ROWS, 0, (cudaStream_t)stream>>>(a);

@@ -14,31 +14,17 @@
 
 #include "d1_common.cuh"
 #include "d1_math.cuh"
+#include "d1_philox.cuh"
 
 namespace d1 {
 namespace head {
 
 constexpr int HID = 256, NOUT = 13, NACT = 12, WARPS = 8;
 
-__device__ __forceinline__ uint4 philox(uint4 c, uint32_t k0, uint32_t k1) {
-#pragma unroll
-    for (int r = 0; r < 10; r++) {
-        if (r) {
-            k0 += 0x9E3779B9u;
-            k1 += 0xBB67AE85u;
-        }
-        const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
-        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
-        c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
-    }
-    return c;
-}
-
 // Uniform in [0, 1) with 24 random bits: word 0 of
 // Philox(ctr = {lo(step), hi(step), hi(seed), 1}, key = {env, lo(seed)}).
 __device__ __forceinline__ float sample_uniform(uint32_t env, uint64_t seed, uint64_t step) {
-    const uint4 o = philox(make_uint4((uint32_t)step, (uint32_t)(step >> 32), (uint32_t)(seed >> 32), 1u), env,
-                           (uint32_t)seed);
+    const uint4 o = policy_draw(env, seed, step, 1u);
     return (float)(o.x >> 8) * (1.0f / 16777216.0f);
 }
 
@@ -53,7 +39,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     head_sample_kernel(const __nv_bfloat16 *__restrict__ h, int n, const __nv_bfloat16 *__restrict__ wh,
                        const float *__restrict__ bh, const uint16_t *__restrict__ legal, uint64_t seed, uint64_t step,
                        int first_env, int64_t *__restrict__ action, float *__restrict__ logp,
-                       float *__restrict__ value, float *__restrict__ logits_out) {
+                       float *__restrict__ value, float *__restrict__ logits_out, int greedy) {
     __shared__ float w_s[NOUT * WROW];
     __shared__ float b_s[NOUT];
     for (int i = threadIdx.x; i < NOUT * HID; i += blockDim.x)
@@ -119,15 +105,22 @@ __global__ void __launch_bounds__(WARPS * 32)
                     z[j] = ((bits >> j) & 1u) ? d1_exp_nonpos(D1_ADD(l[j], -m)) : 0.f;
                     total = D1_ADD(total, z[j]);
                 }
-                const float t = D1_MUL(sample_uniform((uint32_t)(first_env + row), seed, step), total);
                 int a = -1, last = 0;
-                float run = 0.f;
+                if (greedy) {
+                    // first legal action of maximal logit (argmax of the masked probabilities)
 #pragma unroll
-                for (int j = 0; j < NACT; j++) {
-                    if ((bits >> j) & 1u) {
-                        last = j;
-                        run = D1_ADD(run, z[j]);
-                        if (a < 0 && t < run) a = j;
+                    for (int j = 0; j < NACT; j++)
+                        if (a < 0 && ((bits >> j) & 1u) && l[j] == m) a = j;
+                } else {
+                    const float t = D1_MUL(sample_uniform((uint32_t)(first_env + row), seed, step), total);
+                    float run = 0.f;
+#pragma unroll
+                    for (int j = 0; j < NACT; j++) {
+                        if ((bits >> j) & 1u) {
+                            last = j;
+                            run = D1_ADD(run, z[j]);
+                            if (a < 0 && t < run) a = j;
+                        }
                     }
                 }
                 if (a < 0) a = last;
@@ -155,6 +148,20 @@ extern "C" int d1_policy_head_sample(const void *h_bf16, int n, int hidden, cons
     if (blocks > 148 * 8) blocks = 148 * 8;
     head_sample_kernel<<<blocks, WARPS * 32, 0, (cudaStream_t)stream>>>(
         (const __nv_bfloat16 *)h_bf16, n, (const __nv_bfloat16 *)wh_bf16, bh, legal, seed, step, first_env, action,
-        logp, value, logits);
+        logp, value, logits, 0);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int d1_policy_head_greedy(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
+                                     const uint16_t *legal, int64_t *action, float *logp, float *value,
+                                     void *stream) {
+    using namespace d1::head;
+    if (n < 0 || hidden != HID || !h_bf16 || !wh_bf16 || !bh || !action) return D1_ERR_BAD_ARGUMENT;
+    if (n == 0) return 0;
+    int blocks = (n + WARPS * 4 - 1) / (WARPS * 4);
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    head_sample_kernel<<<blocks, WARPS * 32, 0, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16 *)h_bf16, n, (const __nv_bfloat16 *)wh_bf16, bh, legal, 0, 0, 0, action, logp, value,
+        nullptr, 1);
     return (int)cudaGetLastError();
 }

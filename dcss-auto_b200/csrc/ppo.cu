@@ -17,6 +17,74 @@ namespace ppo {
 // delta_t = r_t + gamma * V_{t+1} * (1 - done_t) - V_t, returns = A + V.
 // rewards/dones are read with element strides (they live in the env's
 // outcome rows: reward at out[t, b, 0], done at out[t, b, 1]).
+// Deterministic cross-block sums. Each block reduces its values in a fixed
+// order, writes one partial, and the last block to finish (an integer ticket,
+// whose outcome does not depend on timing) adds the partials in block order.
+// Floating-point atomics would make the sums -- and everything downstream of the
+// advantage normalisation and the gradient-norm clip -- vary from run to run.
+// The partial arrays are fixed in the library: calls on one device are
+// serialised by the caller (one stream per training process).
+constexpr int RED_MAX_BLOCKS = 65536;
+__device__ double g_gae_part[RED_MAX_BLOCKS][2];
+__device__ unsigned g_gae_ticket;
+__device__ double g_sumsq_part[RED_MAX_BLOCKS][2];
+__device__ unsigned g_sumsq_ticket;
+
+// Block-wide ordered sum of (a, b): warp butterflies, then thread 0 over the
+// warps in order. Result valid in thread 0.
+template <int WARPS_>
+__device__ __forceinline__ void block_sum2(double &a, double &b, double (*ws)[2]) {
+    for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(FULL, a, o);
+        b += __shfl_xor_sync(FULL, b, o);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        ws[warp][0] = a;
+        ws[warp][1] = b;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        a = 0.0;
+        b = 0.0;
+        for (int w = 0; w < WARPS_; w++) {
+            a += ws[w][0];
+            b += ws[w][1];
+        }
+    }
+}
+// Thread 0 of every block passes its partial; the last block adds all partials
+// in block order to out[0] (and out[1] when `two`) and resets the ticket.
+__device__ __forceinline__ void finish_sum2(double a, double b, double (*part)[2], unsigned *ticket, double *out,
+                                            bool two) {
+    __shared__ bool last;
+    const int nparts = gridDim.x;
+    if (threadIdx.x == 0) {
+        part[blockIdx.x][0] = a;
+        part[blockIdx.x][1] = b;
+        __threadfence();
+        last = atomicAdd(ticket, 1u) == (unsigned)nparts - 1u;
+    }
+    __syncthreads();
+    if (last && threadIdx.x < 32) {
+        __threadfence();
+        double s1 = 0.0, s2 = 0.0;
+        for (int i = threadIdx.x; i < nparts; i += 32) {
+            s1 += *((volatile double *)&part[i][0]);
+            s2 += *((volatile double *)&part[i][1]);
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            s1 += __shfl_xor_sync(FULL, s1, o);
+            s2 += __shfl_xor_sync(FULL, s2, o);
+        }
+        if (threadIdx.x == 0) {
+            out[0] += s1;
+            if (two) out[1] += s2;
+            *ticket = 0u;
+        }
+    }
+}
+
 struct GaeArgs {
     const float *reward, *done, *value;  // value: [T+1, B]
     int64_t r_step, r_env;               // element strides of reward (and done)
@@ -47,14 +115,9 @@ __global__ void gae_sequential_kernel(GaeArgs a) {
         }
     }
     if (a.stats) {
-        for (int o = 16; o > 0; o >>= 1) {
-            s1 += __shfl_xor_sync(FULL, s1, o);
-            s2 += __shfl_xor_sync(FULL, s2, o);
-        }
-        if ((threadIdx.x & 31) == 0) {
-            atomicAdd(a.stats, s1);
-            atomicAdd(a.stats + 1, s2);
-        }
+        __shared__ double ws[8][2];
+        block_sum2<8>(s1, s2, ws);
+        finish_sum2(s1, s2, g_gae_part, &g_gae_ticket, a.stats, true);
     }
 }
 
@@ -131,14 +194,9 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32) gae_scan_kernel(GaeArgs a) {
         }
     }
     if (a.stats) {
-        for (int o = 16; o > 0; o >>= 1) {
-            s1 += __shfl_xor_sync(FULL, s1, o);
-            s2 += __shfl_xor_sync(FULL, s2, o);
-        }
-        if (lane == 0) {
-            atomicAdd(a.stats, s1);
-            atomicAdd(a.stats + 1, s2);
-        }
+        __shared__ double ws[SCAN_WARPS][2];
+        block_sum2<SCAN_WARPS>(s1, s2, ws);
+        finish_sum2(s1, s2, g_gae_part, &g_gae_ticket, a.stats, true);
     }
 }
 
@@ -591,15 +649,10 @@ __global__ void __launch_bounds__(256) sumsq_kernel(const float *__restrict__ g,
     }
     if (blockIdx.x == 0)
         for (int64_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) s += (double)g[i] * g[i];
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
-    __shared__ double ws[8];
-    if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (int w = 0; w < 8; w++) t += ws[w];
-        atomicAdd(out, t);
-    }
+    __shared__ double ws[8][2];
+    double zero = 0.0;
+    block_sum2<8>(s, zero, ws);
+    finish_sum2(s, 0.0, g_sumsq_part, &g_sumsq_ticket, out, false);
 }
 
 // Adam (torch.optim.Adam semantics) on fp32 masters with the gradient scaled by
@@ -781,6 +834,8 @@ int d1_gae(const float *reward, const float *done, int64_t r_step, int64_t r_env
            float gamma, float lambda, float *adv, float *ret, double *stats, int mode, void *stream) {
     if (T <= 0 || B <= 0 || !reward || !done || !value || !adv || !ret) return D1_ERR_BAD_ARGUMENT;
     ppo::GaeArgs a{reward, done, value, r_step, r_env, adv, ret, stats, T, B, gamma, (float)((double)gamma * lambda)};
+    const int64_t grid = mode == 0 ? (B + 255) / 256 : (B + ppo::SCAN_ENVS - 1) / ppo::SCAN_ENVS;
+    if (stats && grid > ppo::RED_MAX_BLOCKS) return D1_ERR_TOO_LARGE;
     if (mode == 0) {
         ppo::gae_sequential_kernel<<<(B + 255) / 256, 256, 0, (cudaStream_t)stream>>>(a);
     } else {

@@ -48,6 +48,11 @@ SIGNATURES = {
     'd1_conv_layer': [_I, _P, _I, _P, _P, _P, _P],
     'd1_conv_error': [],
     'd1_ar_head_sample': [_P, _I, _P, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P, _P, _P, _P],
+    'd1_ar_head_greedy': [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    'd1_policy_head_greedy': [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
+    'd1_eval_accumulate': [_P, _I, _I, _P, _P, _P, _I, _P],
+    'd1_sample_uniform_legal': [_P, _I, _I, _U64, _U64, _I, _P, _P],
+    'd1_frame_stack': [_P, _P, _I, _I, _I, _P, _I, _P, _P],
 }
 
 _LIB = None

@@ -85,7 +85,7 @@ class Env:
         with torch.cuda.device(self.device):
             self.arrays = device_tables(self.device)
         self.tables = Tables(*(a.data_ptr() for a in self.arrays), self.arrays[1].shape[0])
-        self.state = torch.empty((batch, self.lib.learn_state_bytes()), dtype=torch.uint8, device=self.device)
+        self.state = torch.zeros((batch, self.lib.learn_state_bytes()), dtype=torch.uint8, device=self.device)
         self.obs = torch.empty((batch, self.lib.learn_obs_size()), device=self.device)
         self.mask = torch.empty((batch, self.lib.learn_action_size()), device=self.device)
         self.out = torch.zeros((batch, self.lib.learn_out_size()), device=self.device)

@@ -104,7 +104,7 @@ class SpecEnv:
         assert C.sizeof(self.config) == self.lib.d1_spec_config_bytes()
         with torch.cuda.device(self.device):
             self.rays = device_rays(self.device)
-        self.state = torch.empty((batch, self.lib.d1_spec_state_bytes()), dtype=torch.uint8, device=self.device)
+        self.state = torch.zeros((batch, self.lib.d1_spec_state_bytes()), dtype=torch.uint8, device=self.device)  # row tail is padding
         self.obs = torch.empty((batch, OBS), dtype=torch.bfloat16, device=self.device) if observe else None
         self.legal = torch.empty(batch, dtype=torch.int16, device=self.device)  # u16 bits
         self.out = torch.zeros((batch, OUT), device=self.device)

@@ -166,6 +166,11 @@ int d1_spec_crop(const void *state, int n, int g, uint16_t *crop, void *stream);
 int d1_policy_head_sample(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
                           const uint16_t *legal, uint64_t seed, uint64_t step, int first_env, int64_t *action,
                           float *logp, float *value, float *logits, void *stream);
+/* Greedy variant of the head (the reference's dist.probs.argmax(-1) evaluation
+ * mode, gpu-d1/scripts/train_clear.py:57): action = the first legal action of
+ * maximal logit; logp and value as in d1_policy_head_sample (may be NULL). */
+int d1_policy_head_greedy(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
+                          const uint16_t *legal, int64_t *action, float *logp, float *value, void *stream);
 /* Tensor-core dense layer (tcgen05 + TMA): C = act(A . B^T + bias) [* (mask > 0)] with
  * A bf16[M, K] (row pitch lda), B bf16[N, K] (row pitch ldb), fp32 accumulation,
  * act = ReLU when relu != 0; when mask (bf16 [M, ldm]) is given, entries whose mask
@@ -223,6 +228,32 @@ int d1_ar_head_sample(const float *hb, int n, const float *cond, const float *wt
                       const uint16_t *legal, uint64_t seed, uint64_t step, int first_env, int64_t *joint,
                       int64_t *env_action, float *logp, float *value, float *entropy, float *verb_logits,
                       float *target_logits, void *stream);
+/* Greedy variant (ActionDistribution.greedy, tactical_models.py:22-25): argmax
+ * verb, then the argmax target of a directional verb. */
+int d1_ar_head_greedy(const float *hb, int n, const float *cond, const float *wt, const float *bt,
+                      const uint16_t *legal, int64_t *joint, int64_t *env_action, float *logp, float *value,
+                      void *stream);
+
+/* Evaluation and observation wrappers (reference: gpu-d1/scripts/train_clear.py:42-76,
+ * run_ring_ablations.py:231-267, vision15-centered-map-v1/scripts/frame_stack.py). */
+/* One step of the evaluation bookkeeping for envs with active[i]: returns[i] +=
+ * out[i, 0]; when out[i, 1] > 0 the first tcols outcome columns go to
+ * terminal[i] and active[i] becomes false. out f32 [n, out_cols]. */
+int d1_eval_accumulate(const float *out, int out_cols, int n, bool *active, float *returns, float *terminal,
+                       int tcols, void *stream);
+/* Random baseline: a uniform draw over the set bits 0..nact-1 of legal[i], the
+ * k-th set bit with k = mulhi(word, count), word = Philox word 0 of
+ * (ctr = {lo(step), hi(step), hi(seed), 3}, key = {first_env + i, lo(seed)});
+ * -1 when no bit is set. */
+int d1_sample_uniform_legal(const uint16_t *legal, int nact, int n, uint64_t seed, uint64_t step, int first_env,
+                            int64_t *action, void *stream);
+/* Frame stack of `frames` observations per env, stack [n, frames, row_bytes]
+ * (oldest first), obs [n, row_bytes], row_bytes % 4 == 0. With out == NULL every
+ * frame becomes obs (reset). Otherwise frames shift one slot older and obs is
+ * appended, except that envs whose episode ended (out[i, 1] > 0, and active[i]
+ * when active is given) get obs in every frame. */
+int d1_frame_stack(void *stack, const void *obs, int row_bytes, int frames, int n, const float *out, int out_cols,
+                   const bool *active, void *stream);
 /* Nonzero when a GEMM pipeline wait expired (the kernel then skipped its work
  * and freed its tensor memory); reading clears it. Synchronises the device. */
 int d1_gemm_error(void);
@@ -233,7 +264,10 @@ int d1_gemm_error(void);
  * `stats` (double[2]) is given, sum(adv) and sum(adv^2) are added to it (the
  * advantage-normalisation statistics; all-reduced across ranks by the caller).
  * mode 0 replays the reference's per-step op order exactly; mode 1 is the
- * warp-level segmented scan over time (within 1e-5 relative). */
+ * warp-level segmented scan over time (within 1e-5 relative). The sums are
+ * deterministic (block partials added in block order through a fixed array in
+ * the library, so calls on one device must not overlap); with stats, B is at
+ * most 16,777,216 (mode 0) or 2,097,152 (mode 1), else D1_ERR_TOO_LARGE. */
 int d1_gae(const float *reward, const float *done, int64_t r_step, int64_t r_env, const float *value, int T, int B,
            float gamma, float lambda, float *adv, float *ret, double *stats, int mode, void *stream);
 /* Minibatch gather: x[i] = obs[idx[i]] (bf16 [n, F]) and xt = x^T (bf16 [F, ldt]);
@@ -261,7 +295,8 @@ int d1_sum_rows(const float *parts, int nparts, int stride, int len, float *out,
 int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, void *stream);
 /* out[r] = sum of row r of bf16 m [rows, cols] (pitch ld): bias gradients. */
 int d1_row_sum_bf16(const void *m, int rows, int cols, int ld, float *out, void *stream);
-/* *out += sum g[i]^2 (double). */
+/* *out += sum g[i]^2 (double), deterministic like d1_gae's statistics (calls on
+ * one device must not overlap). */
 int d1_sumsq(const float *g, int64_t n, double *out, void *stream);
 /* A parameter segment whose bf16 compute copy the optimizer refreshes: elements
  * [offset, offset + count) form a [rows, cols] matrix; bf16 receives the same

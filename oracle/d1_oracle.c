@@ -1423,3 +1423,35 @@ int oracle_sample_ar(const float *vl, const float *tl, const uint16_t *legal, in
     }
     return 0;
 }
+
+/* Random baseline (the reference samples the legal mask uniformly,
+ * gpu-d1/scripts/train_clear.py:52-53): the k-th set bit of legal & (2^nact - 1)
+ * with k = floor(word * count / 2^32), word = Philox word 0 of
+ * (ctr = {lo(step), hi(step), hi(seed), 3}, key = {first_env + i, lo(seed)}). */
+int oracle_sample_uniform_legal(const uint16_t *legal, int nact, int n, uint64_t seed, uint64_t step, int first_env,
+                                int64_t *action) {
+    for (int i = 0; i < n; i++) {
+        uint32_t bits = (uint32_t)legal[i] & ((1u << nact) - 1u);
+        int count = 0;
+        for (int j = 0; j < nact; j++) count += (bits >> j) & 1u;
+        if (!count) {
+            action[i] = -1;
+            continue;
+        }
+        uint32_t ctr[4] = {(uint32_t)step, (uint32_t)(step >> 32), (uint32_t)(seed >> 32), 3u};
+        uint32_t key[2] = {(uint32_t)(first_env + i), (uint32_t)seed}, o[4];
+        oracle_philox(ctr, key, o);
+        uint32_t k = (uint32_t)(((uint64_t)o[0] * (uint32_t)count) >> 32);
+        int a = -1;
+        for (int j = 0; j < nact; j++)
+            if ((bits >> j) & 1u) {
+                if (k == 0) {
+                    a = j;
+                    break;
+                }
+                k--;
+            }
+        action[i] = a;
+    }
+    return 0;
+}

@@ -88,6 +88,9 @@ int oracle_spec_planes(const void *states, int n, uint32_t *floor, uint32_t *vie
 int oracle_exp_nonpos(const float *x, int n, float *y);
 int oracle_sample_actions(const float *logits, const uint16_t *legal, int n, uint64_t seed, uint64_t step,
                           int first_env, int64_t *action, float *logp);
+/* Uniform draw over the legal actions (random baseline; see d1_oracle.c). */
+int oracle_sample_uniform_legal(const uint16_t *legal, int nact, int n, uint64_t seed, uint64_t step, int first_env,
+                                int64_t *action);
 /* Conv-policy inputs: 63x63 u16 crops (pitch 64) under D4 element g (see d1_oracle.c). */
 int oracle_spec_crop(const void *states, int n, int g, uint16_t *out);
 /* Autoregressive verb (12) x target (9) sampling: verb_logits [n, 12],

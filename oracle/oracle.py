@@ -259,6 +259,7 @@ def spec_library():
         lib.oracle_spec_planes.argtypes = [p, i, p, p]
         lib.oracle_spec_crop.argtypes = [p, i, i, p]
         lib.oracle_sample_ar.argtypes = [p, p, p, i, C.c_uint64, C.c_uint64, i, p, p, p, p]
+        lib.oracle_sample_uniform_legal.argtypes = [p, i, i, C.c_uint64, C.c_uint64, i, p]
         ex, ey, blk = rays()
         lib._rays_keep = (ex, ey, blk)
         assert lib.oracle_set_rays(ex.ctypes.data, ey.ctypes.data, blk.ctypes.data, len(ex)) == 0
@@ -361,3 +362,12 @@ def sample_ar(verb_logits, target_logits, legal, seed, step, first_env=0):
     lib.oracle_sample_ar(vl.ctypes.data, tl.ctypes.data, legal.ctypes.data, n, seed, step, first_env, j.ctypes.data,
                          a.ctypes.data, lp.ctypes.data, ent.ctypes.data)
     return j, a, lp, ent
+
+
+def sample_uniform_legal(legal, nact, seed, step, first_env=0):
+    """Oracle of the random baseline: int64 actions (-1 where nothing is legal)."""
+    lib = spec_library()
+    legal = np.ascontiguousarray(legal, np.uint16)
+    a = np.empty(legal.shape[0], np.int64)
+    lib.oracle_sample_uniform_legal(legal.ctypes.data, nact, legal.shape[0], seed, step, first_env, a.ctypes.data)
+    return a
