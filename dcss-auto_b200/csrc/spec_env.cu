@@ -1068,6 +1068,44 @@ __global__ void __launch_bounds__(CROP_WARPS * 32) crop_kernel(const uint8_t *st
     }
 }
 
+// ------------------------------------------------------------------ map compiler: LOS table
+// The per-origin LOS masks of a map in the reference's corpus format
+// (gpu-d1/scripts/compile_corpus.py:67-85: 17x17 window, bit (dy+8)*17 + dx+8,
+// 10 x u32 per origin, rays from the native fan) for every one of the 5600
+// cells, one warp per origin with the env step's own ray evaluation. Replaces
+// the reference's per-map Python loop over origins x quadrants x rays.
+constexpr int LOS_WARPS = 4;
+__global__ void __launch_bounds__(LOS_WARPS * 32) los_table_kernel(const uint8_t *floor_u8, RayArgs ra, uint32_t *out) {
+    __shared__ Smem sms[LOS_WARPS];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int origin = blockIdx.x * LOS_WARPS + w;
+    if (blockIdx.x * LOS_WARPS + w >= N) return;  // warp-uniform
+    Smem &s = sms[w];
+    for (int r = lane; r < PL; r += 32) {
+        const int y = r / 3, x0 = (r % 3) * 32;
+        uint32_t bits = 0;
+        for (int b = 0; b < 32 && x0 + b < W; b++) bits |= (floor_u8[y * W + x0 + b] ? 1u : 0u) << b;
+        s.floor[r] = bits;
+    }
+    __syncwarp();
+    Env e;
+    e.lane = lane;
+    e.sm = &s;
+    e.player = origin;
+    compute_los(e, ra);
+    // row dy = lane - 7 (15 bits, dx = -7..7) lands at bit (lane + 1) * 17 + 1
+    const uint32_t row = lane < 15 ? s.vis[lane] : 0u;
+    const int base = (lane + 1) * 17 + 1, w0 = base >> 5, sh = base & 31;
+    const uint32_t c0 = row << sh, c1 = sh ? row >> (32 - sh) : 0u;
+    uint32_t mine = 0;
+#pragma unroll
+    for (int i = 0; i < 10; i++) {
+        const uint32_t v = __reduce_or_sync(FULL, (w0 == i ? c0 : 0u) | (w0 + 1 == i ? c1 : 0u));
+        if (lane == i) mine = v;
+    }
+    if (lane < 10) out[(size_t)origin * 10 + lane] = mine;
+}
+
 __global__ void compact_kernel(const uint8_t *state, int n, int64_t *rows) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n * COMPACT) return;
@@ -1149,6 +1187,14 @@ int d1_spec_init(void *state, int n, const D1SpecConfig *c, uint64_t seed, int f
     if (n == 0) return 0;
     spec::init_kernel<<<(n + spec::WARPS - 1) / spec::WARPS, spec::WARPS * 32, 0, (cudaStream_t)stream>>>(
         (uint8_t *)state, n, *c, g_rays, seed, first_env, (__nv_bfloat16 *)obs_bf16, legal);
+    return (int)cudaGetLastError();
+}
+
+int d1_los_table(const uint8_t *floor, uint32_t *masks, void *stream) {
+    if (!floor || !masks) return D1_ERR_BAD_ARGUMENT;
+    if (!g_rays.ray) return D1_ERR_BAD_ARGUMENT;
+    spec::los_table_kernel<<<(d1::N + spec::LOS_WARPS - 1) / spec::LOS_WARPS, spec::LOS_WARPS * 32, 0,
+                             (cudaStream_t)stream>>>(floor, g_rays, masks);
     return (int)cudaGetLastError();
 }
 

@@ -42,6 +42,7 @@ SIGNATURES = {
     'd1_gemm_error': [],
     'd1_gemm_wgrad_noalloc': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _I, _P],
     'd1_spec_crop': [_P, _I, _I, _P, _P],
+    'd1_los_table': [_P, _P, _P],
     'd1_conv_in_bytes': [_I],
     'd1_conv_weight_bytes': [_I],
     'd1_conv_pack_weights': [_I, _P, _P, _P],

@@ -140,6 +140,11 @@ int d1_spec_step(void *state, int n, const D1SpecConfig *c, const int64_t *actio
 int d1_spec_compact(const void *state, int n, int64_t *rows, void *stream);
 /* Floor and remembered-cell bit planes, u32[n, 210] each (row y = words 3y..3y+2). */
 int d1_spec_planes(const void *state, int n, uint32_t *floor, uint32_t *viewed, void *stream);
+/* Map compiler: the LOS masks of one 80x70 map for all 5600 origins in the
+ * reference's corpus format (gpu-d1/scripts/compile_corpus.py:67-85; 17x17
+ * window, bit (dy+8)*17 + dx+8, 10 x u32 per origin). floor u8[5600] (nonzero =
+ * floor), masks u32[5600, 10]; uses the ray fan of d1_spec_set_rays. */
+int d1_los_table(const uint8_t *floor, uint32_t *masks, void *stream);
 /* Conv-policy input: the egocentric 63x63 crop of each env
  * under D4 element g (0-7), u16 [n, 63, 64] (column 63 zero). Pixel (x, y) shows
  * the map cell at offset d4(g, x - 31, y - 31) from the player, d4 = rotation by
