@@ -241,50 +241,35 @@ def run_ours(args, rank, world, local_rank):
     ms = t.item()
     value = B * world * args.steps / (ms / 1e3)
 
-    # End to end through the public API with host buffers: actions come from
-    # pinned host memory, the outcome rows and next actions go back every step.
-    progress(f'rollout timed: {value / 1e6:.1f} M decisions/s')
+    # End to end through the public API with host buffers: every step copies the
+    # actions in from pinned host memory, steps the env, runs the policy and
+    # copies the outcome rows and the next actions back (d1.rollout.DecisionGraph:
+    # the decision is one captured CUDA graph, replayed and synchronised per step).
     e2e = None
     if not args.no_e2e:
-        h_act = torch.zeros(B, dtype=torch.int64).pin_memory()
-        h_out = torch.empty((B, env.out.shape[1])).pin_memory()
-        h_next = torch.empty(B, dtype=torch.int64).pin_memory()
-        d_act = torch.empty(B, dtype=torch.int64, device=dev)
-        obs, legal = env.obs, env.legal
-        logp = torch.empty(B, device=dev)
-        val = torch.empty(B, device=dev)
-        nxt = torch.empty(B, dtype=torch.int64, device=dev)
+        from d1.rollout import DecisionGraph
         env.reset(2)
-        e2e_steps = max(8, args.steps // 4)
+        dg = DecisionGraph(env, policy, seed=3, first_env=rank * B, step=0)
         for k in range(3):
-            d_act.copy_(h_act, non_blocking=True)
-            env.step(d_act)
-            policy.act(obs, legal, 3, k, rank * B, action=nxt, logp=logp, value=val)
-            h_out.copy_(env.out, non_blocking=True)
-            h_next.copy_(nxt, non_blocking=True)
+            dg.replay()
             torch.cuda.synchronize()
-            h_act.copy_(h_next)
+            dg.h_act.copy_(dg.h_next)
+        e2e_steps = max(8, args.steps // 4)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for k in range(e2e_steps):
-            d_act.copy_(h_act, non_blocking=True)
-            env.step(d_act)
-            policy.act(obs, legal, 3, 100 + k, rank * B, action=nxt, logp=logp, value=val)
-            h_out.copy_(env.out, non_blocking=True)
-            h_next.copy_(nxt, non_blocking=True)
+            dg.replay()
             torch.cuda.synchronize()
-            h_act.copy_(h_next)
+            dg.h_act.copy_(dg.h_next)
         e2e_s = torch.tensor([time.perf_counter() - t0], device=dev)
         if world > 1:
             dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
         e2e = {'value': B * world * e2e_steps / e2e_s.item(), 'unit': UNIT,
                'h2d_bytes_per_step': B * 8, 'd2h_bytes_per_step': B * (env.out.shape[1] * 4 + 8),
-               'steps': e2e_steps}
-
-    # Tensor-core layer alone (policy layer 1, M = envs, N = 256, K = 1832), timed
-    # with events on its launching stream after the rollout measurement.
+               'steps': e2e_steps, 'path': 'd1.rollout.DecisionGraph (captured decision, host copies inside)'}
+        del dg
     progress('e2e done')
     from d1 import gemm as G
     x = roll.obs[0]

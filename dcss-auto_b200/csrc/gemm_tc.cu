@@ -25,6 +25,7 @@
 #include <stdint.h>
 
 #include "../../include/d1.h"
+#include "d1_sampler.cuh"
 
 
 namespace d1 {
@@ -34,6 +35,10 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, EPI_WARPS = 8, THREADS = 
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int BIAS_BYTES = EPI_WARPS * (BN / 2) * 4;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + BIAS_BYTES;
+// Fused policy head (N = 256 in one tile): head weights fp32 [13][256] and the
+// per-row partial dot products of the two column halves [2][128][13].
+constexpr int HEAD_OUT = 13, HEAD_W_BYTES = HEAD_OUT * BN * 4, HEAD_PART_BYTES = 2 * BM * HEAD_OUT * 4;
+constexpr int SMEM_HEAD_BYTES = SMEM_BYTES + HEAD_W_BYTES + HEAD_PART_BYTES + 16;  // + abort flag
 constexpr int SM_COUNT = 148;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
@@ -53,6 +58,16 @@ struct Params {
     int ldct;
     float *cf;           // fp32 row-major [splits][M, ldcf] (may be null)
     int ldcf;
+    // fused head + sampler (head != 0): logits/value = bf16(C) . Wh^T + bh, then
+    // the masked draw of d1_sampler.cuh
+    int head;
+    const __nv_bfloat16 *head_w;  // [13, 256]
+    const float *head_b;          // [13]
+    const uint16_t *legal;        // [M] (null: all 12 legal)
+    uint64_t seed, step;
+    int first_env;
+    int64_t *action;              // [M] (null: value only)
+    float *logp, *value, *logits; // [M], [M], [M, 12] (each may be null)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -132,6 +147,7 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 // ... (tile -> (m block, n block, K split)). The TMA ring runs continuously
 // across tile boundaries and the accumulator is double-buffered in TMEM
 // (2 x 256 columns), so the epilogue of one tile overlaps the MMAs of the next.
+template <bool HEAD>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p,
                 int tiles_m, int tiles_n, int tiles_total) {
@@ -229,6 +245,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         // and column half (w - 2) / 4 of the accumulator.
         const int q = warp & 3, half = (warp - 2) >> 2;
         float *bias_s = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES + 256) + (warp - 2) * (BN / 2);
+        float *head_w = reinterpret_cast<float *>(smem + SMEM_BYTES - 1024);  // [13][256] (head mode)
+        float *head_part = head_w + HEAD_OUT * BN;                             // [2][128][13]
+        volatile int *head_abort = reinterpret_cast<volatile int *>(head_part + 2 * BM * HEAD_OUT);
+        if constexpr (HEAD) {
+            for (int i = threadIdx.x - 64; i < HEAD_OUT * BN; i += EPI_WARPS * 32)
+                head_w[i] = __bfloat162float(p.head_w[i]);
+            if (threadIdx.x == 64) *head_abort = 0;
+            asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+        }
         int local = 0;
         for (int t = blockIdx.x; t < tiles_total; t += gridDim.x, local++) {
             const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
@@ -242,13 +267,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 bias_s[lane * 4 + j] = (p.bias && col < p.N) ? __ldg(p.bias + col) : 0.f;
             }
             __syncwarp();
-            if (!mbar_wait(accf0 + 8 * b, (uint32_t)(local >> 1) & 1u)) {
+            const bool waited = mbar_wait(accf0 + 8 * b, (uint32_t)(local >> 1) & 1u);
+            if (!waited) {
                 atomicExch(&g_error, 3);
-                break;
+                if constexpr (!HEAD) break;
+                *head_abort = 1;  // every epilogue warp leaves after this tile's barriers
             }
             fence_after();
+            float hacc[HEAD ? HEAD_OUT : 1];
+#pragma unroll
+            for (int j = 0; j < (HEAD ? HEAD_OUT : 1); j++) hacc[j] = 0.f;
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 64; cc++) {
+            for (int cc = 0; cc < BN / 64 && waited; cc++) {
                 uint32_t v[32];
                 const uint32_t taddr = tmem + (uint32_t)(b * TMEM_COLS) + ((uint32_t)(q * 32) << 16) +
                                        (uint32_t)(half * (BN / 2) + cc * 32);
@@ -270,6 +300,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (p.relu) {
 #pragma unroll
                     for (int j = 0; j < 32; j++) f[j] = fmaxf(f[j], 0.f);
+                }
+                if constexpr (HEAD) {
+                    // the head sees the activation as stored (bf16), like the unfused path
+                    const float *wcol = head_w + col0;
+#pragma unroll 4
+                    for (int i = 0; i < 32; i++) {
+                        const float x = __bfloat162float(__float2bfloat16_rn(f[i]));
+#pragma unroll
+                        for (int j = 0; j < HEAD_OUT; j++) hacc[j] = fmaf(x, wcol[j * BN + i], hacc[j]);
+                    }
                 }
                 if (p.mask) {
                     const __nv_bfloat16 *mk = p.mask + (size_t)row * p.ldm + col0;
@@ -333,6 +373,36 @@ __global__ void __launch_bounds__(THREADS, 1)
             fence_before();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce0 + 8 * b) : "memory");
+            if constexpr (HEAD) {
+                // combine the two column halves, then one thread per row draws
+                const int r = q * 32 + lane;
+#pragma unroll
+                for (int j = 0; j < HEAD_OUT; j++) head_part[(half * BM + r) * HEAD_OUT + j] = hacc[j];
+                asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+                const bool abort = *head_abort != 0;
+                const int grow = mt * BM + r;
+                if (half == 0 && !abort && grow < p.M) {
+                    float l[HEAD_OUT];
+#pragma unroll
+                    for (int j = 0; j < HEAD_OUT; j++)
+                        l[j] = head_part[r * HEAD_OUT + j] + head_part[(BM + r) * HEAD_OUT + j] + __ldg(p.head_b + j);
+                    if (p.value) p.value[grow] = l[12];
+                    if (p.logits) {
+#pragma unroll
+                        for (int j = 0; j < 12; j++) p.logits[(size_t)grow * 12 + j] = l[j];
+                    }
+                    if (p.action) {
+                        int a;
+                        float lp;
+                        sample_masked(l, p.legal ? (uint32_t)p.legal[grow] : 0xfffu, (uint32_t)(p.first_env + grow),
+                                      p.seed, p.step, false, a, lp);
+                        p.action[grow] = a;
+                        if (p.logp) p.logp[grow] = lp;
+                    }
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+                if (abort) break;
+            }
         }
     }
     fence_before();
@@ -379,6 +449,22 @@ static bool make_map(CUtensorMap *m, const void *base, int rows, int cols, int l
 
 using namespace d1::tc;
 
+// Dynamic shared memory above 48 KB, opted into once per device (the head
+// variant's larger figure covers both).
+static int gemm_attr() {
+    static uint64_t ready = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 64 && ((ready >> dev) & 1)) return 0;
+    e = cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_HEAD_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 64) ready |= 1ull << dev;
+    return 0;
+}
+
 extern "C" {
 
 int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
@@ -400,12 +486,7 @@ int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K,
     splits = (kt + per - 1) / per;  // every split gets at least one K block
     CUtensorMap ma, mb;
     if (!make_map(&ma, a, M, K, lda, BM) || !make_map(&mb, b, N, K, ldb, BN)) return D1_ERR_BAD_ARGUMENT;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return (int)e;
-        attr = true;
-    }
+    if (int e = gemm_attr()) return e;
     Params p{M, N, K, per, kt, bias, relu, (const __nv_bfloat16 *)mask, ldm, (__nv_bfloat16 *)c, ldc,
              (__nv_bfloat16 *)ct, ldct, cf, ldcf};
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
@@ -417,7 +498,29 @@ int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K,
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = SM_COUNT;
     }
     const int grid = tiles < sms ? tiles : sms;
-    gemm_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, p, tiles_m, tiles_n, tiles);
+    gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, p, tiles_m, tiles_n, tiles);
+    return (int)cudaGetLastError();
+}
+
+int d1_gemm_head_sample(const void *a, int lda, const void *b, int ldb, int M, int K, const float *bias,
+                        const void *wh_bf16, const float *bh, const uint16_t *legal, uint64_t seed, uint64_t step,
+                        int first_env, int64_t *action, float *logp, float *value, float *logits, void *stream) {
+    if (M <= 0 || K <= 0 || !a || !b || !wh_bf16 || !bh) return D1_ERR_BAD_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) || (lda * 2) % 16 ||
+        (ldb * 2) % 16 || lda < K || ldb < K)
+        return D1_ERR_BAD_ARGUMENT;
+    const int kt = (K + BK - 1) / BK;
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, a, M, K, lda, BM) || !make_map(&mb, b, BN, K, ldb, BN)) return D1_ERR_BAD_ARGUMENT;
+    if (int e = gemm_attr()) return e;
+    Params p{M, BN, K, kt, kt, bias, 1, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0,
+             1, (const __nv_bfloat16 *)wh_bf16, bh, legal, seed, step, first_env, action, logp, value, logits};
+    const int tiles = (M + BM - 1) / BM;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = SM_COUNT;
+    const int grid = tiles < sms ? tiles : sms;
+    gemm_kernel<true><<<grid, THREADS, SMEM_HEAD_BYTES, (cudaStream_t)stream>>>(ma, mb, p, tiles, 1, tiles);
     return (int)cudaGetLastError();
 }
 

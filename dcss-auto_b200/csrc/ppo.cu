@@ -841,7 +841,9 @@ int d1_gae(const float *reward, const float *done, int64_t r_step, int64_t r_env
     } else {
         const size_t sm = (size_t)3 * T * ppo::SCAN_ENVS * sizeof(float);
         if (sm > 200 * 1024) return D1_ERR_BAD_ARGUMENT;
-        if (sm > 48 * 1024) {
+        // the kernel also holds a little static shared memory, so opt in to the
+        // dynamic size whenever it is near the 48 KB default
+        if (sm > 40 * 1024) {
             cudaError_t e = cudaFuncSetAttribute(ppo::gae_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)sm);
             if (e != cudaSuccess) return (int)e;

@@ -39,6 +39,7 @@ SIGNATURES = {
     'd1_adam': [_P, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _P, _P, _I, _P],
     'd1_counter_add': [_P, C.c_int64, _P],
     'd1_gemm_splits': [_I, _I],
+    'd1_gemm_head_sample': [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],
     'd1_gemm_error': [],
     'd1_gemm_wgrad_noalloc': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _I, _P],
     'd1_spec_crop': [_P, _I, _I, _P, _P],
@@ -51,6 +52,7 @@ SIGNATURES = {
     'd1_ar_head_sample': [_P, _I, _P, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P, _P, _P, _P],
     'd1_ar_head_greedy': [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     'd1_policy_head_greedy': [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
+    'd1_policy_head_sample_dev': [_P, _I, _I, _P, _P, _P, _U64, _P, _I, _P, _P, _P, _P, _P],
     'd1_eval_accumulate': [_P, _I, _I, _P, _P, _P, _I, _P],
     'd1_sample_uniform_legal': [_P, _I, _I, _U64, _U64, _I, _P, _P],
     'd1_frame_stack': [_P, _P, _I, _I, _I, _P, _I, _P, _P],

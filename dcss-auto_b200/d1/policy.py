@@ -69,8 +69,18 @@ class Policy:
         return h1, h2
 
     def head(self, h2, legal, seed, step, first_env, action, logp, value, logits=None):
+        """`step` is an int, or an int64 device tensor of one element read when
+        the kernel runs (for CUDA graphs that advance it themselves)."""
         stream = torch.cuda.current_stream(self.device).cuda_stream
         n = h2.shape[0]
+        if isinstance(step, torch.Tensor):
+            check(self.lib.d1_policy_head_sample_dev(
+                h2.data_ptr(), n, self.hidden, self.bf16['wh'].data_ptr(), self.params['bh'].data_ptr(),
+                None if legal is None else legal.data_ptr(), seed, step.data_ptr(), first_env,
+                None if action is None else action.data_ptr(), None if logp is None else logp.data_ptr(),
+                None if value is None else value.data_ptr(), None if logits is None else logits.data_ptr(), stream),
+                'd1_policy_head_sample_dev')
+            return
         check(self.lib.d1_policy_head_sample(h2.data_ptr(), n, self.hidden, self.bf16['wh'].data_ptr(),
                                              self.params['bh'].data_ptr(),
                                              None if legal is None else legal.data_ptr(), seed, step, first_env,
@@ -80,10 +90,26 @@ class Policy:
                                              None if logits is None else logits.data_ptr(), stream),
               'd1_policy_head_sample')
 
+    def _h1(self, obs):
+        h1 = self._h1_buffer(obs.shape[0])
+        gemm.gemm(obs, self.bf16['w1'], bias=self.params['b1'], relu=True, out=h1)
+        return h1
+
+    def fused_head(self, h1, legal, seed, step, first_env, action, logp, value, logits=None):
+        """Layer 2 with the head and sampler in its epilogue (h2 is never stored)."""
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        ptr = lambda t: None if t is None else t.data_ptr()
+        check(self.lib.d1_gemm_head_sample(h1.data_ptr(), h1.stride(0), self.bf16['w2'].data_ptr(), self.hidden,
+                                           h1.shape[0], self.hidden, self.params['b2'].data_ptr(),
+                                           self.bf16['wh'].data_ptr(), self.params['bh'].data_ptr(), ptr(legal),
+                                           seed, step, first_env, ptr(action), ptr(logp), ptr(value), ptr(logits),
+                                           stream), 'd1_gemm_head_sample')
+
     def act(self, obs, legal, seed, step, first_env=0, action=None, logp=None, value=None, logits=None):
-        """Forward + sample. Writes into the given buffers (allocated if None)."""
+        """Forward + sample: two tcgen05 GEMMs, then the head + sampler kernel.
+        Writes into the given buffers (allocated if None)."""
         n = obs.shape[0]
-        _, h2 = self.hidden_layers(obs)
+        _, h2 = self.hidden_layers(obs, h1=self._h1_buffer(n), h2=self._h2_buffer(n))
         if action is None:
             action = torch.empty(n, dtype=torch.int64, device=self.device)
         if logp is None:
@@ -93,9 +119,34 @@ class Policy:
         self.head(h2, legal, seed, step, first_env, action, logp, value, logits)
         return action, logp, value
 
+    def act_fused(self, obs, legal, seed, step, first_env=0, action=None, logp=None, value=None, logits=None):
+        """The same draw with layer 2, the head and the sampler in one GEMM
+        (d1_gemm_head_sample). Measured slower than act() on B200 at 65,536
+        rows: the 13 x 256 head FMAs per row then run on the GEMM's 8 epilogue
+        warps only."""
+        n = obs.shape[0]
+        if action is None:
+            action = torch.empty(n, dtype=torch.int64, device=self.device)
+        if logp is None:
+            logp = torch.empty(n, device=self.device)
+        if value is None:
+            value = torch.empty(n, device=self.device)
+        self.fused_head(self._h1(obs), legal, seed, step, first_env, action, logp, value, logits)
+        return action, logp, value
+
+    def _h2_buffer(self, n):
+        if getattr(self, '_h2_buf', None) is None or self._h2_buf.shape[0] < n:
+            self._h2_buf = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=self.device)
+        return self._h2_buf[:n]
+
+    def _h1_buffer(self, n):
+        if getattr(self, '_h1_buf', None) is None or self._h1_buf.shape[0] < n:
+            self._h1_buf = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=self.device)
+        return self._h1_buf[:n]
+
     def value(self, obs, out=None):
         n = obs.shape[0]
-        _, h2 = self.hidden_layers(obs)
+        _, h2 = self.hidden_layers(obs, h1=self._h1_buffer(n), h2=self._h2_buffer(n))
         value = torch.empty(n, device=self.device) if out is None else out
         self.head(h2, None, 0, 0, 0, None, None, value)
         return value

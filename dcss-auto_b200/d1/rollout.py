@@ -51,3 +51,50 @@ class Rollout:
     @property
     def dones(self):
         return self.out[:, :, 1]
+
+
+class DecisionGraph:
+    """One decision of a host-driven loop captured once as a CUDA graph:
+    copy the actions in from pinned host memory, step the env, run the policy on
+    the new observation (two GEMMs + head + masked draw) and copy the outcome
+    rows and the next actions back to pinned host memory. The sampling step is a
+    device counter that the graph advances, so every replay draws fresh
+    uniforms. replay() launches it; the caller synchronises before reading the
+    host buffers."""
+
+    def __init__(self, env, policy, seed, first_env=0, step=0):
+        import torch
+        from ._lib import check, library
+        dev, n = env.device, env.batch
+        self.env, self.policy = env, policy
+        self.h_act = torch.zeros(n, dtype=torch.int64).pin_memory()
+        self.h_out = torch.empty((n, env.out.shape[1])).pin_memory()
+        self.h_next = torch.empty(n, dtype=torch.int64).pin_memory()
+        self.d_act = torch.empty(n, dtype=torch.int64, device=dev)
+        self.next = torch.empty(n, dtype=torch.int64, device=dev)
+        self.logp = torch.empty(n, device=dev)
+        self.value = torch.empty(n, device=dev)
+        self.step = torch.full((1,), step, dtype=torch.int64, device=dev)
+        lib = library()
+
+        def body():
+            s = torch.cuda.current_stream(dev).cuda_stream
+            self.d_act.copy_(self.h_act, non_blocking=True)
+            env.step(self.d_act)
+            policy.act(env.obs, env.legal, seed, self.step, first_env, action=self.next, logp=self.logp,
+                       value=self.value)
+            check(lib.d1_counter_add(self.step.data_ptr(), 1, s), 'd1_counter_add')
+            self.h_out.copy_(env.out, non_blocking=True)
+            self.h_next.copy_(self.next, non_blocking=True)
+
+        body()  # warm-up: kernel attributes and workspaces exist before capture
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.cuda.graph(self.graph, stream=side):
+            body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+
+    def replay(self):
+        self.graph.replay()

@@ -171,6 +171,12 @@ int d1_spec_crop(const void *state, int n, int g, uint16_t *crop, void *stream);
 int d1_policy_head_sample(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
                           const uint16_t *legal, uint64_t seed, uint64_t step, int first_env, int64_t *action,
                           float *logp, float *value, float *logits, void *stream);
+/* As d1_policy_head_sample with the step read from device memory (*step_dev)
+ * when the kernel runs, so a captured CUDA graph that also advances the counter
+ * (d1_counter_add) draws fresh uniforms on every replay. */
+int d1_policy_head_sample_dev(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
+                              const uint16_t *legal, uint64_t seed, const int64_t *step_dev, int first_env,
+                              int64_t *action, float *logp, float *value, float *logits, void *stream);
 /* Greedy variant of the head (the reference's dist.probs.argmax(-1) evaluation
  * mode, gpu-d1/scripts/train_clear.py:57): action = the first legal action of
  * maximal logit; logp and value as in d1_policy_head_sample (may be NULL). */
@@ -189,6 +195,14 @@ int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K,
             const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits,
             void *stream);
 int d1_gemm_splits(int K, int splits);
+/* The policy's second layer with the head and sampler fused into the GEMM
+ * epilogue: h = ReLU(A . B^T + bias) with N = 256 (B bf16 [256, K]), never
+ * stored; logits/value = bf16(h) . wh^T + bh (wh bf16 [13, 256], bh f32 [13]);
+ * then the draw of d1_policy_head_sample (same stream keys and arithmetic).
+ * Any of action/logp/value/logits may be NULL (value-only for bootstrapping). */
+int d1_gemm_head_sample(const void *a, int lda, const void *b, int ldb, int M, int K, const float *bias,
+                        const void *wh_bf16, const float *bh, const uint16_t *legal, uint64_t seed, uint64_t step,
+                        int first_env, int64_t *action, float *logp, float *value, float *logits, void *stream);
 /* No counterpart in the reference. The split-K weight-gradient product
  * out = A . B^T (fp32 [M, ldo], A bf16 [M, K], B bf16 [N, K], same operand rules as
  * d1_gemm) for callers that cannot allocate device memory (a host framework that

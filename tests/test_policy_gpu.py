@@ -66,3 +66,63 @@ def test_sampling_frequencies_follow_the_softmax(lib):
                                                           device='cuda'), -1e9), -1).double().cpu()
     assert counts[2] == 0 and counts[10] == 0
     assert torch.allclose(counts, p, atol=4e-3)
+
+
+@pytest.mark.parametrize('n', [65536, 1000])
+def test_fused_layer2_head_matches_the_unfused_path_and_the_oracle(lib, n):
+    """d1_gemm_head_sample (layer 2 + head + sampler in the GEMM epilogue): logits
+    and value against the separate GEMM + head kernel (same bf16 activations,
+    another summation order: 1e-5), draws against the oracle given its logits
+    (exact), and the same action as the unfused path for nearly every row."""
+    from d1.policy import Policy
+    from d1.spec_env import SpecEnv
+    env = SpecEnv(n, seed=2)
+    pol = Policy(seed=3)
+    out = {}
+    for name, fn in (('fused', pol.act_fused), ('unfused', pol.act)):
+        lg = torch.empty((n, 12), device='cuda')
+        a, lp, v = fn(env.obs, env.legal, 11, 5, 7, logits=lg)
+        out[name] = (a.clone(), lp.clone(), v.clone(), lg)
+    torch.cuda.synchronize()
+    fa, flp, fv, flg = out['fused']
+    ua, ulp, uv, ulg = out['unfused']
+    assert torch.allclose(flg, ulg, rtol=1e-5, atol=1e-5)
+    assert torch.allclose(fv, uv, rtol=1e-5, atol=1e-5)
+    legal = env.legal.cpu().numpy().view(np.uint16)
+    ora, olp = oracle.sample_actions(flg.cpu().numpy(), legal, 11, 5, 7)
+    assert np.array_equal(fa.cpu().numpy(), ora)
+    assert np.allclose(flp.cpu().numpy(), olp, rtol=1e-5, atol=1e-5)
+    assert (fa == ua).float().mean().item() > 0.999
+    vals = torch.empty(n, device='cuda')
+    pol.value(env.obs, out=vals)
+    assert torch.equal(vals, uv)
+    from d1 import gemm
+    assert gemm.gemm_error() == 0
+
+
+def test_decision_graph_replays_the_eager_loop(lib):
+    """DecisionGraph (one captured decision with host copies and a device step
+    counter) reproduces the eager host-driven loop exactly."""
+    from d1.policy import Policy
+    from d1.rollout import DecisionGraph
+    from d1.spec_env import SpecEnv
+    n = 4096
+    pol = Policy(seed=4)
+    eager, graphed = SpecEnv(n, seed=6), SpecEnv(n, seed=6)
+    dg = DecisionGraph(graphed, pol, seed=9, step=0)
+    # DecisionGraph ran one warm-up decision with zero actions and step 0
+    act = torch.zeros(n, dtype=torch.int64, device='cuda')
+    eager.step(act)
+    a, _, _ = pol.act(eager.obs, eager.legal, 9, 0)
+    dg.h_act.copy_(dg.h_next)
+    act = a.clone()
+    for k in range(1, 4):
+        dg.replay()
+        torch.cuda.synchronize()
+        eager.step(act)
+        a, _, _ = pol.act(eager.obs, eager.legal, 9, k)
+        torch.cuda.synchronize()
+        assert torch.equal(dg.h_out, eager.out.cpu()), k
+        assert torch.equal(dg.h_next, a.cpu()), k
+        dg.h_act.copy_(dg.h_next)
+        act = a.clone()

@@ -185,3 +185,15 @@ def test_full_iteration_runs_and_learns_something(mods):
     assert gemm.gemm_error() == 0
     assert torch.isfinite(pol.flat).all()
     assert not torch.equal(pol.flat, start)
+
+
+def test_gae_scan_at_the_bench_horizon(mods):
+    """T = 128: the scan stages 48 KB of shared memory."""
+    pol, roll, tr = small_setup(mods, B=1024, T=128, mb=4096, seed=9)
+    rew, done = roll.out[:, :, 0], roll.out[:, :, 1]
+    ref_adv, _ = torch_gae(rew, done, roll.values, tr.gamma, tr.lam)
+    tr.gae_mode = 1
+    adv, _ = tr.advantages()
+    assert (adv - ref_adv).abs().max().item() <= 1e-5 * max(ref_adv.abs().max().item(), 1.0)
+    s1 = tr.stats[0].item()
+    assert abs(s1 - ref_adv.double().sum().item()) <= 1e-4 * max(1.0, abs(s1))
