@@ -303,10 +303,6 @@ __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__rest
 // and its gradient with respect to logits/value, then dh2 = dhead . Wh masked by
 // ReLU'(h2) (bf16, row-major and transposed). Block partials of dWh, dbh, db2
 // and of the loss terms go to `part` for a deterministic reduction.
-//
-// A warp owns four rows at a time: lanes split the 256 hidden units for the 13
-// dot products and the dh2 row; lanes 0-11 then each own one action for the
-// softmax, entropy and logit gradient (warp shuffles do the reductions).
 struct LossArgs {
     const __nv_bfloat16 *h2;   // [n, 256]
     const __nv_bfloat16 *wh;   // [13, 256]
@@ -323,54 +319,94 @@ struct LossArgs {
     int ldt;
     float *part;               // per block: dWh[13*256], dbh[13], db2[256], terms[8]
 };
-constexpr int L_ROWS = 32, L_HID = 256, L_NOUT = 13, L_NACT = 12;
+constexpr int L_HID = 256, L_NOUT = 13, L_NACT = 12;
 constexpr int L_PART = L_NOUT * L_HID + L_NOUT + L_HID + 8;
 
-struct LossSmem {
-    float w_s[L_NOUT][L_HID];
-    float hs[L_ROWS][L_HID + 4];  // h2 rows (fp32)
-    float gs[L_ROWS][L_HID + 4];  // dh2 rows (fp32, masked)
-    float dh_s[L_ROWS][16];       // dlogits[12], dvalue, 0, 0, 0
-    float accw[L_NOUT][L_HID];    // dWh column accumulators between row batches
-    float terms_s[8][8];
-    // the batch's per-row rollout values, fetched in one round of parallel loads
-    float r_olp[L_ROWS], r_adv[L_ROWS], r_ret[L_ROWS], r_vold[L_ROWS];
-    int r_bits[L_ROWS], r_act[L_ROWS];
+// ------------------------------------------------------------------ loss on warp-level tensor-core MMAs
+// Its three small products run on mma.sync.m16n8k16 (bf16 in, fp32 accumulate):
+//   logits [16 rows x 16]   = h2 [16 x 256] . Wh^T          (per warp, 16 k-steps)
+//   dWh    [16 x 256]      += dhead^T [16 x 64 rows] . h2    (warp w: columns 64w..)
+//   dh2    [16 rows x 256]  = dhead [16 x 16] . Wh           (per warp, 32 n-tiles)
+// The head gradient dhead (fp32) enters the MMAs as two bf16 parts, hi + lo,
+// so its ~16-bit precision survives. The softmax, loss and dhead are computed
+// on the accumulator layout: lane (g, q) holds rows g and g + 8, columns
+// 2q, 2q+1, 2q+8, 2q+9; row statistics are quad shuffles. A block (4 warps)
+// takes 64 rows per pass; dh2 overwrites the staged h2 tile in place (masked by
+// h2 > 0) and leaves as row-major and transposed 16-byte stores.
+constexpr int M_ROWS = 64, M_WARPS = 4, M_PITCH = L_HID + 8, D_PITCH = 24;
+struct MmaSmem {
+    __nv_bfloat16 h2[M_ROWS][M_PITCH];     // h2 tile, then dh2
+    __nv_bfloat16 wh[16][M_PITCH];         // head weights, rows 13-15 zero
+    __nv_bfloat16 dhi[M_ROWS][D_PITCH];    // dhead, bf16 high part
+    __nv_bfloat16 dlo[M_ROWS][D_PITCH];    // dhead, bf16 remainder
+    float dhf[M_ROWS][16];                 // dhead fp32 (for dbh)
+    float r_olp[M_ROWS], r_adv[M_ROWS], r_ret[M_ROWS], r_vold[M_ROWS];
+    int r_bits[M_ROWS], r_act[M_ROWS];
+    float terms[M_WARPS][8];
 };
 
-__device__ __forceinline__ float group16_max(float v) {
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
-    return v;
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
 }
-__device__ __forceinline__ float group16_sum(float v) {
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
-    return v;
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
 }
+__device__ __forceinline__ void mma16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ float quad_max(float v) {
+    v = fmaxf(v, __shfl_xor_sync(FULL, v, 1));
+    return fmaxf(v, __shfl_xor_sync(FULL, v, 2));
+}
+__device__ __forceinline__ float quad_sum(float v) {
+    v += __shfl_xor_sync(FULL, v, 1);
+    return v + __shfl_xor_sync(FULL, v, 2);
+}
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__global__ void __launch_bounds__(256, 2) loss_kernel(LossArgs a) {
-    extern __shared__ __align__(16) uint8_t loss_raw[];
-    LossSmem &S = *reinterpret_cast<LossSmem *>(loss_raw);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < L_NOUT * L_HID; i += 256) S.w_s[i / L_HID][i % L_HID] = __bfloat162float(a.wh[i]);
+__global__ void __launch_bounds__(M_WARPS * 32) loss_mma_kernel(LossArgs a) {
+    extern __shared__ __align__(16) uint8_t mma_raw[];
+    MmaSmem &S = *reinterpret_cast<MmaSmem *>(mma_raw);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, q = lane & 3;
+    for (int i = tid; i < 16 * (L_HID / 8); i += blockDim.x) {
+        const int j = i / (L_HID / 8), c = (i % (L_HID / 8)) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (j < L_NOUT) v = *reinterpret_cast<const uint4 *>(a.wh + j * L_HID + c);
+        *reinterpret_cast<uint4 *>(&S.wh[j][c]) = v;
+    }
     const double mean = a.adv_stats[0] / a.adv_count;
     const double var = (a.adv_stats[1] - a.adv_stats[0] * mean) / (a.adv_count - 1.0);
     const float amean = (float)mean, astd = (float)sqrt(var > 0 ? var : 0.0);
     const float inv_n = 1.f / (float)a.n;
-    float bh_l = 0.f;  // this lane's action bias (lanes 0-11), value bias on all lanes
-    for (int j = 0; j < L_NACT; j++)
-        if (lane == j) bh_l = a.bh[j];
-    const float bh_v = a.bh[L_NACT];
+    // this lane's four head columns and their biases
+    int col[4];
+    float bias[4];
 #pragma unroll
-    for (int j = 0; j < L_NOUT; j++) S.accw[j][tid] = 0.f;
-    float acc_b2 = 0.f, acc_bh = 0.f;
+    for (int e = 0; e < 4; e++) {
+        col[e] = (e < 2 ? 0 : 8) + 2 * q + (e & 1);
+        bias[e] = col[e] < L_NOUT ? a.bh[col[e]] : 0.f;
+    }
+    float acc_w[8][4];  // dWh for columns 64*warp + 8*nt .. (rows j = g, g + 8)
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc_w[nt][e] = 0.f;
+    float acc_b2[2] = {0.f, 0.f}, acc_bh = 0.f;
     float t_pg = 0.f, t_vf = 0.f, t_ent = 0.f, t_clip = 0.f, t_kl = 0.f;
-    __syncthreads();
-    const int nb = (a.n + L_ROWS - 1) / L_ROWS;
+    const int nb = (a.n + M_ROWS - 1) / M_ROWS;
     for (int blk = blockIdx.x; blk < nb; blk += gridDim.x) {
-        const int r0 = blk * L_ROWS;
-        if (tid < L_ROWS && r0 + tid < a.n) {
+        const int r0 = blk * M_ROWS;
+        __syncthreads();  // the previous pass's readers are done
+        if (tid < M_ROWS && r0 + tid < a.n) {
             const int64_t sidx = a.idx[r0 + tid];
             S.r_bits[tid] = a.legal[sidx];
             S.r_act[tid] = (int)a.action[sidx];
@@ -379,67 +415,84 @@ __global__ void __launch_bounds__(256, 2) loss_kernel(LossArgs a) {
             S.r_ret[tid] = a.ret[sidx];
             S.r_vold[tid] = a.old_value[sidx];
         }
-        for (int i = tid; i < L_ROWS * (L_HID / 8); i += 256) {
+        for (int i = tid; i < M_ROWS * (L_HID / 8); i += blockDim.x) {
             const int r = i / (L_HID / 8), c = (i % (L_HID / 8)) * 8;
-            float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            if (r0 + r < a.n) {
-                const uint4 raw = *reinterpret_cast<const uint4 *>(a.h2 + (size_t)(r0 + r) * L_HID + c);
-                const __nv_bfloat162 *p2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const float2 ff = __bfloat1622float2(p2[j]);
-                    f[2 * j] = ff.x;
-                    f[2 * j + 1] = ff.y;
-                }
-            }
-            *reinterpret_cast<float4 *>(&S.hs[r][c]) = make_float4(f[0], f[1], f[2], f[3]);
-            *reinterpret_cast<float4 *>(&S.hs[r][c + 4]) = make_float4(f[4], f[5], f[6], f[7]);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r0 + r < a.n) v = *reinterpret_cast<const uint4 *>(a.h2 + (size_t)(r0 + r) * L_HID + c);
+            *reinterpret_cast<uint4 *>(&S.h2[r][c]) = v;
         }
         __syncthreads();
-        for (int rr = warp; rr < L_ROWS; rr += 8) {
-            const int row = r0 + rr;
-            float acc[L_NOUT];
+        // ---- logits: rows 16*warp .. +15
+        const int wr = warp * 16;
+        float lg[2][4];  // n-tile 0 (cols 0-7), n-tile 1 (cols 8-15); c0..c3
 #pragma unroll
-            for (int j = 0; j < L_NOUT; j++) {
-                float sum = 0.f;
+        for (int t = 0; t < 2; t++)
 #pragma unroll
-                for (int i = 0; i < 8; i++) sum += S.hs[rr][lane + 32 * i] * S.w_s[j][lane + 32 * i];
-                acc[j] = sum;
+            for (int e = 0; e < 4; e++) lg[t][e] = 0.f;
+        {
+            // A: matrix m = lane / 8: rows wr + (m & 1) * 8 + lane % 8, cols k + (m >> 1) * 8
+            const int am = lane >> 3;
+            const uint32_t a_base = smem_addr(&S.h2[wr + (am & 1) * 8 + (lane & 7)][(am >> 1) * 8]);
+            // B (Wh as [n = j][k]): matrix m: rows j = (m >> 1) * 8 + lane % 8, cols k + (m & 1) * 8
+            const uint32_t b_base = smem_addr(&S.wh[(am >> 1) * 8 + (lane & 7)][(am & 1) * 8]);
+#pragma unroll 4
+            for (int ks = 0; ks < L_HID / 16; ks++) {
+                uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+                ldsm_x4(a_base + ks * 32, a0, a1, a2, a3);
+                ldsm_x4(b_base + ks * 32, b0, b1, b2, b3);
+                mma16816(lg[0], a0, a1, a2, a3, b0, b1);
+                mma16816(lg[1], a0, a1, a2, a3, b2, b3);
             }
+        }
+        // ---- per-row loss and dhead on the accumulator layout (rows g, g + 8)
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
+        for (int h = 0; h < 2; h++) {
+            const int lr = wr + g + 8 * h, row = r0 + lr;
+            const bool live = row < a.n;
+            const uint32_t bits = live ? (uint32_t)S.r_bits[lr] : 0u;
+            const int act = live ? S.r_act[lr] : 0;
+            float l[4];
+            bool ok[4];
 #pragma unroll
-                for (int j = 0; j < L_NOUT; j++) acc[j] += __shfl_xor_sync(FULL, acc[j], o);
-            float dl = 0.f, dv = 0.f;  // this lane's dlogit (lanes 0-11) and the value gradient
-            if (row < a.n) {
-                const uint32_t bits = (uint32_t)S.r_bits[rr];
-                const int act = S.r_act[rr];
-                float l = acc[0];
+            for (int e = 0; e < 4; e++) {
+                l[e] = lg[e >> 1][(e & 1) + 2 * h] + bias[e];
+                ok[e] = col[e] < L_NACT && ((bits >> col[e]) & 1u);
+            }
+            float m = -3.402823466e38f;
 #pragma unroll
-                for (int j = 1; j < L_NACT; j++)
-                    if (lane == j) l = acc[j];
-                l += bh_l;
-                const bool ok = lane < L_NACT && ((bits >> lane) & 1u);
-                const float m = group16_max(ok ? l : -3.402823466e38f);
-                const float z = group16_sum(ok ? expf(l - m) : 0.f);
-                const float lz = logf(z);
-                const float lp = l - m - lz;
-                const float p = ok ? expf(lp) : 0.f;
-                const float ent = -group16_sum(ok ? p * lp : 0.f);
-                const float la = __shfl_sync(FULL, lp, act & 15);
-                const float value = acc[L_NACT] + bh_v;
-                const float adv = (S.r_adv[rr] - amean) / (astd + 1e-8f);
-                const float olp = S.r_olp[rr];
+            for (int e = 0; e < 4; e++)
+                if (ok[e]) m = fmaxf(m, l[e]);
+            m = quad_max(m);
+            float z = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (ok[e]) z += expf(l[e] - m);
+            z = quad_sum(z);
+            const float lz = logf(z);
+            float lp[4], p[4], ent = 0.f, la = 0.f, value = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                lp[e] = l[e] - m - lz;
+                p[e] = ok[e] ? expf(lp[e]) : 0.f;
+                if (ok[e]) ent -= p[e] * lp[e];
+                if (col[e] == act) la = lp[e];
+                if (col[e] == L_NACT) value = l[e];
+            }
+            ent = quad_sum(ent);
+            la = quad_sum(la);
+            value = quad_sum(value);
+            float dl[4] = {0.f, 0.f, 0.f, 0.f};
+            if (live) {
+                const float adv = (S.r_adv[lr] - amean) / (astd + 1e-8f);
+                const float olp = S.r_olp[lr];
                 const float ratio = expf(la - olp);
                 const float s1 = ratio * adv, rc = fminf(fmaxf(ratio, 1.f - a.clip), 1.f + a.clip), s2 = rc * adv;
                 const float pg = -fminf(s1, s2);
-                // d pg / d logp(a): only the selected branch carries gradient
-                // (the clamped branch is flat outside [1-clip, 1+clip])
                 float dpg_dr = 0.f;
                 if (s1 <= s2) dpg_dr = -adv;
                 else if (ratio > 1.f - a.clip && ratio < 1.f + a.clip) dpg_dr = -adv;
                 const float dlogp = dpg_dr * ratio * inv_n;
-                const float R = S.r_ret[rr], vold = S.r_vold[rr];
+                const float R = S.r_ret[lr], vold = S.r_vold[lr];
                 float vf, dvf;
                 const float e1 = value - R;
                 if (a.vclip > 0.f) {
@@ -456,10 +509,15 @@ __global__ void __launch_bounds__(256, 2) loss_kernel(LossArgs a) {
                     vf = e1 * e1;
                     dvf = 2.f * e1;
                 }
-                dv = a.vf_coef * dvf * inv_n;
-                // d(-ent_coef * H)/dl_j = ent_coef * p_j * (log p_j + H)
-                if (ok) dl = dlogp * ((lane == act ? 1.f : 0.f) - p) + a.ent_coef * inv_n * p * (lp + ent);
-                if (lane == 0) {
+                const float dv = a.vf_coef * dvf * inv_n;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    if (ok[e])
+                        dl[e] = dlogp * ((col[e] == act ? 1.f : 0.f) - p[e]) + a.ent_coef * inv_n * p[e] * (lp[e] + ent);
+                    else if (col[e] == L_NACT)
+                        dl[e] = dv;
+                }
+                if (q == 0) {
                     t_pg += pg;
                     t_vf += vf;
                     t_ent += ent;
@@ -467,95 +525,160 @@ __global__ void __launch_bounds__(256, 2) loss_kernel(LossArgs a) {
                     t_kl += olp - la;
                 }
             }
-            if (lane < 16) S.dh_s[rr][lane] = lane < L_NACT ? dl : (lane == L_NACT ? dv : 0.f);
-            float dls[L_NACT];
 #pragma unroll
-            for (int j = 0; j < L_NACT; j++) dls[j] = __shfl_sync(FULL, dl, j);
-            // dh2 = dhead . Wh, masked by ReLU'(h2)
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int k = lane + 32 * i;
-                float g = dv * S.w_s[L_NACT][k];
-#pragma unroll
-                for (int j = 0; j < L_NACT; j++) g += dls[j] * S.w_s[j][k];
-                S.gs[rr][k] = (row < a.n && S.hs[rr][k] > 0.f) ? g : 0.f;
+            for (int e = 0; e < 4; e += 2) {
+                const __nv_bfloat162 hi = __floats2bfloat162_rn(dl[e], dl[e + 1]);
+                const float2 hf = __bfloat1622float2(hi);
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(dl[e] - hf.x, dl[e + 1] - hf.y);
+                *reinterpret_cast<__nv_bfloat162 *>(&S.dhi[lr][col[e]]) = hi;
+                *reinterpret_cast<__nv_bfloat162 *>(&S.dlo[lr][col[e]]) = lo;
+                S.dhf[lr][col[e]] = dl[e];
+                S.dhf[lr][col[e] + 1] = dl[e + 1];
             }
         }
         __syncthreads();
-        // partial dWh[j][k] += sum_r dhead[r][j] * h2[r][k]; db2[k] += sum_r dh2[r][k]; dbh
+        // ---- dWh[j][c] += sum_r dhead[r][j] h2[r][c], warp w: columns 64w .. 64w+63
         {
-            const int k = tid;
-            float b2 = 0.f;
-            float acc_w[L_NOUT];
+            const int am = lane >> 3;
 #pragma unroll
-            for (int j = 0; j < L_NOUT; j++) acc_w[j] = S.accw[j][k];
-#pragma unroll 4
-            for (int r = 0; r < L_ROWS; r++) {
-                const float h = S.hs[r][k];
-                const float4 d0 = *reinterpret_cast<const float4 *>(&S.dh_s[r][0]);
-                const float4 d1 = *reinterpret_cast<const float4 *>(&S.dh_s[r][4]);
-                const float4 d2 = *reinterpret_cast<const float4 *>(&S.dh_s[r][8]);
-                const float d3 = S.dh_s[r][12];
-                acc_w[0] += d0.x * h; acc_w[1] += d0.y * h; acc_w[2] += d0.z * h; acc_w[3] += d0.w * h;
-                acc_w[4] += d1.x * h; acc_w[5] += d1.y * h; acc_w[6] += d1.z * h; acc_w[7] += d1.w * h;
-                acc_w[8] += d2.x * h; acc_w[9] += d2.y * h; acc_w[10] += d2.z * h; acc_w[11] += d2.w * h;
-                acc_w[12] += d3 * h;
-                b2 += S.gs[r][k];
-            }
+            for (int ks = 0; ks < M_ROWS / 16; ks++) {
+                // A = dhead^T (m = j, k = r) from dhead stored [r][j]: transposed loads,
+                // matrix m: rows r = ks*16 + (m >> 1) * 8 + lane % 8, cols j = (m & 1) * 8
+                uint32_t ah[4], al[4];
+                ldsm_x4_t(smem_addr(&S.dhi[ks * 16 + (am >> 1) * 8 + (lane & 7)][(am & 1) * 8]), ah[0], ah[1], ah[2],
+                          ah[3]);
+                ldsm_x4_t(smem_addr(&S.dlo[ks * 16 + (am >> 1) * 8 + (lane & 7)][(am & 1) * 8]), al[0], al[1], al[2],
+                          al[3]);
 #pragma unroll
-            for (int j = 0; j < L_NOUT; j++) S.accw[j][k] = acc_w[j];
-            acc_b2 += b2;
-            if (tid < L_NOUT)
-                for (int r = 0; r < L_ROWS; r++) acc_bh += S.dh_s[r][tid];
-        }
-        // dh2 row-major (a row is 512 B) and transposed (a feature row of 32
-        // consecutive samples is 64 B)
-        if (a.dh2) {
-            for (int i = tid; i < L_ROWS * (L_HID / 8); i += 256) {
-                const int r = i / (L_HID / 8), c = (i % (L_HID / 8)) * 8;
-                if (r0 + r < a.n) {
-                    __align__(16) __nv_bfloat16 o[8];
-#pragma unroll
-                    for (int j = 0; j < 8; j++) o[j] = __float2bfloat16_rn(S.gs[r][c + j]);
-                    *reinterpret_cast<uint4 *>(a.dh2 + (size_t)(r0 + r) * L_HID + c) = *reinterpret_cast<uint4 *>(o);
+                for (int np = 0; np < 4; np++) {
+                    // B = h2 (k = r, n = c) from h2 stored [r][c]: transposed loads,
+                    // matrix m: rows r = ks*16 + (m & 1) * 8 + lane % 8, cols c = base + (m >> 1) * 8
+                    const int c0 = warp * 64 + np * 16;
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(smem_addr(&S.h2[ks * 16 + (am & 1) * 8 + (lane & 7)][c0 + (am >> 1) * 8]), b0, b1, b2,
+                              b3);
+                    mma16816(acc_w[2 * np], ah[0], ah[1], ah[2], ah[3], b0, b1);
+                    mma16816(acc_w[2 * np], al[0], al[1], al[2], al[3], b0, b1);
+                    mma16816(acc_w[2 * np + 1], ah[0], ah[1], ah[2], ah[3], b2, b3);
+                    mma16816(acc_w[2 * np + 1], al[0], al[1], al[2], al[3], b2, b3);
                 }
             }
         }
-        if (a.dh2t) {
-            for (int i = tid; i < L_HID * (L_ROWS / 8); i += 256) {
-                const int k = i / (L_ROWS / 8), q = (i % (L_ROWS / 8)) * 8;
-                if (r0 + q < a.n) {
-                    __align__(16) __nv_bfloat16 o[8];
+        __syncthreads();  // every warp has read h2 for dWh: it may now become dh2
+        // ---- dh2 = (dhead . Wh) masked by ReLU'(h2), rows 16*warp .. +15, in place
+        {
+            const int am = lane >> 3;
+            uint32_t ah[4], al[4];
+            ldsm_x4(smem_addr(&S.dhi[wr + (am & 1) * 8 + (lane & 7)][(am >> 1) * 8]), ah[0], ah[1], ah[2], ah[3]);
+            ldsm_x4(smem_addr(&S.dlo[wr + (am & 1) * 8 + (lane & 7)][(am >> 1) * 8]), al[0], al[1], al[2], al[3]);
+#pragma unroll 4
+            for (int np = 0; np < L_HID / 16; np++) {
+                // B = Wh (k = j, n = c) from Wh stored [j][c]: transposed loads,
+                // matrix m: rows j = (m & 1) * 8 + lane % 8, cols c = 16 np + (m >> 1) * 8
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(smem_addr(&S.wh[(am & 1) * 8 + (lane & 7)][np * 16 + (am >> 1) * 8]), b0, b1, b2, b3);
+                float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(d0, ah[0], ah[1], ah[2], ah[3], b0, b1);
+                mma16816(d0, al[0], al[1], al[2], al[3], b0, b1);
+                mma16816(d1, ah[0], ah[1], ah[2], ah[3], b2, b3);
+                mma16816(d1, al[0], al[1], al[2], al[3], b2, b3);
 #pragma unroll
-                    for (int j = 0; j < 8; j++) o[j] = __float2bfloat16_rn(S.gs[q + j][k]);
-                    if (r0 + q + 8 <= a.n)
-                        *reinterpret_cast<uint4 *>(a.dh2t + (size_t)k * a.ldt + r0 + q) = *reinterpret_cast<uint4 *>(o);
-                    else
-                        for (int j = 0; j < 8 && r0 + q + j < a.n; j++) a.dh2t[(size_t)k * a.ldt + r0 + q + j] = o[j];
+                for (int t = 0; t < 2; t++) {
+                    const float *d = t ? d1 : d0;
+                    const int c = np * 16 + t * 8 + 2 * q;
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        __nv_bfloat162 *cell = reinterpret_cast<__nv_bfloat162 *>(&S.h2[wr + g + 8 * h][c]);
+                        const float2 hv = __bfloat1622float2(*cell);
+                        const float x = hv.x > 0.f ? d[2 * h] : 0.f, y = hv.y > 0.f ? d[2 * h + 1] : 0.f;
+                        *cell = __floats2bfloat162_rn(x, y);
+                    }
                 }
             }
         }
         __syncthreads();
+        // ---- dbh (threads 0-12), db2 (two columns per thread), dh2 and dh2^T out
+        if (tid < L_NOUT)
+            for (int r = 0; r < M_ROWS; r++) acc_bh += S.dhf[r][tid];
+        if (a.dh2) {
+            for (int i = tid; i < M_ROWS * (L_HID / 8); i += blockDim.x) {
+                const int r = i / (L_HID / 8), c = (i % (L_HID / 8)) * 8;
+                if (r0 + r < a.n)
+                    *reinterpret_cast<uint4 *>(a.dh2 + (size_t)(r0 + r) * L_HID + c) =
+                        *reinterpret_cast<const uint4 *>(&S.h2[r][c]);
+            }
+        }
+        {
+            // thread t owns columns 2t, 2t+1: sums them (db2) and writes their
+            // transposed rows in 8-sample chunks
+#pragma unroll 1
+            for (int ch = 0; ch < M_ROWS / 8; ch++) {
+                __align__(16) __nv_bfloat16 o0[8], o1[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162 *>(&S.h2[ch * 8 + j][2 * tid]);
+                    o0[j] = v.x;
+                    o1[j] = v.y;
+                    const float2 f = __bfloat1622float2(v);
+                    acc_b2[0] += f.x;
+                    acc_b2[1] += f.y;
+                }
+                const int rb = r0 + ch * 8;
+                if (a.dh2t && rb < a.n) {
+                    if (rb + 8 <= a.n) {
+                        *reinterpret_cast<uint4 *>(a.dh2t + (size_t)(2 * tid) * a.ldt + rb) = *reinterpret_cast<uint4 *>(o0);
+                        *reinterpret_cast<uint4 *>(a.dh2t + (size_t)(2 * tid + 1) * a.ldt + rb) =
+                            *reinterpret_cast<uint4 *>(o1);
+                    } else {
+                        for (int j = 0; j < 8 && rb + j < a.n; j++) {
+                            a.dh2t[(size_t)(2 * tid) * a.ldt + rb + j] = o0[j];
+                            a.dh2t[(size_t)(2 * tid + 1) * a.ldt + rb + j] = o1[j];
+                        }
+                    }
+                }
+            }
+        }
     }
+    // ---- block partials: dWh [13][256], dbh [13], db2 [256], terms [8]
     float *out = a.part + (size_t)blockIdx.x * L_PART;
 #pragma unroll
-    for (int j = 0; j < L_NOUT; j++) out[j * L_HID + tid] = S.accw[j][tid];
+    for (int nt = 0; nt < 8; nt++) {
+        const int c = warp * 64 + nt * 8 + 2 * q;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int j = g + 8 * h;
+            if (j < L_NOUT) {
+                out[j * L_HID + c] = acc_w[nt][2 * h];
+                out[j * L_HID + c + 1] = acc_w[nt][2 * h + 1];
+            }
+        }
+    }
     if (tid < L_NOUT) out[L_NOUT * L_HID + tid] = acc_bh;
-    out[L_NOUT * L_HID + L_NOUT + tid] = acc_b2;
+    out[L_NOUT * L_HID + L_NOUT + 2 * tid] = acc_b2[0];
+    out[L_NOUT * L_HID + L_NOUT + 2 * tid + 1] = acc_b2[1];
+    // loss terms: q == 0 lanes hold them; warp sums, then warps in order
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        t_pg += __shfl_xor_sync(FULL, t_pg, o);
+        t_vf += __shfl_xor_sync(FULL, t_vf, o);
+        t_ent += __shfl_xor_sync(FULL, t_ent, o);
+        t_clip += __shfl_xor_sync(FULL, t_clip, o);
+        t_kl += __shfl_xor_sync(FULL, t_kl, o);
+    }
     if (lane == 0) {
-        S.terms_s[warp][0] = t_pg;
-        S.terms_s[warp][1] = t_vf;
-        S.terms_s[warp][2] = t_ent;
-        S.terms_s[warp][3] = t_clip;
-        S.terms_s[warp][4] = t_kl;
+        S.terms[warp][0] = t_pg;
+        S.terms[warp][1] = t_vf;
+        S.terms[warp][2] = t_ent;
+        S.terms[warp][3] = t_clip;
+        S.terms[warp][4] = t_kl;
     }
     __syncthreads();
-    if (tid < 5) {
+    if (tid < 8) {
         float v = 0.f;
-        for (int w = 0; w < 8; w++) v += S.terms_s[w][tid];
+        if (tid < 5)
+            for (int w = 0; w < M_WARPS; w++) v += S.terms[w][tid];
         out[L_NOUT * L_HID + L_NOUT + L_HID + tid] = v;
     }
-    if (tid >= 5 && tid < 8) out[L_NOUT * L_HID + L_NOUT + L_HID + tid] = 0.f;
 }
 
 // out[i] = sum over p of parts[p * stride + i] (loss-kernel block partials).
@@ -754,13 +877,15 @@ int d1_ppo_loss(const void *h2, const void *wh, const float *bh, const int64_t *
     if (n <= 0 || blocks <= 0 || !h2 || !wh || !bh || !idx || !legal || !action || !old_logp || !adv || !ret ||
         !old_value || !adv_stats || !part || adv_count < 2 || (dh2t && ldt < n))
         return D1_ERR_BAD_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(h2) | reinterpret_cast<uintptr_t>(wh)) & 15) return D1_ERR_BAD_ARGUMENT;
+    if (dh2t && (ldt % 8 || reinterpret_cast<uintptr_t>(dh2t) & 15)) return D1_ERR_BAD_ARGUMENT;
     static uint64_t ready = 0;
-    const int err = ppo::opt_in_smem((const void *)ppo::loss_kernel, (int)sizeof(ppo::LossSmem), &ready);
+    const int err = ppo::opt_in_smem((const void *)ppo::loss_mma_kernel, (int)sizeof(ppo::MmaSmem), &ready);
     if (err) return err;
     ppo::LossArgs a{(const __nv_bfloat16 *)h2, (const __nv_bfloat16 *)wh, bh, idx, legal, action, old_logp, adv,
                     ret, old_value, adv_stats, adv_count, n, clip, vclip, vf_coef, ent_coef,
                     (__nv_bfloat16 *)dh2, (__nv_bfloat16 *)dh2t, ldt, part};
-    ppo::loss_kernel<<<blocks, 256, sizeof(ppo::LossSmem), (cudaStream_t)stream>>>(a);
+    ppo::loss_mma_kernel<<<blocks, ppo::M_WARPS * 32, sizeof(ppo::MmaSmem), (cudaStream_t)stream>>>(a);
     return (int)cudaGetLastError();
 }
 

@@ -76,8 +76,8 @@ class PPO:
         self.s2 = G.splits_for(mb, splits)
         self.slab2 = torch.empty((self.s2, HID, HID), **f32)
         self.part_len = self.lib.d1_ppo_loss_part_len()
-        batches = (mb + 31) // 32                     # the loss kernel takes 32 rows per pass
-        per = (batches + 295) // 296                  # passes per block with two blocks per SM
+        batches = (mb + 63) // 64                     # the loss kernel takes 64 rows per pass
+        per = (batches + 591) // 592                  # passes per block with four blocks per SM
         self.loss_blocks = (batches + per - 1) // per
         self.part = torch.empty((self.loss_blocks, self.part_len), **f32)
         self.terms = torch.zeros(8, **f32)
