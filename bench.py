@@ -58,6 +58,8 @@ def parse():
     ap.add_argument('--no-conv', action='store_true', help='skip the config-3 conv-policy rollout line')
     ap.add_argument('--conv-envs', type=int, default=131072, help='envs per GPU of the config-3 line')
     ap.add_argument('--conv-steps', type=int, default=16)
+    ap.add_argument('--kernels', action='store_true',
+                    help='run every hot kernel twice at bench sizes for profiler captures, print nothing else')
     return ap.parse_args()
 
 
@@ -407,8 +409,58 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_kernels(args):
+    """Every hot kernel once for warm-up and once more to be captured (ncu -k
+    <kernel> -s <skip> -c <count>), at the bench's sizes, ~4 GB on the device.
+    Launch order: an 8-step rollout of 65,536 envs (8 x (step_kernel, 2
+    gemm_kernel, head_sample_kernel), then 2 gemm_kernel + head_sample_kernel for
+    the bootstrap value) and GAE; then per pass: gemm_kernel (rollout layer 1),
+    one PPO minibatch of 16,384 (gather_kernel, 5 gemm_kernel, loss_mma_kernel,
+    reductions, adam_kernel), gemm_kernel (layer 2), head_sample_kernel,
+    step_kernel, gae_scan_kernel, and the config-3 policy on 16,384 envs
+    (crop_kernel, conv_kernel<1..3>, 2 gemm_kernel, ar_kernel)."""
+    import torch
+    from d1 import gemm as G
+    from d1.conv_policy import ConvPolicy
+    from d1.policy import Policy
+    from d1.ppo import PPO
+    from d1.rollout import Rollout
+    from d1.spec_env import SpecEnv
+    torch.cuda.set_device(0)
+    B = args.envs
+    env = SpecEnv(B, seed=1)
+    pol = Policy(seed=0)
+    roll = Rollout(env, pol, 8, seed=1)
+    roll.collect()
+    tr = PPO(pol, roll, minibatch=args.minibatch, epochs=1, graph=False)
+    tr.advantages()
+    idx = torch.randperm(tr.total, device='cuda', generator=torch.Generator(device='cuda').manual_seed(0))[:tr.mb]
+    x = roll.obs[0]
+    h1 = torch.empty((B, 256), dtype=torch.bfloat16, device='cuda')
+    h2 = torch.empty((B, 256), dtype=torch.bfloat16, device='cuda')
+    act = torch.empty(B, dtype=torch.int64, device='cuda')
+    lp, val = torch.empty(B, device='cuda'), torch.empty(B, device='cuda')
+    n3 = 16384
+    env3 = SpecEnv(n3, seed=3, observe=False)
+    cp = ConvPolicy(seed=0, chunk=n3)
+    buf = cp.buffers(n3)
+    torch.cuda.synchronize()
+    for rep in range(2):
+        G.gemm(x, pol.bf16['w1'], bias=pol.params['b1'], relu=True, out=h1)
+        tr.minibatch(idx)
+        G.gemm(h1, pol.bf16['w2'], bias=pol.params['b2'], relu=True, out=h2)
+        pol.head(h2, env.legal, 1, rep, 0, act, lp, val)
+        env.step(act)
+        tr.advantages()
+        cp.act(env3.state, env3.legal, n3, buf, 1, rep)
+        torch.cuda.synchronize()
+
+
 def main():
     args = parse()
+    if args.kernels:
+        run_kernels(args)
+        return
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local_rank = int(os.environ.get('LOCAL_RANK', '0'))
