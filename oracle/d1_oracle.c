@@ -806,7 +806,7 @@ static void spec_reset(Spec *s, const D1SpecConfig *c) {
 /* Full FIFO BFS from the player over 8-neighbour floor (the distance field the
  * reference precomputes per player cell, learn.cu:168-176). */
 static void spec_bfs(const Spec *s, uint16_t *ds) {
-    static int queue[N];
+    static _Thread_local int queue[N]; /* per host thread: the CPU baseline steps env slices in parallel */
     for (int p = 0; p < N; p++) ds[p] = 65535;
     int head = 0, tail = 0;
     ds[s->player] = 0;
@@ -925,7 +925,7 @@ typedef struct { float reward; int done, descended, death, timeout; } Prim;
 /* One physical turn: learn.cu:505-598 with the sleep/exploration variants of
  * semantic-actions-v1 learn.cu:638-730 and the stairs clear of d1-stairs-v2. */
 static Prim spec_primitive(Spec *s, const D1SpecConfig *c, int d) {
-    static uint16_t dist[N];
+    static _Thread_local uint16_t dist[N];
     Prim r = {0};
     int reward_milli = -1;
     s->blocks = 0;

@@ -134,3 +134,20 @@ def test_oracle_is_deterministic_and_env_ids_are_independent(oracle_lib):
         b.step(acts[k][16:])
     assert np.array_equal(a.compact()[16:], b.compact())
     assert np.array_equal(a.obs[16:], b.obs)
+
+
+def test_oracle_slices_stepped_in_parallel_threads_match_one_run(oracle_lib):
+    """The CPU baseline steps env slices from a thread pool (ctypes releases the
+    GIL); the oracle must keep no shared scratch between calls."""
+    from concurrent.futures import ThreadPoolExecutor
+    from golden.schedule import random_actions
+    n, per, steps = 128, 32, 40
+    whole = oracle.OracleSpec(n, SPEC, seed=4)
+    parts = [oracle.OracleSpec(per, SPEC, seed=4, first_env=i * per) for i in range(n // per)]
+    acts = random_actions(8, steps, n, 12)
+    with ThreadPoolExecutor(len(parts)) as pool:
+        for k in range(steps):
+            whole.step(acts[k])
+            list(pool.map(lambda i: parts[i].step(acts[k][i * per:(i + 1) * per]), range(len(parts))))
+    assert np.array_equal(np.concatenate([p.compact() for p in parts]), whole.compact())
+    assert np.array_equal(np.concatenate([p.obs for p in parts]), whole.obs)
