@@ -98,7 +98,6 @@ struct RayArgs {
     const uint4 *ray;  // {blocker mask lo, hi, end bit index ey*8+ex, 0}
     int n;
 };
-constexpr int RAY_ITERS = MAX_RAYS / 32;
 
 struct Env {
     WarpPhilox rng;
@@ -184,16 +183,13 @@ __device__ void compute_los(Env &e, const RayArgs &ra) {
     const unsigned long long o2 = *reinterpret_cast<const unsigned long long *>(s.opqb + 16);
     const unsigned long long o3 = *reinterpret_cast<const unsigned long long *>(s.opqb + 24);
     unsigned long long v0 = 0, v1 = 0, v2 = 0, v3 = 0;
-    uint4 rr[RAY_ITERS];
-#pragma unroll
-    for (int i = 0; i < RAY_ITERS; i++) {
+    // Rolled for the same reason as observe's cell loop (instruction fetch).
+#pragma unroll 1
+    for (int i = 0; i < (ra.n + 31) / 32; i++) {
         const int r = lane + 32 * i;
-        rr[i] = r < ra.n ? __ldg(ra.ray + r) : make_uint4(0xffffffffu, 0xffffffffu, 0u, 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < RAY_ITERS; i++) {
-        const unsigned long long blk = (unsigned long long)rr[i].x | ((unsigned long long)rr[i].y << 32);
-        const unsigned long long endb = 1ull << rr[i].z;
+        const uint4 rv = r < ra.n ? __ldg(ra.ray + r) : make_uint4(0xffffffffu, 0xffffffffu, 0u, 0u);
+        const unsigned long long blk = (unsigned long long)rv.x | ((unsigned long long)rv.y << 32);
+        const unsigned long long endb = 1ull << rv.z;
         if (!(blk & o0)) v0 |= endb;
         if (!(blk & o1)) v1 |= endb;
         if (!(blk & o2)) v2 |= endb;
@@ -504,14 +500,20 @@ __device__ void pursuit_bfs(Env &e, int extra_layers) {
             }
         }
         __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 3; i++) {
+        // Rolled (instruction fetch bound): the word is picked by predication so
+        // nw stays in registers.
+#pragma unroll 1
+        for (int ij = 0; ij < 9; ij++) {
+            const int i = ij / 3, j = ij - 3 * i;
             const int y = ylo + e.lane + 32 * i;
             if (y <= yhi) {
-#pragma unroll
-                for (int j = 0; j < 3; j++) {
+                {
                     const int r = y * 3 + j;
-                    uint32_t w = nw[i][j];
+                    uint32_t w = 0;
+#pragma unroll
+                    for (int ii = 0; ii < 3; ii++)
+#pragma unroll
+                        for (int jj = 0; jj < 3; jj++) w = (ii == i && jj == j) ? nw[ii][jj] : w;
                     s.seen[r] |= w;
                     s.cur[r] = w;
                     while (w) {
@@ -802,7 +804,9 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
     const int sdx = e.stairs % W - px, sdy = e.stairs / W - py;
     const int sj = (sdx >= -7 && sdx <= 7 && sdy >= -7 && sdy <= 7) ? (sdy + 7) * 15 + sdx + 7 : -1;
     uint4 *dst = reinterpret_cast<uint4 *>(obs);
-#pragma unroll
+    // Rolled: this kernel is bound by instruction fetch (ncu: "no instruction"
+    // is the top stall), so compact code beats unrolled code here.
+#pragma unroll 1
     for (int k = 0; k < (CELLS + 31) / 32; k++) {
         const int j = lane + 32 * k;
         const int jc = j < CELLS ? j : CELLS - 1;
