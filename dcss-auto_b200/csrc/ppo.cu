@@ -709,26 +709,45 @@ __global__ void __launch_bounds__(256) sum_rows_kernel(const float *parts, int n
     }
 }
 
-// out[i] = sum over splits of slabs[s][i] (split-K partial products), i < count;
-// four elements per thread when count is a multiple of 4.
-__global__ void reduce_slabs_kernel(const float *__restrict__ slabs, int splits, int64_t count, float *out) {
-    const int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if ((count & 3) == 0) {
-        if (i4 * 4 >= count) return;
-        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = 0; k < splits; k++) {
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(slabs + (size_t)k * count) + i4);
-            s.x += v.x;
-            s.y += v.y;
-            s.z += v.z;
-            s.w += v.w;
+// out[i] = sum over splits of slabs[s][i] (split-K partial products), i < count.
+// A block owns 64 float4 columns and G = blockDim.x / 64 groups of threads
+// (G grows with the number of slabs, up to 4); group y adds slabs y, y+G, ...
+// of its column, and the group sums are added in group order, so the result
+// does not depend on scheduling.
+constexpr int RS_COLS = 64, RS_GROUPS = 4;
+__global__ void __launch_bounds__(RS_COLS * RS_GROUPS) reduce_slabs_kernel(const float *__restrict__ slabs, int splits,
+                                                                          int64_t count, float *out) {
+    __shared__ float4 part[RS_GROUPS][RS_COLS];
+    const int cx = threadIdx.x % RS_COLS, gy = threadIdx.x / RS_COLS, groups = blockDim.x / RS_COLS;
+    const int64_t i4 = (int64_t)blockIdx.x * RS_COLS + cx;
+    const bool vec = (count & 3) == 0;
+    const int64_t n4 = vec ? count / 4 : count;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i4 < n4) {
+        for (int k = gy; k < splits; k += groups) {
+            if (vec) {
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(slabs + (size_t)k * count) + i4);
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            } else {
+                acc.x += slabs[(size_t)k * count + i4];
+            }
         }
-        reinterpret_cast<float4 *>(out)[i4] = s;
-    } else {
-        if (i4 >= count) return;
-        float s = 0.f;
-        for (int k = 0; k < splits; k++) s += slabs[(size_t)k * count + i4];
-        out[i4] = s;
+    }
+    part[gy][cx] = acc;
+    __syncthreads();
+    if (gy == 0 && i4 < n4) {
+        float4 t = part[0][cx];
+        for (int g = 1; g < groups; g++) {
+            t.x += part[g][cx].x;
+            t.y += part[g][cx].y;
+            t.z += part[g][cx].z;
+            t.w += part[g][cx].w;
+        }
+        if (vec) reinterpret_cast<float4 *>(out)[i4] = t;
+        else out[i4] = t.x;
     }
 }
 
@@ -796,39 +815,73 @@ struct AdamArgs {
     int nseg;
     int64_t total;
 };
-__global__ void adam_kernel(AdamArgs a) {
-    const double norm = sqrt(*a.sumsq);
-    const double t = (double)*a.step;
-    const float bc1 = (float)(1.0 - pow((double)a.beta1, t));
-    const float bc2_sqrt = (float)sqrt(1.0 - pow((double)a.beta2, t));
-    float scale = 1.f;
-    if (a.max_norm > 0.f) {
-        const float coef = a.max_norm / ((float)norm + 1e-6f);
-        if (coef < 1.f) scale = coef;
-    }
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const float g = a.grad[i] * scale;
-        const float m = a.beta1 * a.m[i] + (1.f - a.beta1) * g;
-        const float v = a.beta2 * a.v[i] + (1.f - a.beta2) * g * g;
-        a.m[i] = m;
-        a.v[i] = v;
-        const float denom = sqrtf(v) / bc2_sqrt + a.eps;
-        const float p = a.param[i] - (a.lr / bc1) * m / denom;
-        a.param[i] = p;
-        for (int s = 0; s < a.nseg; s++) {
-            const AdamSeg &g2 = a.seg[s];
-            if (i >= g2.offset && i < g2.offset + g2.count) {
-                const int64_t j = i - g2.offset;
-                const __nv_bfloat16 pb = __float2bfloat16_rn(p);
-                if (g2.bf16) g2.bf16[j] = pb;
-                if (g2.bf16_t) {
-                    const int r = (int)(j / g2.cols), c = (int)(j % g2.cols);
-                    g2.bf16_t[(size_t)c * g2.rows + r] = pb;
-                }
+// Four elements per thread (float4 loads and stores of the four fp32 arrays);
+// the bf16 compute copies are written element by element.
+__device__ __forceinline__ float adam_one(const AdamArgs &a, float g, float &m, float &v, float p, float scale,
+                                          float bc1, float bc2_sqrt) {
+    g *= scale;
+    m = a.beta1 * m + (1.f - a.beta1) * g;
+    v = a.beta2 * v + (1.f - a.beta2) * g * g;
+    const float denom = sqrtf(v) / bc2_sqrt + a.eps;
+    return p - (a.lr / bc1) * m / denom;
+}
+__device__ __forceinline__ void adam_copies(const AdamArgs &a, int64_t i, float p) {
+    for (int s = 0; s < a.nseg; s++) {
+        const AdamSeg &g2 = a.seg[s];
+        if (i >= g2.offset && i < g2.offset + g2.count) {
+            const int64_t j = i - g2.offset;
+            const __nv_bfloat16 pb = __float2bfloat16_rn(p);
+            if (g2.bf16) g2.bf16[j] = pb;
+            if (g2.bf16_t) {
+                const int r = (int)(j / g2.cols), c = (int)(j % g2.cols);
+                g2.bf16_t[(size_t)c * g2.rows + r] = pb;
             }
         }
     }
+}
+__global__ void adam_kernel(AdamArgs a) {
+    // step scalars once per block (double-precision pow is slow per thread)
+    __shared__ float sc[3];
+    if (threadIdx.x == 0) {
+        const double norm = sqrt(*a.sumsq);
+        const double t = (double)*a.step;
+        sc[0] = (float)(1.0 - pow((double)a.beta1, t));
+        sc[1] = (float)sqrt(1.0 - pow((double)a.beta2, t));
+        float scale = 1.f;
+        if (a.max_norm > 0.f) {
+            const float coef = a.max_norm / ((float)norm + 1e-6f);
+            if (coef < 1.f) scale = coef;
+        }
+        sc[2] = scale;
+    }
+    __syncthreads();
+    const float bc1 = sc[0], bc2_sqrt = sc[1], scale = sc[2];
+    const int64_t n4 = a.total / 4, stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4; q += stride) {
+        const float4 g4 = reinterpret_cast<const float4 *>(a.grad)[q];
+        float4 m4 = reinterpret_cast<const float4 *>(a.m)[q], v4 = reinterpret_cast<const float4 *>(a.v)[q];
+        float4 p4 = reinterpret_cast<const float4 *>(a.param)[q];
+        p4.x = adam_one(a, g4.x, m4.x, v4.x, p4.x, scale, bc1, bc2_sqrt);
+        p4.y = adam_one(a, g4.y, m4.y, v4.y, p4.y, scale, bc1, bc2_sqrt);
+        p4.z = adam_one(a, g4.z, m4.z, v4.z, p4.z, scale, bc1, bc2_sqrt);
+        p4.w = adam_one(a, g4.w, m4.w, v4.w, p4.w, scale, bc1, bc2_sqrt);
+        reinterpret_cast<float4 *>(a.m)[q] = m4;
+        reinterpret_cast<float4 *>(a.v)[q] = v4;
+        reinterpret_cast<float4 *>(a.param)[q] = p4;
+        adam_copies(a, 4 * q, p4.x);
+        adam_copies(a, 4 * q + 1, p4.y);
+        adam_copies(a, 4 * q + 2, p4.z);
+        adam_copies(a, 4 * q + 3, p4.w);
+    }
+    if (blockIdx.x == 0)
+        for (int64_t i = 4 * n4 + threadIdx.x; i < a.total; i += blockDim.x) {
+            float m = a.m[i], v = a.v[i];
+            const float p = adam_one(a, a.grad[i], m, v, a.param[i], scale, bc1, bc2_sqrt);
+            a.m[i] = m;
+            a.v[i] = v;
+            a.param[i] = p;
+            adam_copies(a, i, p);
+        }
 }
 
 __global__ void counter_add_kernel(int64_t *c, int64_t delta) { *c += delta; }
@@ -897,11 +950,10 @@ int d1_sum_rows(const float *parts, int nparts, int stride, int len, float *out,
 
 int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, void *stream) {
     if (!slabs || !out || splits <= 0 || count <= 0) return D1_ERR_BAD_ARGUMENT;
-    const int64_t threads = (count & 3) == 0 ? count / 4 : count;
-    if (((count & 3) == 0) && ((reinterpret_cast<uintptr_t>(slabs) | reinterpret_cast<uintptr_t>(out)) & 15))
-        return D1_ERR_BAD_ARGUMENT;
-    ppo::reduce_slabs_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(slabs, splits, count,
-                                                                                                    out);
+    const int64_t n = (count & 3) == 0 ? count / 4 : count;
+    const int groups = splits >= 32 ? ppo::RS_GROUPS : splits >= 16 ? 2 : 1;
+    ppo::reduce_slabs_kernel<<<(unsigned)((n + ppo::RS_COLS - 1) / ppo::RS_COLS), ppo::RS_COLS * groups, 0,
+                               (cudaStream_t)stream>>>(slabs, splits, count, out);
     return (int)cudaGetLastError();
 }
 
@@ -951,6 +1003,9 @@ int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, 
         a.seg[i].bf16 = (__nv_bfloat16 *)segs[i].bf16;
         a.seg[i].bf16_t = (__nv_bfloat16 *)segs[i].bf16_t;
     }
+    if ((reinterpret_cast<uintptr_t>(param) | reinterpret_cast<uintptr_t>(grad) | reinterpret_cast<uintptr_t>(m) |
+         reinterpret_cast<uintptr_t>(v)) & 15)
+        return D1_ERR_BAD_ARGUMENT;  // float4 access
     ppo::adam_kernel<<<592, 256, 0, (cudaStream_t)stream>>>(a);
     return (int)cudaGetLastError();
 }

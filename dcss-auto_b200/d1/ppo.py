@@ -73,7 +73,9 @@ class PPO:
         self.dh1t = torch.empty((HID, mb), **bf)
         self.s1 = G.splits_for(mb, splits)
         self.slab1 = torch.empty((self.s1, HID, OBS), **f32)
-        self.s2 = G.splits_for(mb, splits)
+        # dW2 is 256 x 256: its output has only 2 tiles, so it needs 8x the K splits
+        # of dW1 (2 x 8 tiles) to put ~128 CTAs to work
+        self.s2 = G.splits_for(mb, splits * 8)
         self.slab2 = torch.empty((self.s2, HID, HID), **f32)
         self.part_len = self.lib.d1_ppo_loss_part_len()
         batches = (mb + 63) // 64                     # the loss kernel takes 64 rows per pass

@@ -328,7 +328,7 @@ int d1_counter_add(int64_t *counter, int64_t delta, void *stream);
  * 1-based; eps outside the sqrt) on fp32 master params after scaling grad by
  * min(1, max_norm / (sqrt(*sumsq) + 1e-6)) (torch.nn.utils.clip_grad_norm_;
  * max_norm <= 0 disables), then refreshes the bf16 copies of `segs` (host
- * array of nseg <= 8). */
+ * array of nseg <= 8). param, grad, m and v are 16-byte aligned. */
 int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, int64_t total, float lr, float beta1,
             float beta2, float eps, float max_norm, const int64_t *step, const D1AdamSegment *segs, int nseg,
             void *stream);
