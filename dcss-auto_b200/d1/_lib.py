@@ -39,6 +39,7 @@ SIGNATURES = {
     'd1_adam': [_P, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _P, _P, _I, _P],
     'd1_counter_add': [_P, C.c_int64, _P],
     'd1_gemm_splits': [_I, _I],
+    'd1_gemm_bkn': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_head_sample': [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],
     'd1_gemm_error': [],
     'd1_gemm_wgrad_noalloc': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _I, _P],

@@ -38,3 +38,21 @@ def linear_relu(x, w, b, out=None):
 
 def gemm_error():
     return library().d1_gemm_error()
+
+
+def gemm_bkn(a, b_kn, bias=None, relu=False, out=None, out_f32=None, splits=1):
+    """act(a @ b_kn + bias) with b_kn stored [K, N] (N contiguous; the tensor-core
+    operand is read MN-major). a: bf16 [M, K]. out (bf16 [M, N]) and/or out_f32
+    (fp32 [splits, M, N])."""
+    M, K = a.shape
+    N = b_kn.shape[1]
+    assert b_kn.shape[0] == K and a.dtype == torch.bfloat16 and b_kn.dtype == torch.bfloat16
+    assert a.stride(1) == 1 and b_kn.stride(1) == 1
+    if out is None and out_f32 is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    check(library().d1_gemm_bkn(a.data_ptr(), a.stride(0), b_kn.data_ptr(), b_kn.stride(0), M, N, K,
+                                None if bias is None else bias.data_ptr(), int(relu),
+                                None if out is None else out.data_ptr(), 0 if out is None else out.stride(0),
+                                None if out_f32 is None else out_f32.data_ptr(),
+                                0 if out_f32 is None else out_f32.stride(-2), splits, _stream(a)), 'd1_gemm_bkn')
+    return out if out is not None else out_f32

@@ -4,14 +4,15 @@ coefficients) and a switch for the reference loss (0.25 * MSE, no value clip).
 
 Per minibatch (all device work is libd1 kernels, launched on the current stream):
 
-  gather     X = obs[idx], X^T                    d1_ppo_gather
+  gather     X = obs[idx]                          d1_ppo_gather
   layer 1    h1 = relu(X W1^T + b1), h1^T          d1_gemm (tcgen05)
   layer 2    h2 = relu(h1 W2^T + b2)               d1_gemm
   loss       head, PPO loss, dlogits/dvalue,       d1_ppo_loss (fused)
              dh2 = dhead Wh * relu'(h2), dh2^T, partials of dWh, dbh, db2
   dW2        dh2^T h1 (split-K fp32 slabs)         d1_gemm + d1_reduce_slabs
   dh1^T      (dh2 W2) * relu'(h1), transposed      d1_gemm (mask epilogue)
-  dW1        dh1^T X (split-K fp32 slabs)          d1_gemm + d1_reduce_slabs
+  dW1        dh1^T X (split-K fp32 slabs; X read    d1_gemm_bkn + d1_reduce_slabs
+             as the MN-major B operand, no X^T)
   db1        row sums of dh1^T                     d1_row_sum_bf16
   all-reduce flat fp32 gradient (NCCL, multi-GPU)  torch.distributed
   optimizer  grad-norm clip + Adam + bf16 copies   d1_sumsq + d1_adam
@@ -64,7 +65,6 @@ class PPO:
         self.perm = torch.empty(self.total, dtype=torch.int64, device=dev)
         mb = minibatch
         self.x = torch.empty((mb, OBS), **bf)
-        self.xt = torch.empty((OBS, mb), **bf)
         self.h1 = torch.empty((mb, HID), **bf)
         self.h1t = torch.empty((HID, mb), **bf)
         self.h2 = torch.empty((mb, HID), **bf)
@@ -121,8 +121,8 @@ class PPO:
         p, r, lib, s = self.policy, self.rollout, self.lib, self.stream
         mb = self.mb
         obs = r.obs[:r.T].reshape(self.total, OBS)
-        check(lib.d1_ppo_gather(obs.data_ptr(), OBS, idx.data_ptr(), mb, self.x.data_ptr(), self.xt.data_ptr(),
-                                mb, s), 'd1_ppo_gather')
+        check(lib.d1_ppo_gather(obs.data_ptr(), OBS, idx.data_ptr(), mb, self.x.data_ptr(), None, mb, s),
+              'd1_ppo_gather')
         p.hidden_layers(self.x, h1=self.h1, h1t=self.h1t, h2=self.h2)
         g = self.grad
         check(lib.d1_ppo_loss(self.h2.data_ptr(), p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(),
@@ -141,8 +141,8 @@ class PPO:
         check(lib.d1_reduce_slabs(self.slab2.data_ptr(), self.s2, HID * HID, g[self.off['w2']:].data_ptr(), s))
         # dh1^T = ((dh2 W2) * relu'(h1))^T
         G.gemm(self.dh2, p.bf16['w2t'], mask=self.h1, out_t=self.dh1t)
-        # dW1 = dh1^T X, db1 = row sums of dh1^T
-        G.gemm(self.dh1t, self.xt, out_f32=self.slab1, splits=self.s1)
+        # dW1 = dh1^T X (X read as the MN-major operand), db1 = row sums of dh1^T
+        G.gemm_bkn(self.dh1t, self.x, out_f32=self.slab1, splits=self.s1)
         check(lib.d1_reduce_slabs(self.slab1.data_ptr(), self.s1, HID * OBS, g[self.off['w1']:].data_ptr(), s))
         check(lib.d1_row_sum_bf16(self.dh1t.data_ptr(), HID, mb, mb, g[self.off['b1']:].data_ptr(), s))
         if self.group is not None:

@@ -195,6 +195,12 @@ int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K,
             const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits,
             void *stream);
 int d1_gemm_splits(int K, int splits);
+/* As d1_gemm with B stored [K, N] (row pitch ldb >= N, N contiguous: "MN-major")
+ * instead of [N, K], so a weight gradient A^T-style product can read a row-major
+ * activation matrix without a transposed copy. Outputs c (bf16) and/or cf
+ * (fp32 split-K slabs) only. */
+int d1_gemm_bkn(const void *a, int lda, const void *b_kn, int ldb, int M, int N, int K, const float *bias, int relu,
+                void *c, int ldc, float *cf, int ldcf, int splits, void *stream);
 /* The policy's second layer with the head and sampler fused into the GEMM
  * epilogue: h = ReLU(A . B^T + bias) with N = 256 (B bf16 [256, K]), never
  * stored; logits/value = bf16(h) . wh^T + bh (wh bf16 [13, 256], bh f32 [13]);

@@ -59,3 +59,26 @@ def test_split_k_partials_sum_to_the_product(G):
     r = ref(a, b)
     got = cf[:, :, :N].sum(0)
     assert torch.allclose(got, r, rtol=1e-4, atol=1e-2)
+
+
+@pytest.mark.parametrize('M,N,K,splits', [(128, 256, 64, 1), (256, 1832, 16384, 8), (300, 200, 640, 1), (256, 1832, 4096, 4)])
+def test_b_stored_k_by_n(G, M, N, K, splits):
+    """d1_gemm_bkn: B given as [K, N] (MN-major operand) -- bf16 out and split-K
+    fp32 slabs against the fp32 product."""
+    g = torch.Generator(device='cuda').manual_seed(M + N + K)
+    a = (torch.randn(M, K, device='cuda', generator=g) / K ** 0.5).to(torch.bfloat16)
+    b = torch.randn(K, N, device='cuda', generator=g).to(torch.bfloat16)
+    ref = a.float() @ b.float()
+    ld = (N + 7) // 8 * 8
+    if splits == 1:
+        bias = torch.randn(N, device='cuda', generator=g)
+        out = torch.empty((M, ld), dtype=torch.bfloat16, device='cuda')[:, :N]
+        G.gemm_bkn(a, b, bias=bias, relu=True, out=out)
+        want = torch.relu(ref + bias)
+        assert torch.allclose(out.float(), want, rtol=2e-2, atol=2e-2 * want.abs().max().item())
+    used = G.splits_for(K, splits)
+    slabs = torch.empty((used, M, ld), device='cuda')
+    G.gemm_bkn(a, b, out_f32=slabs[:, :, :N], splits=splits)
+    got = slabs[:, :, :N].sum(0)
+    assert torch.allclose(got, ref, rtol=1e-3, atol=1e-3 * ref.abs().max().item())
+    assert G.gemm_error() == 0
