@@ -50,6 +50,7 @@ struct Params {
     int k_tiles_per_split, k_tiles_total;
     const float *bias;   // may be null
     int relu;
+    int a_mn;            // A stored [K, M] (M contiguous) instead of [M, K]
     int b_mn;            // B stored [K, N] (N contiguous) instead of [N, K]
     const __nv_bfloat16 *mask;  // row-major [M, ldm]: zero where mask <= 0 (may be null)
     int ldm;
@@ -121,8 +122,9 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 // Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, both
 // K-major, N >> 3 at bit 17, M >> 4 at bit 24.
 constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-// B given MN-major (stored [K, N], N contiguous): "transpose B" bit 16.
-constexpr uint32_t IDESC_BMN = IDESC | (1u << 16);
+// A given MN-major (stored [K, M]): "transpose A" bit 15; B given MN-major
+// (stored [K, N], N contiguous): "transpose B" bit 16.
+constexpr uint32_t IDESC_AMN = 1u << 15, IDESC_BMN_BIT = 1u << 16;
 
 __device__ __forceinline__ void mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate,
                                     uint32_t idesc = IDESC) {
@@ -216,7 +218,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (it >= STAGES) inflight_lo = it - STAGES + 1;
                 const uint32_t a_dst = smem_u32(smem + s * STAGE_BYTES), b_dst = a_dst + A_BYTES;
                 mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
-                tma_load_2d(a_dst, &map_a, full0 + 8 * s, kt * BK, mt * BM);
+                if (p.a_mn) {
+#pragma unroll
+                    for (int j = 0; j < BM / 64; j++)
+                        tma_load_2d(a_dst + j * 8192, &map_a, full0 + 8 * s, mt * BM + 64 * j, kt * BK);
+                } else {
+                    tma_load_2d(a_dst, &map_a, full0 + 8 * s, kt * BK, mt * BM);
+                }
                 if (p.b_mn) {
 #pragma unroll
                     for (int j = 0; j < BN / 64; j++)
@@ -257,9 +265,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES), b_base = a_base + A_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; kk++)
-                    mma(acc, sw128_desc(a_base + kk * 32),
+                    mma(acc, p.a_mn ? sw128_mn_desc(a_base + kk * 2048) : sw128_desc(a_base + kk * 32),
                         p.b_mn ? sw128_mn_desc(b_base + kk * 2048) : sw128_desc(b_base + kk * 32),
-                        (kt > kt0 || kk > 0) ? 1u : 0u, p.b_mn ? IDESC_BMN : IDESC);
+                        (kt > kt0 || kk > 0) ? 1u : 0u,
+                        IDESC | (p.a_mn ? IDESC_AMN : 0u) | (p.b_mn ? IDESC_BMN_BIT : 0u));
                 mma_commit(empty0 + 8 * s);
             }
             mma_commit(accf0 + 8 * b);
@@ -493,11 +502,11 @@ extern "C" {
 
 static int gemm_launch(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias,
                        int relu, const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf,
-                       int splits, int b_mn, void *stream) {
+                       int splits, int a_mn, int b_mn, void *stream) {
     if (M <= 0 || N <= 0 || K <= 0 || !a || !b || (!c && !ct && !cf) || splits < 1) return D1_ERR_BAD_ARGUMENT;
     // TMA rules: 16-byte aligned bases and row pitches.
     if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) || (lda * 2) % 16 ||
-        (ldb * 2) % 16 || lda < K || ldb < (b_mn ? N : K))
+        (ldb * 2) % 16 || lda < (a_mn ? M : K) || ldb < (b_mn ? N : K))
         return D1_ERR_BAD_ARGUMENT;
     if (c && ((reinterpret_cast<uintptr_t>(c) & 15) || ldc % 8 || ldc < N)) return D1_ERR_BAD_ARGUMENT;
     if (cf && ((reinterpret_cast<uintptr_t>(cf) & 15) || ldcf % 4 || ldcf < N)) return D1_ERR_BAD_ARGUMENT;
@@ -509,11 +518,11 @@ static int gemm_launch(const void *a, int lda, const void *b, int ldb, int M, in
     const int per = (kt + splits - 1) / splits;
     splits = (kt + per - 1) / per;  // every split gets at least one K block
     CUtensorMap ma, mb;
-    if (!make_map(&ma, a, M, K, lda, BM)) return D1_ERR_BAD_ARGUMENT;
+    if (!(a_mn ? make_map(&ma, a, K, M, lda, 64) : make_map(&ma, a, M, K, lda, BM))) return D1_ERR_BAD_ARGUMENT;
     // B [N, K]: boxes of BN rows x 64 K; B [K, N]: boxes of 64 K rows x 64 N
     if (!(b_mn ? make_map(&mb, b, K, N, ldb, 64) : make_map(&mb, b, N, K, ldb, BN))) return D1_ERR_BAD_ARGUMENT;
     if (int e = gemm_attr()) return e;
-    Params p{M, N, K, per, kt, bias, relu, b_mn, (const __nv_bfloat16 *)mask, ldm, (__nv_bfloat16 *)c, ldc,
+    Params p{M, N, K, per, kt, bias, relu, a_mn, b_mn, (const __nv_bfloat16 *)mask, ldm, (__nv_bfloat16 *)c, ldc,
              (__nv_bfloat16 *)ct, ldct, cf, ldcf};
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n * splits;
@@ -531,13 +540,21 @@ static int gemm_launch(const void *a, int lda, const void *b, int ldb, int M, in
 int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
             const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits,
             void *stream) {
-    return gemm_launch(a, lda, b, ldb, M, N, K, bias, relu, mask, ldm, c, ldc, ct, ldct, cf, ldcf, splits, 0, stream);
+    return gemm_launch(a, lda, b, ldb, M, N, K, bias, relu, mask, ldm, c, ldc, ct, ldct, cf, ldcf, splits, 0, 0,
+                       stream);
+}
+
+int d1_gemm_ex(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,
+               const float *bias, int relu, const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf,
+               int ldcf, int splits, void *stream) {
+    return gemm_launch(a, lda, b, ldb, M, N, K, bias, relu, mask, ldm, c, ldc, ct, ldct, cf, ldcf, splits, a_mn != 0,
+                       b_mn != 0, stream);
 }
 
 int d1_gemm_bkn(const void *a, int lda, const void *b_kn, int ldb, int M, int N, int K, const float *bias, int relu,
                 void *c, int ldc, float *cf, int ldcf, int splits, void *stream) {
-    return gemm_launch(a, lda, b_kn, ldb, M, N, K, bias, relu, nullptr, 0, c, ldc, nullptr, 0, cf, ldcf, splits, 1,
-                       stream);
+    return gemm_launch(a, lda, b_kn, ldb, M, N, K, bias, relu, nullptr, 0, c, ldc, nullptr, 0, cf, ldcf, splits, 0,
+                       1, stream);
 }
 
 int d1_gemm_head_sample(const void *a, int lda, const void *b, int ldb, int M, int K, const float *bias,
@@ -551,7 +568,7 @@ int d1_gemm_head_sample(const void *a, int lda, const void *b, int ldb, int M, i
     CUtensorMap ma, mb;
     if (!make_map(&ma, a, M, K, lda, BM) || !make_map(&mb, b, BN, K, ldb, BN)) return D1_ERR_BAD_ARGUMENT;
     if (int e = gemm_attr()) return e;
-    Params p{M, BN, K, kt, kt, bias, 1, 0, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0,
+    Params p{M, BN, K, kt, kt, bias, 1, 0, 0, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0,
              1, (const __nv_bfloat16 *)wh_bf16, bh, legal, seed, step, first_env, action, logp, value, logits};
     const int tiles = (M + BM - 1) / BM;
     int dev = 0, sms = 0;

@@ -780,6 +780,29 @@ __global__ void __launch_bounds__(256) row_sum_bf16_kernel(const __nv_bfloat16 *
     }
 }
 
+// Column sums of a bf16 [rows, cols] matrix (pitch ld) in two deterministic
+// passes: block (x, y) sums rows [y*CS_ROWS, (y+1)*CS_ROWS) of 32 columns
+// (8 thread groups of every 8th row, added in group order) into
+// part[y][cols]; sum_rows_kernel then adds the chunk partials in chunk order.
+constexpr int CS_ROWS = 128;
+__global__ void __launch_bounds__(256) col_sum_bf16_kernel(const __nv_bfloat16 *__restrict__ m, int rows, int cols,
+                                                           int ld, float *__restrict__ part) {
+    __shared__ float ps[8][33];
+    const int cx = threadIdx.x & 31, gy = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + cx, r0 = blockIdx.y * CS_ROWS;
+    float acc = 0.f;
+    if (c < cols)
+        for (int r = r0 + gy; r < min(rows, r0 + CS_ROWS); r += 8) acc += __bfloat162float(m[(size_t)r * ld + c]);
+    ps[gy][cx] = acc;
+    __syncthreads();
+    if (gy == 0 && c < cols) {
+        float t = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; g++) t += ps[g][cx];
+        part[(size_t)blockIdx.y * cols + c] = t;
+    }
+}
+
 // ------------------------------------------------------------------ optimizer
 // sum of squares of g[0..n) into *out (double, accumulated)
 __global__ void __launch_bounds__(256) sumsq_kernel(const float *__restrict__ g, int64_t n, double *out) {
@@ -954,6 +977,17 @@ int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, v
     const int groups = splits >= 32 ? ppo::RS_GROUPS : splits >= 16 ? 2 : 1;
     ppo::reduce_slabs_kernel<<<(unsigned)((n + ppo::RS_COLS - 1) / ppo::RS_COLS), ppo::RS_COLS * groups, 0,
                                (cudaStream_t)stream>>>(slabs, splits, count, out);
+    return (int)cudaGetLastError();
+}
+
+int d1_col_sum_part_len(int rows, int cols) { return ((rows + ppo::CS_ROWS - 1) / ppo::CS_ROWS) * cols; }
+
+int d1_col_sum_bf16(const void *m, int rows, int cols, int ld, float *part, float *out, void *stream) {
+    if (!m || !part || !out || rows <= 0 || cols <= 0 || ld < cols) return D1_ERR_BAD_ARGUMENT;
+    const int chunks = (rows + ppo::CS_ROWS - 1) / ppo::CS_ROWS;
+    const dim3 grid((cols + 31) / 32, chunks);
+    ppo::col_sum_bf16_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16 *)m, rows, cols, ld, part);
+    ppo::sum_rows_kernel<<<(cols + 31) / 32, 256, 0, (cudaStream_t)stream>>>(part, chunks, cols, cols, out);
     return (int)cudaGetLastError();
 }
 

@@ -5,17 +5,20 @@ coefficients) and a switch for the reference loss (0.25 * MSE, no value clip).
 Per minibatch (all device work is libd1 kernels, launched on the current stream):
 
   gather     X = obs[idx]                          d1_ppo_gather
-  layer 1    h1 = relu(X W1^T + b1), h1^T          d1_gemm (tcgen05)
+  layer 1    h1 = relu(X W1^T + b1)                d1_gemm (tcgen05)
   layer 2    h2 = relu(h1 W2^T + b2)               d1_gemm
-  loss       head, PPO loss, dlogits/dvalue,       d1_ppo_loss (fused)
-             dh2 = dhead Wh * relu'(h2), dh2^T, partials of dWh, dbh, db2
-  dW2        dh2^T h1 (split-K fp32 slabs)         d1_gemm + d1_reduce_slabs
-  dh1^T      (dh2 W2) * relu'(h1), transposed      d1_gemm (mask epilogue)
-  dW1        dh1^T X (split-K fp32 slabs; X read    d1_gemm_bkn + d1_reduce_slabs
-             as the MN-major B operand, no X^T)
-  db1        row sums of dh1^T                     d1_row_sum_bf16
+  loss       head, PPO loss, dlogits/dvalue,       d1_ppo_loss (fused, warp MMAs)
+             dh2 = dhead Wh * relu'(h2), partials of dWh, dbh, db2
+  dW2        dh2^T h1 (split-K fp32 slabs)         d1_gemm_ex + d1_reduce_slabs
+  dh1        (dh2 W2) * relu'(h1)                  d1_gemm (mask epilogue)
+  dW1        dh1^T X (split-K fp32 slabs)          d1_gemm_ex + d1_reduce_slabs
+  db1        column sums of dh1                    d1_col_sum_bf16
   all-reduce flat fp32 gradient (NCCL, multi-GPU)  torch.distributed
   optimizer  grad-norm clip + Adam + bf16 copies   d1_sumsq + d1_adam
+
+The weight-gradient GEMMs read dh2, h1, dh1 and X as stored (row-major, so
+[K, M] / [K, N] with K = samples): their tensor-core operands are MN-major and
+no kernel writes a transposed copy.
 
 The gradient of every minibatch is a mean over that rank's minibatch; with R
 ranks the all-reduced gradient is divided by R, so it equals the gradient of the
@@ -66,11 +69,10 @@ class PPO:
         mb = minibatch
         self.x = torch.empty((mb, OBS), **bf)
         self.h1 = torch.empty((mb, HID), **bf)
-        self.h1t = torch.empty((HID, mb), **bf)
         self.h2 = torch.empty((mb, HID), **bf)
         self.dh2 = torch.empty((mb, HID), **bf)
-        self.dh2t = torch.empty((HID, mb), **bf)
-        self.dh1t = torch.empty((HID, mb), **bf)
+        self.dh1 = torch.empty((mb, HID), **bf)
+        self.colsum_part = torch.empty(self.lib.d1_col_sum_part_len(mb, HID), **f32)
         self.s1 = G.splits_for(mb, splits)
         self.slab1 = torch.empty((self.s1, HID, OBS), **f32)
         # dW2 is 256 x 256: its output has only 2 tiles, so it needs 8x the K splits
@@ -123,13 +125,13 @@ class PPO:
         obs = r.obs[:r.T].reshape(self.total, OBS)
         check(lib.d1_ppo_gather(obs.data_ptr(), OBS, idx.data_ptr(), mb, self.x.data_ptr(), None, mb, s),
               'd1_ppo_gather')
-        p.hidden_layers(self.x, h1=self.h1, h1t=self.h1t, h2=self.h2)
+        p.hidden_layers(self.x, h1=self.h1, h2=self.h2)
         g = self.grad
         check(lib.d1_ppo_loss(self.h2.data_ptr(), p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(),
                               idx.data_ptr(), r.legal.data_ptr(), r.actions.data_ptr(), r.logp.data_ptr(),
                               self.adv.data_ptr(), self.ret.data_ptr(), r.values.data_ptr(), self.stats.data_ptr(),
                               self.adv_count, mb, self.clip, self.vclip, self.vf_coef, self.ent_coef,
-                              self.dh2.data_ptr(), self.dh2t.data_ptr(), mb, self.part.data_ptr(), self.loss_blocks,
+                              self.dh2.data_ptr(), None, mb, self.part.data_ptr(), self.loss_blocks,
                               s), 'd1_ppo_loss')
         # dWh, dbh, db2 straight into the flat gradient; loss terms aside
         check(lib.d1_sum_rows(self.part.data_ptr(), self.loss_blocks, self.part_len, self.head_len,
@@ -137,14 +139,15 @@ class PPO:
         check(lib.d1_sum_rows(self.part[:, self.head_len:].data_ptr(), self.loss_blocks, self.part_len, 8,
                               self.terms.data_ptr(), s), 'd1_sum_rows')
         # dW2 = dh2^T h1
-        G.gemm(self.dh2t, self.h1t, out_f32=self.slab2, splits=self.s2)
+        G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
         check(lib.d1_reduce_slabs(self.slab2.data_ptr(), self.s2, HID * HID, g[self.off['w2']:].data_ptr(), s))
-        # dh1^T = ((dh2 W2) * relu'(h1))^T
-        G.gemm(self.dh2, p.bf16['w2t'], mask=self.h1, out_t=self.dh1t)
-        # dW1 = dh1^T X (X read as the MN-major operand), db1 = row sums of dh1^T
-        G.gemm_bkn(self.dh1t, self.x, out_f32=self.slab1, splits=self.s1)
+        # dh1 = (dh2 W2) * relu'(h1)
+        G.gemm(self.dh2, p.bf16['w2t'], mask=self.h1, out=self.dh1)
+        # dW1 = dh1^T X, db1 = column sums of dh1
+        G.gemm_ex(self.dh1, self.x, a_kn=True, b_kn=True, out_f32=self.slab1, splits=self.s1)
         check(lib.d1_reduce_slabs(self.slab1.data_ptr(), self.s1, HID * OBS, g[self.off['w1']:].data_ptr(), s))
-        check(lib.d1_row_sum_bf16(self.dh1t.data_ptr(), HID, mb, mb, g[self.off['b1']:].data_ptr(), s))
+        check(lib.d1_col_sum_bf16(self.dh1.data_ptr(), mb, HID, HID, self.colsum_part.data_ptr(),
+                                  g[self.off['b1']:].data_ptr(), s), 'd1_col_sum_bf16')
         if self.group is not None:
             import torch.distributed as dist
             dist.all_reduce(g, group=self.group)

@@ -201,6 +201,11 @@ int d1_gemm_splits(int K, int splits);
  * (fp32 split-K slabs) only. */
 int d1_gemm_bkn(const void *a, int lda, const void *b_kn, int ldb, int M, int N, int K, const float *bias, int relu,
                 void *c, int ldc, float *cf, int ldcf, int splits, void *stream);
+/* The general form: a_mn / b_mn select A stored [K, M] / B stored [K, N]
+ * (M / N contiguous) instead of [M, K] / [N, K]; other arguments as d1_gemm. */
+int d1_gemm_ex(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,
+               const float *bias, int relu, const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf,
+               int ldcf, int splits, void *stream);
 /* The policy's second layer with the head and sampler fused into the GEMM
  * epilogue: h = ReLU(A . B^T + bias) with N = 256 (B bf16 [256, K]), never
  * stored; logits/value = bf16(h) . wh^T + bh (wh bf16 [13, 256], bh f32 [13]);
@@ -320,6 +325,11 @@ int d1_sum_rows(const float *parts, int nparts, int stride, int len, float *out,
 int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, void *stream);
 /* out[r] = sum of row r of bf16 m [rows, cols] (pitch ld): bias gradients. */
 int d1_row_sum_bf16(const void *m, int rows, int cols, int ld, float *out, void *stream);
+/* out[c] = sum over rows of a bf16 [rows, cols] matrix (pitch ld), in chunks
+ * of 128 rows: part is a caller workspace of d1_col_sum_part_len(rows, cols)
+ * floats; chunk partials are added in order (deterministic). */
+int d1_col_sum_part_len(int rows, int cols);
+int d1_col_sum_bf16(const void *m, int rows, int cols, int ld, float *part, float *out, void *stream);
 /* *out += sum g[i]^2 (double), deterministic like d1_gae's statistics (calls on
  * one device must not overlap). */
 int d1_sumsq(const float *g, int64_t n, double *out, void *stream);

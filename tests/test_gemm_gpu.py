@@ -82,3 +82,25 @@ def test_b_stored_k_by_n(G, M, N, K, splits):
     got = slabs[:, :, :N].sum(0)
     assert torch.allclose(got, ref, rtol=1e-3, atol=1e-3 * ref.abs().max().item())
     assert G.gemm_error() == 0
+
+
+@pytest.mark.parametrize('M,N,K,splits', [(256, 256, 16384, 64), (256, 1832, 16384, 8), (192, 100, 320, 1)])
+def test_both_operands_stored_k_major_rows(G, M, N, K, splits):
+    """d1_gemm_ex with A stored [K, M] and B stored [K, N] (both MN-major
+    operands): the weight-gradient shape dW = dY^T X of the PPO backward."""
+    g = torch.Generator(device='cuda').manual_seed(M * 7 + N + K)
+    ld = (N + 7) // 8 * 8  # TMA row pitches are multiples of 16 bytes
+    lm = (M + 7) // 8 * 8
+    a_km = (torch.randn(K, lm, device='cuda', generator=g) / K ** 0.5).to(torch.bfloat16)[:, :M]
+    b_kn = torch.randn(K, ld, device='cuda', generator=g).to(torch.bfloat16)[:, :N]
+    ref = a_km.float().T @ b_kn.float()
+    used = G.splits_for(K, splits)
+    slabs = torch.empty((used, M, ld), device='cuda')
+    G.gemm_ex(a_km, b_kn, a_kn=True, b_kn=True, out_f32=slabs[:, :, :N], splits=splits)
+    got = slabs[:, :, :N].sum(0)
+    assert torch.allclose(got, ref, rtol=1e-3, atol=1e-3 * ref.abs().max().item())
+    if splits == 1:
+        out = torch.empty((M, ld), dtype=torch.bfloat16, device='cuda')[:, :N]
+        G.gemm_ex(a_km, b_kn, a_kn=True, b_kn=True, out=out)
+        assert torch.allclose(out.float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
+    assert G.gemm_error() == 0
