@@ -25,6 +25,7 @@ REPO = pathlib.Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / 'dcss-auto_b200'))
 
 METRIC = 'env decisions/sec (sim+policy, device-timed)'
+ENV_TRAFFIC_BYTES = 455.4e6  # step_kernel DRAM bytes per 65,536-env launch (ncu: 135.0 MB read + 320.4 MB write)
 UNIT = 'decisions/s'
 ENVS, HORIZON = 65536, 128
 # Algorithmic bytes per decision of the env step (sim + bf16 observation write):
@@ -387,7 +388,10 @@ def run_ours(args, rank, world, local_rank):
                    'l2': 'inputs larger than L2 (240 MB obs slot + 134 MB env state per step)'},
         'roofline': {'kernel': 'd1::spec::step_kernel', 'bound': 'hbm', 'achieved': achieved,
                      'peak': pk['hbm_gbs'], 'unit': 'GB/s', 'frac': achieved / pk['hbm_gbs'],
-                     'traffic': None, 'peak_kind': pk_kind,
+                     # DRAM read + write of one launch at 65,536 envs, from the ncu
+                     # capture summarised in profiles/spec_step_kernel_config1.md
+                     'traffic': ENV_TRAFFIC_BYTES * B / 65536, 'traffic_unit': 'bytes per launch (ncu)',
+                     'peak_kind': pk_kind,
                      'algorithmic_bytes_per_decision': ENV_BYTES_PER_DECISION,
                      'kernel_ms_per_step': env_ms},
         'roofline_policy_gemm': {'kernel': 'd1::tc::gemm_kernel (layer 1: M=%d, N=256, K=1832)' % B,
