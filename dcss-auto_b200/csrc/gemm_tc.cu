@@ -51,6 +51,8 @@ struct Params {
     const float *bias;   // may be null
     int relu;
     int a_mn;            // A stored [K, M] (M contiguous) instead of [M, K]
+    const int64_t *a_rows;  // A row m = row a_rows[m] of a [rows, K] table (K-major A; null: plain)
+    const int64_t *b_rows;  // B K-row k = row b_rows[k] of a [rows, N] table (MN-major B; null: plain)
     int b_mn;            // B stored [K, N] (N contiguous) instead of [N, K]
     const __nv_bfloat16 *mask;  // row-major [M, ldm]: zero where mask <= 0 (may be null)
     int ldm;
@@ -101,6 +103,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+// tile::gather4: four rows r[0..3] of a tensor map whose box is one row of 64
+// elements, landing as four consecutive 128-byte rows at dst (swizzled by the map).
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, const int *r) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(bar)
         : "memory");
 }
 __device__ __forceinline__ bool full_cols_m(int col0, int n) { return col0 + 32 <= n; }
@@ -201,40 +212,76 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // ---- TMA producer: k blocks of every tile of this CTA, one ring
+    if (warp == 0) {
+        // ---- TMA producer warp: k blocks of every tile of this CTA, one ring.
+        // Lane 0 owns the barriers and the plain tile loads; with gathered rows
+        // (a_rows / b_rows) every lane issues tile::gather4 loads of 4 rows.
         int it = 0, inflight_lo = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles_total && ok; t += gridDim.x) {
             const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
             const int kt0 = split * p.k_tiles_per_split;
             const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
+            // A rows of this tile for gathered A: lane l owns rows 4l .. 4l+3
+            int ar[4] = {0, 0, 0, 0};
+            if (p.a_rows) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int m = mt * BM + 4 * lane + i;
+                    ar[i] = m < p.M ? (int)p.a_rows[m] : (int)p.a_rows[0];
+                }
+            }
             for (int kt = kt0; kt < kt1; kt++, it++) {
                 const int s = it % STAGES;
-                if (it >= STAGES && !mbar_wait(empty0 + 8 * s, ((uint32_t)(it / STAGES) & 1u) ^ 1u)) {
+                int good = 1;
+                if (lane == 0 && it >= STAGES && !mbar_wait(empty0 + 8 * s, ((uint32_t)(it / STAGES) & 1u) ^ 1u))
+                    good = 0;
+                if (!__shfl_sync(0xffffffffu, good, 0)) {
                     ok = false;
                     break;
                 }
                 if (it >= STAGES) inflight_lo = it - STAGES + 1;
                 const uint32_t a_dst = smem_u32(smem + s * STAGE_BYTES), b_dst = a_dst + A_BYTES;
-                mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
-                if (p.a_mn) {
+                if (lane == 0) mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
+                __syncwarp();
+                if (p.a_rows) {
+                    tma_gather4(a_dst + lane * 512, &map_a, full0 + 8 * s, kt * BK, ar);
+                } else if (lane == 0) {
+                    if (p.a_mn) {
 #pragma unroll
-                    for (int j = 0; j < BM / 64; j++)
-                        tma_load_2d(a_dst + j * 8192, &map_a, full0 + 8 * s, mt * BM + 64 * j, kt * BK);
-                } else {
-                    tma_load_2d(a_dst, &map_a, full0 + 8 * s, kt * BK, mt * BM);
+                        for (int j = 0; j < BM / 64; j++)
+                            tma_load_2d(a_dst + j * 8192, &map_a, full0 + 8 * s, mt * BM + 64 * j, kt * BK);
+                    } else {
+                        tma_load_2d(a_dst, &map_a, full0 + 8 * s, kt * BK, mt * BM);
+                    }
                 }
-                if (p.b_mn) {
+                if (p.b_rows) {
+                    // MN-major B from gathered K rows: lanes 0-15 load N chunks 0 and 2,
+                    // lanes 16-31 chunks 1 and 3; lane l % 16 owns K rows 4(l%16) .. +3
+                    const int q = lane & 15, c0 = lane >> 4;
+                    int br[4];
 #pragma unroll
-                    for (int j = 0; j < BN / 64; j++)
-                        tma_load_2d(b_dst + j * 8192, &map_b, full0 + 8 * s, nt * BN + 64 * j, kt * BK);
-                } else {
-                    tma_load_2d(b_dst, &map_b, full0 + 8 * s, kt * BK, nt * BN);
+                    for (int i = 0; i < 4; i++) {
+                        const int k = kt * BK + 4 * q + i;
+                        br[i] = k < p.K ? (int)p.b_rows[k] : (int)p.b_rows[0];
+                    }
+#pragma unroll
+                    for (int cc = 0; cc < 2; cc++) {
+                        const int j = c0 + 2 * cc;
+                        tma_gather4(b_dst + j * 8192 + q * 512, &map_b, full0 + 8 * s, nt * BN + 64 * j, br);
+                    }
+                } else if (lane == 0) {
+                    if (p.b_mn) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; j++)
+                            tma_load_2d(b_dst + j * 8192, &map_b, full0 + 8 * s, nt * BN + 64 * j, kt * BK);
+                    } else {
+                        tma_load_2d(b_dst, &map_b, full0 + 8 * s, kt * BK, nt * BN);
+                    }
                 }
             }
         }
-        if (!ok) {
+        if (!ok && lane == 0) {
             atomicExch(&g_error, 1);
             for (int i = inflight_lo; i < it; i++) mbar_wait(full0 + 8 * (i % STAGES), (uint32_t)(i / STAGES) & 1u);
         }
@@ -502,7 +549,10 @@ extern "C" {
 
 static int gemm_launch(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias,
                        int relu, const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf,
-                       int splits, int a_mn, int b_mn, void *stream) {
+                       int splits, int a_mn, int b_mn, void *stream, const int64_t *a_rows = nullptr,
+                       int a_table_rows = 0, const int64_t *b_rows = nullptr, int b_table_rows = 0) {
+    if ((a_rows && (a_mn || a_table_rows <= 0)) || (b_rows && (!b_mn || b_table_rows <= 0)))
+        return D1_ERR_BAD_ARGUMENT;
     if (M <= 0 || N <= 0 || K <= 0 || !a || !b || (!c && !ct && !cf) || splits < 1) return D1_ERR_BAD_ARGUMENT;
     // TMA rules: 16-byte aligned bases and row pitches.
     if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) || (lda * 2) % 16 ||
@@ -518,11 +568,20 @@ static int gemm_launch(const void *a, int lda, const void *b, int ldb, int M, in
     const int per = (kt + splits - 1) / splits;
     splits = (kt + per - 1) / per;  // every split gets at least one K block
     CUtensorMap ma, mb;
-    if (!(a_mn ? make_map(&ma, a, K, M, lda, 64) : make_map(&ma, a, M, K, lda, BM))) return D1_ERR_BAD_ARGUMENT;
+    // A [M, K]: boxes of BM rows x 64 K; A [K, M]: 64 K rows x 64 M; gathered A
+    // rows: one-row boxes of the [a_table_rows, K] table (tile::gather4)
+    if (!(a_rows  ? make_map(&ma, a, a_table_rows, K, lda, 1)
+          : a_mn ? make_map(&ma, a, K, M, lda, 64)
+                 : make_map(&ma, a, M, K, lda, BM)))
+        return D1_ERR_BAD_ARGUMENT;
     // B [N, K]: boxes of BN rows x 64 K; B [K, N]: boxes of 64 K rows x 64 N
-    if (!(b_mn ? make_map(&mb, b, K, N, ldb, 64) : make_map(&mb, b, N, K, ldb, BN))) return D1_ERR_BAD_ARGUMENT;
+    if (!(b_rows ? make_map(&mb, b, b_table_rows, N, ldb, 1)
+          : b_mn ? make_map(&mb, b, K, N, ldb, 64)
+                 : make_map(&mb, b, N, K, ldb, BN)))
+        return D1_ERR_BAD_ARGUMENT;
     if (int e = gemm_attr()) return e;
-    Params p{M, N, K, per, kt, bias, relu, a_mn, b_mn, (const __nv_bfloat16 *)mask, ldm, (__nv_bfloat16 *)c, ldc,
+    Params p{M, N, K, per, kt, bias, relu, a_mn, a_rows, b_rows, b_mn, (const __nv_bfloat16 *)mask, ldm,
+             (__nv_bfloat16 *)c, ldc,
              (__nv_bfloat16 *)ct, ldct, cf, ldcf};
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n * splits;
@@ -551,6 +610,13 @@ int d1_gemm_ex(const void *a, int lda, int a_mn, const void *b, int ldb, int b_m
                        b_mn != 0, stream);
 }
 
+int d1_gemm_rows(const void *a, int lda, int a_mn, const int64_t *a_rows, int a_table_rows, const void *b, int ldb,
+                 int b_mn, const int64_t *b_rows, int b_table_rows, int M, int N, int K, const float *bias, int relu,
+                 const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf, int splits, void *stream) {
+    return gemm_launch(a, lda, b, ldb, M, N, K, bias, relu, mask, ldm, c, ldc, nullptr, 0, cf, ldcf, splits,
+                       a_mn != 0, b_mn != 0, stream, a_rows, a_table_rows, b_rows, b_table_rows);
+}
+
 int d1_gemm_bkn(const void *a, int lda, const void *b_kn, int ldb, int M, int N, int K, const float *bias, int relu,
                 void *c, int ldc, float *cf, int ldcf, int splits, void *stream) {
     return gemm_launch(a, lda, b_kn, ldb, M, N, K, bias, relu, nullptr, 0, c, ldc, nullptr, 0, cf, ldcf, splits, 0,
@@ -568,7 +634,7 @@ int d1_gemm_head_sample(const void *a, int lda, const void *b, int ldb, int M, i
     CUtensorMap ma, mb;
     if (!make_map(&ma, a, M, K, lda, BM) || !make_map(&mb, b, BN, K, ldb, BN)) return D1_ERR_BAD_ARGUMENT;
     if (int e = gemm_attr()) return e;
-    Params p{M, BN, K, kt, kt, bias, 1, 0, 0, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0,
+    Params p{M, BN, K, kt, kt, bias, 1, 0, nullptr, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0,
              1, (const __nv_bfloat16 *)wh_bf16, bh, legal, seed, step, first_env, action, logp, value, logits};
     const int tiles = (M + BM - 1) / BM;
     int dev = 0, sms = 0;

@@ -40,6 +40,7 @@ SIGNATURES = {
     'd1_counter_add': [_P, C.c_int64, _P],
     'd1_gemm_splits': [_I, _I],
     'd1_gemm_bkn': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _I, _P],
+    'd1_gemm_rows': [_P, _I, _I, _P, _I, _P, _I, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_ex': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_col_sum_part_len': [_I, _I],
     'd1_col_sum_bf16': [_P, _I, _I, _I, _P, _P, _P],

@@ -76,3 +76,28 @@ def gemm_ex(a, b, a_kn=False, b_kn=False, bias=None, relu=False, out=None, out_t
                                p(out_f32), 0 if out_f32 is None else out_f32.stride(-2), splits, _stream(a)),
           'd1_gemm_ex')
     return out if out is not None else (out_t if out_t is not None else out_f32)
+
+
+def gemm_rows(a, b, M=None, a_rows=None, b_rows=None, a_kn=False, b_kn=False, bias=None, relu=False, out=None,
+              out_f32=None, splits=1, mask=None):
+    """gemm_ex with gathered operands: with a_rows (int64 [M]), A's row m is row
+    a_rows[m] of the table a [rows, K]; with b_rows (int64 [K], b_kn), B's K-row k
+    is row b_rows[k] of the table b [rows, N]."""
+    if a_rows is not None:
+        M, K = a_rows.shape[0], a.shape[1]
+    else:
+        M, K = (a.shape[1], a.shape[0]) if a_kn else a.shape
+    if b_rows is not None:
+        assert b_kn and b_rows.shape[0] == K
+        N = b.shape[1]
+    else:
+        N = b.shape[1] if b_kn else b.shape[0]
+    if out is None and out_f32 is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    p = lambda t: None if t is None else t.data_ptr()
+    check(library().d1_gemm_rows(a.data_ptr(), a.stride(0), int(a_kn), p(a_rows), a.shape[0] if a_rows is not None else 0,
+                                 b.data_ptr(), b.stride(0), int(b_kn), p(b_rows), b.shape[0] if b_rows is not None else 0,
+                                 M, N, K, p(bias), int(relu), p(mask), 0 if mask is None else mask.stride(0), p(out),
+                                 0 if out is None else out.stride(0), p(out_f32),
+                                 0 if out_f32 is None else out_f32.stride(-2), splits, _stream(a)), 'd1_gemm_rows')
+    return out if out is not None else out_f32

@@ -201,6 +201,16 @@ int d1_gemm_splits(int K, int splits);
  * (fp32 split-K slabs) only. */
 int d1_gemm_bkn(const void *a, int lda, const void *b_kn, int ldb, int M, int N, int K, const float *bias, int relu,
                 void *c, int ldc, float *cf, int ldcf, int splits, void *stream);
+/* Gathered operands (TMA tile::gather4): with a_rows, row m of A is row
+ * a_rows[m] of the K-major table a [a_table_rows, K]; with b_rows (b_mn = 1),
+ * K-row k of B is row b_rows[k] of the table b [b_table_rows, N]. Other
+ * arguments as d1_gemm_ex (no transposed output). Measured for the PPO
+ * minibatch (rows of the rollout buffer): no faster than gathering X once into
+ * an L2-resident copy for layer 1, and 4x slower for dW1, whose tiles re-read
+ * the rows piecewise from HBM -- the update therefore gathers X once. */
+int d1_gemm_rows(const void *a, int lda, int a_mn, const int64_t *a_rows, int a_table_rows, const void *b, int ldb,
+                 int b_mn, const int64_t *b_rows, int b_table_rows, int M, int N, int K, const float *bias, int relu,
+                 const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf, int splits, void *stream);
 /* The general form: a_mn / b_mn select A stored [K, M] / B stored [K, N]
  * (M / N contiguous) instead of [M, K] / [N, K]; other arguments as d1_gemm. */
 int d1_gemm_ex(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,

@@ -104,3 +104,31 @@ def test_both_operands_stored_k_major_rows(G, M, N, K, splits):
         G.gemm_ex(a_km, b_kn, a_kn=True, b_kn=True, out=out)
         assert torch.allclose(out.float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
     assert G.gemm_error() == 0
+
+
+def test_gathered_rows_match_the_gathered_copy(G):
+    """d1_gemm_rows: A rows and MN-major B K-rows taken from a table through an
+    index array (TMA tile::gather4) equal the product over the explicit gather
+    -- the PPO's layer 1 and dW1 on a minibatch of the rollout buffer."""
+    g = torch.Generator(device='cuda').manual_seed(5)
+    rows, F, mb = 40000, 1832, 4096
+    table = (torch.randn(rows, F, device='cuda', generator=g) / F ** 0.5).to(torch.bfloat16)
+    idx = torch.randperm(rows, device='cuda', generator=g)[:mb]
+    x = table[idx]
+    w = torch.randn(256, F, device='cuda', generator=g).to(torch.bfloat16)
+    b = torch.randn(256, device='cuda', generator=g)
+    h_ref = torch.empty((mb, 256), dtype=torch.bfloat16, device='cuda')
+    G.gemm(x, w, bias=b, relu=True, out=h_ref)
+    h = G.gemm_rows(table, w, a_rows=idx, bias=b, relu=True)
+    assert torch.equal(h, h_ref)
+    dy = torch.randn(mb, 256, device='cuda', generator=g).to(torch.bfloat16)
+    used = G.splits_for(mb, 8)
+    s_ref = torch.empty((used, 256, F), device='cuda')
+    s = torch.empty((used, 256, F), device='cuda')
+    G.gemm_ex(dy, x, a_kn=True, b_kn=True, out_f32=s_ref, splits=8)
+    G.gemm_rows(dy, table, b_rows=idx, a_kn=True, b_kn=True, out_f32=s, splits=8)
+    assert torch.equal(s, s_ref)
+    # M tail: 1000 rows
+    h2 = G.gemm_rows(table, w, a_rows=idx[:1000], bias=b, relu=True)
+    assert torch.equal(h2, h_ref[:1000])
+    assert G.gemm_error() == 0
