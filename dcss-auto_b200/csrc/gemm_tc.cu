@@ -494,6 +494,289 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------- 2-SM pair kernel
+// A cluster of two CTAs computes one 256 x 256 tile with tcgen05.mma.cta_group::2
+// (M = 256): CTA rank r holds A rows m0 + 128r .. +127 and B rows (N)
+// n0 + 128r .. +127 of every K block in its own shared memory, so each SM
+// streams 32 KB per K block instead of 48 KB (A 16 KB + all of B's 32 KB) --
+// the B re-reads that bound the one-CTA kernel. Both CTAs' TMA loads complete
+// on the leader's (rank 0) full barrier; the leader's one thread issues the
+// MMAs and commits to the empty and accumulator barriers of both CTAs; each CTA
+// drains its own 128 TMEM lanes (its 128 rows of the tile) and arrives on the
+// leader's accumulator-empty barrier. Six 32 KB stages; accumulators
+// double-buffered (2 x 256 columns). Epilogue: bias, ReLU, ReLU-mask, bf16 and
+// split-K fp32 slabs (no transposed output, no fused head).
+constexpr int P_STAGES = 6, P_B_BYTES = 128 * BK * 2, P_STAGE_BYTES = A_BYTES + P_B_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + BIAS_BYTES;
+constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory that completes on the pair leader's barrier.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster, int x,
+                                                 int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+__device__ __forceinline__ void arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p,
+                     int tiles_m, int tiles_n, int tiles_total) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * P_STAGES + 4);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + P_STAGES);
+    const uint32_t accf0 = smem_u32(bars + 2 * P_STAGES), acce0 = smem_u32(bars + 2 * P_STAGES + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < P_STAGES; s++) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(accf0 + 8 * b, 1);
+            mbar_init(acce0 + 8 * b, 2 * EPI_WARPS);  // the epilogue warps of both CTAs
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(2 * TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer (both CTAs): this CTA's A rows and B half, signalling the leader
+        int it = 0, inflight_lo = 0;
+        bool ok = true;
+        for (int t = cluster; t < tiles_total && ok; t += clusters) {
+            const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
+            const int kt0 = split * p.k_tiles_per_split;
+            const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
+            const int m0 = mt * 256 + 128 * (int)rank, n0 = nt * BN + 128 * (int)rank;
+            for (int kt = kt0; kt < kt1; kt++, it++) {
+                const int s = it % P_STAGES;
+                if (it >= P_STAGES && !mbar_wait(empty0 + 8 * s, ((uint32_t)(it / P_STAGES) & 1u) ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                if (it >= P_STAGES) inflight_lo = it - P_STAGES + 1;
+                const uint32_t a_dst = smem_u32(smem + s * P_STAGE_BYTES), b_dst = a_dst + A_BYTES;
+                const uint32_t leader_full = mapa(full0 + 8 * s, 0);
+                if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * P_STAGE_BYTES);
+                if (p.a_mn) {
+#pragma unroll
+                    for (int j = 0; j < 2; j++) tma_load_2d_pair(a_dst + j * 8192, &map_a, leader_full, m0 + 64 * j, kt * BK);
+                } else {
+                    tma_load_2d_pair(a_dst, &map_a, leader_full, kt * BK, m0);
+                }
+                if (p.b_mn) {
+#pragma unroll
+                    for (int j = 0; j < 2; j++) tma_load_2d_pair(b_dst + j * 8192, &map_b, leader_full, n0 + 64 * j, kt * BK);
+                } else {
+                    tma_load_2d_pair(b_dst, &map_b, leader_full, kt * BK, n0);
+                }
+            }
+        }
+        if (!ok) {
+            atomicExch(&g_error, 5);
+            if (rank == 0)
+                for (int i = inflight_lo; i < it; i++) mbar_wait(full0 + 8 * (i % P_STAGES), (uint32_t)(i / P_STAGES) & 1u);
+        } else {
+            // the leader's last commits to this CTA's empty barriers land before it exits
+            for (int i = it > P_STAGES ? it - P_STAGES : 0; i < it; i++)
+                mbar_wait(empty0 + 8 * (i % P_STAGES), (uint32_t)(i / P_STAGES) & 1u);
+        }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ---- MMA issuer (leader only)
+        int it = 0, local = 0;
+        bool ok = true;
+        const uint32_t idesc = P_IDESC | (p.a_mn ? (1u << 15) : 0u) | (p.b_mn ? (1u << 16) : 0u);
+        for (int t = cluster; t < tiles_total && ok; t += clusters, local++) {
+            const int split = t / (tiles_m * tiles_n);
+            const int kt0 = split * p.k_tiles_per_split;
+            const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
+            const int b = local & 1;
+            const uint32_t acc = tmem + (uint32_t)(b * TMEM_COLS);
+            if (local >= 2 && !mbar_wait(acce0 + 8 * b, ((uint32_t)(local >> 1) & 1u) ^ 1u)) {
+                atomicExch(&g_error, 6);
+                ok = false;
+                break;
+            }
+            fence_after();
+            for (int kt = kt0; kt < kt1; kt++, it++) {
+                const int s = it % P_STAGES;
+                if (!mbar_wait(full0 + 8 * s, (uint32_t)(it / P_STAGES) & 1u)) {
+                    atomicExch(&g_error, 7);
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                const uint32_t a_base = smem_u32(smem + s * P_STAGE_BYTES), b_base = a_base + A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++)
+                    mma_pair(acc, p.a_mn ? sw128_mn_desc(a_base + kk * 2048) : sw128_desc(a_base + kk * 32),
+                             p.b_mn ? sw128_mn_desc(b_base + kk * 2048) : sw128_desc(b_base + kk * 32), idesc,
+                             (kt > kt0 || kk > 0) ? 1u : 0u);
+                commit_pair(empty0 + 8 * s);
+                commit_pair(mapa(empty0 + 8 * s, 1));
+            }
+            if (!ok) break;
+            commit_pair(accf0 + 8 * b);
+            commit_pair(mapa(accf0 + 8 * b, 1));
+        }
+    } else if (warp >= 2) {
+        // ---- epilogue (both CTAs): this CTA's 128 rows of the tile
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        float *bias_s = reinterpret_cast<float *>(smem + P_STAGES * P_STAGE_BYTES + 256) + (warp - 2) * (BN / 2);
+        int local = 0;
+        for (int t = cluster; t < tiles_total; t += clusters, local++) {
+            const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
+            const int b = local & 1;
+            const int row = mt * 256 + 128 * (int)rank + q * 32 + lane;
+            const int c0 = nt * BN + half * (BN / 2);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int col = c0 + lane * 4 + j;
+                bias_s[lane * 4 + j] = (p.bias && col < p.N) ? __ldg(p.bias + col) : 0.f;
+            }
+            __syncwarp();
+            if (!mbar_wait(accf0 + 8 * b, (uint32_t)(local >> 1) & 1u)) {
+                atomicExch(&g_error, 8);
+                break;
+            }
+            fence_after();
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 64; cc++) {
+                uint32_t v[32];
+                const uint32_t taddr = tmem + (uint32_t)(b * TMEM_COLS) + ((uint32_t)(q * 32) << 16) +
+                                       (uint32_t)(half * (BN / 2) + cc * 32);
+                __syncwarp();
+                D1_TMEM_LD32(taddr, v);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                const int col0 = c0 + cc * 32;
+                if (row >= p.M || col0 >= p.N) continue;
+                float f[32];
+                const float4 *bs = reinterpret_cast<const float4 *>(bias_s + cc * 32);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 bb = bs[j / 4];
+                    f[j] = __uint_as_float(v[j]) + bb.x;
+                    f[j + 1] = __uint_as_float(v[j + 1]) + bb.y;
+                    f[j + 2] = __uint_as_float(v[j + 2]) + bb.z;
+                    f[j + 3] = __uint_as_float(v[j + 3]) + bb.w;
+                }
+                if (p.relu) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) f[j] = fmaxf(f[j], 0.f);
+                }
+                const bool full_cols = col0 + 32 <= p.N;
+                if (p.mask) {
+                    const __nv_bfloat16 *mk = p.mask + (size_t)row * p.ldm + col0;
+                    if (full_cols) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            const uint4 raw = *reinterpret_cast<const uint4 *>(mk + j);
+                            const __nv_bfloat16 *h = reinterpret_cast<const __nv_bfloat16 *>(&raw);
+#pragma unroll
+                            for (int i = 0; i < 8; i++)
+                                if (!(__bfloat162float(h[i]) > 0.f)) f[j + i] = 0.f;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j >= p.N || !(__bfloat162float(mk[j]) > 0.f)) f[j] = 0.f;
+                    }
+                }
+                if (p.cf) {
+                    float *dst = p.cf + (size_t)split * p.M * p.ldcf + (size_t)row * p.ldcf + col0;
+                    if (full_cols) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4 *>(dst + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j < p.N) dst[j] = f[j];
+                    }
+                }
+                if (p.c) {
+                    __nv_bfloat16 *dst = p.c + (size_t)row * p.ldc + col0;
+                    if (full_cols) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            uint4 w;
+                            __nv_bfloat162 h0 = __floats2bfloat162_rn(f[j], f[j + 1]);
+                            __nv_bfloat162 h1 = __floats2bfloat162_rn(f[j + 2], f[j + 3]);
+                            __nv_bfloat162 h2 = __floats2bfloat162_rn(f[j + 4], f[j + 5]);
+                            __nv_bfloat162 h3 = __floats2bfloat162_rn(f[j + 6], f[j + 7]);
+                            w.x = *reinterpret_cast<uint32_t *>(&h0);
+                            w.y = *reinterpret_cast<uint32_t *>(&h1);
+                            w.z = *reinterpret_cast<uint32_t *>(&h2);
+                            w.w = *reinterpret_cast<uint32_t *>(&h3);
+                            *reinterpret_cast<uint4 *>(dst + j) = w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j < p.N) dst[j] = __float2bfloat16_rn(f[j]);
+                    }
+                }
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_cluster(mapa(acce0 + 8 * b, 0));
+        }
+    }
+    fence_before();
+    __syncthreads();
+    cluster_sync();  // no cross-CTA signal is outstanding past this point
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TMEM_COLS)
+                     : "memory");
+    }
+}
+
 // ---------------------------------------------------------------- host side
 typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -545,12 +828,30 @@ static int gemm_attr() {
     return 0;
 }
 
+// The pair kernel wins where each tile's K range is long (B traffic per SM
+// dominates): measured 1.2-1.3x on 512+-deep K ranges with N > 128, and no gain
+// on 256-deep ones.
+static bool pair_pays(int N, int K, int splits, bool ct, bool gathered) {
+    if (ct || gathered || N <= 128) return false;
+    const int kt = (K + BK - 1) / BK;
+    if (splits > kt) splits = kt;
+    const int per = (kt + splits - 1) / splits;
+    return per >= 8;
+}
+
 extern "C" {
+
+static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
+                       const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf, int splits, int a_mn,
+                       int b_mn, void *stream);
 
 static int gemm_launch(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias,
                        int relu, const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf,
                        int splits, int a_mn, int b_mn, void *stream, const int64_t *a_rows = nullptr,
-                       int a_table_rows = 0, const int64_t *b_rows = nullptr, int b_table_rows = 0) {
+                       int a_table_rows = 0, const int64_t *b_rows = nullptr, int b_table_rows = 0,
+                       bool allow_pair = true) {
+    if (allow_pair && splits >= 1 && pair_pays(N, K, splits, ct != nullptr, a_rows || b_rows))
+        return pair_launch(a, lda, b, ldb, M, N, K, bias, relu, mask, ldm, c, ldc, cf, ldcf, splits, a_mn, b_mn, stream);
     if ((a_rows && (a_mn || a_table_rows <= 0)) || (b_rows && (!b_mn || b_table_rows <= 0)))
         return D1_ERR_BAD_ARGUMENT;
     if (M <= 0 || N <= 0 || K <= 0 || !a || !b || (!c && !ct && !cf) || splits < 1) return D1_ERR_BAD_ARGUMENT;
@@ -610,6 +911,13 @@ int d1_gemm_ex(const void *a, int lda, int a_mn, const void *b, int ldb, int b_m
                        b_mn != 0, stream);
 }
 
+int d1_gemm_single(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,
+                   const float *bias, int relu, const void *mask, int ldm, void *c, int ldc, void *ct, int ldct,
+                   float *cf, int ldcf, int splits, void *stream) {
+    return gemm_launch(a, lda, b, ldb, M, N, K, bias, relu, mask, ldm, c, ldc, ct, ldct, cf, ldcf, splits, a_mn != 0,
+                       b_mn != 0, stream, nullptr, 0, nullptr, 0, false);
+}
+
 int d1_gemm_rows(const void *a, int lda, int a_mn, const int64_t *a_rows, int a_table_rows, const void *b, int ldb,
                  int b_mn, const int64_t *b_rows, int b_table_rows, int M, int N, int K, const float *bias, int relu,
                  const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf, int splits, void *stream) {
@@ -643,6 +951,65 @@ int d1_gemm_head_sample(const void *a, int lda, const void *b, int ldb, int M, i
     const int grid = tiles < sms ? tiles : sms;
     gemm_kernel<true><<<grid, THREADS, SMEM_HEAD_BYTES, (cudaStream_t)stream>>>(ma, mb, p, tiles, 1, tiles);
     return (int)cudaGetLastError();
+}
+
+// 2-SM pair kernel: 256 x 256 tiles (see gemm_pair_kernel). Same operands and
+// output forms as gemm_launch except the transposed output and row gathers.
+static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
+                       const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf, int splits, int a_mn,
+                       int b_mn, void *stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || !a || !b || (!c && !cf) || splits < 1) return D1_ERR_BAD_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) || (lda * 2) % 16 ||
+        (ldb * 2) % 16 || lda < (a_mn ? M : K) || ldb < (b_mn ? N : K))
+        return D1_ERR_BAD_ARGUMENT;
+    if (c && ((reinterpret_cast<uintptr_t>(c) & 15) || ldc % 8 || ldc < N)) return D1_ERR_BAD_ARGUMENT;
+    if (cf && ((reinterpret_cast<uintptr_t>(cf) & 15) || ldcf % 4 || ldcf < N)) return D1_ERR_BAD_ARGUMENT;
+    if (mask && ((reinterpret_cast<uintptr_t>(mask) & 15) || ldm % 8 || ldm < N)) return D1_ERR_BAD_ARGUMENT;
+    if (splits > 1 && c) return D1_ERR_BAD_ARGUMENT;
+    const int kt = (K + BK - 1) / BK;
+    if (splits > kt) splits = kt;
+    const int per = (kt + splits - 1) / splits;
+    splits = (kt + per - 1) / per;
+    CUtensorMap ma, mb;
+    // each CTA loads 128 rows (K-major) or two 64-wide MN atoms (MN-major) of A and of B
+    if (!(a_mn ? make_map(&ma, a, K, M, lda, 64) : make_map(&ma, a, M, K, lda, 128))) return D1_ERR_BAD_ARGUMENT;
+    if (!(b_mn ? make_map(&mb, b, K, N, ldb, 64) : make_map(&mb, b, N, K, ldb, 128))) return D1_ERR_BAD_ARGUMENT;
+    static uint64_t ready = 0;
+    int dev = 0;
+    if (cudaError_t e = cudaGetDevice(&dev)) return (int)e;
+    if (!(dev < 64 && ((ready >> dev) & 1))) {
+        if (cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 P_SMEM_BYTES))
+            return (int)e;
+        if (dev < 64) ready |= 1ull << dev;
+    }
+    Params p{M, N, K, per, kt, bias, relu, a_mn, nullptr, nullptr, b_mn, (const __nv_bfloat16 *)mask, ldm,
+             (__nv_bfloat16 *)c, ldc, nullptr, 0, cf, ldcf};
+    const int tiles_m = (M + 255) / 256, tiles_n = (N + BN - 1) / BN;
+    const int tiles = tiles_m * tiles_n * splits;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = SM_COUNT;
+    const int clusters = tiles < sms / 2 ? tiles : sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ma, mb, p, tiles_m, tiles_n, tiles);
+}
+
+int d1_gemm_pair(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,
+                 const float *bias, int relu, const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf,
+                 int splits, void *stream) {
+    return pair_launch(a, lda, b, ldb, M, N, K, bias, relu, mask, ldm, c, ldc, cf, ldcf, splits, a_mn != 0, b_mn != 0,
+                       stream);
 }
 
 // Splits actually used for (K, requested splits): callers size fp32 slabs with it.

@@ -42,6 +42,8 @@ SIGNATURES = {
     'd1_gemm_bkn': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_rows': [_P, _I, _I, _P, _I, _P, _I, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_ex': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
+    'd1_gemm_single': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
+    'd1_gemm_pair': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_col_sum_part_len': [_I, _I],
     'd1_col_sum_bf16': [_P, _I, _I, _I, _P, _P, _P],
     'd1_gemm_head_sample': [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],

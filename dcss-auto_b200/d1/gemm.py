@@ -59,10 +59,11 @@ def gemm_bkn(a, b_kn, bias=None, relu=False, out=None, out_f32=None, splits=1):
 
 
 def gemm_ex(a, b, a_kn=False, b_kn=False, bias=None, relu=False, out=None, out_t=None, out_f32=None, splits=1,
-            mask=None):
+            mask=None, single=False):
     """act(A @ B^T + bias) with A given as [M, K] (or [K, M] when a_kn) and B as
     [N, K] (or [K, N] when b_kn); the tensor-core operands are then read
-    MN-major instead of K-major. Outputs as gemm()."""
+    MN-major instead of K-major. Outputs as gemm(). single=True keeps the
+    one-CTA kernel for shapes the library would give to the pair kernel."""
     M, K = (a.shape[1], a.shape[0]) if a_kn else a.shape
     N = b.shape[1] if b_kn else b.shape[0]
     assert (b.shape[0] if b_kn else b.shape[1]) == K
@@ -70,12 +71,28 @@ def gemm_ex(a, b, a_kn=False, b_kn=False, bias=None, relu=False, out=None, out_t
     if out is None and out_t is None and out_f32 is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     p = lambda t: None if t is None else t.data_ptr()
-    check(library().d1_gemm_ex(a.data_ptr(), a.stride(0), int(a_kn), b.data_ptr(), b.stride(0), int(b_kn), M, N, K,
-                               p(bias), int(relu), p(mask), 0 if mask is None else mask.stride(0), p(out),
-                               0 if out is None else out.stride(0), p(out_t), 0 if out_t is None else out_t.stride(0),
-                               p(out_f32), 0 if out_f32 is None else out_f32.stride(-2), splits, _stream(a)),
-          'd1_gemm_ex')
+    fn = library().d1_gemm_single if single else library().d1_gemm_ex
+    check(fn(a.data_ptr(), a.stride(0), int(a_kn), b.data_ptr(), b.stride(0), int(b_kn), M, N, K, p(bias), int(relu),
+             p(mask), 0 if mask is None else mask.stride(0), p(out), 0 if out is None else out.stride(0), p(out_t),
+             0 if out_t is None else out_t.stride(0), p(out_f32), 0 if out_f32 is None else out_f32.stride(-2), splits,
+             _stream(a)), 'd1_gemm_ex')
     return out if out is not None else (out_t if out_t is not None else out_f32)
+
+
+def gemm_pair(a, b, a_kn=False, b_kn=False, bias=None, relu=False, out=None, out_f32=None, splits=1, mask=None):
+    """gemm_ex on the 2-SM pair kernel (256 x 256 tiles, one per CTA pair)."""
+    M, K = (a.shape[1], a.shape[0]) if a_kn else a.shape
+    N = b.shape[1] if b_kn else b.shape[0]
+    assert (b.shape[0] if b_kn else b.shape[1]) == K
+    assert a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16 and a.stride(1) == 1 and b.stride(1) == 1
+    if out is None and out_f32 is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    p = lambda t: None if t is None else t.data_ptr()
+    check(library().d1_gemm_pair(a.data_ptr(), a.stride(0), int(a_kn), b.data_ptr(), b.stride(0), int(b_kn), M, N, K,
+                                 p(bias), int(relu), p(mask), 0 if mask is None else mask.stride(0), p(out),
+                                 0 if out is None else out.stride(0), p(out_f32),
+                                 0 if out_f32 is None else out_f32.stride(-2), splits, _stream(a)), 'd1_gemm_pair')
+    return out if out is not None else out_f32
 
 
 def gemm_rows(a, b, M=None, a_rows=None, b_rows=None, a_kn=False, b_kn=False, bias=None, relu=False, out=None,

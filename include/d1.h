@@ -190,7 +190,10 @@ int d1_policy_head_greedy(const void *h_bf16, int n, int hidden, const void *wh_
  * bf16[N, ldct] (C transposed), cf fp32 (row-major, pitch ldcf, one [M, ldcf]
  * slab per K split). splits > 1 splits K across CTAs and requires c == ct ==
  * NULL; the number of slabs written is d1_gemm_splits(K, splits). Bases and
- * pitches must be 16-byte aligned (TMA). */
+ * pitches must be 16-byte aligned (TMA). When no transposed output is asked
+ * for, N > 128 and each split spans at least 512 of K, the call runs the 2-SM
+ * pair kernel (d1_gemm_pair); otherwise one CTA per 128 x 256 tile
+ * (d1_gemm_single). Both give bit-identical results. */
 int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
             const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits,
             void *stream);
@@ -211,6 +214,18 @@ int d1_gemm_bkn(const void *a, int lda, const void *b_kn, int ldb, int M, int N,
 int d1_gemm_rows(const void *a, int lda, int a_mn, const int64_t *a_rows, int a_table_rows, const void *b, int ldb,
                  int b_mn, const int64_t *b_rows, int b_table_rows, int M, int N, int K, const float *bias, int relu,
                  const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf, int splits, void *stream);
+/* 2-SM form of d1_gemm_ex: each cluster of two CTAs computes a 256 x 256 tile
+ * with tcgen05.mma.cta_group::2, each CTA streaming its 128 rows of A and its
+ * half of B, so an SM reads 32 KB per 64-deep K block instead of 48 KB. Same
+ * arguments as d1_gemm_ex without the transposed output. */
+int d1_gemm_pair(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,
+                 const float *bias, int relu, const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf,
+                 int splits, void *stream);
+/* d1_gemm_ex on the one-CTA kernel whatever the shape (the pair kernel's
+ * comparison point). */
+int d1_gemm_single(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,
+                   const float *bias, int relu, const void *mask, int ldm, void *c, int ldc, void *ct, int ldct,
+                   float *cf, int ldcf, int splits, void *stream);
 /* The general form: a_mn / b_mn select A stored [K, M] / B stored [K, N]
  * (M / N contiguous) instead of [M, K] / [N, K]; other arguments as d1_gemm. */
 int d1_gemm_ex(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,

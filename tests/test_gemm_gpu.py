@@ -132,3 +132,42 @@ def test_gathered_rows_match_the_gathered_copy(G):
     h2 = G.gemm_rows(table, w, a_rows=idx[:1000], bias=b, relu=True)
     assert torch.equal(h2, h_ref[:1000])
     assert G.gemm_error() == 0
+
+
+@pytest.mark.parametrize('M,N,K,a_kn,b_kn,splits', [(65536, 256, 1832, False, False, 1), (1000, 256, 1832, False, False, 1),
+                                                     (128, 13, 256, False, False, 1), (300, 1832, 256, False, False, 1),
+                                                     (4096, 256, 4096, True, True, 8), (256, 1832, 8192, True, True, 16),
+                                                     (8192, 256, 256, False, True, 1), (2048, 512, 1024, True, False, 4)])
+def test_pair_kernel_matches_the_product(G, M, N, K, a_kn, b_kn, splits):
+    """2-SM pair kernel: K-major and MN-major operands, ragged M and N, split-K
+    slabs; bf16 output with bias + ReLU + mask, and fp32 slabs equal to the
+    one-CTA kernel's."""
+    g = torch.Generator(device='cuda').manual_seed(M + 3 * N + K)
+    a = torch.randn(M, K, device='cuda', generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, device='cuda', generator=g) / K ** 0.5).to(torch.bfloat16)
+    pad = lambda t: torch.nn.functional.pad(t, (0, (-t.shape[1]) % 8)).contiguous()[:, :t.shape[1]]
+    aa = pad(a.T.contiguous()) if a_kn else a
+    bb = pad(b.T.contiguous()) if b_kn else b
+    r = ref(a, b)
+    ld = (N + 7) // 8 * 8
+    s = G.splits_for(K, splits)
+    cf = torch.empty((s, M, ld), device='cuda')
+    G.gemm_pair(aa, bb, a_kn, b_kn, out_f32=cf[:, :, :N], splits=splits)
+    one = torch.empty((s, M, ld), device='cuda')
+    G.gemm_ex(aa, bb, a_kn, b_kn, out_f32=one[:, :, :N], splits=splits, single=True)
+    torch.cuda.synchronize()
+    assert G.gemm_error() == 0
+    assert torch.allclose(cf[:, :, :N].sum(0), r, rtol=1e-3, atol=1e-2)
+    assert torch.equal(cf[:, :, :N], one[:, :, :N])
+    if splits == 1:
+        bias = torch.randn(N, device='cuda', generator=g)
+        mask = pad(torch.randn(M, N, device='cuda', generator=g).to(torch.bfloat16))
+        out = torch.empty((M, ld), dtype=torch.bfloat16, device='cuda')[:, :N]
+        G.gemm_pair(aa, bb, a_kn, b_kn, bias=bias, relu=True, mask=mask, out=out)
+        want = torch.empty((M, ld), dtype=torch.bfloat16, device='cuda')[:, :N]
+        G.gemm_ex(aa, bb, a_kn, b_kn, bias=bias, relu=True, mask=mask, out=want, single=True)
+        torch.cuda.synchronize()
+        assert G.gemm_error() == 0
+        assert torch.equal(out, want)
+        rr = torch.where(mask.float() > 0, ref(a, b, bias, True), 0.)
+        assert (out.float() - rr).abs().max().item() <= 2e-3 * rr.abs().max().item() + 1e-2
