@@ -43,6 +43,9 @@ SIGNATURES = {
     'd1_gemm_rows': [_P, _I, _I, _P, _I, _P, _I, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_ex': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_single': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
+    'd1_spec_d4_observe': [_P, _P, _P, _I, _P, _P, _P],
+    'd1_spec_d4_actions': [_P, _P, _I, _P, _P],
+    'd1_spec_d4_draw': [_P, _I, _P, _I, _P, _U64, _U64, _I, _P],
     'd1_gemm_pair': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_col_sum_part_len': [_I, _I],
     'd1_col_sum_bf16': [_P, _I, _I, _I, _P, _P, _P],

@@ -309,6 +309,26 @@ int d1_sample_uniform_legal(const uint16_t *legal, int nact, int n, uint64_t see
  * when active is given) get obs in every frame. */
 int d1_frame_stack(void *stack, const void *obs, int row_bytes, int frames, int n, const float *out, int out_cols,
                    const bool *active, void *stream);
+/* Per-episode D4 camera augmentation of the spec observation (reference:
+ * gpu-d1/branches/vision15-symmetry-v1/scripts/symmetry.py:19-102, D4 and
+ * EpisodeSymmetry). groups u8[n] in 0..7: mirror x when g >= 4, then g % 4
+ * quarter turns (x, y) -> (-y, x).
+ * d1_spec_d4_observe: camera observation and legal bits of the world ones
+ * (cells permuted, coordinate scalars rotated with the reference's scale and
+ * offset tables, legal bits 0-7 permuted); obs_out may equal obs (in place),
+ * both 16-byte aligned.
+ * d1_spec_d4_actions: camera action -> world action (directions 0-7 permuted,
+ * others unchanged; the reference's to_world).
+ * d1_spec_d4_draw: groups[i] = Philox word 0 >> 29 of (ctr = {lo(step),
+ * hi(step), hi(seed), 4}, key = {first_env + i, lo(seed)}) for every env when
+ * out == NULL, else only where the episode ended (out[i, 1] > 0, and active[i]
+ * when given). */
+int d1_spec_d4_observe(const void *obs_bf16, const uint16_t *legal, const uint8_t *groups, int n, void *obs_out_bf16,
+                       uint16_t *legal_out, void *stream);
+int d1_spec_d4_actions(const int64_t *camera_actions, const uint8_t *groups, int n, int64_t *world_actions,
+                       void *stream);
+int d1_spec_d4_draw(uint8_t *groups, int n, const float *out, int out_cols, const bool *active, uint64_t seed,
+                    uint64_t step, int first_env, void *stream);
 /* Nonzero when a GEMM pipeline wait expired (the kernel then skipped its work
  * and freed its tensor memory); reading clears it. Synchronises the device. */
 int d1_gemm_error(void);
