@@ -416,13 +416,16 @@ def run_ours(args, rank, world, local_rank):
 def run_kernels(args):
     """Every hot kernel once for warm-up and once more to be captured (ncu -k
     <kernel> -s <skip> -c <count>), at the bench's sizes, ~4 GB on the device.
-    Launch order: an 8-step rollout of 65,536 envs (8 x (step_kernel, 2
-    gemm_kernel, head_sample_kernel), then 2 gemm_kernel + head_sample_kernel for
-    the bootstrap value) and GAE; then per pass: gemm_kernel (rollout layer 1),
-    one PPO minibatch of 16,384 (gather_kernel, 5 gemm_kernel, loss_mma_kernel,
-    reductions, adam_kernel), gemm_kernel (layer 2), head_sample_kernel,
-    step_kernel, gae_scan_kernel, and the config-3 policy on 16,384 envs
-    (crop_kernel, conv_kernel<1..3>, 2 gemm_kernel, ar_kernel)."""
+    Launch order: an 8-step rollout of 65,536 envs (8 x (step_kernel, layer 1 on
+    gemm_pair_kernel, layer 2 on gemm_kernel, head_sample_kernel), then the same
+    two GEMMs + head_sample_kernel for the bootstrap value) and GAE; then per
+    pass: rollout layer 1 (gemm_pair_kernel), one PPO minibatch of 16,384
+    (gather_kernel; layer 1 gemm_pair_kernel; layer 2, dW2 and dh1 gemm_kernel;
+    dW1 gemm_pair_kernel; loss_mma_kernel, reductions, adam_kernel), layer 2
+    (gemm_kernel), head_sample_kernel, step_kernel, gae_scan_kernel, and the
+    config-3 policy on 16,384 envs (crop_kernel, conv_kernel<1..3>, FC
+    gemm_pair_kernel, head gemm_kernel, ar_kernel). A `gemm` regex therefore
+    sees 18 launches in the rollout and 9 per pass."""
     import torch
     from d1 import gemm as G
     from d1.conv_policy import ConvPolicy
