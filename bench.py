@@ -253,11 +253,13 @@ def run_ours(args, rank, world, local_rank):
         from d1.rollout import DecisionGraph
         env.reset(2)
         dg = DecisionGraph(env, policy, seed=3, first_env=rank * B, step=0)
-        for k in range(3):
+        # the same step range as the device-timed rollout: W warm-up decisions
+        # after a reset, then K timed ones
+        for k in range(max(3, args.warmup)):
             dg.replay()
             torch.cuda.synchronize()
             dg.h_act.copy_(dg.h_next)
-        e2e_steps = max(8, args.steps // 4)
+        e2e_steps = args.steps
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
