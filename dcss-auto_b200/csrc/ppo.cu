@@ -6,6 +6,7 @@
 // Reference update: gpu-d1/scripts/run_ring_ablations.py:354-372.
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "d1_common.cuh"
 
@@ -227,7 +228,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__restrict__ obs, int F,
                                                      const int64_t *__restrict__ idx, int n, __nv_bfloat16 *x,
-                                                     __nv_bfloat16 *xt, int ldt) {
+                                                     int ldx, int ones, __nv_bfloat16 *xt, int ldt) {
     extern __shared__ __align__(16) __nv_bfloat16 gbuf[];  // [G_STAGES][G_SAMPLES][G_PITCH]
     const int s0 = blockIdx.x * G_SAMPLES;
     const int t = threadIdx.x, part = t & 7;
@@ -266,7 +267,7 @@ __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__rest
             for (int h = 0; h < 2; h++) {
                 const int ls = (t >> 3) + 32 * h, f = f0 + part * 8;
                 if (live[h] && f < F)
-                    *reinterpret_cast<uint4 *>(x + (size_t)(s0 + ls) * F + f) =
+                    *reinterpret_cast<uint4 *>(x + (size_t)(s0 + ls) * ldx + f) =
                         *reinterpret_cast<const uint4 *>(buf + g_swz(ls, part));
             }
         }
@@ -290,6 +291,10 @@ __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__rest
         __syncthreads();
     }
     cp_async_wait<0>();
+    // columns F..F+7 = (1, 0, ..., 0): the product dh^T X then carries the
+    // column sums of dh (the bias gradient) in its column F
+    if (x && ones && blockIdx.y == 0 && t < G_SAMPLES && s0 + t < n)
+        *reinterpret_cast<uint4 *>(x + (size_t)(s0 + t) * ldx + F) = make_uint4(0x3f80u, 0u, 0u, 0u);
 }
 
 // ------------------------------------------------------------------ fused head + loss + backward to h2
@@ -909,6 +914,207 @@ __global__ void adam_kernel(AdamArgs a) {
 
 __global__ void counter_add_kernel(int64_t *c, int64_t delta) { *c += delta; }
 
+// ------------------------------------------------------------------ fused optimizer step
+// One launch for the end of a minibatch: (1) reduce the gradient's partial
+// products into the flat gradient, (2) its global sum of squares, (3) grid
+// barrier, (4) clip + Adam + bf16 copies, with the step counter advanced on the
+// device. Job j: element e < rows * cols_in of every partial p < nsrc sits at
+// src[p * stride + e]; element (r, c) goes to dst[r * cols_out + c] when
+// c < cols_out, to dst_extra[r] when c == cols_out (a bias carried as an extra
+// product column), else nowhere. A block owns 32 consecutive elements of a
+// job at a time; its 8 warps sum the partials p = warp, warp + 8, ... and the
+// warp sums are added in warp order, so the result does not depend on
+// scheduling. Without jobs (the multi-GPU path, after the gradient
+// all-reduce) step (1) is skipped and (2) reads the gradient.
+constexpr int STEP_BLOCKS_PER_SM = 4, STEP_MAX_JOBS = 4, STEP_MAX_BLOCKS = 2048;
+struct StepJob {
+    const float *src;
+    int64_t stride;
+    int nsrc, rows, cols_in, cols_out, in_norm;
+    float *dst, *dst_extra;
+    int64_t chunk_begin;
+    int vec;  // 4: float4 loads (a chunk is 128 elements), 1: scalar (32)
+};
+struct StepArgs {
+    StepJob job[STEP_MAX_JOBS];
+    int njobs;
+    int64_t chunks, wide_chunks;  // chunks of all jobs; of the leading jobs with > 16 partials
+    const float *grad;  // without jobs: the gradient whose sum of squares is taken
+    int64_t total;
+    int norm;           // write this block's sum of squares to g_step_part[block]
+};
+__device__ double g_step_part[STEP_MAX_BLOCKS];
+__device__ unsigned g_step_ticket;
+// Sum of partials p = first, first + step, ... of the chunk's elements (vec of
+// them per lane); returns the lane's first element index.
+__device__ __forceinline__ int64_t chunk_partial(const StepJob &jb, int64_t ch, int lane, int first, int step,
+                                                 float4 &sum) {
+    const int vw = jb.vec;
+    const int64_t e = ((ch - jb.chunk_begin) * 32 + lane) * vw, n_el = (int64_t)jb.rows * jb.cols_in;
+    sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e < n_el) {
+        if (vw == 4) {
+#pragma unroll 8
+            for (int pp = first; pp < jb.nsrc; pp += step) {
+                const float4 q = __ldg(reinterpret_cast<const float4 *>(jb.src + (size_t)pp * jb.stride + e));
+                sum.x += q.x;
+                sum.y += q.y;
+                sum.z += q.z;
+                sum.w += q.w;
+            }
+        } else {
+#pragma unroll 8
+            for (int pp = first; pp < jb.nsrc; pp += step) sum.x += __ldg(jb.src + (size_t)pp * jb.stride + e);
+        }
+    }
+    return e;
+}
+// Writes the lane's summed elements where the job sends them; returns their
+// sum of squares when the job counts toward the gradient norm.
+__device__ __forceinline__ double chunk_store(const StepJob &jb, int64_t e, float4 t4) {
+    const int64_t n_el = (int64_t)jb.rows * jb.cols_in;
+    const float t[4] = {t4.x, t4.y, t4.z, t4.w};
+    double sq = 0.0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        if (k >= jb.vec || e + k >= n_el) break;
+        const int64_t ek = e + k;
+        const int r = (int)(ek / jb.cols_in), c = (int)(ek - (int64_t)r * jb.cols_in);
+        bool kept = false;
+        if (c < jb.cols_out) {
+            jb.dst[(size_t)r * jb.cols_out + c] = t[k];
+            kept = true;
+        } else if (c == jb.cols_out && jb.dst_extra) {
+            jb.dst_extra[r] = t[k];
+            kept = true;
+        }
+        if (kept && jb.in_norm) sq += (double)t[k] * t[k];
+    }
+    return sq;
+}
+
+__global__ void __launch_bounds__(256) step_kernel(const __grid_constant__ StepArgs a) {
+    __shared__ float4 ps[8][32];
+    __shared__ double ws[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    double sq = 0.0;
+    if (a.njobs > 0) {
+        // jobs with many partials: a block per chunk, its 8 warps splitting the partials
+        for (int64_t ch = blockIdx.x; ch < a.wide_chunks; ch += gridDim.x) {
+            int j = 0;
+            while (j + 1 < a.njobs && ch >= a.job[j + 1].chunk_begin) j++;
+            const StepJob &jb = a.job[j];
+            float4 sum;
+            const int64_t e = chunk_partial(jb, ch, lane, warp, 8, sum);
+            ps[warp][lane] = sum;
+            __syncthreads();
+            if (warp == 0) {
+                float4 t = ps[0][lane];
+#pragma unroll
+                for (int w = 1; w < 8; w++) {
+                    const float4 q = ps[w][lane];
+                    t.x += q.x;
+                    t.y += q.y;
+                    t.z += q.z;
+                    t.w += q.w;
+                }
+                sq += chunk_store(jb, e, t);
+            }
+            __syncthreads();
+        }
+        // jobs with few partials: a warp per chunk, no block synchronisation
+        const int64_t warps = (int64_t)gridDim.x * 8;
+        for (int64_t ch = a.wide_chunks + (int64_t)blockIdx.x * 8 + warp; ch < a.chunks; ch += warps) {
+            int j = 0;
+            while (j + 1 < a.njobs && ch >= a.job[j + 1].chunk_begin) j++;
+            const StepJob &jb = a.job[j];
+            float4 t;
+            const int64_t e = chunk_partial(jb, ch, lane, 0, 1, t);
+            sq += chunk_store(jb, e, t);
+        }
+    } else {
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.total; i += (int64_t)gridDim.x * blockDim.x) {
+            const float g = a.grad[i];
+            sq += (double)g * g;
+        }
+    }
+    if (!a.norm) return;
+    // block partial of the sum of squares (fixed shuffle tree, then warp order)
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(FULL, sq, o);
+    if (lane == 0) ws[warp] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < 8; w++) t += ws[w];
+        g_step_part[blockIdx.x] = t;
+    }
+}
+
+// Adam after step_kernel: the global sum of squares is the sum of that
+// launch's block partials, added in block order by every block (so the clip
+// coefficient is the same everywhere), and *step advances on the device.
+__global__ void __launch_bounds__(256) adam_step_kernel(AdamArgs d, int nparts, int64_t *step) {
+    __shared__ float sc[3];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t step0 = *step;
+    if (warp == 0) {
+        double t = 0.0;
+        for (int b = lane; b < nparts; b += 32) t += g_step_part[b];
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(FULL, t, o);
+        if (lane == 0) {
+            const double tstep = (double)(step0 + 1);
+            sc[0] = (float)(1.0 - pow((double)d.beta1, tstep));
+            sc[1] = (float)sqrt(1.0 - pow((double)d.beta2, tstep));
+            float scale = 1.f;
+            if (d.max_norm > 0.f) {
+                const float coef = d.max_norm / ((float)sqrt(t) + 1e-6f);
+                if (coef < 1.f) scale = coef;
+            }
+            sc[2] = scale;
+        }
+    }
+    __syncthreads();
+    const float bc1 = sc[0], bc2_sqrt = sc[1], scale = sc[2];
+    const int64_t n4 = d.total / 4, stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4; q += stride) {
+        const float4 g4 = reinterpret_cast<const float4 *>(d.grad)[q];
+        float4 m4 = reinterpret_cast<const float4 *>(d.m)[q], v4 = reinterpret_cast<const float4 *>(d.v)[q];
+        float4 p4 = reinterpret_cast<const float4 *>(d.param)[q];
+        p4.x = adam_one(d, g4.x, m4.x, v4.x, p4.x, scale, bc1, bc2_sqrt);
+        p4.y = adam_one(d, g4.y, m4.y, v4.y, p4.y, scale, bc1, bc2_sqrt);
+        p4.z = adam_one(d, g4.z, m4.z, v4.z, p4.z, scale, bc1, bc2_sqrt);
+        p4.w = adam_one(d, g4.w, m4.w, v4.w, p4.w, scale, bc1, bc2_sqrt);
+        reinterpret_cast<float4 *>(d.m)[q] = m4;
+        reinterpret_cast<float4 *>(d.v)[q] = v4;
+        reinterpret_cast<float4 *>(d.param)[q] = p4;
+        adam_copies(d, 4 * q, p4.x);
+        adam_copies(d, 4 * q + 1, p4.y);
+        adam_copies(d, 4 * q + 2, p4.z);
+        adam_copies(d, 4 * q + 3, p4.w);
+    }
+    if (blockIdx.x == 0)
+        for (int64_t i = 4 * n4 + threadIdx.x; i < d.total; i += blockDim.x) {
+            float m = d.m[i], v = d.v[i];
+            const float p = adam_one(d, d.grad[i], m, v, d.param[i], scale, bc1, bc2_sqrt);
+            d.m[i] = m;
+            d.v[i] = v;
+            d.param[i] = p;
+            adam_copies(d, i, p);
+        }
+    // every block has read *step above; the last block to finish advances it
+    __shared__ unsigned last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(&g_step_ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        *step = step0 + 1;
+        g_step_ticket = 0;
+    }
+}
+
 // Dynamic shared memory above 48 KB is opted into once per kernel and device;
 // `ready` is that kernel's bitmask of devices already set up.
 static int opt_in_smem(const void *fn, int bytes, uint64_t *ready) {
@@ -939,7 +1145,22 @@ int d1_ppo_gather(const void *obs, int F, const int64_t *idx, int n, void *x, vo
     const int groups = ((F + ppo::G_FEAT - 1) / ppo::G_FEAT + ppo::G_GROUP - 1) / ppo::G_GROUP;
     const dim3 grid((n + ppo::G_SAMPLES - 1) / ppo::G_SAMPLES, groups);
     ppo::gather_kernel<<<grid, 256, ppo::G_SMEM, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16 *)obs, F, idx, n, (__nv_bfloat16 *)x, (__nv_bfloat16 *)xt, ldt);
+        (const __nv_bfloat16 *)obs, F, idx, n, (__nv_bfloat16 *)x, F, 0, (__nv_bfloat16 *)xt, ldt);
+    return (int)cudaGetLastError();
+}
+
+int d1_ppo_gather_x(const void *obs, int F, const int64_t *idx, int n, void *x, int ldx, int ones_col,
+                    void *stream) {
+    if (!obs || !idx || !x || n <= 0 || F <= 0 || F % 8 || ldx % 8 || ldx < F + (ones_col ? 8 : 0) ||
+        (reinterpret_cast<uintptr_t>(x) & 15))
+        return D1_ERR_BAD_ARGUMENT;
+    static uint64_t ready = 0;
+    const int err = ppo::opt_in_smem((const void *)ppo::gather_kernel, ppo::G_SMEM, &ready);
+    if (err) return err;
+    const int groups = ((F + ppo::G_FEAT - 1) / ppo::G_FEAT + ppo::G_GROUP - 1) / ppo::G_GROUP;
+    const dim3 grid((n + ppo::G_SAMPLES - 1) / ppo::G_SAMPLES, groups);
+    ppo::gather_kernel<<<grid, 256, ppo::G_SMEM, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16 *)obs, F, idx, n, (__nv_bfloat16 *)x, ldx, ones_col != 0, nullptr, 0);
     return (int)cudaGetLastError();
 }
 
@@ -1002,6 +1223,82 @@ int d1_sumsq(const float *g, int64_t n, double *out, void *stream) {
     const int64_t blocks = (n / 4 + 255) / 256;
     ppo::sumsq_kernel<<<(unsigned)(blocks < 1 ? 1 : (blocks > 1184 ? 1184 : blocks)), 256, 0, (cudaStream_t)stream>>>(g, n, out);
     return (int)cudaGetLastError();
+}
+
+static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                       float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
+                       const D1AdamSegment *segs, int nseg, int do_adam, void *stream) {
+    using namespace ppo;
+    if (njobs < 0 || njobs > STEP_MAX_JOBS || (njobs > 0 && !jobs) || (!do_adam && njobs == 0)) return D1_ERR_BAD_ARGUMENT;
+    StepArgs a;
+    memset(&a, 0, sizeof(a));
+    int64_t chunks = 0;
+    int order[STEP_MAX_JOBS], n_ord = 0;
+    for (int j = 0; j < njobs; j++)
+        if (jobs[j].nsrc > 16) order[n_ord++] = j;
+    const int n_wide = n_ord;
+    for (int j = 0; j < njobs; j++)
+        if (jobs[j].nsrc <= 16) order[n_ord++] = j;
+    for (int jj = 0; jj < njobs; jj++) {
+        const D1GradJob &q = jobs[order[jj]];
+        if (!q.src || !q.dst || q.nsrc <= 0 || q.rows <= 0 || q.cols_in <= 0 || q.cols_out <= 0 ||
+            q.cols_out > q.cols_in || q.stride < (int64_t)q.rows * q.cols_in)
+            return D1_ERR_BAD_ARGUMENT;
+        const int vec = ((q.cols_in | q.cols_out) % 4 == 0 && q.stride % 4 == 0 &&
+                         (reinterpret_cast<uintptr_t>(q.src) & 15) == 0) ? 4 : 1;
+        a.job[jj] = StepJob{q.src, q.stride, q.nsrc, q.rows, q.cols_in, q.cols_out, q.in_norm, q.dst, q.dst_extra,
+                            chunks, vec};
+        chunks += ((int64_t)q.rows * q.cols_in + 32 * vec - 1) / (32 * vec);
+        if (jj + 1 == n_wide) a.wide_chunks = chunks;
+    }
+    a.njobs = njobs;
+    a.chunks = chunks;
+    a.norm = do_adam;
+    AdamArgs d;
+    if (do_adam) {
+        if (!param || !grad || !m || !v || !step || total <= 0 || nseg < 0 || nseg > 8) return D1_ERR_BAD_ARGUMENT;
+        if ((reinterpret_cast<uintptr_t>(param) | reinterpret_cast<uintptr_t>(grad) | reinterpret_cast<uintptr_t>(m) |
+             reinterpret_cast<uintptr_t>(v)) & 15)
+            return D1_ERR_BAD_ARGUMENT;
+        a.grad = grad;
+        a.total = total;
+        d.param = param;
+        d.grad = grad;
+        d.m = m;
+        d.v = v;
+        d.sumsq = nullptr;
+        d.step = step;
+        d.lr = lr;
+        d.beta1 = beta1;
+        d.beta2 = beta2;
+        d.eps = eps;
+        d.max_norm = max_norm;
+        d.nseg = nseg;
+        d.total = total;
+        for (int i = 0; i < nseg; i++)
+            d.seg[i] = AdamSeg{segs[i].offset, segs[i].count, segs[i].rows, segs[i].cols,
+                               (__nv_bfloat16 *)segs[i].bf16, (__nv_bfloat16 *)segs[i].bf16_t};
+    }
+    int dev = 0, sms = 0;
+    if (cudaError_t e = cudaGetDevice(&dev)) return (int)e;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    int blocks = sms * STEP_BLOCKS_PER_SM;
+    if (blocks > STEP_MAX_BLOCKS) blocks = STEP_MAX_BLOCKS;
+    step_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
+    if (do_adam) adam_step_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d, blocks, step);
+    return (int)cudaGetLastError();
+}
+
+int d1_ppo_step(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step, const D1AdamSegment *segs,
+                int nseg, void *stream) {
+    return step_launch(jobs, njobs, param, grad, m, v, total, lr, beta1, beta2, eps, max_norm, step, segs, nseg, 1,
+                       stream);
+}
+
+int d1_grad_reduce(const D1GradJob *jobs, int njobs, void *stream) {
+    return step_launch(jobs, njobs, nullptr, nullptr, nullptr, nullptr, 0, 0.f, 0.f, 0.f, 0.f, 0.f, nullptr, nullptr, 0,
+                       0, stream);
 }
 
 int d1_counter_add(int64_t *counter, int64_t delta, void *stream) {

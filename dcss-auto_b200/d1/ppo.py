@@ -4,17 +4,20 @@ coefficients) and a switch for the reference loss (0.25 * MSE, no value clip).
 
 Per minibatch (all device work is libd1 kernels, launched on the current stream):
 
-  gather     X = obs[idx]                          d1_ppo_gather
-  layer 1    h1 = relu(X W1^T + b1)                d1_gemm (tcgen05)
+  gather     X = [obs[idx] | 1 0 ... 0]            d1_ppo_gather_x (pitch 1840)
+  layer 1    h1 = relu(X W1^T + b1)                d1_gemm (tcgen05, K = 1832)
   layer 2    h2 = relu(h1 W2^T + b2)               d1_gemm
   loss       head, PPO loss, dlogits/dvalue,       d1_ppo_loss (fused, warp MMAs)
              dh2 = dhead Wh * relu'(h2), partials of dWh, dbh, db2
-  dW2        dh2^T h1 (split-K fp32 slabs)         d1_gemm_ex + d1_reduce_slabs
+  dW2        dh2^T h1 (split-K fp32 slabs)         d1_gemm_ex
   dh1        (dh2 W2) * relu'(h1)                  d1_gemm (mask epilogue)
-  dW1        dh1^T X (split-K fp32 slabs)          d1_gemm_ex + d1_reduce_slabs
-  db1        column sums of dh1                    d1_col_sum_bf16
-  all-reduce flat fp32 gradient (NCCL, multi-GPU)  torch.distributed
-  optimizer  grad-norm clip + Adam + bf16 copies   d1_sumsq + d1_adam
+  dW1, db1   dh1^T X (split-K fp32 slabs; X's      d1_gemm_ex
+             ones column makes column 1832 = db1)
+  step       slab and loss-partial reductions      d1_ppo_step (a reduction
+             into the flat gradient, its norm,     launch, then the Adam launch)
+             clip + Adam + bf16 copies
+  (multi-GPU: d1_grad_reduce, NCCL all-reduce of the flat fp32 gradient, then
+  d1_ppo_step without reductions)
 
 The weight-gradient GEMMs read dh2, h1, dh1 and X as stored (row-major, so
 [K, M] / [K, N] with K = samples): their tensor-core operands are MN-major and
@@ -40,6 +43,12 @@ class AdamSegment(C.Structure):
                 ('bf16', C.c_void_p), ('bf16_t', C.c_void_p)]
 
 
+class GradJob(C.Structure):
+    _fields_ = [('src', C.c_void_p), ('stride', C.c_int64), ('nsrc', C.c_int), ('rows', C.c_int),
+                ('cols_in', C.c_int), ('cols_out', C.c_int), ('in_norm', C.c_int), ('dst', C.c_void_p),
+                ('dst_extra', C.c_void_p)]
+
+
 class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
@@ -62,19 +71,18 @@ class PPO:
         self.grad = torch.zeros(policy.size, **f32)
         self.m = torch.zeros(policy.size, **f32)
         self.v = torch.zeros(policy.size, **f32)
-        self.sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
         self.step_dev = torch.zeros(1, dtype=torch.int64, device=dev)  # Adam step count
         self.use_graph, self.graph = graph, None
         self.perm = torch.empty(self.total, dtype=torch.int64, device=dev)
         mb = minibatch
-        self.x = torch.empty((mb, OBS), **bf)
+        self.xw = OBS + 8  # X row pitch: the 8-column tail carries the ones column
+        self.x = torch.empty((mb, self.xw), **bf)
         self.h1 = torch.empty((mb, HID), **bf)
         self.h2 = torch.empty((mb, HID), **bf)
         self.dh2 = torch.empty((mb, HID), **bf)
         self.dh1 = torch.empty((mb, HID), **bf)
-        self.colsum_part = torch.empty(self.lib.d1_col_sum_part_len(mb, HID), **f32)
         self.s1 = G.splits_for(mb, splits)
-        self.slab1 = torch.empty((self.s1, HID, OBS), **f32)
+        self.slab1 = torch.empty((self.s1, HID, self.xw), **f32)
         # dW2 is 256 x 256: its output has only 2 tiles, so it needs 8x the K splits
         # of dW1 (2 x 8 tiles) to put ~128 CTAs to work
         self.s2 = G.splits_for(mb, splits * 8)
@@ -96,6 +104,15 @@ class PPO:
                 AdamSegment(self.off['w2'], HID * HID, HID, HID, bfc['w2'].data_ptr(), bfc['w2t'].data_ptr()),
                 AdamSegment(self.off['wh'], NOUT * HID, NOUT, HID, bfc['wh'].data_ptr(), None)]
         self.segs = (AdamSegment * len(segs))(*segs)
+        g, ptr = self.grad, lambda t: t.data_ptr()
+        jobs = [GradJob(ptr(self.slab1), HID * self.xw, self.s1, HID, self.xw, OBS, 1, ptr(g[self.off['w1']:]),
+                        ptr(g[self.off['b1']:])),
+                GradJob(ptr(self.slab2), HID * HID, self.s2, 1, HID * HID, HID * HID, 1, ptr(g[self.off['w2']:]), None),
+                GradJob(ptr(self.part), self.part_len, self.loss_blocks, 1, head_len, head_len, 1,
+                        ptr(g[self.off['wh']:]), None),
+                GradJob(ptr(self.part[:, head_len:]), self.part_len, self.loss_blocks, 1, 8, 8, 0, ptr(self.terms),
+                        None)]
+        self.jobs = (GradJob * len(jobs))(*jobs)
 
     @property
     def stream(self):
@@ -123,9 +140,9 @@ class PPO:
         p, r, lib, s = self.policy, self.rollout, self.lib, self.stream
         mb = self.mb
         obs = r.obs[:r.T].reshape(self.total, OBS)
-        check(lib.d1_ppo_gather(obs.data_ptr(), OBS, idx.data_ptr(), mb, self.x.data_ptr(), None, mb, s),
-              'd1_ppo_gather')
-        p.hidden_layers(self.x, h1=self.h1, h2=self.h2)
+        check(lib.d1_ppo_gather_x(obs.data_ptr(), OBS, idx.data_ptr(), mb, self.x.data_ptr(), self.xw, 1, s),
+              'd1_ppo_gather_x')
+        p.hidden_layers(self.x[:, :OBS], h1=self.h1, h2=self.h2)
         g = self.grad
         check(lib.d1_ppo_loss(self.h2.data_ptr(), p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(),
                               idx.data_ptr(), r.legal.data_ptr(), r.actions.data_ptr(), r.logp.data_ptr(),
@@ -133,31 +150,22 @@ class PPO:
                               self.adv_count, mb, self.clip, self.vclip, self.vf_coef, self.ent_coef,
                               self.dh2.data_ptr(), None, mb, self.part.data_ptr(), self.loss_blocks,
                               s), 'd1_ppo_loss')
-        # dWh, dbh, db2 straight into the flat gradient; loss terms aside
-        check(lib.d1_sum_rows(self.part.data_ptr(), self.loss_blocks, self.part_len, self.head_len,
-                              g[self.off['wh']:].data_ptr(), s), 'd1_sum_rows')
-        check(lib.d1_sum_rows(self.part[:, self.head_len:].data_ptr(), self.loss_blocks, self.part_len, 8,
-                              self.terms.data_ptr(), s), 'd1_sum_rows')
         # dW2 = dh2^T h1
         G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
-        check(lib.d1_reduce_slabs(self.slab2.data_ptr(), self.s2, HID * HID, g[self.off['w2']:].data_ptr(), s))
         # dh1 = (dh2 W2) * relu'(h1)
         G.gemm(self.dh2, p.bf16['w2t'], mask=self.h1, out=self.dh1)
-        # dW1 = dh1^T X, db1 = column sums of dh1
+        # dW1 = dh1^T X; X's ones column makes slab column 1832 the column sums of dh1 (db1)
         G.gemm_ex(self.dh1, self.x, a_kn=True, b_kn=True, out_f32=self.slab1, splits=self.s1)
-        check(lib.d1_reduce_slabs(self.slab1.data_ptr(), self.s1, HID * OBS, g[self.off['w1']:].data_ptr(), s))
-        check(lib.d1_col_sum_bf16(self.dh1.data_ptr(), mb, HID, HID, self.colsum_part.data_ptr(),
-                                  g[self.off['b1']:].data_ptr(), s), 'd1_col_sum_bf16')
+        jobs, njobs = self.jobs, len(self.jobs)
         if self.group is not None:
             import torch.distributed as dist
+            check(lib.d1_grad_reduce(jobs, njobs, s), 'd1_grad_reduce')
             dist.all_reduce(g, group=self.group)
             g.div_(dist.get_world_size(self.group))
-        self.sumsq.zero_()
-        check(lib.d1_sumsq(g.data_ptr(), g.numel(), self.sumsq.data_ptr(), s))
-        check(lib.d1_counter_add(self.step_dev.data_ptr(), 1, s))
-        check(lib.d1_adam(p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
-                          self.sumsq.data_ptr(), g.numel(), self.lr, self.betas[0], self.betas[1], self.eps,
-                          self.max_grad_norm, self.step_dev.data_ptr(), self.segs, len(self.segs), s), 'd1_adam')
+            jobs, njobs = None, 0
+        check(lib.d1_ppo_step(jobs, njobs, p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
+                              g.numel(), self.lr, self.betas[0], self.betas[1], self.eps, self.max_grad_norm,
+                              self.step_dev.data_ptr(), self.segs, len(self.segs), s), 'd1_ppo_step')
         return self.terms
 
     def _epoch(self):

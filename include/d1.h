@@ -394,6 +394,37 @@ int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, 
             float beta2, float eps, float max_norm, const int64_t *step, const D1AdamSegment *segs, int nseg,
             void *stream);
 
+/* End of a minibatch in two launches: (1) reduce the gradient's partial
+ * products into the flat gradient, with per-block sums of squares; (2) the
+ * d1_adam step (clip by the global norm, Adam, bf16 copies) with *step advanced
+ * by one on the device (the step taken is the old *step + 1). Job j
+ * (njobs <= 4): element e < rows * cols_in of partial p < nsrc is
+ * src[p * stride + e]; element (r, c) of the sum goes to
+ * dst[r * cols_out + c] when c < cols_out, to dst_extra[r] when c == cols_out
+ * (a bias carried as an extra product column), else nowhere; in_norm = 0 keeps
+ * a job (loss statistics) out of the gradient norm. Sums are deterministic
+ * (fixed partial and block order). With njobs == 0 the gradient is taken as it
+ * is in `grad` (after a cross-rank all-reduce). The block partials live in a
+ * file-scope array: calls must not overlap on one device. */
+typedef struct {
+    const float *src;
+    int64_t stride;
+    int nsrc, rows, cols_in, cols_out, in_norm;
+    float *dst, *dst_extra;
+} D1GradJob;
+int d1_ppo_step(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step, const D1AdamSegment *segs,
+                int nseg, void *stream);
+/* Step (1) of d1_ppo_step alone (multi-GPU: reduce, all-reduce, then
+ * d1_ppo_step with no jobs). */
+int d1_grad_reduce(const D1GradJob *jobs, int njobs, void *stream);
+/* Gather x[i, 0..F) = obs[idx[i], 0..F) into rows of pitch ldx; with ones_col,
+ * columns F..F+7 of every row are (1, 0, ..., 0), so that a weight-gradient
+ * product dh^T x also yields the bias gradient (column sums of dh) in its
+ * column F. F and ldx multiples of 8, ldx >= F + 8 with ones_col. */
+int d1_ppo_gather_x(const void *obs, int F, const int64_t *idx, int n, void *x, int ldx, int ones_col,
+                    void *stream);
+
 #ifdef __cplusplus
 }
 #endif
