@@ -9,7 +9,7 @@
 // bitset BFS that stops one layer past the farthest awake monster, and each
 // observation cell is one 16-byte store of eight bf16 channels.
 //
-// State row (2048 B per env):
+// State row (7680 B per env):
 //   0    u64 ctr (Philox draws consumed)   8 u32 env, seed_lo, seed_hi, episode
 //   24   i32 hp, regen, blocks, player     40 i32 ticks, killed, stairs, nmon
 //   56   i32 floor_seen                    64 u16 vis[16] (LOS window rows, dy+7 -> bit dx+7)
@@ -17,6 +17,10 @@
 //   128  i16 pos[16]  160 i16 energy[16]  192 i16 hp[16]  224 u8 kind[16]  240 u8 awake[16]
 //   256  u32 floor[210]  (row y = words 3y..3y+2, bit x%32 of word x/32)
 //   1096 u32 viewed[210] (cells ever in view: remembered terrain)
+//   2048 u8 dist[5600]   (pursuit BFS distance mod 256, valid where reached;
+//                         scratch of the step, kept in the row so that the
+//                         shared memory per env -- the occupancy limit -- is
+//                         4.6 KB instead of 10.2 KB)
 #include <cuda_bf16.h>
 
 #include "d1_common.cuh"
@@ -25,15 +29,18 @@ namespace d1 {
 namespace spec {
 
 constexpr int MAXM = 11, OBS = 1832, CELLS = 225, ACTIONS = 12, OUT = 10, COMPACT = 56;
-constexpr int ROW = 2048, PL = 210, OFF_VIS = 64, OFF_MON = 128, OFF_FLOOR = 256, OFF_VIEWED = 256 + 4 * PL;
+constexpr int ROW = 7680, OFF_DIST = 2048, PL = 210, OFF_VIS = 64, OFF_MON = 128, OFF_FLOOR = 256, OFF_VIEWED = 256 + 4 * PL;
 #ifndef D1_SPEC_WARPS
 #define D1_SPEC_WARPS 1
 #endif
 #ifndef D1_SPEC_MIN_WARPS
-#define D1_SPEC_MIN_WARPS 24
+#define D1_SPEC_MIN_WARPS 32
 #endif
 // Warps (envs) per block, and the resident warps per SM the register budget is
-// sized for (a launch-bounds hint).
+// sized for (a launch-bounds hint). The step is latency bound (an SM with 15 %
+// fewer resident envs took 7 % longer), so the budget is 32 warps: 62
+// registers without spills, 4.6 KB of shared memory per env, and 32 one-warp
+// blocks -- the SM's block limit -- resident per SM.
 constexpr int WARPS = D1_SPEC_WARPS, MIN_BLOCKS = (D1_SPEC_MIN_WARPS + D1_SPEC_WARPS - 1) / D1_SPEC_WARPS;
 constexpr int MAX_RAYS = 320;
 constexpr int PRIM_WAIT = 8, PRIM_DESCEND = 9;
@@ -88,7 +95,6 @@ struct Smem {
     uint32_t occ[PL];  // live monster positions during the monster phase
     uint32_t vis[16];  // LOS window rows: vis[dy+7] bit dx+7
     uint16_t vmask[16], fmask[16];  // remembered / floor bits of the window rows
-    uint8_t dist8[N];  // BFS distance mod 256 (valid where `seen`)
     uint8_t opqb[32];
     uint8_t occ_ch[CELLS + 7];
 };
@@ -108,6 +114,7 @@ struct Env {
     int lane, dirty_lo, dirty_hi;
     bool floor_dirty;
     Smem *sm;
+    uint8_t *dist;  // this env's BFS distance field (global, in the state row)
 };
 
 __device__ __forceinline__ int bitp(const uint32_t *plane, int p) {
@@ -471,7 +478,7 @@ __device__ void pursuit_bfs(Env &e, int extra_layers) {
         const uint32_t bit = 1u << ((e.player % W) % 32);
         s.seen[r] = bit;
         s.cur[r] = bit;
-        s.dist8[e.player] = 0;
+        e.dist[e.player] = 0;
     }
     __syncwarp();
     const int py = e.player / W;
@@ -518,7 +525,7 @@ __device__ void pursuit_bfs(Env &e, int extra_layers) {
                     s.cur[r] = w;
                     while (w) {
                         const int b = __ffs(w) - 1;
-                        s.dist8[y * W + j * 32 + b] = (uint8_t)k;
+                        e.dist[y * W + j * 32 + b] = (uint8_t)k;
                         w &= w - 1;
                     }
                 }
@@ -539,7 +546,7 @@ __device__ void pursuit_bfs(Env &e, int extra_layers) {
 // 127 steps of it; 65535 when q was not reached.
 __device__ __forceinline__ int dist_rel(const Env &e, int q, int D) {
     if (!bitp(e.sm->seen, q)) return 65535;
-    return D + (int)(int8_t)(uint8_t)(e.sm->dist8[q] - (uint8_t)D);
+    return D + (int)(int8_t)(uint8_t)(e.dist[q] - (uint8_t)D);
 }
 
 // ------------------------------------------------------------------ monster turn
@@ -956,6 +963,7 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     Env e;
     e.lane = threadIdx.x & 31;
     e.sm = &sms[w];
+    e.dist = state + (size_t)env * ROW + OFF_DIST;
     e.env = (uint32_t)(first_env + env);
     e.episode = 0;
     e.rng.n = 0;
@@ -986,6 +994,7 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     e.rng.lane = e.lane;
     e.sm = &sms[w];
     uint8_t *row = state + (size_t)env * ROW;
+    e.dist = row + OFF_DIST;
     load(e, row);
     const float o = decision(e, c, ra, extra_layers, (int)actions[env]);
     if (e.lane < OUT) out[(size_t)env * OUT + e.lane] = o;
@@ -1095,6 +1104,7 @@ __global__ void __launch_bounds__(LOS_WARPS * 32) los_table_kernel(const uint8_t
     Env e;
     e.lane = lane;
     e.sm = &s;
+    e.dist = nullptr;  // no pursuit search here
     e.player = origin;
     compute_los(e, ra);
     // row dy = lane - 7 (15 bits, dx = -7..7) lands at bit (lane + 1) * 17 + 1

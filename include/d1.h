@@ -110,7 +110,7 @@ typedef struct {
     D1Kind kinds[5];                                          /* rat, jackal, goblin, kobold, ogre */
 } D1SpecConfig;
 
-/* 2048 */
+/* 7680 */
 int d1_spec_state_bytes(void);
 /* 1832 */
 int d1_spec_obs_size(void);
@@ -126,7 +126,7 @@ int d1_spec_config_bytes(void);
  * n <= 320. Must be called before any other d1_spec_* compute call. */
 int d1_spec_set_rays(const void *rays, int n);
 /* Generate env i's first map from Philox(key = {first_env + i, lo32(seed)}),
- * reset it and write its observation. state u8[n, 2048]; obs bf16[n, 1832];
+ * reset it and write its observation. state u8[n, 7680]; obs bf16[n, 1832];
  * legal u16[n]. */
 int d1_spec_init(void *state, int n, const D1SpecConfig *c, uint64_t seed, int first_env, void *obs_bf16,
                  uint16_t *legal, void *stream);
