@@ -993,7 +993,7 @@ __device__ __forceinline__ double chunk_store(const StepJob &jb, int64_t e, floa
     return sq;
 }
 
-__global__ void __launch_bounds__(256) step_kernel(const __grid_constant__ StepArgs a) {
+__global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant__ StepArgs a) {
     __shared__ float4 ps[8][32];
     __shared__ double ws[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1050,10 +1050,10 @@ __global__ void __launch_bounds__(256) step_kernel(const __grid_constant__ StepA
     }
 }
 
-// Adam after step_kernel: the global sum of squares is the sum of that
+// Adam after grad_reduce_kernel: the global sum of squares is the sum of that
 // launch's block partials, added in block order by every block (so the clip
 // coefficient is the same everywhere), and *step advances on the device.
-__global__ void __launch_bounds__(256) adam_step_kernel(AdamArgs d, int nparts, int64_t *step) {
+__global__ void __launch_bounds__(256) adam_update_kernel(AdamArgs d, int nparts, int64_t *step) {
     __shared__ float sc[3];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t step0 = *step;
@@ -1284,8 +1284,8 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
     int blocks = sms * STEP_BLOCKS_PER_SM;
     if (blocks > STEP_MAX_BLOCKS) blocks = STEP_MAX_BLOCKS;
-    step_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
-    if (do_adam) adam_step_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d, blocks, step);
+    grad_reduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
+    if (do_adam) adam_update_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d, blocks, step);
     return (int)cudaGetLastError();
 }
 
