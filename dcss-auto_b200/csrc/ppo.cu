@@ -935,6 +935,7 @@ struct StepJob {
     int64_t chunk_begin;
     int vec;  // 4: float4 loads (a chunk is 128 elements), 1: scalar (32)
 };
+constexpr int PEER_MAX = 8;
 struct StepArgs {
     StepJob job[STEP_MAX_JOBS];
     int njobs;
@@ -942,9 +943,29 @@ struct StepArgs {
     const float *grad;  // without jobs: the gradient whose sum of squares is taken
     int64_t total;
     int norm;           // write this block's sum of squares to g_step_part[block]
+    // Peer exchange (multi-GPU): job writes that fall in the flat gradient
+    // [remap_from, remap_from + remap_len) go to half (epoch & 1) of this rank's
+    // exchange buffer instead, and the last block to finish tells every peer
+    // (flag[rank] = epoch in the peer's flag array, a system-scope release).
+    const float *remap_from;
+    int64_t remap_len, xstride;
+    float *xbuf;
+    const int64_t *epoch_src;  // epoch = *epoch_src + 1 (the optimizer's step count)
+    unsigned long long *peer_flags[PEER_MAX];
+    int world, rank;
 };
 __device__ double g_step_part[STEP_MAX_BLOCKS];
-__device__ unsigned g_step_ticket;
+__device__ unsigned g_step_ticket, g_peer_ticket;
+__device__ int g_peer_error;
+
+struct Remap {
+    const float *from;
+    float *to;
+    int64_t len;
+};
+__device__ __forceinline__ float *remap(const Remap &m, float *p) {
+    return (m.to && p >= m.from && p < m.from + m.len) ? m.to + (p - m.from) : p;
+}
 // Sum of partials p = first, first + step, ... of the chunk's elements (vec of
 // them per lane); returns the lane's first element index.
 __device__ __forceinline__ int64_t chunk_partial(const StepJob &jb, int64_t ch, int lane, int first, int step,
@@ -971,7 +992,7 @@ __device__ __forceinline__ int64_t chunk_partial(const StepJob &jb, int64_t ch, 
 }
 // Writes the lane's summed elements where the job sends them; returns their
 // sum of squares when the job counts toward the gradient norm.
-__device__ __forceinline__ double chunk_store(const StepJob &jb, int64_t e, float4 t4) {
+__device__ __forceinline__ double chunk_store(const StepJob &jb, int64_t e, float4 t4, const Remap &rm) {
     const int64_t n_el = (int64_t)jb.rows * jb.cols_in;
     const float t[4] = {t4.x, t4.y, t4.z, t4.w};
     double sq = 0.0;
@@ -982,10 +1003,10 @@ __device__ __forceinline__ double chunk_store(const StepJob &jb, int64_t e, floa
         const int r = (int)(ek / jb.cols_in), c = (int)(ek - (int64_t)r * jb.cols_in);
         bool kept = false;
         if (c < jb.cols_out) {
-            jb.dst[(size_t)r * jb.cols_out + c] = t[k];
+            *remap(rm, jb.dst + (size_t)r * jb.cols_out + c) = t[k];
             kept = true;
         } else if (c == jb.cols_out && jb.dst_extra) {
-            jb.dst_extra[r] = t[k];
+            *remap(rm, jb.dst_extra + r) = t[k];
             kept = true;
         }
         if (kept && jb.in_norm) sq += (double)t[k] * t[k];
@@ -997,6 +1018,8 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
     __shared__ float4 ps[8][32];
     __shared__ double ws[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t epoch = a.xbuf ? (uint64_t)(*a.epoch_src + 1) : 0;
+    const Remap rm{a.remap_from, a.xbuf ? a.xbuf + (epoch & 1) * a.xstride : nullptr, a.remap_len};
     double sq = 0.0;
     if (a.njobs > 0) {
         // jobs with many partials: a block per chunk, its 8 warps splitting the partials
@@ -1018,7 +1041,7 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
                     t.z += q.z;
                     t.w += q.w;
                 }
-                sq += chunk_store(jb, e, t);
+                sq += chunk_store(jb, e, t, rm);
             }
             __syncthreads();
         }
@@ -1030,7 +1053,7 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
             const StepJob &jb = a.job[j];
             float4 t;
             const int64_t e = chunk_partial(jb, ch, lane, 0, 1, t);
-            sq += chunk_store(jb, e, t);
+            sq += chunk_store(jb, e, t, rm);
         }
     } else {
         for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -1038,8 +1061,100 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
             sq += (double)g * g;
         }
     }
+    if (a.xbuf) {
+        // the last block to finish publishes this rank's gradient to the peers
+        __shared__ unsigned last;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            last = atomicAdd(&g_peer_ticket, 1u) == gridDim.x - 1;
+        }
+        __syncthreads();
+        if (last && threadIdx.x == 0) {
+            g_peer_ticket = 0;
+            __threadfence_system();
+            for (int p = 0; p < a.world; p++)
+                if (p != a.rank)
+                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.peer_flags[p] + a.rank), "l"(epoch)
+                                 : "memory");
+        }
+    }
     if (!a.norm) return;
     // block partial of the sum of squares (fixed shuffle tree, then warp order)
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(FULL, sq, o);
+    if (lane == 0) ws[warp] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < 8; w++) t += ws[w];
+        g_step_part[blockIdx.x] = t;
+    }
+}
+
+// Cross-rank mean of the gradient through peer memory (one shot): every block
+// first waits (bounded) until each peer has flagged this epoch, then sums a
+// contiguous range of all ranks' exchange buffers in rank order, divides by the
+// world size, writes the flat gradient and its block partial of the sum of
+// squares. A wait that gives up sets g_peer_error (d1_peer_error) and leaves
+// the block's range as it was.
+struct PeerArgs {
+    const float *xbuf[PEER_MAX];  // each rank's exchange buffer (this rank's is local)
+    int64_t xstride;
+    const unsigned long long *flags;  // this rank's flag array, written by the peers
+    const int64_t *epoch_src;
+    float *grad;
+    int64_t total;
+    int world, rank;
+};
+constexpr uint32_t PEER_WAIT_LIMIT = 1u << 24;
+__global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_constant__ PeerArgs a) {
+    __shared__ int ok;
+    __shared__ double ws[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t epoch = (uint64_t)(*a.epoch_src + 1);
+    if (threadIdx.x == 0) {
+        int good = 1;
+        for (int p = 0; p < a.world && good; p++) {
+            if (p == a.rank) continue;
+            for (uint32_t it = 0;; it++) {
+                unsigned long long v;
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.flags + p) : "memory");
+                if (v >= epoch) break;
+                if (it >= PEER_WAIT_LIMIT) {
+                    good = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        if (!good) atomicExch(&g_peer_error, 1);
+        ok = good;
+    }
+    __syncthreads();
+    double sq = 0.0;
+    if (ok) {
+        const int64_t half = (int64_t)(epoch & 1) * a.xstride;
+        const int64_t n4 = (a.total + 3) / 4, per = (n4 + gridDim.x - 1) / gridDim.x;
+        const int64_t q0 = (int64_t)blockIdx.x * per, q1 = q0 + per < n4 ? q0 + per : n4;
+        const float inv = (float)a.world;
+        for (int64_t q = q0 + threadIdx.x; q < q1; q += blockDim.x) {
+            float4 t = __ldcv(reinterpret_cast<const float4 *>(a.xbuf[0] + half) + q);
+            for (int r = 1; r < a.world; r++) {
+                const float4 v = __ldcv(reinterpret_cast<const float4 *>(a.xbuf[r] + half) + q);
+                t.x += v.x;
+                t.y += v.y;
+                t.z += v.z;
+                t.w += v.w;
+            }
+            const float f[4] = {__fdiv_rn(t.x, inv), __fdiv_rn(t.y, inv), __fdiv_rn(t.z, inv), __fdiv_rn(t.w, inv)};
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                if (4 * q + k < a.total) {
+                    a.grad[4 * q + k] = f[k];
+                    sq += (double)f[k] * f[k];
+                }
+        }
+    }
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(FULL, sq, o);
     if (lane == 0) ws[warp] = sq;
     __syncthreads();
@@ -1225,11 +1340,22 @@ int d1_sumsq(const float *g, int64_t n, double *out, void *stream) {
     return (int)cudaGetLastError();
 }
 
+struct PeerSetup {
+    void *const *xbufs;
+    void *const *flags;
+    int64_t xstride;
+    int world, rank;
+};
+
 static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
                        float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
-                       const D1AdamSegment *segs, int nseg, int do_adam, void *stream) {
+                       const D1AdamSegment *segs, int nseg, int do_adam, void *stream, const PeerSetup *peer = nullptr) {
     using namespace ppo;
     if (njobs < 0 || njobs > STEP_MAX_JOBS || (njobs > 0 && !jobs) || (!do_adam && njobs == 0)) return D1_ERR_BAD_ARGUMENT;
+    if (peer && (njobs == 0 || !do_adam || peer->world < 2 || peer->world > PEER_MAX || peer->rank < 0 ||
+                 peer->rank >= peer->world || !peer->xbufs || !peer->flags || peer->xstride < total ||
+                 peer->xstride % 4 || !step))
+        return D1_ERR_BAD_ARGUMENT;
     StepArgs a;
     memset(&a, 0, sizeof(a));
     int64_t chunks = 0;
@@ -1253,7 +1379,31 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     }
     a.njobs = njobs;
     a.chunks = chunks;
-    a.norm = do_adam;
+    a.norm = do_adam && !peer;
+    PeerArgs pa;
+    memset(&pa, 0, sizeof(pa));
+    if (peer) {
+        a.remap_from = grad;
+        a.remap_len = total;
+        a.xstride = peer->xstride;
+        a.xbuf = (float *)peer->xbufs[peer->rank];
+        a.epoch_src = step;
+        a.world = peer->world;
+        a.rank = peer->rank;
+        for (int i = 0; i < peer->world; i++) {
+            if (!peer->xbufs[i] || !peer->flags[i] || (reinterpret_cast<uintptr_t>(peer->xbufs[i]) & 15))
+                return D1_ERR_BAD_ARGUMENT;
+            a.peer_flags[i] = (unsigned long long *)peer->flags[i];
+            pa.xbuf[i] = (const float *)peer->xbufs[i];
+        }
+        pa.xstride = peer->xstride;
+        pa.flags = (const unsigned long long *)peer->flags[peer->rank];
+        pa.epoch_src = step;
+        pa.grad = grad;
+        pa.total = total;
+        pa.world = peer->world;
+        pa.rank = peer->rank;
+    }
     AdamArgs d;
     if (do_adam) {
         if (!param || !grad || !m || !v || !step || total <= 0 || nseg < 0 || nseg > 8) return D1_ERR_BAD_ARGUMENT;
@@ -1285,6 +1435,7 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     int blocks = sms * STEP_BLOCKS_PER_SM;
     if (blocks > STEP_MAX_BLOCKS) blocks = STEP_MAX_BLOCKS;
     grad_reduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
+    if (peer) peer_allreduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(pa);
     if (do_adam) adam_update_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d, blocks, step);
     return (int)cudaGetLastError();
 }
@@ -1294,6 +1445,46 @@ int d1_ppo_step(const D1GradJob *jobs, int njobs, float *param, float *grad, flo
                 int nseg, void *stream) {
     return step_launch(jobs, njobs, param, grad, m, v, total, lr, beta1, beta2, eps, max_norm, step, segs, nseg, 1,
                        stream);
+}
+
+int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                     float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
+                     const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
+                     int world, int rank, void *stream) {
+    const PeerSetup peer{xbufs, flags, xstride, world, rank};
+    return step_launch(jobs, njobs, param, grad, m, v, total, lr, beta1, beta2, eps, max_norm, step, segs, nseg, 1,
+                       stream, &peer);
+}
+
+// Exchange buffers: plain device allocations shared with the other ranks'
+// processes through CUDA IPC handles (set-up time only, not the hot path).
+int d1_peer_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int d1_peer_alloc(int64_t bytes, void **ptr, void *handle) {
+    if (bytes <= 0 || !ptr || !handle) return D1_ERR_BAD_ARGUMENT;
+    cudaError_t e = cudaMalloc(ptr, (size_t)bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, (size_t)bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle((cudaIpcMemHandle_t *)handle, *ptr);
+    return (int)e;
+}
+
+int d1_peer_open(const void *handle, void **ptr) {
+    if (!handle || !ptr) return D1_ERR_BAD_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return (int)cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+int d1_peer_close(void *ptr) { return ptr ? (int)cudaIpcCloseMemHandle(ptr) : D1_ERR_BAD_ARGUMENT; }
+
+int d1_peer_free(void *ptr) { return ptr ? (int)cudaFree(ptr) : D1_ERR_BAD_ARGUMENT; }
+
+// Nonzero when a peer all-reduce gave up waiting for a peer; reading clears it.
+int d1_peer_error(void) {
+    int h = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&h, ppo::g_peer_error, sizeof(int)) != cudaSuccess) return -1;
+    if (h) cudaMemcpyToSymbol(ppo::g_peer_error, &z, sizeof(int));
+    return h;
 }
 
 int d1_grad_reduce(const D1GradJob *jobs, int njobs, void *stream) {

@@ -48,6 +48,14 @@ SIGNATURES = {
     'd1_spec_d4_draw': [_P, _I, _P, _I, _P, _U64, _U64, _I, _P],
     'd1_ppo_step': [_P, _I, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _P, _P, _I, _P],
     'd1_grad_reduce': [_P, _I, _P],
+    'd1_ppo_step_peer': [_P, _I, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _P, _P, _I, _P, _P, C.c_int64, _I,
+                         _I, _P],
+    'd1_peer_handle_bytes': [],
+    'd1_peer_alloc': [C.c_int64, _P, _P],
+    'd1_peer_open': [_P, _P],
+    'd1_peer_close': [_P],
+    'd1_peer_free': [_P],
+    'd1_peer_error': [],
     'd1_ppo_gather_x': [_P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_pair': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_col_sum_part_len': [_I, _I],

@@ -16,8 +16,10 @@ Per minibatch (all device work is libd1 kernels, launched on the current stream)
   step       slab and loss-partial reductions      d1_ppo_step (a reduction
              into the flat gradient, its norm,     launch, then the Adam launch)
              clip + Adam + bf16 copies
-  (multi-GPU: d1_grad_reduce, NCCL all-reduce of the flat fp32 gradient, then
-  d1_ppo_step without reductions)
+  (multi-GPU, default: d1_ppo_step_peer -- the reduction publishes each rank's
+  gradient in an exchange buffer that the other ranks map through CUDA IPC, a
+  kernel sums all ranks' buffers over NVLink peer loads after per-rank flags,
+  then Adam; peer=False: d1_grad_reduce, NCCL all-reduce, d1_ppo_step)
 
 The weight-gradient GEMMs read dh2, h1, dh1 and X as stored (row-major, so
 [K, M] / [K, N] with K = samples): their tensor-core operands are MN-major and
@@ -52,7 +54,7 @@ class GradJob(C.Structure):
 class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
-                 gae_mode=1, splits=8, group=None, graph=True):
+                 gae_mode=1, splits=8, group=None, graph=True, peer=True):
         self.policy, self.rollout = policy, rollout
         self.mb, self.epochs = minibatch, epochs
         self.lr, self.clip, self.vclip, self.vf_coef, self.ent_coef = lr, clip, vclip, vf_coef, ent_coef
@@ -113,6 +115,37 @@ class PPO:
                 GradJob(ptr(self.part[:, head_len:]), self.part_len, self.loss_blocks, 1, 8, 8, 0, ptr(self.terms),
                         None)]
         self.jobs = (GradJob * len(jobs))(*jobs)
+        self.peer = None
+        if group is not None and peer:
+            self._peer_setup(group)
+
+    def _peer_setup(self, group):
+        """Exchange buffers for the peer all-reduce: each rank allocates two
+        halves of the flat gradient plus one flag per rank, shares the CUDA IPC
+        handle over the process group and maps every peer's buffer."""
+        import torch.distributed as dist
+        lib, world, rank = self.lib, dist.get_world_size(group), dist.get_rank(group)
+        if world > 8:
+            raise ValueError('the peer all-reduce supports up to 8 ranks')
+        P = self.grad.numel()
+        self.xstride = (P + 3) // 4 * 4
+        flag_off = 2 * self.xstride * 4
+        base, handle = C.c_void_p(), (C.c_char * lib.d1_peer_handle_bytes())()
+        with torch.cuda.device(self.policy.device):
+            check(lib.d1_peer_alloc(flag_off + 8 * 8, C.byref(base), handle), 'd1_peer_alloc')
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            ptrs = []
+            for p, h in enumerate(handles):
+                if p == rank:
+                    ptrs.append(base.value)
+                else:
+                    q = C.c_void_p()
+                    check(lib.d1_peer_open(h, C.byref(q)), 'd1_peer_open')
+                    ptrs.append(q.value)
+        self.peer = dict(world=world, rank=rank, base=base.value, ptrs=ptrs,
+                         xbufs=(C.c_void_p * world)(*ptrs),
+                         flags=(C.c_void_p * world)(*[q + flag_off for q in ptrs]))
 
     @property
     def stream(self):
@@ -157,6 +190,14 @@ class PPO:
         # dW1 = dh1^T X; X's ones column makes slab column 1832 the column sums of dh1 (db1)
         G.gemm_ex(self.dh1, self.x, a_kn=True, b_kn=True, out_f32=self.slab1, splits=self.s1)
         jobs, njobs = self.jobs, len(self.jobs)
+        if self.peer is not None:
+            pr = self.peer
+            check(lib.d1_ppo_step_peer(jobs, njobs, p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(),
+                                       self.v.data_ptr(), g.numel(), self.lr, self.betas[0], self.betas[1], self.eps,
+                                       self.max_grad_norm, self.step_dev.data_ptr(), self.segs, len(self.segs),
+                                       pr['xbufs'], pr['flags'], self.xstride, pr['world'], pr['rank'], s),
+                  'd1_ppo_step_peer')
+            return self.terms
         if self.group is not None:
             import torch.distributed as dist
             check(lib.d1_grad_reduce(jobs, njobs, s), 'd1_grad_reduce')
@@ -198,8 +239,20 @@ class PPO:
                 self.graph.replay()
 
     def release(self):
-        """Free the captured graph (before destroying a process group it uses)."""
+        """Free the captured graph (before destroying a process group it uses)
+        and, after every rank has finished with them, the exchange buffers."""
         self.graph = None
+        if self.peer is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.policy.device)
+            dist.barrier(group=self.group)
+            pr = self.peer
+            for p, q in enumerate(pr['ptrs']):
+                if p != pr['rank']:
+                    self.lib.d1_peer_close(C.c_void_p(q))
+            dist.barrier(group=self.group)
+            self.lib.d1_peer_free(C.c_void_p(pr['base']))
+            self.peer = None
 
     def iteration(self, generator=None):
         """Collect a rollout, compute advantages, update: one PPO iteration."""

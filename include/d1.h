@@ -418,6 +418,34 @@ int d1_ppo_step(const D1GradJob *jobs, int njobs, float *param, float *grad, flo
 /* Step (1) of d1_ppo_step alone (multi-GPU: reduce, all-reduce, then
  * d1_ppo_step with no jobs). */
 int d1_grad_reduce(const D1GradJob *jobs, int njobs, void *stream);
+/* d1_ppo_step for data-parallel ranks with the gradient all-reduce done through
+ * peer memory instead of a collective library: (1) the reduction writes this
+ * rank's gradient into half (epoch & 1) of its exchange buffer xbufs[rank]
+ * (epoch = *step + 1) and its last block stores flags[p][rank] = epoch on every
+ * peer p (system-scope release); (2) every block waits, bounded, for
+ * flags[rank][p] >= epoch from each peer, then sums a contiguous range of all
+ * ranks' halves in rank order (peer loads over NVLink), divides by world and
+ * writes `grad` -- the same bits on every rank -- with its sums of squares;
+ * (3) Adam as d1_ppo_step. xbufs[p] / flags[p] are rank p's exchange buffer
+ * (2 * xstride floats, xstride >= total, a multiple of 4) and flag array
+ * (world u64) as mapped in this process (d1_peer_open); world <= 8. The two
+ * halves make a rank's next write safe: before it, every peer has flagged the
+ * epoch in between, which it does only after reading. */
+int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                     float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
+                     const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
+                     int world, int rank, void *stream);
+/* Exchange-buffer set-up through CUDA IPC (not on the hot path): allocate
+ * `bytes` of zeroed device memory and its handle (d1_peer_handle_bytes()
+ * bytes), map another process's buffer from its handle, unmap, free. */
+int d1_peer_handle_bytes(void);
+int d1_peer_alloc(int64_t bytes, void **ptr, void *handle);
+int d1_peer_open(const void *handle, void **ptr);
+int d1_peer_close(void *ptr);
+int d1_peer_free(void *ptr);
+/* Nonzero when a peer all-reduce gave up waiting for a peer (that block's
+ * range of the gradient kept its old values); reading clears it. */
+int d1_peer_error(void);
 /* Gather x[i, 0..F) = obs[idx[i], 0..F) into rows of pitch ldx; with ones_col,
  * columns F..F+7 of every row are (1, 0, ..., 0), so that a weight-gradient
  * product dh^T x also yields the bias gradient (column sums of dh) in its

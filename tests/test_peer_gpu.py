@@ -1,0 +1,86 @@
+"""Multi-GPU PPO update with the gradient all-reduce through peer memory
+(d1_ppo_step_peer) against the same update with NCCL's all-reduce
+(peer=False), on 2 GPUs as 2 processes: after every minibatch both give the
+same parameters bit for bit (the mean of two values is one add and one divide
+either way), and every rank holds the same parameters. Several minibatches in a
+row exercise both halves of the exchange buffer; a captured epoch exercises the
+path inside a CUDA graph. Skipped with fewer than 2 GPUs."""
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, results):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, 'dcss-auto_b200'))
+    import datetime
+    import torch.distributed as dist
+    from d1 import policy, ppo, rollout, spec_env
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device('cuda', rank))
+    try:
+        B, T, mb = 512, 16, 2048
+
+        def make(peer, graph):
+            env = spec_env.SpecEnv(B, seed=3, first_env=rank * B, device=f'cuda:{rank}')
+            pol = policy.Policy(seed=0, device=f'cuda:{rank}')
+            roll = rollout.Rollout(env, pol, T, seed=3)
+            roll.collect()
+            tr = ppo.PPO(pol, roll, minibatch=mb, epochs=2, group=dist.group.WORLD, peer=peer, graph=graph)
+            tr.advantages()
+            return tr
+
+        a, b = make(True, False), make(False, False)
+        g = torch.Generator(device=f'cuda:{rank}').manual_seed(7)
+        same, ranks_agree = True, True
+        for k in range(5):
+            idx = torch.randperm(a.total, device=f'cuda:{rank}', generator=g)[:mb]
+            a.minibatch(idx)
+            b.minibatch(idx)
+            torch.cuda.synchronize()
+            same &= torch.equal(a.policy.flat, b.policy.flat) and torch.equal(a.grad, b.grad)
+            both = [torch.empty_like(a.policy.flat) for _ in range(world)]
+            dist.all_gather(both, a.policy.flat)
+            ranks_agree &= all(torch.equal(both[0], x) for x in both)
+        # a captured epoch (the second update epoch replays a CUDA graph)
+        c, d = make(True, True), make(False, True)
+        gc, gd = torch.Generator(device=f'cuda:{rank}').manual_seed(9), torch.Generator(device=f'cuda:{rank}').manual_seed(9)
+        c.update(gc)
+        d.update(gd)
+        torch.cuda.synchronize()
+        graphed_same = torch.equal(c.policy.flat, d.policy.flat)
+        err = a.lib.d1_peer_error()
+        for tr in (a, b, c, d):
+            tr.release()
+        results[rank] = dict(same=bool(same), ranks_agree=bool(ranks_agree), graphed_same=bool(graphed_same),
+                             err=int(err))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allreduce_update_equals_the_nccl_update():
+    if torch.cuda.device_count() < 2:
+        pytest.skip('needs 2 GPUs')
+    import torch.multiprocessing as mp
+    ctx = mp.get_context('spawn')
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = 29600 + os.getpid() % 200
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    for r in range(2):
+        assert results[r] == dict(same=True, ranks_agree=True, graphed_same=True, err=0), results[r]
