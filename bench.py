@@ -317,7 +317,8 @@ def run_ours(args, rank, world, local_rank):
         p3.record(stream)
         torch.cuda.synchronize()
         roll.roll()
-        trainer.release()  # its captured graph holds NCCL calls: free it before the process group goes
+        peer_error = trainer.lib.d1_peer_error() if trainer.peer is not None else 0
+        trainer.release()  # graph and exchange buffers go before the process group does
         it_ms = torch.tensor([p0.elapsed_time(p3)], device=dev)
         if world > 1:
             dist.all_reduce(it_ms, op=dist.ReduceOp.MAX)
@@ -326,7 +327,9 @@ def run_ours(args, rank, world, local_rank):
                     'rollout_ms': p0.elapsed_time(p1), 'gae_ms': p1.elapsed_time(p2),
                     'update_ms': p2.elapsed_time(p3), 'minibatch_ms': p2.elapsed_time(p3) / updates,
                     'samples_per_iteration': T * B * world, 'minibatch': args.minibatch, 'epochs': args.epochs,
-                    'finite': bool(torch.isfinite(policy.flat).all().item())}
+                    'finite': bool(torch.isfinite(policy.flat).all().item()),
+                    'gradient_exchange': ('peer memory (NVLink)' if trainer.peer is not None else 'NCCL') if world > 1
+                    else None, 'peer_error': int(peer_error)}
     # centered-map conv policy with the autoregressive head,
     # 131,072 envs per GPU; a step = crop + conv stack + FC + head + AR sampling
     # + env step (no 1832-feature observation is written).
