@@ -28,8 +28,6 @@ namespace ppo {
 constexpr int RED_MAX_BLOCKS = 65536;
 __device__ double g_gae_part[RED_MAX_BLOCKS][2];
 __device__ unsigned g_gae_ticket;
-__device__ double g_sumsq_part[RED_MAX_BLOCKS][2];
-__device__ unsigned g_sumsq_ticket;
 
 // Block-wide ordered sum of (a, b): warp butterflies, then thread 0 over the
 // warps in order. Result valid in thread 0.
@@ -228,7 +226,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__restrict__ obs, int F,
                                                      const int64_t *__restrict__ idx, int n, __nv_bfloat16 *x,
-                                                     int ldx, int ones, __nv_bfloat16 *xt, int ldt) {
+                                                     int ldx, int ones) {
     extern __shared__ __align__(16) __nv_bfloat16 gbuf[];  // [G_STAGES][G_SAMPLES][G_PITCH]
     const int s0 = blockIdx.x * G_SAMPLES;
     const int t = threadIdx.x, part = t & 7;
@@ -269,23 +267,6 @@ __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__rest
                 if (live[h] && f < F)
                     *reinterpret_cast<uint4 *>(x + (size_t)(s0 + ls) * ldx + f) =
                         *reinterpret_cast<const uint4 *>(buf + g_swz(ls, part));
-            }
-        }
-        if (xt) {
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int feat = (t >> 3) + 32 * h;  // 8 threads = 64 samples of one feature
-                const int ff = f0 + feat, sb = s0 + part * 8;
-                if (ff < F && sb < n) {
-                    __align__(16) __nv_bfloat16 o[8];
-#pragma unroll
-                    for (int i = 0; i < 8; i++) o[i] = buf[g_swz(part * 8 + i, feat >> 3) + (feat & 7)];
-                    if (sb + 8 <= n) {
-                        *reinterpret_cast<uint4 *>(xt + (size_t)ff * ldt + sb) = *reinterpret_cast<uint4 *>(o);
-                    } else {
-                        for (int i = 0; i < 8 && sb + i < n; i++) xt[(size_t)ff * ldt + sb + i] = o[i];
-                    }
-                }
             }
         }
         __syncthreads();
@@ -686,34 +667,6 @@ __global__ void __launch_bounds__(M_WARPS * 32) loss_mma_kernel(LossArgs a) {
     }
 }
 
-// out[i] = sum over p of parts[p * stride + i] (loss-kernel block partials).
-// A block owns 32 consecutive i; its 8 warps sum interleaved part subsets
-// (p = warp, warp + 8, ...) and the per-warp sums are added in warp order, so
-// the result does not depend on scheduling.
-__global__ void __launch_bounds__(256) sum_rows_kernel(const float *parts, int nparts, int stride, int len,
-                                                       float *out) {
-    __shared__ float part_s[8][32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int i = blockIdx.x * 32 + lane;
-    float s0 = 0.f, s1 = 0.f;
-    if (i < len) {
-        int p = warp;
-        for (; p + 8 < nparts; p += 16) {
-            s0 += parts[(size_t)p * stride + i];
-            s1 += parts[(size_t)(p + 8) * stride + i];
-        }
-        if (p < nparts) s0 += parts[(size_t)p * stride + i];
-    }
-    part_s[warp][lane] = s0 + s1;
-    __syncthreads();
-    if (warp == 0 && i < len) {
-        float t = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8; w++) t += part_s[w][lane];
-        out[i] = t;
-    }
-}
-
 // out[i] = sum over splits of slabs[s][i] (split-K partial products), i < count.
 // A block owns 64 float4 columns and G = blockDim.x / 64 groups of threads
 // (G grows with the number of slabs, up to 4); group y adds slabs y, y+G, ...
@@ -756,75 +709,7 @@ __global__ void __launch_bounds__(RS_COLS * RS_GROUPS) reduce_slabs_kernel(const
     }
 }
 
-// out[r] = sum of row r of a bf16 [rows, cols] matrix (pitch ld); one block per row.
-__global__ void __launch_bounds__(256) row_sum_bf16_kernel(const __nv_bfloat16 *__restrict__ m, int rows, int cols,
-                                                           int ld, float *out) {
-    __shared__ float ws[8];
-    const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float s = 0.f;
-    for (int c = threadIdx.x * 8; c < cols; c += 256 * 8) {
-        if (c + 8 <= cols) {
-            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(m + (size_t)r * ld + c));
-            const __nv_bfloat162 *p2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float2 f = __bfloat1622float2(p2[j]);
-                s += f.x + f.y;
-            }
-        } else {
-            for (int j = c; j < cols; j++) s += __bfloat162float(m[(size_t)r * ld + j]);
-        }
-    }
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
-    if (lane == 0) ws[warp] = s;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float t = 0.f;
-        for (int w = 0; w < 8; w++) t += ws[w];
-        out[r] = t;
-    }
-}
-
-// Column sums of a bf16 [rows, cols] matrix (pitch ld) in two deterministic
-// passes: block (x, y) sums rows [y*CS_ROWS, (y+1)*CS_ROWS) of 32 columns
-// (8 thread groups of every 8th row, added in group order) into
-// part[y][cols]; sum_rows_kernel then adds the chunk partials in chunk order.
-constexpr int CS_ROWS = 128;
-__global__ void __launch_bounds__(256) col_sum_bf16_kernel(const __nv_bfloat16 *__restrict__ m, int rows, int cols,
-                                                           int ld, float *__restrict__ part) {
-    __shared__ float ps[8][33];
-    const int cx = threadIdx.x & 31, gy = threadIdx.x >> 5;
-    const int c = blockIdx.x * 32 + cx, r0 = blockIdx.y * CS_ROWS;
-    float acc = 0.f;
-    if (c < cols)
-        for (int r = r0 + gy; r < min(rows, r0 + CS_ROWS); r += 8) acc += __bfloat162float(m[(size_t)r * ld + c]);
-    ps[gy][cx] = acc;
-    __syncthreads();
-    if (gy == 0 && c < cols) {
-        float t = 0.f;
-#pragma unroll
-        for (int g = 0; g < 8; g++) t += ps[g][cx];
-        part[(size_t)blockIdx.y * cols + c] = t;
-    }
-}
-
 // ------------------------------------------------------------------ optimizer
-// sum of squares of g[0..n) into *out (double, accumulated)
-__global__ void __launch_bounds__(256) sumsq_kernel(const float *__restrict__ g, int64_t n, double *out) {
-    double s = 0.0;
-    const int64_t n4 = n / 4;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(g) + i);
-        s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-    }
-    if (blockIdx.x == 0)
-        for (int64_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) s += (double)g[i] * g[i];
-    __shared__ double ws[8][2];
-    double zero = 0.0;
-    block_sum2<8>(s, zero, ws);
-    finish_sum2(s, 0.0, g_sumsq_part, &g_sumsq_ticket, out, false);
-}
-
 // Adam (torch.optim.Adam semantics) on fp32 masters with the gradient scaled by
 // min(1, max_norm / (||g|| + 1e-6)) (torch.nn.utils.clip_grad_norm_). Segments
 // that feed the GEMMs are also written as bf16 copies: seg_bf16[i] (same
@@ -836,8 +721,6 @@ struct AdamSeg {
 };
 struct AdamArgs {
     float *param, *grad, *m, *v;
-    const double *sumsq;
-    const int64_t *step;  // device counter: the step being taken (1-based)
     float lr, beta1, beta2, eps, max_norm;
     AdamSeg seg[8];
     int nseg;
@@ -867,51 +750,6 @@ __device__ __forceinline__ void adam_copies(const AdamArgs &a, int64_t i, float 
         }
     }
 }
-__global__ void adam_kernel(AdamArgs a) {
-    // step scalars once per block (double-precision pow is slow per thread)
-    __shared__ float sc[3];
-    if (threadIdx.x == 0) {
-        const double norm = sqrt(*a.sumsq);
-        const double t = (double)*a.step;
-        sc[0] = (float)(1.0 - pow((double)a.beta1, t));
-        sc[1] = (float)sqrt(1.0 - pow((double)a.beta2, t));
-        float scale = 1.f;
-        if (a.max_norm > 0.f) {
-            const float coef = a.max_norm / ((float)norm + 1e-6f);
-            if (coef < 1.f) scale = coef;
-        }
-        sc[2] = scale;
-    }
-    __syncthreads();
-    const float bc1 = sc[0], bc2_sqrt = sc[1], scale = sc[2];
-    const int64_t n4 = a.total / 4, stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4; q += stride) {
-        const float4 g4 = reinterpret_cast<const float4 *>(a.grad)[q];
-        float4 m4 = reinterpret_cast<const float4 *>(a.m)[q], v4 = reinterpret_cast<const float4 *>(a.v)[q];
-        float4 p4 = reinterpret_cast<const float4 *>(a.param)[q];
-        p4.x = adam_one(a, g4.x, m4.x, v4.x, p4.x, scale, bc1, bc2_sqrt);
-        p4.y = adam_one(a, g4.y, m4.y, v4.y, p4.y, scale, bc1, bc2_sqrt);
-        p4.z = adam_one(a, g4.z, m4.z, v4.z, p4.z, scale, bc1, bc2_sqrt);
-        p4.w = adam_one(a, g4.w, m4.w, v4.w, p4.w, scale, bc1, bc2_sqrt);
-        reinterpret_cast<float4 *>(a.m)[q] = m4;
-        reinterpret_cast<float4 *>(a.v)[q] = v4;
-        reinterpret_cast<float4 *>(a.param)[q] = p4;
-        adam_copies(a, 4 * q, p4.x);
-        adam_copies(a, 4 * q + 1, p4.y);
-        adam_copies(a, 4 * q + 2, p4.z);
-        adam_copies(a, 4 * q + 3, p4.w);
-    }
-    if (blockIdx.x == 0)
-        for (int64_t i = 4 * n4 + threadIdx.x; i < a.total; i += blockDim.x) {
-            float m = a.m[i], v = a.v[i];
-            const float p = adam_one(a, a.grad[i], m, v, a.param[i], scale, bc1, bc2_sqrt);
-            a.m[i] = m;
-            a.v[i] = v;
-            a.param[i] = p;
-            adam_copies(a, i, p);
-        }
-}
-
 __global__ void counter_add_kernel(int64_t *c, int64_t delta) { *c += delta; }
 
 // ------------------------------------------------------------------ fused optimizer step
@@ -1252,18 +1090,6 @@ using namespace d1;
 
 extern "C" {
 
-int d1_ppo_gather(const void *obs, int F, const int64_t *idx, int n, void *x, void *xt, int ldt, void *stream) {
-    if (!obs || !idx || n <= 0 || F <= 0 || F % 8 || (xt && (ldt < n || ldt % 8))) return D1_ERR_BAD_ARGUMENT;
-    static uint64_t ready = 0;
-    const int err = ppo::opt_in_smem((const void *)ppo::gather_kernel, ppo::G_SMEM, &ready);
-    if (err) return err;
-    const int groups = ((F + ppo::G_FEAT - 1) / ppo::G_FEAT + ppo::G_GROUP - 1) / ppo::G_GROUP;
-    const dim3 grid((n + ppo::G_SAMPLES - 1) / ppo::G_SAMPLES, groups);
-    ppo::gather_kernel<<<grid, 256, ppo::G_SMEM, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16 *)obs, F, idx, n, (__nv_bfloat16 *)x, F, 0, (__nv_bfloat16 *)xt, ldt);
-    return (int)cudaGetLastError();
-}
-
 int d1_ppo_gather_x(const void *obs, int F, const int64_t *idx, int n, void *x, int ldx, int ones_col,
                     void *stream) {
     if (!obs || !idx || !x || n <= 0 || F <= 0 || F % 8 || ldx % 8 || ldx < F + (ones_col ? 8 : 0) ||
@@ -1275,7 +1101,7 @@ int d1_ppo_gather_x(const void *obs, int F, const int64_t *idx, int n, void *x, 
     const int groups = ((F + ppo::G_FEAT - 1) / ppo::G_FEAT + ppo::G_GROUP - 1) / ppo::G_GROUP;
     const dim3 grid((n + ppo::G_SAMPLES - 1) / ppo::G_SAMPLES, groups);
     ppo::gather_kernel<<<grid, 256, ppo::G_SMEM, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16 *)obs, F, idx, n, (__nv_bfloat16 *)x, ldx, ones_col != 0, nullptr, 0);
+        (const __nv_bfloat16 *)obs, F, idx, n, (__nv_bfloat16 *)x, ldx, ones_col != 0);
     return (int)cudaGetLastError();
 }
 
@@ -1301,42 +1127,12 @@ int d1_ppo_loss(const void *h2, const void *wh, const float *bh, const int64_t *
     return (int)cudaGetLastError();
 }
 
-int d1_sum_rows(const float *parts, int nparts, int stride, int len, float *out, void *stream) {
-    if (!parts || !out || nparts <= 0 || len <= 0 || stride < len) return D1_ERR_BAD_ARGUMENT;
-    ppo::sum_rows_kernel<<<(len + 31) / 32, 256, 0, (cudaStream_t)stream>>>(parts, nparts, stride, len, out);
-    return (int)cudaGetLastError();
-}
-
 int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, void *stream) {
     if (!slabs || !out || splits <= 0 || count <= 0) return D1_ERR_BAD_ARGUMENT;
     const int64_t n = (count & 3) == 0 ? count / 4 : count;
     const int groups = splits >= 32 ? ppo::RS_GROUPS : splits >= 16 ? 2 : 1;
     ppo::reduce_slabs_kernel<<<(unsigned)((n + ppo::RS_COLS - 1) / ppo::RS_COLS), ppo::RS_COLS * groups, 0,
                                (cudaStream_t)stream>>>(slabs, splits, count, out);
-    return (int)cudaGetLastError();
-}
-
-int d1_col_sum_part_len(int rows, int cols) { return ((rows + ppo::CS_ROWS - 1) / ppo::CS_ROWS) * cols; }
-
-int d1_col_sum_bf16(const void *m, int rows, int cols, int ld, float *part, float *out, void *stream) {
-    if (!m || !part || !out || rows <= 0 || cols <= 0 || ld < cols) return D1_ERR_BAD_ARGUMENT;
-    const int chunks = (rows + ppo::CS_ROWS - 1) / ppo::CS_ROWS;
-    const dim3 grid((cols + 31) / 32, chunks);
-    ppo::col_sum_bf16_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16 *)m, rows, cols, ld, part);
-    ppo::sum_rows_kernel<<<(cols + 31) / 32, 256, 0, (cudaStream_t)stream>>>(part, chunks, cols, cols, out);
-    return (int)cudaGetLastError();
-}
-
-int d1_row_sum_bf16(const void *m, int rows, int cols, int ld, float *out, void *stream) {
-    if (!m || !out || rows <= 0 || cols <= 0 || ld < cols || ld % 8) return D1_ERR_BAD_ARGUMENT;
-    ppo::row_sum_bf16_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16 *)m, rows, cols, ld, out);
-    return (int)cudaGetLastError();
-}
-
-int d1_sumsq(const float *g, int64_t n, double *out, void *stream) {
-    if (!g || !out || n <= 0 || (reinterpret_cast<uintptr_t>(g) & 15)) return D1_ERR_BAD_ARGUMENT;
-    const int64_t blocks = (n / 4 + 255) / 256;
-    ppo::sumsq_kernel<<<(unsigned)(blocks < 1 ? 1 : (blocks > 1184 ? 1184 : blocks)), 256, 0, (cudaStream_t)stream>>>(g, n, out);
     return (int)cudaGetLastError();
 }
 
@@ -1416,8 +1212,6 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
         d.grad = grad;
         d.m = m;
         d.v = v;
-        d.sumsq = nullptr;
-        d.step = step;
         d.lr = lr;
         d.beta1 = beta1;
         d.beta2 = beta2;
@@ -1495,40 +1289,6 @@ int d1_grad_reduce(const D1GradJob *jobs, int njobs, void *stream) {
 int d1_counter_add(int64_t *counter, int64_t delta, void *stream) {
     if (!counter) return D1_ERR_BAD_ARGUMENT;
     ppo::counter_add_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(counter, delta);
-    return (int)cudaGetLastError();
-}
-
-int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, int64_t total, float lr, float beta1,
-            float beta2, float eps, float max_norm, const int64_t *step, const D1AdamSegment *segs, int nseg,
-            void *stream) {
-    if (!param || !grad || !m || !v || !sumsq || !step || total <= 0 || nseg < 0 || nseg > 8)
-        return D1_ERR_BAD_ARGUMENT;
-    ppo::AdamArgs a;
-    a.param = param;
-    a.grad = grad;
-    a.m = m;
-    a.v = v;
-    a.sumsq = sumsq;
-    a.lr = lr;
-    a.beta1 = beta1;
-    a.beta2 = beta2;
-    a.eps = eps;
-    a.max_norm = max_norm;
-    a.step = step;
-    a.nseg = nseg;
-    a.total = total;
-    for (int i = 0; i < nseg; i++) {
-        a.seg[i].offset = segs[i].offset;
-        a.seg[i].count = segs[i].count;
-        a.seg[i].rows = segs[i].rows;
-        a.seg[i].cols = segs[i].cols;
-        a.seg[i].bf16 = (__nv_bfloat16 *)segs[i].bf16;
-        a.seg[i].bf16_t = (__nv_bfloat16 *)segs[i].bf16_t;
-    }
-    if ((reinterpret_cast<uintptr_t>(param) | reinterpret_cast<uintptr_t>(grad) | reinterpret_cast<uintptr_t>(m) |
-         reinterpret_cast<uintptr_t>(v)) & 15)
-        return D1_ERR_BAD_ARGUMENT;  // float4 access
-    ppo::adam_kernel<<<592, 256, 0, (cudaStream_t)stream>>>(a);
     return (int)cudaGetLastError();
 }
 

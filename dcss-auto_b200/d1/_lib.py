@@ -29,14 +29,9 @@ SIGNATURES = {
     'd1_policy_head_sample': [_P, _I, _I, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],
     'd1_gemm': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gae': [_P, _P, C.c_int64, C.c_int64, _P, _I, _I, _F, _F, _P, _P, _P, _I, _P],
-    'd1_ppo_gather': [_P, _I, _P, _I, _P, _P, _I, _P],
     'd1_ppo_loss_part_len': [],
     'd1_ppo_loss': [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_double, _I, _F, _F, _F, _F, _P, _P, _I, _P, _I, _P],
-    'd1_sum_rows': [_P, _I, _I, _I, _P, _P],
     'd1_reduce_slabs': [_P, _I, C.c_int64, _P, _P],
-    'd1_row_sum_bf16': [_P, _I, _I, _I, _P, _P],
-    'd1_sumsq': [_P, C.c_int64, _P, _P],
-    'd1_adam': [_P, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _P, _P, _I, _P],
     'd1_counter_add': [_P, C.c_int64, _P],
     'd1_gemm_splits': [_I, _I],
     'd1_gemm_bkn': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _I, _P],
@@ -58,8 +53,6 @@ SIGNATURES = {
     'd1_peer_error': [],
     'd1_ppo_gather_x': [_P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_pair': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
-    'd1_col_sum_part_len': [_I, _I],
-    'd1_col_sum_bf16': [_P, _I, _I, _I, _P, _P, _P],
     'd1_gemm_head_sample': [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],
     'd1_gemm_error': [],
     'd1_gemm_wgrad_noalloc': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _I, _P],

@@ -345,9 +345,6 @@ int d1_gemm_error(void);
  * most 16,777,216 (mode 0) or 2,097,152 (mode 1), else D1_ERR_TOO_LARGE. */
 int d1_gae(const float *reward, const float *done, int64_t r_step, int64_t r_env, const float *value, int T, int B,
            float gamma, float lambda, float *adv, float *ret, double *stats, int mode, void *stream);
-/* Minibatch gather: x[i] = obs[idx[i]] (bf16 [n, F]) and xt = x^T (bf16 [F, ldt]);
- * either output may be NULL. F % 8 == 0. */
-int d1_ppo_gather(const void *obs, int F, const int64_t *idx, int n, void *x, void *xt, int ldt, void *stream);
 /* Length of one block partial written by d1_ppo_loss: dWh[13*256], dbh[13], db2[256],
  * then 8 loss terms (sum pg, sum vf, sum entropy, clipped count, sum approx-kl, 0, 0, 0). */
 int d1_ppo_loss_part_len(void);
@@ -364,20 +361,8 @@ int d1_ppo_loss(const void *h2, const void *wh, const float *bh, const int64_t *
                 const float *old_value, const double *adv_stats, double adv_count, int n, float clip, float vclip,
                 float vf_coef, float ent_coef, void *dh2, void *dh2t, int ldt, float *part, int blocks,
                 void *stream);
-/* out[i] = sum_p parts[p * stride + i], i < len. */
-int d1_sum_rows(const float *parts, int nparts, int stride, int len, float *out, void *stream);
 /* out[i] = sum_s slabs[s * count + i] (split-K partial products, deterministic order). */
 int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, void *stream);
-/* out[r] = sum of row r of bf16 m [rows, cols] (pitch ld): bias gradients. */
-int d1_row_sum_bf16(const void *m, int rows, int cols, int ld, float *out, void *stream);
-/* out[c] = sum over rows of a bf16 [rows, cols] matrix (pitch ld), in chunks
- * of 128 rows: part is a caller workspace of d1_col_sum_part_len(rows, cols)
- * floats; chunk partials are added in order (deterministic). */
-int d1_col_sum_part_len(int rows, int cols);
-int d1_col_sum_bf16(const void *m, int rows, int cols, int ld, float *part, float *out, void *stream);
-/* *out += sum g[i]^2 (double), deterministic like d1_gae's statistics (calls on
- * one device must not overlap). */
-int d1_sumsq(const float *g, int64_t n, double *out, void *stream);
 /* A parameter segment whose bf16 compute copy the optimizer refreshes: elements
  * [offset, offset + count) form a [rows, cols] matrix; bf16 receives the same
  * layout and bf16_t (when not NULL) its transpose. */
@@ -385,19 +370,14 @@ typedef struct { int64_t offset, count; int rows, cols; void *bf16, *bf16_t; } D
 /* *counter += delta on the device (the optimizer's step count lives on the
  * device so that a captured CUDA graph of many updates stays correct). */
 int d1_counter_add(int64_t *counter, int64_t delta, void *stream);
-/* torch.optim.Adam step (bias-corrected with the device step count *step,
- * 1-based; eps outside the sqrt) on fp32 master params after scaling grad by
- * min(1, max_norm / (sqrt(*sumsq) + 1e-6)) (torch.nn.utils.clip_grad_norm_;
- * max_norm <= 0 disables), then refreshes the bf16 copies of `segs` (host
- * array of nseg <= 8). param, grad, m and v are 16-byte aligned. */
-int d1_adam(float *param, float *grad, float *m, float *v, const double *sumsq, int64_t total, float lr, float beta1,
-            float beta2, float eps, float max_norm, const int64_t *step, const D1AdamSegment *segs, int nseg,
-            void *stream);
-
 /* End of a minibatch in two launches: (1) reduce the gradient's partial
- * products into the flat gradient, with per-block sums of squares; (2) the
- * d1_adam step (clip by the global norm, Adam, bf16 copies) with *step advanced
- * by one on the device (the step taken is the old *step + 1). Job j
+ * products into the flat gradient, with per-block sums of squares; (2) a
+ * torch.optim.Adam step (eps outside the sqrt, bias correction with the device
+ * step count) on the fp32 master params after scaling the gradient by
+ * min(1, max_norm / (||grad|| + 1e-6)) (torch.nn.utils.clip_grad_norm_;
+ * max_norm <= 0 disables), refreshing the bf16 copies of `segs` (host array of
+ * nseg <= 8); *step advances by one on the device (the step taken is the old
+ * *step + 1). param, grad, m and v are 16-byte aligned. Job j
  * (njobs <= 4): element e < rows * cols_in of partial p < nsrc is
  * src[p * stride + e]; element (r, c) of the sum goes to
  * dst[r * cols_out + c] when c < cols_out, to dst_extra[r] when c == cols_out
@@ -426,7 +406,7 @@ int d1_grad_reduce(const D1GradJob *jobs, int njobs, void *stream);
  * flags[rank][p] >= epoch from each peer, then sums a contiguous range of all
  * ranks' halves in rank order (peer loads over NVLink), divides by world and
  * writes `grad` -- the same bits on every rank -- with its sums of squares;
- * (3) Adam as d1_ppo_step. xbufs[p] / flags[p] are rank p's exchange buffer
+ * (3) the Adam step of d1_ppo_step. xbufs[p] / flags[p] are rank p's exchange buffer
  * (2 * xstride floats, xstride >= total, a multiple of 4) and flag array
  * (world u64) as mapped in this process (d1_peer_open); world <= 8. The two
  * halves make a rank's next write safe: before it, every peer has flagged the
