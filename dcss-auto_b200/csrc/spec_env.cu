@@ -95,6 +95,7 @@ struct Smem {
     uint32_t occ[PL];  // live monster positions during the monster phase
     uint32_t vis[16];  // LOS window rows: vis[dy+7] bit dx+7
     uint16_t vmask[16], fmask[16];  // remembered / floor bits of the window rows
+    uint4 onehot[8];  // observation cell of channel c: bf16 1.0 in half-word c
     uint8_t opqb[32];
     uint8_t occ_ch[CELLS + 7];
 };
@@ -788,7 +789,12 @@ __device__ float decision(Env &e, const D1SpecConfig &c, const RayArgs &ra, int 
 __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint16_t *legal) {
     Smem &s = *e.sm;
     const int lane = e.lane, px = e.player % W, py = e.player / W;
-    for (int j = lane; j < CELLS; j += 32) s.occ_ch[j] = 0xff;
+    for (int j = lane; j < (CELLS + 7) / 4; j += 32) reinterpret_cast<uint32_t *>(s.occ_ch)[j] = 0xffffffffu;
+    if (lane < 8) {
+        const uint32_t one = 0x3f80u << (16 * (lane & 1));
+        const int w = lane >> 1;
+        s.onehot[lane] = make_uint4(w == 0 ? one : 0u, w == 1 ? one : 0u, w == 2 ? one : 0u, w == 3 ? one : 0u);
+    }
     __syncwarp();
     const bool alive = lane < e.nmon && e.m_hp > 0;
     const bool mvis = alive && visible(e, e.m_pos);
@@ -811,22 +817,22 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
     const int sdx = e.stairs % W - px, sdy = e.stairs / W - py;
     const int sj = (sdx >= -7 && sdx <= 7 && sdy >= -7 && sdy <= 7) ? (sdy + 7) * 15 + sdx + 7 : -1;
     uint4 *dst = reinterpret_cast<uint4 *>(obs);
+    // Half-warps take window rows 2k and 2k + 1, a lane per column (lanes 15
+    // and 31 idle), so each store of the warp covers 30 consecutive cells.
     // Rolled: this kernel is bound by instruction fetch (ncu: "no instruction"
     // is the top stall), so compact code beats unrolled code here.
+    const int wx = lane & 15;
 #pragma unroll 1
-    for (int k = 0; k < (CELLS + 31) / 32; k++) {
-        const int j = lane + 32 * k;
-        const int jc = j < CELLS ? j : CELLS - 1;
-        const int wy = jc / 15, wx = jc - wy * 15;
-        const uint32_t vm = s.vmask[wy], fm = s.fmask[wy], vr = s.vis[wy];
-        const int m = s.occ_ch[jc];
-        const int floor_ch = m != 0xff ? m : (jc == sj ? 4 : (((vr >> wx) & 1u) ? 3 : 2));
-        const int ch = ((vm >> wx) & 1u) ? (((fm >> wx) & 1u) ? floor_ch : 1) : 0;
-        // bf16 1.0 = 0x3f80 in half-word `ch`
-        const uint32_t one = 0x3f80u << (16 * (ch & 1));
-        const int w = ch >> 1;
-        const uint4 v = make_uint4(w == 0 ? one : 0u, w == 1 ? one : 0u, w == 2 ? one : 0u, w == 3 ? one : 0u);
-        if (obs && j < CELLS) dst[j] = v;
+    for (int k = 0; k < 8; k++) {
+        const int wy = 2 * k + (lane >> 4);
+        if (obs && wx < 15 && wy < 15) {
+            const int jc = wy * 15 + wx;
+            const uint32_t vm = s.vmask[wy], fm = s.fmask[wy], vr = s.vis[wy];
+            const int m = s.occ_ch[jc];
+            const int floor_ch = m != 0xff ? m : (jc == sj ? 4 : (((vr >> wx) & 1u) ? 3 : 2));
+            const int ch = ((vm >> wx) & 1u) ? (((fm >> wx) & 1u) ? floor_ch : 1) : 0;
+            dst[jc] = s.onehot[ch];
+        }
     }
     // scalars
     const int nvis = __popc(__ballot_sync(FULL, mvis));
