@@ -508,6 +508,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // split-K fp32 slabs (no transposed output, no fused head).
 constexpr int P_STAGES = 6, P_B_BYTES = 128 * BK * 2, P_STAGE_BYTES = A_BYTES + P_B_BYTES;
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + BIAS_BYTES;
+constexpr int P2_SMEM_BYTES = 4 * (2 * A_BYTES + P_B_BYTES) + 1024 + 256 + BIAS_BYTES;
 constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -548,21 +549,27 @@ __device__ __forceinline__ void arrive_cluster(uint32_t bar_cluster) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
+// SUB = 2: each CTA holds two 128-row blocks of A per K block (a 512-row pair
+// tile) and issues two MMAs against the same B half, so B is streamed half as
+// often; the two accumulators fill the 512 TMEM columns, so the accumulator is
+// single-buffered (the next tile's loads still run during the epilogue).
+template <int SUB>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p,
                      int tiles_m, int tiles_n, int tiles_total) {
+    constexpr int STG = SUB == 1 ? P_STAGES : 4, STG_BYTES = SUB * A_BYTES + P_B_BYTES, NBUF = SUB == 1 ? 2 : 1;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * P_STAGES + 4);
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + P_STAGES);
-    const uint32_t accf0 = smem_u32(bars + 2 * P_STAGES), acce0 = smem_u32(bars + 2 * P_STAGES + 2);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STG * STG_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STG + 4);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STG);
+    const uint32_t accf0 = smem_u32(bars + 2 * STG), acce0 = smem_u32(bars + 2 * STG + 2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
 
     if (warp == 0 && lane == 0) {
-        for (int s = 0; s < P_STAGES; s++) {
+        for (int s = 0; s < STG; s++) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
@@ -592,22 +599,27 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
             const int kt0 = split * p.k_tiles_per_split;
             const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
-            const int m0 = mt * 256 + 128 * (int)rank, n0 = nt * BN + 128 * (int)rank;
+            const int m0 = mt * 256 * SUB + 128 * (int)rank, n0 = nt * BN + 128 * (int)rank;
             for (int kt = kt0; kt < kt1; kt++, it++) {
-                const int s = it % P_STAGES;
-                if (it >= P_STAGES && !mbar_wait(empty0 + 8 * s, ((uint32_t)(it / P_STAGES) & 1u) ^ 1u)) {
+                const int s = it % STG;
+                if (it >= STG && !mbar_wait(empty0 + 8 * s, ((uint32_t)(it / STG) & 1u) ^ 1u)) {
                     ok = false;
                     break;
                 }
-                if (it >= P_STAGES) inflight_lo = it - P_STAGES + 1;
-                const uint32_t a_dst = smem_u32(smem + s * P_STAGE_BYTES), b_dst = a_dst + A_BYTES;
+                if (it >= STG) inflight_lo = it - STG + 1;
+                const uint32_t a_dst = smem_u32(smem + s * STG_BYTES), b_dst = a_dst + SUB * A_BYTES;
                 const uint32_t leader_full = mapa(full0 + 8 * s, 0);
-                if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * P_STAGE_BYTES);
-                if (p.a_mn) {
+                if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * STG_BYTES);
 #pragma unroll
-                    for (int j = 0; j < 2; j++) tma_load_2d_pair(a_dst + j * 8192, &map_a, leader_full, m0 + 64 * j, kt * BK);
-                } else {
-                    tma_load_2d_pair(a_dst, &map_a, leader_full, kt * BK, m0);
+                for (int sb = 0; sb < SUB; sb++) {
+                    if (p.a_mn) {
+#pragma unroll
+                        for (int j = 0; j < 2; j++)
+                            tma_load_2d_pair(a_dst + sb * A_BYTES + j * 8192, &map_a, leader_full, m0 + 256 * sb + 64 * j,
+                                             kt * BK);
+                    } else {
+                        tma_load_2d_pair(a_dst + sb * A_BYTES, &map_a, leader_full, kt * BK, m0 + 256 * sb);
+                    }
                 }
                 if (p.b_mn) {
 #pragma unroll
@@ -620,11 +632,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok) {
             atomicExch(&g_error, 5);
             if (rank == 0)
-                for (int i = inflight_lo; i < it; i++) mbar_wait(full0 + 8 * (i % P_STAGES), (uint32_t)(i / P_STAGES) & 1u);
+                for (int i = inflight_lo; i < it; i++) mbar_wait(full0 + 8 * (i % STG), (uint32_t)(i / STG) & 1u);
         } else {
             // the leader's last commits to this CTA's empty barriers land before it exits
-            for (int i = it > P_STAGES ? it - P_STAGES : 0; i < it; i++)
-                mbar_wait(empty0 + 8 * (i % P_STAGES), (uint32_t)(i / P_STAGES) & 1u);
+            for (int i = it > STG ? it - STG : 0; i < it; i++)
+                mbar_wait(empty0 + 8 * (i % STG), (uint32_t)(i / STG) & 1u);
         }
     } else if (warp == 1 && lane == 0 && rank == 0) {
         // ---- MMA issuer (leader only)
@@ -635,28 +647,32 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int split = t / (tiles_m * tiles_n);
             const int kt0 = split * p.k_tiles_per_split;
             const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
-            const int b = local & 1;
-            const uint32_t acc = tmem + (uint32_t)(b * TMEM_COLS);
-            if (local >= 2 && !mbar_wait(acce0 + 8 * b, ((uint32_t)(local >> 1) & 1u) ^ 1u)) {
+            const int b = local % NBUF;
+            const uint32_t acc = tmem + (uint32_t)(b * SUB * TMEM_COLS);
+            if (local >= NBUF && !mbar_wait(acce0 + 8 * b, ((uint32_t)(local / NBUF) & 1u) ^ 1u)) {
                 atomicExch(&g_error, 6);
                 ok = false;
                 break;
             }
             fence_after();
             for (int kt = kt0; kt < kt1; kt++, it++) {
-                const int s = it % P_STAGES;
-                if (!mbar_wait(full0 + 8 * s, (uint32_t)(it / P_STAGES) & 1u)) {
+                const int s = it % STG;
+                if (!mbar_wait(full0 + 8 * s, (uint32_t)(it / STG) & 1u)) {
                     atomicExch(&g_error, 7);
                     ok = false;
                     break;
                 }
                 fence_after();
-                const uint32_t a_base = smem_u32(smem + s * P_STAGE_BYTES), b_base = a_base + A_BYTES;
+                const uint32_t a_base = smem_u32(smem + s * STG_BYTES), b_base = a_base + SUB * A_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; kk++)
-                    mma_pair(acc, p.a_mn ? sw128_mn_desc(a_base + kk * 2048) : sw128_desc(a_base + kk * 32),
-                             p.b_mn ? sw128_mn_desc(b_base + kk * 2048) : sw128_desc(b_base + kk * 32), idesc,
-                             (kt > kt0 || kk > 0) ? 1u : 0u);
+                for (int sb = 0; sb < SUB; sb++)
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; kk++)
+                        mma_pair(acc + (uint32_t)(sb * TMEM_COLS),
+                                 p.a_mn ? sw128_mn_desc(a_base + sb * A_BYTES + kk * 2048)
+                                        : sw128_desc(a_base + sb * A_BYTES + kk * 32),
+                                 p.b_mn ? sw128_mn_desc(b_base + kk * 2048) : sw128_desc(b_base + kk * 32), idesc,
+                                 (kt > kt0 || kk > 0) ? 1u : 0u);
                 commit_pair(empty0 + 8 * s);
                 commit_pair(mapa(empty0 + 8 * s, 1));
             }
@@ -667,12 +683,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp >= 2) {
         // ---- epilogue (both CTAs): this CTA's 128 rows of the tile
         const int q = warp & 3, half = (warp - 2) >> 2;
-        float *bias_s = reinterpret_cast<float *>(smem + P_STAGES * P_STAGE_BYTES + 256) + (warp - 2) * (BN / 2);
+        float *bias_s = reinterpret_cast<float *>(smem + STG * STG_BYTES + 256) + (warp - 2) * (BN / 2);
         int local = 0;
         for (int t = cluster; t < tiles_total; t += clusters, local++) {
             const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
-            const int b = local & 1;
-            const int row = mt * 256 + 128 * (int)rank + q * 32 + lane;
+            const int b = local % NBUF;
             const int c0 = nt * BN + half * (BN / 2);
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -680,15 +695,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                 bias_s[lane * 4 + j] = (p.bias && col < p.N) ? __ldg(p.bias + col) : 0.f;
             }
             __syncwarp();
-            if (!mbar_wait(accf0 + 8 * b, (uint32_t)(local >> 1) & 1u)) {
+            if (!mbar_wait(accf0 + 8 * b, (uint32_t)(local / NBUF) & 1u)) {
                 atomicExch(&g_error, 8);
                 break;
             }
             fence_after();
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 64; cc++) {
+            for (int ci = 0; ci < SUB * (BN / 64); ci++) {
+                const int sb = ci / (BN / 64), cc = ci % (BN / 64);
+                const int row = mt * 256 * SUB + 256 * sb + 128 * (int)rank + q * 32 + lane;
                 uint32_t v[32];
-                const uint32_t taddr = tmem + (uint32_t)(b * TMEM_COLS) + ((uint32_t)(q * 32) << 16) +
+                const uint32_t taddr = tmem + (uint32_t)((b * SUB + sb) * TMEM_COLS) + ((uint32_t)(q * 32) << 16) +
                                        (uint32_t)(half * (BN / 2) + cc * 32);
                 __syncwarp();
                 D1_TMEM_LD32(taddr, v);
@@ -978,17 +995,24 @@ static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, in
     int dev = 0;
     if (cudaError_t e = cudaGetDevice(&dev)) return (int)e;
     if (!(dev < 64 && ((ready >> dev) & 1))) {
-        if (cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 P_SMEM_BYTES))
-            return (int)e;
+        cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             P_SMEM_BYTES);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_pair_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM_BYTES);
+        if (e != cudaSuccess) return (int)e;
         if (dev < 64) ready |= 1ull << dev;
     }
     Params p{M, N, K, per, kt, bias, relu, a_mn, nullptr, nullptr, b_mn, (const __nv_bfloat16 *)mask, ldm,
              (__nv_bfloat16 *)c, ldc, nullptr, 0, cf, ldcf};
-    const int tiles_m = (M + 255) / 256, tiles_n = (N + BN - 1) / BN;
-    const int tiles = tiles_m * tiles_n * splits;
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = SM_COUNT;
+    const int tiles_n = (N + BN - 1) / BN;
+    // 512-row pair tiles (B streamed half as often) once M is large enough for
+    // them to still give every pair a tile (measured: rollout layer 1, 65,536 x
+    // 256 x 1832: 74.7 -> 68.0 us)
+    const int sub = (M >= 8192 && ((M + 511) / 512) * tiles_n * splits >= sms / 2) ? 2 : 1;
+    const int tiles_m = (M + 256 * sub - 1) / (256 * sub);
+    const int tiles = tiles_m * tiles_n * splits;
     const int clusters = tiles < sms / 2 ? tiles : sms / 2;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -998,11 +1022,12 @@ static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, in
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.dynamicSmemBytes = sub == 2 ? P2_SMEM_BYTES : P_SMEM_BYTES;
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ma, mb, p, tiles_m, tiles_n, tiles);
+    return sub == 2 ? (int)cudaLaunchKernelEx(&cfg, gemm_pair_kernel<2>, ma, mb, p, tiles_m, tiles_n, tiles)
+                    : (int)cudaLaunchKernelEx(&cfg, gemm_pair_kernel<1>, ma, mb, p, tiles_m, tiles_n, tiles);
 }
 
 int d1_gemm_pair(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,

@@ -137,10 +137,12 @@ def test_gathered_rows_match_the_gathered_copy(G):
 @pytest.mark.parametrize('M,N,K,a_kn,b_kn,splits', [(65536, 256, 1832, False, False, 1), (1000, 256, 1832, False, False, 1),
                                                      (128, 13, 256, False, False, 1), (300, 1832, 256, False, False, 1),
                                                      (4096, 256, 4096, True, True, 8), (256, 1832, 8192, True, True, 16),
-                                                     (8192, 256, 256, False, True, 1), (2048, 512, 1024, True, False, 4)])
+                                                     (8192, 256, 256, False, True, 1), (2048, 512, 1024, True, False, 4),
+                                                     (40000, 256, 640, False, False, 1), (38000, 384, 512, True, True, 1)])
 def test_pair_kernel_matches_the_product(G, M, N, K, a_kn, b_kn, splits):
     """2-SM pair kernel: K-major and MN-major operands, ragged M and N, split-K
-    slabs; bf16 output with bias + ReLU + mask, and fp32 slabs equal to the
+    slabs, 256- and 512-row pair tiles (65,536, 40,000 and 38,000 rows take the
+    latter); bf16 output with bias + ReLU + mask, and fp32 slabs equal to the
     one-CTA kernel's."""
     g = torch.Generator(device='cuda').manual_seed(M + 3 * N + K)
     a = torch.randn(M, K, device='cuda', generator=g).to(torch.bfloat16)
