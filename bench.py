@@ -399,7 +399,7 @@ def run_ours(args, rank, world, local_rank):
                      'peak_kind': pk_kind,
                      'algorithmic_bytes_per_decision': ENV_BYTES_PER_DECISION,
                      'kernel_ms_per_step': env_ms},
-        'roofline_policy_gemm': {'kernel': 'd1::tc::gemm_pair_kernel (layer 1: M=%d, N=256, K=1832; 2-SM pairs)' % B,
+        'roofline_policy_gemm': {'kernel': 'd1::tc::gemm_pair_kernel<2> (layer 1: M=%d, N=256, K=1832; 512-row 2-SM pair tiles)' % B,
                                  'bound': 'tensor', 'achieved': gemm_tflops, 'peak': pk['bf16_tflops'],
                                  'unit': 'TFLOP/s', 'frac': gemm_tflops / pk['bf16_tflops'],
                                  'ms_per_launch': gemm_ms, 'peak_kind': pk_kind + ' burst'},
