@@ -845,8 +845,10 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
     const int weakest = wk == 0xffffffffu ? 0 : (int)wk;
     const unsigned og = __ballot_sync(FULL, mvis && e.m_kind == 4);
     const int ogre = og ? __ffs(og) - 1 : -1;
-    const bool rest_ok = e.hp < c.hp && c.regen > 0 && !visible_awake(e);
-    const bool attack_ok = adjacent_attack(e) >= 0;
+    // visible_awake(e) is any(mvis && awake) and adjacent_attack(e) >= 0 is any(adj):
+    // both reuse the ballots above
+    const bool rest_ok = e.hp < c.hp && c.regen > 0 && nvis_awake == 0;
+    const bool attack_ok = nadj > 0;
     const bool known = bitp(s.viewed, e.stairs);
     const int np = __shfl_sync(FULL, e.m_pos, near < 0 ? 0 : near), nh = __shfl_sync(FULL, e.m_hp, near < 0 ? 0 : near);
     const int na = __shfl_sync(FULL, e.m_awake, near < 0 ? 0 : near), nk = __shfl_sync(FULL, e.m_kind, near < 0 ? 0 : near);
