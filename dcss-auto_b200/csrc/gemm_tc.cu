@@ -849,7 +849,7 @@ static int gemm_attr() {
 // dominates): measured 1.2-1.3x on 512+-deep K ranges with N > 128, and no gain
 // on 256-deep ones.
 static bool pair_pays(int N, int K, int splits, bool ct, bool gathered) {
-    if (ct || gathered || N <= 128) return false;
+    if (ct || gathered || N <= 128 || K <= 0 || splits < 1) return false;
     const int kt = (K + BK - 1) / BK;
     if (splits > kt) splits = kt;
     const int per = (kt + splits - 1) / splits;
@@ -1039,6 +1039,7 @@ int d1_gemm_pair(const void *a, int lda, int a_mn, const void *b, int ldb, int b
 
 // Splits actually used for (K, requested splits): callers size fp32 slabs with it.
 int d1_gemm_splits(int K, int splits) {
+    if (K <= 0) return D1_ERR_BAD_ARGUMENT;
     const int kt = (K + BK - 1) / BK;
     if (splits < 1) splits = 1;
     if (splits > kt) splits = kt;

@@ -197,6 +197,8 @@ int d1_policy_head_greedy(const void *h_bf16, int n, int hidden, const void *wh_
 int d1_gemm(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
             const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf, int splits,
             void *stream);
+/* Number of fp32 slabs a split-K call writes for (K, splits); D1_ERR_BAD_ARGUMENT
+ * when K <= 0. */
 int d1_gemm_splits(int K, int splits);
 /* As d1_gemm with B stored [K, N] (row pitch ldb >= N, N contiguous: "MN-major")
  * instead of [N, K], so a weight gradient A^T-style product can read a row-major
