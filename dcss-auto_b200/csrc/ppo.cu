@@ -278,6 +278,45 @@ __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16 *__rest
         *reinterpret_cast<uint4 *>(x + (size_t)(s0 + t) * ldx + F) = make_uint4(0x3f80u, 0u, 0u, 0u);
 }
 
+// ------------------------------------------------------------------ compact-observation gather
+// X[i] = one-hot expansion of the compact observation row cobs[idx[i]] (320 B:
+// the channel 0-7 of each of the 225 window cells as a byte, then the 32
+// scalars as bf16 at byte 256) into the 1832-feature bf16 layout the policy
+// reads (cell c, channel k at element 8c + k; scalars at 1800), plus the ones
+// column (1, 0, ..., 0) at 1832 when asked for. One warp per sample: the row is
+// staged in shared memory, then each lane writes 16-byte units (one cell's 8
+// channels, or 8 scalars) from a table of the 8 one-hot patterns.
+constexpr int CG_WARPS = 8, COBS_BYTES = 320, COBS_CELLS = 225, COBS_SCALARS = 256;
+__global__ void __launch_bounds__(CG_WARPS * 32)
+    gather_cobs_kernel(const uint8_t *__restrict__ cobs, const int64_t *__restrict__ idx, int n, uint4 *x, int ldx16,
+                       int ones) {
+    __shared__ uint4 rows[CG_WARPS][COBS_BYTES / 16];
+    __shared__ uint4 onehot[8];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < 8) {
+        const uint32_t one = 0x3f80u << (16 * (threadIdx.x & 1));
+        const int k = threadIdx.x >> 1;
+        onehot[threadIdx.x] = make_uint4(k == 0 ? one : 0u, k == 1 ? one : 0u, k == 2 ? one : 0u, k == 3 ? one : 0u);
+    }
+    __syncthreads();
+    for (int i = blockIdx.x * CG_WARPS + w; i < n; i += gridDim.x * CG_WARPS) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(cobs + (size_t)idx[i] * COBS_BYTES);
+        if (lane < COBS_BYTES / 16) rows[w][lane] = __ldg(src + lane);
+        __syncwarp();
+        const uint8_t *codes = reinterpret_cast<const uint8_t *>(rows[w]);
+        uint4 *dst = x + (size_t)i * ldx16;
+        for (int u = lane; u < COBS_CELLS + 5; u += 32) {
+            uint4 v;
+            if (u < COBS_CELLS) v = onehot[codes[u] & 7];
+            else if (u < COBS_CELLS + 4) v = rows[w][COBS_SCALARS / 16 + (u - COBS_CELLS)];
+            else if (ones) v = make_uint4(0x3f80u, 0u, 0u, 0u);
+            else break;
+            dst[u] = v;
+        }
+        __syncwarp();
+    }
+}
+
 // ------------------------------------------------------------------ fused head + loss + backward to h2
 // Per minibatch row (sample index idx[row] into the rollout arrays):
 //   logits, value = h2 . Wh^T + bh; masked log-softmax over the legal bits;
@@ -1102,6 +1141,17 @@ int d1_ppo_gather_x(const void *obs, int F, const int64_t *idx, int n, void *x, 
     const dim3 grid((n + ppo::G_SAMPLES - 1) / ppo::G_SAMPLES, groups);
     ppo::gather_kernel<<<grid, 256, ppo::G_SMEM, (cudaStream_t)stream>>>(
         (const __nv_bfloat16 *)obs, F, idx, n, (__nv_bfloat16 *)x, ldx, ones_col != 0);
+    return (int)cudaGetLastError();
+}
+
+int d1_ppo_gather_cobs(const void *cobs, const int64_t *idx, int n, void *x, int ldx, int ones_col, void *stream) {
+    if (!cobs || !idx || !x || n <= 0 || ldx % 8 || ldx < 1832 + (ones_col ? 8 : 0) ||
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(cobs)) & 15))
+        return D1_ERR_BAD_ARGUMENT;
+    int blocks = (n + ppo::CG_WARPS - 1) / ppo::CG_WARPS;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    ppo::gather_cobs_kernel<<<blocks, ppo::CG_WARPS * 32, 0, (cudaStream_t)stream>>>(
+        (const uint8_t *)cobs, idx, n, (uint4 *)x, ldx / 8, ones_col != 0);
     return (int)cudaGetLastError();
 }
 

@@ -29,6 +29,9 @@ namespace d1 {
 namespace spec {
 
 constexpr int MAXM = 11, OBS = 1832, CELLS = 225, ACTIONS = 12, OUT = 10, COMPACT = 56;
+// Compact observation row: the channel (0-7) of each window cell as a byte
+// (0-224, then zeros to 255), the 32 scalars as bf16 at byte 256.
+constexpr int COBS = 320, COBS_SCALARS = 256;
 constexpr int ROW = 7680, OFF_DIST = 2048, PL = 210, OFF_VIS = 64, OFF_MON = 128, OFF_FLOOR = 256, OFF_VIEWED = 256 + 4 * PL;
 #ifndef D1_SPEC_WARPS
 #define D1_SPEC_WARPS 1
@@ -786,7 +789,7 @@ __device__ float decision(Env &e, const D1SpecConfig &c, const RayArgs &ra, int 
 // floor out of view, 3 visible floor, 4 stairs, 5 visible sleeping monster,
 // 6 visible awake monster, 7 visible ogre. Each cell is one 16-byte store of
 // eight bf16 values; the 32 scalars follow at element 1800.
-__device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint16_t *legal) {
+__device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint8_t *cobs, uint16_t *legal) {
     Smem &s = *e.sm;
     const int lane = e.lane, px = e.player % W, py = e.player / W;
     for (int j = lane; j < (CELLS + 7) / 4; j += 32) reinterpret_cast<uint32_t *>(s.occ_ch)[j] = 0xffffffffu;
@@ -825,15 +828,17 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
 #pragma unroll 1
     for (int k = 0; k < 8; k++) {
         const int wy = 2 * k + (lane >> 4);
-        if (obs && wx < 15 && wy < 15) {
+        if ((obs || cobs) && wx < 15 && wy < 15) {
             const int jc = wy * 15 + wx;
             const uint32_t vm = s.vmask[wy], fm = s.fmask[wy], vr = s.vis[wy];
             const int m = s.occ_ch[jc];
             const int floor_ch = m != 0xff ? m : (jc == sj ? 4 : (((vr >> wx) & 1u) ? 3 : 2));
             const int ch = ((vm >> wx) & 1u) ? (((fm >> wx) & 1u) ? floor_ch : 1) : 0;
-            dst[jc] = s.onehot[ch];
+            if (obs) dst[jc] = s.onehot[ch];
+            if (cobs) cobs[jc] = (uint8_t)ch;
         }
     }
+    if (cobs && lane < COBS_SCALARS - CELLS) cobs[CELLS + lane] = 0;
     // scalars
     const int nvis = __popc(__ballot_sync(FULL, mvis));
     const int nvis_awake = __popc(__ballot_sync(FULL, mvis && e.m_awake));
@@ -872,6 +877,7 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint1
                            1.f, 30.f, 1.f, 1.f};
     const float f = num[lane] / den[lane];
     if (obs) obs[1800 + lane] = __float2bfloat16_rn(f);
+    if (cobs) reinterpret_cast<__nv_bfloat16 *>(cobs + COBS_SCALARS)[lane] = __float2bfloat16_rn(f);
     if (lane < 8) {
         const bool ok = floor_at(e, neighbor(e.player, lane));
         const unsigned b = __ballot_sync(0xffu, ok);
@@ -964,7 +970,7 @@ __device__ void store(const Env &e, uint8_t *row) {
 
 __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     init_kernel(uint8_t *state, int n, D1SpecConfig c, RayArgs ra, uint64_t seed, int first_env,
-                __nv_bfloat16 *obs, uint16_t *legal) {
+                __nv_bfloat16 *obs, uint8_t *cobs, uint16_t *legal) {
     __shared__ Smem sms[WARPS];
     const int w = threadIdx.x >> 5, env = blockIdx.x * WARPS + w;
     if (env >= n) return;
@@ -983,7 +989,7 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     e.dirty_lo = H;
     e.dirty_hi = -1;
     reset(e, c, ra);
-    observe(e, c, obs ? obs + (size_t)env * OBS : nullptr, legal + env);
+    observe(e, c, obs ? obs + (size_t)env * OBS : nullptr, cobs ? cobs + (size_t)env * COBS : nullptr, legal + env);
     uint8_t *row = state + (size_t)env * ROW;
     for (int i = e.lane; i < OFF_FLOOR / 4; i += 32) reinterpret_cast<uint32_t *>(row)[i] = 0;
     __syncwarp();
@@ -992,7 +998,7 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
 
 __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     step_kernel(uint8_t *state, int n, D1SpecConfig c, RayArgs ra, int extra_layers, const int64_t *actions,
-                __nv_bfloat16 *obs, uint16_t *legal, float *out, const bool *active) {
+                __nv_bfloat16 *obs, uint8_t *cobs, uint16_t *legal, float *out, const bool *active) {
     __shared__ Smem sms[WARPS];
     const int w = threadIdx.x >> 5, env = blockIdx.x * WARPS + w;
     if (env >= n) return;
@@ -1006,7 +1012,7 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     load(e, row);
     const float o = decision(e, c, ra, extra_layers, (int)actions[env]);
     if (e.lane < OUT) out[(size_t)env * OUT + e.lane] = o;
-    observe(e, c, obs ? obs + (size_t)env * OBS : nullptr, legal + env);
+    observe(e, c, obs ? obs + (size_t)env * OBS : nullptr, cobs ? cobs + (size_t)env * COBS : nullptr, legal + env);
     store(e, row);
 }
 
@@ -1203,13 +1209,18 @@ static int spec_check(int n, const D1SpecConfig *c) {
     return 0;
 }
 
-int d1_spec_init(void *state, int n, const D1SpecConfig *c, uint64_t seed, int first_env, void *obs_bf16,
-                 uint16_t *legal, void *stream) {
+int d1_spec_init_ex(void *state, int n, const D1SpecConfig *c, uint64_t seed, int first_env, void *obs_bf16,
+                    void *cobs, uint16_t *legal, void *stream) {
     if (int err = spec_check(n, c)) return err;
     if (n == 0) return 0;
     spec::init_kernel<<<(n + spec::WARPS - 1) / spec::WARPS, spec::WARPS * 32, 0, (cudaStream_t)stream>>>(
-        (uint8_t *)state, n, *c, g_rays, seed, first_env, (__nv_bfloat16 *)obs_bf16, legal);
+        (uint8_t *)state, n, *c, g_rays, seed, first_env, (__nv_bfloat16 *)obs_bf16, (uint8_t *)cobs, legal);
     return (int)cudaGetLastError();
+}
+
+int d1_spec_init(void *state, int n, const D1SpecConfig *c, uint64_t seed, int first_env, void *obs_bf16,
+                 uint16_t *legal, void *stream) {
+    return d1_spec_init_ex(state, n, c, seed, first_env, obs_bf16, nullptr, legal, stream);
 }
 
 int d1_los_table(const uint8_t *floor, uint32_t *masks, void *stream) {
@@ -1228,13 +1239,19 @@ int d1_spec_crop(const void *state, int n, int g, uint16_t *crop, void *stream) 
     return (int)cudaGetLastError();
 }
 
-int d1_spec_step(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, uint16_t *legal,
-                 float *out, const bool *active, void *stream) {
+int d1_spec_step_ex(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, void *cobs,
+                    uint16_t *legal, float *out, const bool *active, void *stream) {
     if (int err = spec_check(n, c)) return err;
     if (n == 0) return 0;
     spec::step_kernel<<<(n + spec::WARPS - 1) / spec::WARPS, spec::WARPS * 32, 0, (cudaStream_t)stream>>>(
-        (uint8_t *)state, n, *c, g_rays, spec_extra_layers(*c), actions, (__nv_bfloat16 *)obs_bf16, legal, out, active);
+        (uint8_t *)state, n, *c, g_rays, spec_extra_layers(*c), actions, (__nv_bfloat16 *)obs_bf16, (uint8_t *)cobs,
+        legal, out, active);
     return (int)cudaGetLastError();
+}
+
+int d1_spec_step(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, uint16_t *legal,
+                 float *out, const bool *active, void *stream) {
+    return d1_spec_step_ex(state, n, c, actions, obs_bf16, nullptr, legal, out, active, stream);
 }
 
 int d1_spec_compact(const void *state, int n, int64_t *rows, void *stream) {

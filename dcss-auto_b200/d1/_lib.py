@@ -24,6 +24,9 @@ SIGNATURES = {
     'd1_spec_set_rays': [_P, _I],
     'd1_spec_init': [_P, _I, _P, _U64, _I, _P, _P, _P],
     'd1_spec_step': [_P, _I, _P, _P, _P, _P, _P, _P, _P],
+    'd1_spec_init_ex': [_P, _I, _P, _U64, _I, _P, _P, _P, _P],
+    'd1_spec_step_ex': [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P],
+    'd1_ppo_gather_cobs': [_P, _P, _I, _P, _I, _I, _P],
     'd1_spec_compact': [_P, _I, _P, _P],
     'd1_spec_planes': [_P, _I, _P, _P, _P],
     'd1_policy_head_sample': [_P, _I, _I, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],

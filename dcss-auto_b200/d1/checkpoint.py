@@ -10,7 +10,7 @@ import pathlib
 
 import torch
 
-FORMAT = 1
+FORMAT = 2
 
 
 def job_of(trainer):
@@ -26,7 +26,7 @@ def state_dict(trainer, generator=None, extra=None):
     r, env, p = trainer.rollout, trainer.rollout.env, trainer.policy
     return dict(format=FORMAT, job=job_of(trainer), params=p.flat.cpu(), adam_m=trainer.m.cpu(),
                 adam_v=trainer.v.cpu(), adam_step=trainer.step_dev.cpu(), env_state=env.state.cpu(),
-                obs=r.obs[0].cpu(), legal=r.legal[0].cpu(), global_step=r.global_step,
+                obs=r.obs.cpu(), cobs=r.cobs[0].cpu(), legal=r.legal[0].cpu(), global_step=r.global_step,
                 generator=None if generator is None else generator.get_state(), extra=extra)
 
 
@@ -42,7 +42,8 @@ def load_state_dict(trainer, data, generator=None):
     trainer.v.copy_(data['adam_v'])
     trainer.step_dev.copy_(data['adam_step'])
     env.state.copy_(data['env_state'])
-    r.obs[0].copy_(data['obs'])
+    r.obs.copy_(data['obs'])
+    r.cobs[0].copy_(data['cobs'])
     r.legal[0].copy_(data['legal'])
     r.global_step = data['global_step']
     if generator is not None:

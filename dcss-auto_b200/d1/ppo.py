@@ -4,7 +4,8 @@ coefficients) and a switch for the reference loss (0.25 * MSE, no value clip).
 
 Per minibatch (all device work is libd1 kernels, launched on the current stream):
 
-  gather     X = [obs[idx] | 1 0 ... 0]            d1_ppo_gather_x (pitch 1840)
+  gather     X = [obs[idx] | 1 0 ... 0]            d1_ppo_gather_cobs (pitch 1840; the
+             one-hot rows expanded from the rollout's compact history)
   layer 1    h1 = relu(X W1^T + b1)                d1_gemm (tcgen05, K = 1832)
   layer 2    h2 = relu(h1 W2^T + b2)               d1_gemm
   loss       head, PPO loss, dlogits/dvalue,       d1_ppo_loss (fused, warp MMAs)
@@ -172,9 +173,9 @@ class PPO:
         """One gradient step on the rollout samples `idx` (int64, length mb)."""
         p, r, lib, s = self.policy, self.rollout, self.lib, self.stream
         mb = self.mb
-        obs = r.obs[:r.T].reshape(self.total, OBS)
-        check(lib.d1_ppo_gather_x(obs.data_ptr(), OBS, idx.data_ptr(), mb, self.x.data_ptr(), self.xw, 1, s),
-              'd1_ppo_gather_x')
+        cobs = r.cobs[:r.T].reshape(self.total, r.cobs.shape[2])
+        check(lib.d1_ppo_gather_cobs(cobs.data_ptr(), idx.data_ptr(), mb, self.x.data_ptr(), self.xw, 1, s),
+              'd1_ppo_gather_cobs')
         p.hidden_layers(self.x[:, :OBS], h1=self.h1, h2=self.h2)
         g = self.grad
         check(lib.d1_ppo_loss(self.h2.data_ptr(), p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(),

@@ -4,8 +4,10 @@
 active=None) -> (obs, out)` and resident tensors -- with the spec task's
 buffers: obs bf16 [n, 1832] (one-hot 15x15 window x 8 channels + 32 scalars),
 legal u16 [n] (bit a set when action a is legal), out f32 [n, 10]. The
-observation can be written straight into a caller-provided buffer (a rollout
-slot) via `step(actions, obs_out=...)`.
+observation can be written straight into a caller-provided buffer via
+`step(actions, obs_out=...)`, and the compact observation (320 B per env: a
+channel byte per window cell and the 32 scalars as bf16; `expand_cobs` turns it
+back into the one-hot form) into a rollout slot via `cobs_out=...`.
 
 Env ids are global (`first_env + i`), so a shard of a multi-GPU run produces
 exactly the trajectories the same ids would produce on one GPU.
@@ -89,6 +91,18 @@ def device_rays(device):
     return rays
 
 
+COBS, COBS_SCALARS, CELLS = 320, 256, 225
+
+
+def expand_cobs(cobs):
+    """One-hot bf16 observations [n, 1832] of compact rows u8 [n, 320] (torch
+    ops; the kernels expand the same way inside d1_ppo_gather_cobs)."""
+    codes = cobs[:, :CELLS].long()
+    onehot = torch.nn.functional.one_hot(codes, 8).to(torch.bfloat16).reshape(cobs.shape[0], CELLS * 8)
+    scalars = cobs[:, COBS_SCALARS:COBS].contiguous().view(torch.bfloat16)
+    return torch.cat([onehot, scalars], 1)
+
+
 class SpecEnv:
     def __init__(self, batch, config=None, seed=0, first_env=0, device='cuda', observe=True):
         """observe=False skips the 1832-feature observation writes (the conv
@@ -114,17 +128,18 @@ class SpecEnv:
     def stream(self):
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def reset(self, seed, obs_out=None, legal_out=None):
+    def reset(self, seed, obs_out=None, legal_out=None, cobs_out=None):
         obs = self.obs if obs_out is None else obs_out
         legal = self.legal if legal_out is None else legal_out
-        check(self.lib.d1_spec_init(self.state.data_ptr(), self.batch, C.byref(self.config), seed, self.first_env,
-                                    None if obs is None else obs.data_ptr(), legal.data_ptr(), self.stream),
-              'd1_spec_init')
+        check(self.lib.d1_spec_init_ex(self.state.data_ptr(), self.batch, C.byref(self.config), seed, self.first_env,
+                                       None if obs is None else obs.data_ptr(),
+                                       None if cobs_out is None else cobs_out.data_ptr(), legal.data_ptr(),
+                                       self.stream), 'd1_spec_init_ex')
         return obs
 
-    def step(self, actions, active=None, obs_out=None, legal_out=None, out_out=None):
-        """One semantic decision per env. `obs_out`/`legal_out`/`out_out` let the
-        caller point the writes at rollout-buffer slots (no extra copies)."""
+    def step(self, actions, active=None, obs_out=None, legal_out=None, out_out=None, cobs_out=None):
+        """One semantic decision per env. `obs_out`/`legal_out`/`out_out`/`cobs_out`
+        let the caller point the writes at rollout-buffer slots (no extra copies)."""
         assert actions.device == self.device and actions.dtype == torch.int64 and actions.is_contiguous()
         act = 0
         if active is not None:
@@ -133,10 +148,10 @@ class SpecEnv:
         obs = self.obs if obs_out is None else obs_out
         legal = self.legal if legal_out is None else legal_out
         out = self.out if out_out is None else out_out
-        check(self.lib.d1_spec_step(self.state.data_ptr(), self.batch, C.byref(self.config), actions.data_ptr(),
-                                    None if obs is None else obs.data_ptr(), legal.data_ptr(), out.data_ptr(),
-                                    act or None, self.stream),
-              'd1_spec_step')
+        check(self.lib.d1_spec_step_ex(self.state.data_ptr(), self.batch, C.byref(self.config), actions.data_ptr(),
+                                       None if obs is None else obs.data_ptr(),
+                                       None if cobs_out is None else cobs_out.data_ptr(), legal.data_ptr(),
+                                       out.data_ptr(), act or None, self.stream), 'd1_spec_step_ex')
         return obs, out
 
     def legal_mask(self):

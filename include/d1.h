@@ -134,6 +134,16 @@ int d1_spec_init(void *state, int n, const D1SpecConfig *c, uint64_t seed, int f
  * (when active is not NULL) are left untouched. actions i64[n]; out f32[n, 10]. */
 int d1_spec_step(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, uint16_t *legal,
                  float *out, const bool *active, void *stream);
+/* d1_spec_init / d1_spec_step that also (or only) write the compact
+ * observation: cobs u8[n, 320] -- the channel 0-7 of each of the 225 window
+ * cells as a byte (zeros to byte 255), then the 32 scalars as bf16 at byte 256.
+ * obs_bf16 and cobs may each be NULL. 320 B instead of 3,664 B per env: the
+ * rollout buffer keeps this form and the update expands it
+ * (d1_ppo_gather_cobs). */
+int d1_spec_init_ex(void *state, int n, const D1SpecConfig *c, uint64_t seed, int first_env, void *obs_bf16,
+                    void *cobs, uint16_t *legal, void *stream);
+int d1_spec_step_ex(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, void *cobs,
+                    uint16_t *legal, float *out, const bool *active, void *stream);
 /* Canonical compact view, 56 x i64 per env: Philox draw count, env id, episode,
  * hp, regen, blocks, player, turns, killed, stairs, monster count, floor seen,
  * then pos[11], energy[11], hp[11], kind*2+awake[11]. */
@@ -347,6 +357,12 @@ int d1_gemm_error(void);
  * most 16,777,216 (mode 0) or 2,097,152 (mode 1), else D1_ERR_TOO_LARGE. */
 int d1_gae(const float *reward, const float *done, int64_t r_step, int64_t r_env, const float *value, int T, int B,
            float gamma, float lambda, float *adv, float *ret, double *stats, int mode, void *stream);
+/* Gather + expand of compact observations (d1_spec_step_ex's cobs rows, 320 B
+ * each): x[i] (bf16, row pitch ldx) = the 1832-feature one-hot observation of
+ * row idx[i], plus the ones column (1, 0, ..., 0) at 1832 with ones_col
+ * (ldx >= 1840 then). Equal bit for bit to the one-hot observation the env
+ * writes for the same step. */
+int d1_ppo_gather_cobs(const void *cobs, const int64_t *idx, int n, void *x, int ldx, int ones_col, void *stream);
 /* Length of one block partial written by d1_ppo_loss: dWh[13*256], dbh[13], db2[256],
  * then 8 loss terms (sum pg, sum vf, sum entropy, clipped count, sum approx-kl, 0, 0, 0). */
 int d1_ppo_loss_part_len(void);

@@ -184,7 +184,7 @@ def test_checkpoint_resume_is_exact(d1mods, tmp_path):
         resumed.iteration(g_res)
     torch.cuda.synchronize()
     a, b = ckpt.state_dict(full, g_full), ckpt.state_dict(resumed, g_res)
-    for key in ('params', 'adam_m', 'adam_v', 'adam_step', 'env_state', 'obs', 'legal', 'generator'):
+    for key in ('params', 'adam_m', 'adam_v', 'adam_step', 'env_state', 'obs', 'cobs', 'legal', 'generator'):
         assert torch.equal(a[key], b[key]), key
     assert a['global_step'] == b['global_step']
     # a different job is refused

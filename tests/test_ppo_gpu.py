@@ -79,7 +79,8 @@ class RoundGrad(torch.autograd.Function):
 
 def reference_minibatch(pol, roll, tr, idx, round_grads=True):
     T, B = roll.T, roll.env.batch
-    obs = roll.obs[:T].reshape(T * B, -1)[idx].float()
+    from d1.spec_env import expand_cobs
+    obs = expand_cobs(roll.cobs[:T].reshape(T * B, -1)[idx]).float()
     legal = roll.legal[:T].reshape(-1)[idx].to(torch.int32) & 0xffff
     act = roll.actions.reshape(-1)[idx]
     oldlp = roll.logp.reshape(-1)[idx]
@@ -163,7 +164,8 @@ def test_reference_loss_switch_matches_plain_mse(mods):
     idx = torch.arange(tr.mb, device='cuda')
     T, B = roll.T, roll.env.batch
     # value predictions of the pre-update policy on these samples, plain squared error
-    h1, h2 = pol.hidden_layers(roll.obs[:T].reshape(T * B, -1)[idx].contiguous())
+    from d1.spec_env import expand_cobs
+    h1, h2 = pol.hidden_layers(expand_cobs(roll.cobs[:T].reshape(T * B, -1)[idx]).contiguous())
     v = (h2.float() @ pol.bf16['wh'][12].float() + pol.params['bh'][12])
     vf_ref = ((v - tr.ret.reshape(-1)[idx]) ** 2).sum().item()
     terms = tr.minibatch(idx).clone()

@@ -111,3 +111,29 @@ def test_inactive_envs_are_untouched(spec):
         sub.step(a)  # oracle steps all; compare only the active rows below
     rows = gpu.compact().cpu().numpy()
     assert np.array_equal(rows[act_np], sub.compact()[act_np])
+
+
+def test_compact_observation_expands_to_the_one_hot_observation(spec):
+    """The compact observation (a channel byte per window cell + the 32 scalars)
+    carries exactly the one-hot observation: its expansion -- in torch, and by the
+    update's gather kernel with the ones column -- equals the env's obs bit for bit,
+    at reset and after every step."""
+    from d1._lib import library
+    lib = library()
+    n = 512
+    env = spec.SpecEnv(n, seed=13)
+    cobs = torch.empty((n, spec.COBS), dtype=torch.uint8, device='cuda')
+    env.reset(13, cobs_out=cobs)
+    acts = torch.from_numpy(random_actions(5, 40, n, 12)).cuda()
+    idx = torch.randperm(n, device='cuda')
+    x = torch.empty((n, 1840), dtype=torch.bfloat16, device='cuda')
+    for k in range(41):
+        if k:
+            env.step(acts[k - 1].contiguous(), cobs_out=cobs)
+        assert torch.equal(spec.expand_cobs(cobs).view(torch.int16), env.obs.view(torch.int16)), k
+        assert lib.d1_ppo_gather_cobs(cobs.data_ptr(), idx.data_ptr(), n, x.data_ptr(), 1840, 1,
+                                      torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(x[:, :1832].view(torch.int16), env.obs[idx].view(torch.int16)), k
+        assert torch.equal(x[:, 1832:].float(), torch.tensor([1.] + [0.] * 7, device='cuda').expand(n, 8)), k
+    assert torch.equal(cobs[:, 225:256], torch.zeros_like(cobs[:, 225:256]))
