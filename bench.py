@@ -59,6 +59,10 @@ def parse():
     ap.add_argument('--no-conv', action='store_true', help='skip the config-3 conv-policy rollout line')
     ap.add_argument('--conv-envs', type=int, default=131072, help='envs per GPU of the config-3 line')
     ap.add_argument('--conv-steps', type=int, default=16)
+    ap.add_argument('--no-c4', action='store_true', help='skip the config-4 ogre-pressure iteration line')
+    ap.add_argument('--c4-envs', type=int, default=131072, help='envs per GPU of the config-4 line')
+    ap.add_argument('--c4-horizon', type=int, default=10,
+                    help='rollout steps per config-4 iteration (131,072 x 10 x 8 GPUs = 10.5M decisions)')
     ap.add_argument('--kernels', action='store_true',
                     help='run every hot kernel twice at bench sizes for profiler captures, print nothing else')
     return ap.parse_args()
@@ -379,6 +383,52 @@ def run_ours(args, rank, world, local_rank):
                                   'flop_per_decision': conv_flop // n3, 'features_ms': feat_ms},
                      'conv_error': conv_error()}
         del env3, pol3, buf3, out3
+    # the ogre-pressure scale-out scenario -- 131,072 envs per
+    # GPU on maps with one sleeping ogre, the config-1 MLP, and a full iteration
+    # (rollout of c4-horizon steps + GAE + 4-epoch PPO update with the gradient
+    # exchange and global advantage statistics); decisions/s over the whole
+    # iteration, all ranks.
+    c4_line = None
+    if not args.no_c4:
+        from d1.ppo import PPO
+        from d1.spec_env import OGRE
+        progress('config 4 iteration')
+        n4, t4 = args.c4_envs, args.c4_horizon
+        env4 = SpecEnv(n4, config=OGRE, seed=4, first_env=rank * n4, device=dev)
+        pol4 = Policy(device=dev, seed=0)
+        roll4 = Rollout(env4, pol4, t4, seed=4)
+        tr4 = PPO(pol4, roll4, minibatch=args.minibatch, epochs=args.epochs,
+                  group=dist.group.WORLD if world > 1 else None)
+        gen4 = torch.Generator(device=dev).manual_seed(4321 + rank)
+        tr4.iteration(gen4)  # warm-up iteration (also captures the update graph)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        q0, q1, q2 = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        q0.record(stream)
+        roll4.collect()
+        q1.record(stream)
+        tr4.advantages()
+        tr4.update(gen4)
+        q2.record(stream)
+        torch.cuda.synchronize()
+        roll4.roll()
+        peer_error4 = tr4.lib.d1_peer_error() if tr4.peer is not None else 0
+        tr4.release()
+        t_it = torch.tensor([q0.elapsed_time(q2), q0.elapsed_time(q1)], device=dev)
+        if world > 1:
+            dist.all_reduce(t_it, op=dist.ReduceOp.MAX)
+        decisions = n4 * t4 * world
+        c4_line = {'metric': 'env decisions/sec over full rollout + GAE + PPO iterations (config 4, ogre maps)',
+                   'value': decisions / (t_it[0].item() / 1e3), 'unit': UNIT,
+                   'rollout_decisions_per_s': decisions / (t_it[1].item() / 1e3),
+                   'ms_per_iteration': t_it[0].item(), 'rollout_ms': t_it[1].item(),
+                   'decisions_per_iteration': decisions, 'envs_per_gpu': n4, 'horizon': t4,
+                   'minibatch': args.minibatch, 'epochs': args.epochs,
+                   'gradient_exchange': ('peer memory (NVLink)' if tr4.peer is not None else 'NCCL') if world > 1
+                   else None, 'peer_error': int(peer_error4),
+                   'finite': bool(torch.isfinite(pol4.flat).all().item())}
+        del env4, pol4, roll4, tr4
     if rank != 0:
         return
     pk, pk_kind = peaks()
@@ -393,8 +443,8 @@ def run_ours(args, rank, world, local_rank):
                    'l2': 'inputs larger than L2 (240 MB obs slot + 134 MB env state per step)'},
         'roofline': {'kernel': 'd1::spec::step_kernel', 'bound': 'hbm', 'achieved': achieved,
                      'peak': pk['hbm_gbs'], 'unit': 'GB/s', 'frac': achieved / pk['hbm_gbs'],
-                     # DRAM read + write of one launch at 65,536 envs, from the ncu
-                     # capture summarised in profiles/spec_step_kernel_config1.md
+                     # DRAM read + write of one launch at 65,536 envs, from one ncu
+                     # capture of the kernel
                      'traffic': ENV_TRAFFIC_BYTES * B / 65536, 'traffic_unit': 'bytes per launch (ncu)',
                      'peak_kind': pk_kind,
                      'algorithmic_bytes_per_decision': ENV_BYTES_PER_DECISION,
@@ -405,6 +455,7 @@ def run_ours(args, rank, world, local_rank):
                                  'ms_per_launch': gemm_ms, 'peak_kind': pk_kind + ' burst'},
         'ppo': ppo_line,
         'config3': conv_line,
+        'config4': c4_line,
         'clocks': clk,
         'e2e': e2e,
         'gpu_launches': args.steps * 4,
