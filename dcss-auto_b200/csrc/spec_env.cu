@@ -99,6 +99,7 @@ struct Smem {
     uint32_t vis[16];  // LOS window rows: vis[dy+7] bit dx+7
     uint16_t vmask[16], fmask[16];  // remembered / floor bits of the window rows
     uint4 onehot[8];  // observation cell of channel c: bf16 1.0 in half-word c
+    uint4 crow[COBS / 16];  // the compact observation row, staged for 16-byte stores
     uint8_t opqb[32];
     uint8_t occ_ch[CELLS + 7];
 };
@@ -835,10 +836,10 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint8
             const int floor_ch = m != 0xff ? m : (jc == sj ? 4 : (((vr >> wx) & 1u) ? 3 : 2));
             const int ch = ((vm >> wx) & 1u) ? (((fm >> wx) & 1u) ? floor_ch : 1) : 0;
             if (obs) dst[jc] = s.onehot[ch];
-            if (cobs) cobs[jc] = (uint8_t)ch;
+            if (cobs) reinterpret_cast<uint8_t *>(s.crow)[jc] = (uint8_t)ch;
         }
     }
-    if (cobs && lane < COBS_SCALARS - CELLS) cobs[CELLS + lane] = 0;
+    if (cobs && lane < COBS_SCALARS - CELLS) reinterpret_cast<uint8_t *>(s.crow)[CELLS + lane] = 0;
     // scalars
     const int nvis = __popc(__ballot_sync(FULL, mvis));
     const int nvis_awake = __popc(__ballot_sync(FULL, mvis && e.m_awake));
@@ -877,7 +878,12 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint8
                            1.f, 30.f, 1.f, 1.f};
     const float f = num[lane] / den[lane];
     if (obs) obs[1800 + lane] = __float2bfloat16_rn(f);
-    if (cobs) reinterpret_cast<__nv_bfloat16 *>(cobs + COBS_SCALARS)[lane] = __float2bfloat16_rn(f);
+    if (cobs) {
+        reinterpret_cast<__nv_bfloat16 *>(reinterpret_cast<uint8_t *>(s.crow) + COBS_SCALARS)[lane] =
+            __float2bfloat16_rn(f);
+        __syncwarp();
+        if (lane < COBS / 16) reinterpret_cast<uint4 *>(cobs)[lane] = s.crow[lane];
+    }
     if (lane < 8) {
         const bool ok = floor_at(e, neighbor(e.player, lane));
         const unsigned b = __ballot_sync(0xffu, ok);
