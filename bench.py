@@ -475,9 +475,10 @@ def run_kernels(args):
     Launch order: an 8-step rollout of 65,536 envs (8 x (step_kernel, layer 1 on
     gemm_pair_kernel, layer 2 on gemm_kernel, head_sample_kernel), then the same
     two GEMMs + head_sample_kernel for the bootstrap value) and GAE; then per
-    pass: rollout layer 1 (gemm_pair_kernel), one PPO minibatch of 16,384
-    (gather_kernel; layer 1 gemm_pair_kernel; layer 2, dW2 and dh1 gemm_kernel;
-    dW1 gemm_pair_kernel; loss_mma_kernel, reductions, adam_kernel), layer 2
+    pass: rollout layer 1 (gemm_pair_kernel<2, 0>), one PPO minibatch of 16,384
+    (layer 1 from compact rows gemm_pair_kernel<1, 1>; layer 2, dW2 and dh1
+    gemm_kernel; dW1 from compact rows gemm_pair_kernel<1, 2>; loss_mma_kernel,
+    grad_reduce_kernel, adam_update_kernel), layer 2
     (gemm_kernel), head_sample_kernel, step_kernel, gae_scan_kernel, and the
     config-3 policy on 16,384 envs (crop_kernel, conv_kernel<1..3>, FC
     gemm_pair_kernel, head gemm_kernel, ar_kernel). A `gemm` regex therefore

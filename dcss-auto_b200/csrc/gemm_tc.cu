@@ -54,6 +54,11 @@ struct Params {
     const int64_t *a_rows;  // A row m = row a_rows[m] of a [rows, K] table (K-major A; null: plain)
     const int64_t *b_rows;  // B K-row k = row b_rows[k] of a [rows, N] table (MN-major B; null: plain)
     int b_mn;            // B stored [K, N] (N contiguous) instead of [N, K]
+    // operand expanded from compact observation rows (pair kernel, XM != 0):
+    // row r of the expanded matrix = the 1832 one-hot features of compact row
+    // cidx[r] (or r), then the ones column at 1832, zeros after
+    const uint8_t *cobs;
+    const int64_t *cidx;
     const __nv_bfloat16 *mask;  // row-major [M, ldm]: zero where mask <= 0 (may be null)
     int ldm;
     __nv_bfloat16 *c;    // row-major [M, ldc] (may be null)
@@ -509,6 +514,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 constexpr int P_STAGES = 6, P_B_BYTES = 128 * BK * 2, P_STAGE_BYTES = A_BYTES + P_B_BYTES;
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + BIAS_BYTES;
 constexpr int P2_SMEM_BYTES = 4 * (2 * A_BYTES + P_B_BYTES) + 1024 + 256 + BIAS_BYTES;
+// compact observation rows (d1_spec_step_ex): a channel byte per window cell,
+// zeros to byte 255, then 32 bf16 scalars
+constexpr int X_ROW = 320, X_CELLS = 225, X_SCALARS = 256, X_K = 1832, X_EXPANDERS = 4;
+// compact-operand kernels: channel codes (and sample indices) are copied
+// X_DEPTH K blocks ahead into shared-memory rings; scalar units are staged in
+// shared memory too (XM = 1: 64 bytes per A row of a tile; XM = 2: 64 bytes per
+// sample of X_DEPTH K blocks)
+constexpr int X_DEPTH = 4, X_SCAL_BYTES = 256 * 64, X_SMEM_BYTES = X_SCAL_BYTES + 8192 /*code and index rings*/;
 constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -545,16 +558,96 @@ __device__ __forceinline__ void commit_pair(uint32_t bar_cluster) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
                  : "memory");
 }
+// Arrival on a barrier of either CTA of the pair (default release semantics:
+// measured, a cluster-scope release here serialised every pipeline stage and
+// doubled the kernel's time).
 __device__ __forceinline__ void arrive_cluster(uint32_t bar_cluster) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// bar.red.or over the expander warps: true on every thread if any passed true.
+__device__ __forceinline__ bool expanders_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, 2, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(32 * X_EXPANDERS)
+        : "memory");
+    return r != 0;
+}
+// One-hot unit of channel code c (0..7): bf16 1.0 at feature c of the 8.
+__device__ __forceinline__ uint4 onehot_unit(uint32_t c) {
+    const uint32_t v = 0x3f80u << ((c & 1u) << 4), w = c >> 1;
+    return make_uint4(w == 0 ? v : 0u, w == 1 ? v : 0u, w == 2 ? v : 0u, w == 3 ? v : 0u);
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// The 32 bf16 scalars (64 bytes at byte 256) of compact row `row` copied to
+// shared memory at `dst`.
+__device__ __forceinline__ void x_stage_scalars(uint8_t *dst, const uint8_t *__restrict__ cobs, int64_t row) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) cp_async16(smem_u32(dst + 16 * q), cobs + row * X_ROW + X_SCALARS + 16 * q);
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+// Channel codes of cells c .. c + 7 of compact row `row` (c a multiple of 8;
+// from cell 224 on, the last cell's code and the zero bytes after it) copied to
+// shared memory at `dst`. The copies are asynchronous: a bar.sync waits for a
+// thread's outstanding loads into registers but not for cp.async groups, so the
+// ring stays in flight across the per-stage barriers.
+__device__ __forceinline__ void x_stage_codes(uint8_t *dst, const uint8_t *__restrict__ cobs, int64_t row, int c) {
+    cp_async8(smem_u32(dst), cobs + row * X_ROW + min(c, X_CELLS - 1));
+}
+// The eight 16-byte units of features 8c .. 8c + 63 into one 128-byte row of a
+// 128-byte-swizzled tile (unit u at u ^ sw): the one-hot channels of cells
+// c .. c + 7, or for the last block cell 224, the four scalar units `scal`, the
+// ones unit (feature 1832) and zeros; all zeros where `live` is false.
+__device__ __forceinline__ void x_write_row(uint8_t *dst, int sw, int c, uint2 codes, const uint4 *scal,
+                                            bool live) {
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    if (live && c + 8 <= X_CELLS) {
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            *reinterpret_cast<uint4 *>(dst + ((u ^ sw) << 4)) =
+                onehot_unit(((u < 4 ? codes.x : codes.y) >> (8 * (u & 3))) & 7u);
+    } else if (live && c == X_CELLS - 1) {
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const uint4 v = u == 0   ? onehot_unit(codes.x & 7u)
+                            : u < 5  ? scal[u - 1]
+                            : u == 5 ? make_uint4(0x3f80u, 0u, 0u, 0u)
+                                     : zero;
+            *reinterpret_cast<uint4 *>(dst + ((u ^ sw) << 4)) = v;
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < 8; u++) *reinterpret_cast<uint4 *>(dst + ((u ^ sw) << 4)) = zero;
+    }
 }
 
 // SUB = 2: each CTA holds two 128-row blocks of A per K block (a 512-row pair
 // tile) and issues two MMAs against the same B half, so B is streamed half as
 // often; the two accumulators fill the 512 TMEM columns, so the accumulator is
 // single-buffered (the next tile's loads still run during the epilogue).
-template <int SUB>
-__global__ void __launch_bounds__(THREADS, 1)
+// XM = 1: A (K-major, K = 1832) is expanded from compact observation rows and
+// XM = 2: B (MN-major, [K = samples, N = features + ones column]) is, by four
+// extra warps that write the operand tile into the 128-byte-swizzled layout the
+// TMA would have produced (16-byte unit u of a 128-byte row r at u ^ (r % 8)),
+// fence it for the async proxy and arrive on the leader's full barrier, which
+// then expects the TMA bytes of the other operand plus the two CTAs' expander
+// arrivals. Reading 8 bytes of channel codes instead of 128 bytes of one-hot
+// features per 64-deep K block cuts the operand's L2 and HBM traffic 16-fold.
+template <int SUB, int XM>
+__global__ void __launch_bounds__(THREADS + (XM ? 32 * X_EXPANDERS : 0), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p,
                      int tiles_m, int tiles_n, int tiles_total) {
     constexpr int STG = SUB == 1 ? P_STAGES : 4, STG_BYTES = SUB * A_BYTES + P_B_BYTES, NBUF = SUB == 1 ? 2 : 1;
@@ -570,7 +663,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < STG; s++) {
-            mbar_init(full0 + 8 * s, 1);
+            mbar_init(full0 + 8 * s, XM ? 3 : 1);  // + one arrival per CTA's expanders
             mbar_init(empty0 + 8 * s, 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -609,9 +702,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (it >= STG) inflight_lo = it - STG + 1;
                 const uint32_t a_dst = smem_u32(smem + s * STG_BYTES), b_dst = a_dst + SUB * A_BYTES;
                 const uint32_t leader_full = mapa(full0 + 8 * s, 0);
-                if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * STG_BYTES);
+                if (rank == 0)
+                    mbar_expect_tx(full0 + 8 * s, XM == 1 ? 2 * P_B_BYTES : XM == 2 ? 2 * SUB * A_BYTES : 2 * STG_BYTES);
 #pragma unroll
                 for (int sb = 0; sb < SUB; sb++) {
+                    if (XM == 1) break;
                     if (p.a_mn) {
 #pragma unroll
                         for (int j = 0; j < 2; j++)
@@ -621,7 +716,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         tma_load_2d_pair(a_dst + sb * A_BYTES, &map_a, leader_full, kt * BK, m0 + 256 * sb);
                     }
                 }
-                if (p.b_mn) {
+                if (XM == 2) {
+                } else if (p.b_mn) {
 #pragma unroll
                     for (int j = 0; j < 2; j++) tma_load_2d_pair(b_dst + j * 8192, &map_b, leader_full, n0 + 64 * j, kt * BK);
                 } else {
@@ -680,6 +776,120 @@ __global__ void __launch_bounds__(THREADS, 1)
             commit_pair(accf0 + 8 * b);
             commit_pair(mapa(accf0 + 8 * b, 1));
         }
+    } else if (XM && warp >= 2 + EPI_WARPS) {
+        // ---- expanders (both CTAs): the expanded operand's tile of every stage.
+        // Channel codes, sample indices and scalar units arrive by cp.async
+        // X_DEPTH K blocks ahead of use, so no global load latency sits between a
+        // stage's empty barrier and its arrival. Every expander thread waits for
+        // the empty stage itself; one bar.red after the writes both orders them
+        // before the arrival and agrees on a timed-out wait.
+        const int tx = threadIdx.x - 32 * (2 + EPI_WARPS);
+        uint8_t *xs = smem + STG * STG_BYTES + 256 + BIAS_BYTES;
+        int it = 0;
+        bool ok = true;
+        for (int t = cluster; t < tiles_total && ok; t += clusters) {
+            const int mt = t % tiles_m, nt = (t / tiles_m) % tiles_n, split = t / (tiles_m * tiles_n);
+            const int kt0 = split * p.k_tiles_per_split;
+            const int kt1 = min(p.k_tiles_total, kt0 + p.k_tiles_per_split);
+            const int m0 = mt * 256 * SUB + 128 * (int)rank, n0 = nt * BN + 128 * (int)rank;
+            if (XM == 1) {
+                // A rows m0 + 256 sb + tx; K block kt = features 64 kt .. = cells 8 kt ..
+                // (rows past M read row M - 1 and are written as zeros). Copy groups:
+                // the scalars, then one per K block.
+                uint8_t *xc = xs + X_SCAL_BYTES;
+                int64_t row[SUB];
+#pragma unroll
+                for (int sb = 0; sb < SUB; sb++) {
+                    const int grow = min(m0 + 256 * sb + tx, p.M - 1);
+                    row[sb] = p.cidx ? __ldg(p.cidx + grow) : (int64_t)grow;
+                    x_stage_scalars(xs + (sb * 128 + tx) * 64, p.cobs, row[sb]);
+                }
+                cp_async_commit();
+                for (int d = 0; d < X_DEPTH; d++) {
+                    if (kt0 + d < kt1)
+#pragma unroll
+                        for (int sb = 0; sb < SUB; sb++)
+                            x_stage_codes(xc + ((d * SUB + sb) * 128 + tx) * 8, p.cobs, row[sb], 8 * (kt0 + d));
+                    cp_async_commit();
+                }
+                for (int kt = kt0; kt < kt1; kt++, it++) {
+                    const int s = it % STG, d = (kt - kt0) % X_DEPTH;
+                    const bool got = it < STG || mbar_wait(empty0 + 8 * s, ((uint32_t)(it / STG) & 1u) ^ 1u);
+                    cp_async_wait<X_DEPTH - 1>();
+                    uint8_t *stage = smem + s * STG_BYTES;
+                    if (got)
+#pragma unroll
+                        for (int sb = 0; sb < SUB; sb++)
+                            x_write_row(stage + sb * A_BYTES + tx * 128, tx & 7, 8 * kt,
+                                        *reinterpret_cast<const uint2 *>(xc + ((d * SUB + sb) * 128 + tx) * 8),
+                                        reinterpret_cast<const uint4 *>(xs + (sb * 128 + tx) * 64),
+                                        m0 + 256 * sb + tx < p.M);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    if (expanders_any(!got)) {
+                        ok = false;
+                        break;
+                    }
+                    if (tx == 0) arrive_cluster(mapa(full0 + 8 * s, 0));
+                    if (kt + X_DEPTH < kt1)
+#pragma unroll
+                        for (int sb = 0; sb < SUB; sb++)
+                            x_stage_codes(xc + ((d * SUB + sb) * 128 + tx) * 8, p.cobs, row[sb], 8 * (kt + X_DEPTH));
+                    cp_async_commit();
+                }
+            } else {
+                // B K rows (samples) 64 kt + k, N features n0 + 64 j .. + 63 = cells c0 .. c0 + 7
+                // (samples past K read sample K - 1 and are written as zeros). Sample
+                // indices are copied 2 X_DEPTH K blocks ahead, codes and scalars
+                // X_DEPTH ahead; one copy group per K block.
+                const int k = tx & 63, j = tx >> 6;
+                const int c0 = (n0 + 64 * j) / 8;
+                const bool scal = c0 == X_CELLS - 1;
+                const int dst0 = SUB * A_BYTES + j * 8192 + (k >> 3) * 1024 + (k & 7) * 128;
+                uint8_t *xc = xs + X_SCAL_BYTES, *xi = xc + 4096;
+                auto stage_index = [&](int kt, int d) {
+                    const int g = min(kt * BK + k, p.K - 1);
+                    uint8_t *dst = xi + (d * 128 + tx) * 8;
+                    if (p.cidx)
+                        cp_async8(smem_u32(dst), p.cidx + g);
+                    else
+                        *reinterpret_cast<int64_t *>(dst) = g;
+                };
+                auto stage_sample = [&](int64_t r, int d) {
+                    x_stage_codes(xc + (d * 128 + tx) * 8, p.cobs, r, c0);
+                    if (scal) x_stage_scalars(xs + (d * 64 + k) * 64, p.cobs, r);
+                };
+                for (int d = 0; d < X_DEPTH; d++) {
+                    if (kt0 + d < kt1) {
+                        const int g = min((kt0 + d) * BK + k, p.K - 1);
+                        stage_sample(p.cidx ? __ldg(p.cidx + g) : (int64_t)g, d);
+                        if (kt0 + X_DEPTH + d < kt1) stage_index(kt0 + X_DEPTH + d, d);
+                    }
+                    cp_async_commit();
+                }
+                for (int kt = kt0; kt < kt1; kt++, it++) {
+                    const int s = it % STG, d = (kt - kt0) % X_DEPTH;
+                    const bool got = it < STG || mbar_wait(empty0 + 8 * s, ((uint32_t)(it / STG) & 1u) ^ 1u);
+                    cp_async_wait<X_DEPTH - 1>();
+                    if (got)
+                        x_write_row(smem + s * STG_BYTES + dst0, k & 7, c0,
+                                    *reinterpret_cast<const uint2 *>(xc + (d * 128 + tx) * 8),
+                                    reinterpret_cast<const uint4 *>(xs + (d * 64 + k) * 64), kt * BK + k < p.K);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    if (expanders_any(!got)) {
+                        ok = false;
+                        break;
+                    }
+                    if (tx == 0) arrive_cluster(mapa(full0 + 8 * s, 0));
+                    if (kt + X_DEPTH < kt1) {
+                        stage_sample(*reinterpret_cast<const int64_t *>(xi + (d * 128 + tx) * 8), d);
+                        if (kt + 2 * X_DEPTH < kt1) stage_index(kt + 2 * X_DEPTH, d);
+                    }
+                    cp_async_commit();
+                }
+            }
+        }
+        cp_async_wait<0>();
+        if (!ok) atomicExch(&g_error, 9);
     } else if (warp >= 2) {
         // ---- epilogue (both CTAs): this CTA's 128 rows of the tile
         const int q = warp & 3, half = (warp - 2) >> 2;
@@ -860,7 +1070,8 @@ extern "C" {
 
 static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
                        const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf, int splits, int a_mn,
-                       int b_mn, void *stream);
+                       int b_mn, void *stream, int xm = 0, const uint8_t *cobs = nullptr,
+                       const int64_t *cidx = nullptr);
 
 static int gemm_launch(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias,
                        int relu, const void *mask, int ldm, void *c, int ldc, void *ct, int ldct, float *cf, int ldcf,
@@ -898,9 +1109,8 @@ static int gemm_launch(const void *a, int lda, const void *b, int ldb, int M, in
                  : make_map(&mb, b, N, K, ldb, BN)))
         return D1_ERR_BAD_ARGUMENT;
     if (int e = gemm_attr()) return e;
-    Params p{M, N, K, per, kt, bias, relu, a_mn, a_rows, b_rows, b_mn, (const __nv_bfloat16 *)mask, ldm,
-             (__nv_bfloat16 *)c, ldc,
-             (__nv_bfloat16 *)ct, ldct, cf, ldcf};
+    Params p{M, N, K, per, kt, bias, relu, a_mn, a_rows, b_rows, b_mn, nullptr, nullptr, (const __nv_bfloat16 *)mask,
+             ldm, (__nv_bfloat16 *)c, ldc, (__nv_bfloat16 *)ct, ldct, cf, ldcf};
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n * splits;
     static int sms = 0;
@@ -959,8 +1169,9 @@ int d1_gemm_head_sample(const void *a, int lda, const void *b, int ldb, int M, i
     CUtensorMap ma, mb;
     if (!make_map(&ma, a, M, K, lda, BM) || !make_map(&mb, b, BN, K, ldb, BN)) return D1_ERR_BAD_ARGUMENT;
     if (int e = gemm_attr()) return e;
-    Params p{M, BN, K, kt, kt, bias, 1, 0, nullptr, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, 0,
-             1, (const __nv_bfloat16 *)wh_bf16, bh, legal, seed, step, first_env, action, logp, value, logits};
+    Params p{M, BN, K, kt, kt, bias, 1, 0, nullptr, nullptr, 0, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, 0,
+             nullptr, 0, 1, (const __nv_bfloat16 *)wh_bf16, bh, legal, seed, step, first_env, action, logp, value,
+             logits};
     const int tiles = (M + BM - 1) / BM;
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
@@ -971,13 +1182,18 @@ int d1_gemm_head_sample(const void *a, int lda, const void *b, int ldb, int M, i
 }
 
 // 2-SM pair kernel: 256 x 256 tiles (see gemm_pair_kernel). Same operands and
-// output forms as gemm_launch except the transposed output and row gathers.
+// output forms as gemm_launch except the transposed output and row gathers;
+// xm = 1 / 2 builds A / B from compact observation rows instead (a / b unused).
 static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, int N, int K, const float *bias, int relu,
                        const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf, int splits, int a_mn,
-                       int b_mn, void *stream) {
-    if (M <= 0 || N <= 0 || K <= 0 || !a || !b || (!c && !cf) || splits < 1) return D1_ERR_BAD_ARGUMENT;
-    if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) || (lda * 2) % 16 ||
-        (ldb * 2) % 16 || lda < (a_mn ? M : K) || ldb < (b_mn ? N : K))
+                       int b_mn, void *stream, int xm, const uint8_t *cobs, const int64_t *cidx) {
+    if (M <= 0 || N <= 0 || K <= 0 || (!a && xm != 1) || (!b && xm != 2) || (!c && !cf) || splits < 1)
+        return D1_ERR_BAD_ARGUMENT;
+    if (xm && (!cobs || (reinterpret_cast<uintptr_t>(cobs) & 15))) return D1_ERR_BAD_ARGUMENT;
+    if (xm == 1 && (a_mn || K != X_K)) return D1_ERR_BAD_ARGUMENT;
+    if (xm == 2 && (!b_mn || N > X_K + 8)) return D1_ERR_BAD_ARGUMENT;
+    if ((xm != 1 && ((reinterpret_cast<uintptr_t>(a) & 15) || (lda * 2) % 16 || lda < (a_mn ? M : K))) ||
+        (xm != 2 && ((reinterpret_cast<uintptr_t>(b) & 15) || (ldb * 2) % 16 || ldb < (b_mn ? N : K))))
         return D1_ERR_BAD_ARGUMENT;
     if (c && ((reinterpret_cast<uintptr_t>(c) & 15) || ldc % 8 || ldc < N)) return D1_ERR_BAD_ARGUMENT;
     if (cf && ((reinterpret_cast<uintptr_t>(cf) & 15) || ldcf % 4 || ldcf < N)) return D1_ERR_BAD_ARGUMENT;
@@ -989,21 +1205,33 @@ static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, in
     splits = (kt + per - 1) / per;
     CUtensorMap ma, mb;
     // each CTA loads 128 rows (K-major) or two 64-wide MN atoms (MN-major) of A and of B
-    if (!(a_mn ? make_map(&ma, a, K, M, lda, 64) : make_map(&ma, a, M, K, lda, 128))) return D1_ERR_BAD_ARGUMENT;
-    if (!(b_mn ? make_map(&mb, b, K, N, ldb, 64) : make_map(&mb, b, N, K, ldb, 128))) return D1_ERR_BAD_ARGUMENT;
+    if (xm != 1 && !(a_mn ? make_map(&ma, a, K, M, lda, 64) : make_map(&ma, a, M, K, lda, 128)))
+        return D1_ERR_BAD_ARGUMENT;
+    if (xm != 2 && !(b_mn ? make_map(&mb, b, K, N, ldb, 64) : make_map(&mb, b, N, K, ldb, 128)))
+        return D1_ERR_BAD_ARGUMENT;
+    if (xm == 1) ma = mb;  // unused: the expanded operand has no tensor map
+    if (xm == 2) mb = ma;
     static uint64_t ready = 0;
     int dev = 0;
     if (cudaError_t e = cudaGetDevice(&dev)) return (int)e;
     if (!(dev < 64 && ((ready >> dev) & 1))) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              P_SMEM_BYTES);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_pair_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM_BYTES);
+            e = cudaFuncSetAttribute(gemm_pair_kernel<2, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     P2_SMEM_BYTES);
+        for (int xm = 1; xm <= 2 && e == cudaSuccess; xm++) {
+            e = cudaFuncSetAttribute(xm == 1 ? gemm_pair_kernel<1, 1> : gemm_pair_kernel<1, 2>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES + X_SMEM_BYTES);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(xm == 1 ? gemm_pair_kernel<2, 1> : gemm_pair_kernel<2, 2>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM_BYTES + X_SMEM_BYTES);
+        }
         if (e != cudaSuccess) return (int)e;
         if (dev < 64) ready |= 1ull << dev;
     }
-    Params p{M, N, K, per, kt, bias, relu, a_mn, nullptr, nullptr, b_mn, (const __nv_bfloat16 *)mask, ldm,
-             (__nv_bfloat16 *)c, ldc, nullptr, 0, cf, ldcf};
+    Params p{M, N, K, per, kt, bias, relu, a_mn, nullptr, nullptr, b_mn, cobs, cidx, (const __nv_bfloat16 *)mask,
+             ldm, (__nv_bfloat16 *)c, ldc, nullptr, 0, cf, ldcf};
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = SM_COUNT;
     const int tiles_n = (N + BN - 1) / BN;
@@ -1021,20 +1249,34 @@ static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, in
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * clusters);
-    cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = sub == 2 ? P2_SMEM_BYTES : P_SMEM_BYTES;
+    cfg.blockDim = dim3(THREADS + (xm ? 32 * X_EXPANDERS : 0));
+    cfg.dynamicSmemBytes = (sub == 2 ? P2_SMEM_BYTES : P_SMEM_BYTES) + (xm ? X_SMEM_BYTES : 0);
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return sub == 2 ? (int)cudaLaunchKernelEx(&cfg, gemm_pair_kernel<2>, ma, mb, p, tiles_m, tiles_n, tiles)
-                    : (int)cudaLaunchKernelEx(&cfg, gemm_pair_kernel<1>, ma, mb, p, tiles_m, tiles_n, tiles);
+    void (*kern)(const CUtensorMap, const CUtensorMap, Params, int, int, int) =
+        sub == 2 ? (xm == 1 ? gemm_pair_kernel<2, 1> : xm == 2 ? gemm_pair_kernel<2, 2> : gemm_pair_kernel<2, 0>)
+                 : (xm == 1 ? gemm_pair_kernel<1, 1> : xm == 2 ? gemm_pair_kernel<1, 2> : gemm_pair_kernel<1, 0>);
+    return (int)cudaLaunchKernelEx(&cfg, kern, ma, mb, p, tiles_m, tiles_n, tiles);
 }
 
 int d1_gemm_pair(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,
                  const float *bias, int relu, const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf,
                  int splits, void *stream) {
     return pair_launch(a, lda, b, ldb, M, N, K, bias, relu, mask, ldm, c, ldc, cf, ldcf, splits, a_mn != 0, b_mn != 0,
-                       stream);
+                       stream, 0, nullptr, nullptr);
+}
+
+int d1_gemm_cobs_a(const void *cobs, const int64_t *idx, int M, const void *b, int ldb, int N, const float *bias,
+                   int relu, void *c, int ldc, void *stream) {
+    return pair_launch(nullptr, 0, b, ldb, M, N, X_K, bias, relu, nullptr, 0, c, ldc, nullptr, 0, 1, 0, 0, stream, 1,
+                       (const uint8_t *)cobs, idx);
+}
+
+int d1_gemm_cobs_b(const void *a, int lda, const void *cobs, const int64_t *idx, int M, int N, int K, float *cf,
+                   int ldcf, int splits, void *stream) {
+    return pair_launch(a, lda, nullptr, 0, M, N, K, nullptr, 0, nullptr, 0, nullptr, 0, cf, ldcf, splits, 1, 1, stream,
+                       2, (const uint8_t *)cobs, idx);
 }
 
 // Splits actually used for (K, requested splits): callers size fp32 slabs with it.

@@ -55,6 +55,8 @@ SIGNATURES = {
     'd1_peer_free': [_P],
     'd1_peer_error': [],
     'd1_ppo_gather_x': [_P, _I, _P, _I, _P, _I, _I, _P],
+    'd1_gemm_cobs_a': [_P, _P, _I, _P, _I, _I, _P, _I, _P, _I, _P],
+    'd1_gemm_cobs_b': [_P, _I, _P, _P, _I, _I, _I, _P, _I, _I, _P],
     'd1_gemm_pair': [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_head_sample': [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],
     'd1_gemm_error': [],

@@ -95,6 +95,32 @@ def gemm_pair(a, b, a_kn=False, b_kn=False, bias=None, relu=False, out=None, out
     return out if out is not None else out_f32
 
 
+def gemm_cobs_a(cobs, b, idx=None, M=None, bias=None, relu=False, out=None):
+    """act(X . B^T + bias) with X the one-hot expansion of compact observation
+    rows cobs[idx] (u8 [rows, 320]; idx int64 [M] or None for the first M rows),
+    expanded inside the GEMM; B [N, 1832] bf16."""
+    M = idx.shape[0] if idx is not None else (cobs.shape[0] if M is None else M)
+    N = b.shape[0]
+    assert b.shape[1] == 1832 and b.dtype == torch.bfloat16 and b.stride(1) == 1
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=b.device)
+    p = lambda t: None if t is None else t.data_ptr()
+    check(library().d1_gemm_cobs_a(cobs.data_ptr(), p(idx), M, b.data_ptr(), b.stride(0), N, p(bias), int(relu),
+                                   out.data_ptr(), out.stride(0), _stream(b)), 'd1_gemm_cobs_a')
+    return out
+
+
+def gemm_cobs_b(a_kn, cobs, idx, N, out_f32, splits=1):
+    """fp32 split-K slabs of A . X[:, :N] with A given as [K, M] (M contiguous)
+    and X the one-hot expansion (+ ones column at 1832) of compact rows
+    cobs[idx] (idx int64 [K])."""
+    K, M = a_kn.shape
+    assert idx.shape[0] == K and a_kn.dtype == torch.bfloat16 and a_kn.stride(1) == 1
+    check(library().d1_gemm_cobs_b(a_kn.data_ptr(), a_kn.stride(0), cobs.data_ptr(), idx.data_ptr(), M, N, K,
+                                   out_f32.data_ptr(), out_f32.stride(-2), splits, _stream(a_kn)), 'd1_gemm_cobs_b')
+    return out_f32
+
+
 def gemm_rows(a, b, M=None, a_rows=None, b_rows=None, a_kn=False, b_kn=False, bias=None, relu=False, out=None,
               out_f32=None, splits=1, mask=None):
     """gemm_ex with gathered operands: with a_rows (int64 [M]), A's row m is row

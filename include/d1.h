@@ -233,6 +233,21 @@ int d1_gemm_rows(const void *a, int lda, int a_mn, const int64_t *a_rows, int a_
 int d1_gemm_pair(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,
                  const float *bias, int relu, const void *mask, int ldm, void *c, int ldc, float *cf, int ldcf,
                  int splits, void *stream);
+/* Pair-kernel products with one operand expanded from compact observation rows
+ * (d1_spec_step_ex's 320-byte cobs rows) inside the kernel, so the one-hot
+ * matrix never exists in memory. Row r of the expanded matrix X is the
+ * 1832-feature one-hot observation of compact row idx[r] (idx == NULL: row r)
+ * followed by the ones column (1, 0, ..., 0) at 1832..1839.
+ * d1_gemm_cobs_a: c[M, N] (bf16) = act(X[:, :1832] . B^T + bias), B [N, 1832]
+ * K-major (the policy's first layer on a minibatch).
+ * d1_gemm_cobs_b: fp32 split-K slabs of A^T-form products A . X[:, :N] with A
+ * stored [K, M] (M contiguous, e.g. dh1 [samples, 256]) and the K samples'
+ * rows of X, N <= 1840 (the weight and bias gradient of that layer).
+ * Bit-identical to d1_gemm_ex on the expanded matrix. */
+int d1_gemm_cobs_a(const void *cobs, const int64_t *idx, int M, const void *b, int ldb, int N, const float *bias,
+                   int relu, void *c, int ldc, void *stream);
+int d1_gemm_cobs_b(const void *a, int lda, const void *cobs, const int64_t *idx, int M, int N, int K, float *cf,
+                   int ldcf, int splits, void *stream);
 /* d1_gemm_ex on the one-CTA kernel whatever the shape (the pair kernel's
  * comparison point). */
 int d1_gemm_single(const void *a, int lda, int a_mn, const void *b, int ldb, int b_mn, int M, int N, int K,

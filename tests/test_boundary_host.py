@@ -39,6 +39,14 @@ def test_gemm_rejects_bad_shapes_and_layouts(lib):
     p = lambda **kw: lib.d1_gemm_pair(FAKE, kw.get('lda', 2048), 0, FAKE, 2048, 0, kw.get('M', 65536), 256, 2048,
                                       None, 0, None, 0, FAKE, 256, None, 0, kw.get('splits', 1), None)
     assert p(M=0) == BAD and p(lda=2044) == BAD and p(splits=0) == BAD
+    # compact-operand forms: aligned compact rows, B of the 1832-feature width,
+    # an expanded B no wider than the 1840-column [X | 1] layout
+    ca = lambda **kw: lib.d1_gemm_cobs_a(kw.get('cobs', FAKE), None, kw.get('M', 1024), FAKE, 1832, 256, None, 0,
+                                         FAKE, 256, None)
+    assert ca(M=0) == BAD and ca(cobs=MIS) == BAD and ca(cobs=None) == BAD
+    cb = lambda **kw: lib.d1_gemm_cobs_b(FAKE, 256, kw.get('cobs', FAKE), FAKE, 256, kw.get('N', 1840), 4096, FAKE,
+                                         1840, 8, None)
+    assert cb(N=1848) == BAD and cb(cobs=MIS) == BAD and cb(N=0) == BAD
 
 
 def test_env_and_head_entry_points(lib):

@@ -173,3 +173,40 @@ def test_pair_kernel_matches_the_product(G, M, N, K, a_kn, b_kn, splits):
         assert torch.equal(out, want)
         rr = torch.where(mask.float() > 0, ref(a, b, bias, True), 0.)
         assert (out.float() - rr).abs().max().item() <= 2e-3 * rr.abs().max().item() + 1e-2
+
+
+@pytest.mark.parametrize('M', [16384, 65536, 3000])
+def test_compact_operand_products_equal_the_expanded_products(G, M):
+    """Products with one operand expanded from compact observation rows inside
+    the pair kernel (four expander warps writing the swizzled tile) equal the
+    same products on the explicitly expanded one-hot matrix bit for bit: the
+    layer-1 forward (A expanded, gathered rows; 512-row pair tiles at 65,536)
+    and the weight + bias gradient (B expanded, with the ones column)."""
+    from d1._lib import library
+    lib = library()
+    g = torch.Generator(device='cuda').manual_seed(M)
+    rows = M + 777
+    cobs = torch.zeros((rows, 320), dtype=torch.uint8, device='cuda')
+    cobs[:, :225] = torch.randint(0, 8, (rows, 225), device='cuda', generator=g, dtype=torch.uint8)
+    cobs[:, 256:].view(torch.bfloat16).copy_(torch.randn(rows, 32, device='cuda', generator=g))
+    idx = torch.randperm(rows, device='cuda', generator=g)[:M]
+    x = torch.empty((M, 1840), dtype=torch.bfloat16, device='cuda')
+    assert lib.d1_ppo_gather_cobs(cobs.data_ptr(), idx.data_ptr(), M, x.data_ptr(), 1840, 1,
+                                  torch.cuda.current_stream().cuda_stream) == 0
+    w = (torch.randn(256, 1832, device='cuda', generator=g) / 40).to(torch.bfloat16)
+    bias = torch.randn(256, device='cuda', generator=g)
+    got = G.gemm_cobs_a(cobs, w, idx=idx, bias=bias, relu=True)
+    want = G.gemm_ex(x[:, :1832], w, bias=bias, relu=True)
+    torch.cuda.synchronize()
+    assert G.gemm_error() == 0
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    # weight gradient: A = dh [K = M samples, 256], B = X [K, 1840]
+    dh = (torch.randn(M, 256, device='cuda', generator=g)).to(torch.bfloat16)
+    s = G.splits_for(M, 8)
+    got_s = torch.empty((s, 256, 1840), device='cuda')
+    want_s = torch.empty_like(got_s)
+    G.gemm_cobs_b(dh, cobs, idx, 1840, got_s, splits=8)
+    G.gemm_ex(dh, x, a_kn=True, b_kn=True, out_f32=want_s, splits=8)
+    torch.cuda.synchronize()
+    assert G.gemm_error() == 0
+    assert torch.equal(got_s, want_s)

@@ -199,3 +199,28 @@ def test_gae_scan_at_the_bench_horizon(mods):
     assert (adv - ref_adv).abs().max().item() <= 1e-5 * max(ref_adv.abs().max().item(), 1.0)
     s1 = tr.stats[0].item()
     assert abs(s1 - ref_adv.double().sum().item()) <= 1e-4 * max(1.0, abs(s1))
+
+
+def test_compact_update_equals_the_materialised_update(mods):
+    """The default update expands the compact history inside the layer-1 and dW1
+    GEMMs; compact=False gathers X = [one-hot rows | ones column] first. Same
+    gradients and parameters bit for bit over several minibatches."""
+    policy, ppo, rollout, spec_env = mods
+    env = spec_env.SpecEnv(512, seed=11)
+    pa, pb = policy.Policy(seed=11), policy.Policy(seed=11)
+    roll = rollout.Rollout(env, pa, 32, seed=11)
+    roll.collect()
+    ta = ppo.PPO(pa, roll, minibatch=4096, epochs=1, graph=False, compact=True)
+    tb = ppo.PPO(pb, roll, minibatch=4096, epochs=1, graph=False, compact=False)
+    ta.advantages()
+    tb.advantages()
+    g = torch.Generator(device='cuda').manual_seed(4)
+    for _ in range(3):
+        idx = torch.randperm(ta.total, device='cuda', generator=g)[:ta.mb]
+        ta.minibatch(idx)
+        tb.minibatch(idx)
+        torch.cuda.synchronize()
+        assert torch.equal(ta.grad, tb.grad)
+        assert torch.equal(pa.flat, pb.flat)
+    from d1 import gemm
+    assert gemm.gemm_error() == 0
