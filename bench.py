@@ -322,6 +322,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         roll.roll()
         peer_error = trainer.lib.d1_peer_error() if trainer.peer is not None else 0
+        exchange = ('peer memory (NVLink)' if trainer.peer is not None else 'NCCL') if world > 1 else None
         trainer.release()  # graph and exchange buffers go before the process group does
         it_ms = torch.tensor([p0.elapsed_time(p3)], device=dev)
         if world > 1:
@@ -332,8 +333,7 @@ def run_ours(args, rank, world, local_rank):
                     'update_ms': p2.elapsed_time(p3), 'minibatch_ms': p2.elapsed_time(p3) / updates,
                     'samples_per_iteration': T * B * world, 'minibatch': args.minibatch, 'epochs': args.epochs,
                     'finite': bool(torch.isfinite(policy.flat).all().item()),
-                    'gradient_exchange': ('peer memory (NVLink)' if trainer.peer is not None else 'NCCL') if world > 1
-                    else None, 'peer_error': int(peer_error)}
+                    'gradient_exchange': exchange, 'peer_error': int(peer_error)}
     # centered-map conv policy with the autoregressive head,
     # 131,072 envs per GPU; a step = crop + conv stack + FC + head + AR sampling
     # + env step (no 1832-feature observation is written).
@@ -414,6 +414,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         roll4.roll()
         peer_error4 = tr4.lib.d1_peer_error() if tr4.peer is not None else 0
+        exchange4 = ('peer memory (NVLink)' if tr4.peer is not None else 'NCCL') if world > 1 else None
         tr4.release()
         t_it = torch.tensor([q0.elapsed_time(q2), q0.elapsed_time(q1)], device=dev)
         if world > 1:
@@ -425,8 +426,7 @@ def run_ours(args, rank, world, local_rank):
                    'ms_per_iteration': t_it[0].item(), 'rollout_ms': t_it[1].item(),
                    'decisions_per_iteration': decisions, 'envs_per_gpu': n4, 'horizon': t4,
                    'minibatch': args.minibatch, 'epochs': args.epochs,
-                   'gradient_exchange': ('peer memory (NVLink)' if tr4.peer is not None else 'NCCL') if world > 1
-                   else None, 'peer_error': int(peer_error4),
+                   'gradient_exchange': exchange4, 'peer_error': int(peer_error4),
                    'finite': bool(torch.isfinite(pol4.flat).all().item())}
         del env4, pol4, roll4, tr4
     if rank != 0:

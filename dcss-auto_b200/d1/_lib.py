@@ -100,6 +100,31 @@ def library():
     return _LIB
 
 
+def resolve_device(device):
+    """A CUDA device with its index: 'cuda' (no index) is the current device,
+    as in torch, so an object built after torch.cuda.set_device(r) lives on
+    GPU r. libd1 launches on the current device with the pointers it is given,
+    so an object's tensors and its launches must agree on the device."""
+    import torch
+    dev = torch.device(device)
+    if dev.type != 'cuda':
+        return dev
+    return dev if dev.index is not None else torch.device('cuda', torch.cuda.current_device())
+
+
+def launch_stream(device):
+    """The current stream of `device` for a libd1 launch, after checking that
+    `device` is the current CUDA device: libd1 launches on the current device,
+    so pointers of another GPU would be read by the wrong one."""
+    import torch
+    dev = torch.device(device)
+    cur = torch.cuda.current_device()
+    if dev.index is not None and dev.index != cur:
+        raise D1Error(f'tensors on {dev} but the current CUDA device is cuda:{cur}: '
+                      f'call torch.cuda.set_device({dev.index}) (or use torch.cuda.device) first')
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
 def check(code, what='libd1 call'):
     if code:
         raise D1Error(f'{what} failed with error {code}')

@@ -25,7 +25,7 @@ launch many waves deep, which measured faster than L2-sized chunks.
 """
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, launch_stream, resolve_device
 from . import gemm as G
 
 CROP, CROP_PITCH, FC_IN, WIDTH, HEAD, PRE, NV, NT = 63, 64, 3136, 512, 80, 64, 12, 9
@@ -36,7 +36,7 @@ CONV = [(10, 32), (32, 64), (64, 64)]
 
 class ConvPolicy:
     def __init__(self, device='cuda', seed=0, chunk=16384):
-        self.device = torch.device(device)
+        self.device = resolve_device(device)
         self.lib = library()
         self.chunk = chunk
         g = torch.Generator(device='cpu').manual_seed(seed)
@@ -69,7 +69,7 @@ class ConvPolicy:
     def refresh(self):
         """Re-derive the kernel copies (operand-layout bf16 conv weights, bf16 FC
         and head weights, the type-embedding terms) from the fp32 masters."""
-        s = torch.cuda.current_stream(self.device).cuda_stream
+        s = launch_stream(self.device)
         for i in (1, 2, 3):
             wt = self.params[f'c{i}w'].contiguous()
             check(self.lib.d1_conv_pack_weights(i, wt.data_ptr(), self.packed[i].data_ptr(), s),
@@ -92,12 +92,12 @@ class ConvPolicy:
 
     def encode(self, state, n, buf, g=0):
         """Crops of n env state rows (u16 codes) under D4 element g."""
-        s = torch.cuda.current_stream(self.device).cuda_stream
+        s = launch_stream(self.device)
         check(self.lib.d1_spec_crop(state.data_ptr(), n, g, buf['crop'].data_ptr(), s), 'd1_spec_crop')
 
     def features(self, buf, n):
         """conv stack + FC + head GEMM: fills buf['fc_in'], buf['h'], buf['hb']."""
-        lib, s = self.lib, torch.cuda.current_stream(self.device).cuda_stream
+        lib, s = self.lib, launch_stream(self.device)
         p, pk = self.params, self.packed
         crop, fc_in = buf['crop'], buf['fc_in']
         for c0 in range(0, n, self.chunk):
@@ -129,7 +129,7 @@ class ConvPolicy:
                 out['entropy'] = torch.empty(n, device=dev)
                 out['verb_logits'] = torch.empty((n, NV), device=dev)
                 out['target_logits'] = torch.empty((n, 2, NT), device=dev)
-        s = torch.cuda.current_stream(dev).cuda_stream
+        s = launch_stream(dev)
         ptr = lambda k: out[k].data_ptr() if k in out else None
         p = self.params
         check(self.lib.d1_ar_head_sample(buf['hb'].data_ptr(), n, self.cond.data_ptr(), p['wt'].data_ptr(),

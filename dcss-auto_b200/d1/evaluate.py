@@ -18,7 +18,7 @@ import math
 
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, launch_stream
 
 
 def wilson(successes, n, z=1.96):
@@ -41,7 +41,7 @@ def _legal_bits(env):
 def evaluate(env, policy=None, mode='greedy', seed=900000, steps=None, check_every=32):
     lib = library()
     dev, n = env.device, env.batch
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream = launch_stream(dev)
     spec = hasattr(env, 'values')
     if mode in ('greedy', 'sampled') and policy is None:
         raise ValueError(f'mode {mode!r} needs a policy')

@@ -5,7 +5,7 @@ reset and refilled with the new observation when an episode ends. One kernel
 Wraps either task's env; attributes other than obs pass through to it."""
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, launch_stream
 
 
 class FrameStack:
@@ -24,7 +24,7 @@ class FrameStack:
         return getattr(self.base, name)
 
     def _stream(self):
-        return torch.cuda.current_stream(self.obs.device).cuda_stream
+        return launch_stream(self.obs.device)
 
     def _fill(self):
         check(library().d1_frame_stack(self.obs.data_ptr(), self.base.obs.data_ptr(), self.row_bytes, self.frames,

@@ -1,11 +1,11 @@
 """Dense layers of the policy on the tcgen05 GEMM (d1_gemm): bf16 in/out, fp32 accumulate."""
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, launch_stream
 
 
 def _stream(t):
-    return torch.cuda.current_stream(t.device).cuda_stream
+    return launch_stream(t.device)
 
 
 def gemm(a, b, bias=None, relu=False, out=None, out_t=None, out_f32=None, splits=1, mask=None):

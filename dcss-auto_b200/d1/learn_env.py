@@ -13,7 +13,7 @@ import pathlib
 import numpy as np
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, resolve_device, launch_stream
 
 DATA = pathlib.Path(__file__).resolve().parent / 'data'
 
@@ -65,7 +65,7 @@ def device_tables(device):
         i = torch.from_numpy(index).to(device)
         d = torch.empty((len(cells), 5600), dtype=torch.int16, device=device)  # u16 bits
         check(lib.learn_distance_table(f.data_ptr(), c.data_ptr(), len(cells), d.data_ptr(),
-                                       torch.cuda.current_stream(device).cuda_stream), 'learn_distance_table')
+                                       launch_stream(device)), 'learn_distance_table')
         _DEVICE_TABLES[key] = [f, c, i, d]
     return _DEVICE_TABLES[key]
 
@@ -74,7 +74,7 @@ class Env:
     def __init__(self, batch=512, enemies=6, seed=0, device='cuda', limit=256):
         if not 1 <= enemies <= 8 or limit != 256:
             raise ValueError('Supported: 1..8 enemies, fixed 256-decision deadline')
-        self.device = torch.device('cuda:0' if device == 'cuda' else device)
+        self.device = resolve_device(device)
         if self.device.type != 'cuda':
             raise ValueError('libd1 runs on CUDA devices only; use the oracle for CPU reference runs')
         self.batch, self.enemies, self.limit = batch, enemies, limit
@@ -94,7 +94,7 @@ class Env:
 
     @property
     def stream(self):
-        return torch.cuda.current_stream(self.device).cuda_stream
+        return launch_stream(self.device)
 
     def check(self, code):
         check(code, 'D:1 task call')

@@ -116,7 +116,7 @@ def read_corpus(root, map_limit=None):
 def compile_map(floor, seed=0, hp=15, ac100=200, ev100=794, sh100=906, device='cuda'):
     """Build a corpus map's tables for a u8[5600] floor on the GPU."""
     import torch
-    from ._lib import check, library
+    from ._lib import check, library, launch_stream
     from .spec_env import device_rays
     lib = library()
     dev = torch.device(device)
@@ -130,7 +130,7 @@ def compile_map(floor, seed=0, hp=15, ac100=200, ev100=794, sh100=906, device='c
     los = torch.empty((N, 10), dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):
         device_rays(dev)
-        s = torch.cuda.current_stream(dev).cuda_stream
+        s = launch_stream(dev)
         if len(cells):
             check(lib.learn_distance_table(f.data_ptr(), c.data_ptr(), len(cells), dist.data_ptr(), s),
                   'learn_distance_table')

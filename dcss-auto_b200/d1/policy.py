@@ -9,7 +9,7 @@ N(0, 1/fan_in) weights, zero biases, from a torch CPU generator seed.
 """
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, launch_stream, resolve_device
 from . import gemm
 
 OBS, HID, NACT = 1832, 256, 12
@@ -31,7 +31,7 @@ def layout(obs=OBS, hidden=HID):
 
 class Policy:
     def __init__(self, device='cuda', seed=0, obs=OBS, hidden=HID):
-        self.device = torch.device(device)
+        self.device = resolve_device(device)
         self.obs, self.hidden = obs, hidden
         self.layout, self.size = layout(obs, hidden)
         self.flat = torch.zeros(self.size, device=self.device)
@@ -71,7 +71,7 @@ class Policy:
     def head(self, h2, legal, seed, step, first_env, action, logp, value, logits=None):
         """`step` is an int, or an int64 device tensor of one element read when
         the kernel runs (for CUDA graphs that advance it themselves)."""
-        stream = torch.cuda.current_stream(self.device).cuda_stream
+        stream = launch_stream(self.device)
         n = h2.shape[0]
         if isinstance(step, torch.Tensor):
             check(self.lib.d1_policy_head_sample_dev(
@@ -97,7 +97,7 @@ class Policy:
 
     def fused_head(self, h1, legal, seed, step, first_env, action, logp, value, logits=None):
         """Layer 2 with the head and sampler in its epilogue (h2 is never stored)."""
-        stream = torch.cuda.current_stream(self.device).cuda_stream
+        stream = launch_stream(self.device)
         ptr = lambda t: None if t is None else t.data_ptr()
         check(self.lib.d1_gemm_head_sample(h1.data_ptr(), h1.stride(0), self.bf16['w2'].data_ptr(), self.hidden,
                                            h1.shape[0], self.hidden, self.params['b2'].data_ptr(),

@@ -40,7 +40,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, launch_stream
 from . import gemm as G
 from .policy import HID, NOUT, OBS
 
@@ -157,7 +157,7 @@ class PPO:
 
     @property
     def stream(self):
-        return torch.cuda.current_stream(self.policy.device).cuda_stream
+        return launch_stream(self.policy.device)
 
     # ------------------------------------------------------------------ GAE
     def advantages(self):

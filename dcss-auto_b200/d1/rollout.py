@@ -72,7 +72,7 @@ class DecisionGraph:
 
     def __init__(self, env, policy, seed, first_env=0, step=0):
         import torch
-        from ._lib import check, library
+        from ._lib import check, library, launch_stream
         dev, n = env.device, env.batch
         self.env, self.policy = env, policy
         self.h_act = torch.zeros(n, dtype=torch.int64).pin_memory()
@@ -86,7 +86,7 @@ class DecisionGraph:
         lib = library()
 
         def body():
-            s = torch.cuda.current_stream(dev).cuda_stream
+            s = launch_stream(dev)
             self.d_act.copy_(self.h_act, non_blocking=True)
             env.step(self.d_act)
             policy.act(env.obs, env.legal, seed, self.step, first_env, action=self.next, logp=self.logp,

@@ -18,7 +18,7 @@ import pathlib
 import numpy as np
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, resolve_device, launch_stream
 
 DATA = pathlib.Path(__file__).resolve().parent / 'data'
 
@@ -108,7 +108,7 @@ class SpecEnv:
         """observe=False skips the 1832-feature observation writes (the conv
         policy reads the env state through d1_spec_crop instead); legal bits and
         outcomes are still written."""
-        self.device = torch.device('cuda:0' if device == 'cuda' else device)
+        self.device = resolve_device(device)
         if self.device.type != 'cuda':
             raise ValueError('libd1 runs on CUDA devices only; use the oracle for CPU reference runs')
         self.lib = library()
@@ -126,7 +126,7 @@ class SpecEnv:
 
     @property
     def stream(self):
-        return torch.cuda.current_stream(self.device).cuda_stream
+        return launch_stream(self.device)
 
     def reset(self, seed, obs_out=None, legal_out=None, cobs_out=None):
         obs = self.obs if obs_out is None else obs_out

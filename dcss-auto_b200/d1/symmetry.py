@@ -11,7 +11,7 @@ shard of a multi-GPU run draws the same groups as the whole batch would.
 Attributes other than obs, legal and legal_mask pass through to the wrapped env."""
 import torch
 
-from ._lib import check, library
+from ._lib import check, library, launch_stream
 
 
 class EpisodeSymmetry:
@@ -33,7 +33,7 @@ class EpisodeSymmetry:
         return getattr(self.base, name)
 
     def _stream(self):
-        return torch.cuda.current_stream(self.base.device).cuda_stream
+        return launch_stream(self.base.device)
 
     def _draw(self, out, active):
         p = lambda t: None if t is None else t.data_ptr()

@@ -137,3 +137,14 @@ def test_compact_observation_expands_to_the_one_hot_observation(spec):
         assert torch.equal(x[:, :1832].view(torch.int16), env.obs[idx].view(torch.int16)), k
         assert torch.equal(x[:, 1832:].float(), torch.tensor([1.] + [0.] * 7, device='cuda').expand(n, 8)), k
     assert torch.equal(cobs[:, 225:256], torch.zeros_like(cobs[:, 225:256]))
+
+
+def test_bare_cuda_means_the_current_device():
+    import torch
+    from d1._lib import resolve_device, launch_stream
+    from d1.spec_env import SpecEnv
+    cur = torch.cuda.current_device()
+    assert resolve_device('cuda') == torch.device('cuda', cur)
+    env = SpecEnv(64, seed=2)
+    assert env.device == torch.device('cuda', cur)
+    assert launch_stream(env.device) == torch.cuda.current_stream().cuda_stream
