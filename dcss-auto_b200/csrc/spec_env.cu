@@ -32,6 +32,11 @@ constexpr int MAXM = 11, OBS = 1832, CELLS = 225, ACTIONS = 12, OUT = 10, COMPAC
 // Compact observation row: the channel (0-7) of each window cell as a byte
 // (0-224, then zeros to 255), the 32 scalars as bf16 at byte 256.
 constexpr int COBS = 320, COBS_SCALARS = 256;
+// Divisors of the 32 observation scalars (entries 0 and 2 are the config's HP
+// and turn limit, filled in by the caller).
+__device__ const float SCALAR_DEN[32] = {1.f, 100.f, 1.f,  10.f, 80.f, 70.f, 10.f, 10.f, 1.f, 7.f,  7.f,
+                                         16.f, 1.f,  4.f,  1.f,  80.f, 70.f, 1.f,  8.f,  16.f, 1.f, 1.f,
+                                         1024.f, 2.f, 1.f, 1.f, 7.f,  7.f,  1.f,  30.f, 1.f, 1.f};
 constexpr int ROW = 7680, OFF_DIST = 2048, PL = 210, OFF_VIS = 64, OFF_MON = 128, OFF_FLOOR = 256, OFF_VIEWED = 256 + 4 * PL;
 #ifndef D1_SPEC_WARPS
 #define D1_SPEC_WARPS 1
@@ -860,23 +865,31 @@ __device__ void observe(Env &e, const D1SpecConfig &c, __nv_bfloat16 *obs, uint8
     const int na = __shfl_sync(FULL, e.m_awake, near < 0 ? 0 : near), nk = __shfl_sync(FULL, e.m_kind, near < 0 ? 0 : near);
     const int op = __shfl_sync(FULL, e.m_pos, ogre < 0 ? 0 : ogre), oh = __shfl_sync(FULL, e.m_hp, ogre < 0 ? 0 : ogre);
     const int oa = __shfl_sync(FULL, e.m_awake, ogre < 0 ? 0 : ogre);
-    // Feature `lane` = num[lane] / den[lane] with the same operands as the
-    // oracle's expressions (every value is an int or a 0/1 flag over a float
-    // constant), so one correctly rounded division per lane reproduces it.
+    // Feature `lane` = num / den with the same operands as the oracle's
+    // expressions (every value is an int or a 0/1 flag over a float constant),
+    // so one correctly rounded division per lane reproduces it. Every lane holds
+    // the same 32 numerators: lane 0 stages them in shared memory (the monster
+    // occupancy plane, which the next monster phase re-initialises) and each
+    // lane reads its own, instead of a per-lane array in local memory.
     const int npx = near >= 0 ? np % W - px : 0, npy = near >= 0 ? np / W - py : 0;
     const int opx = ogre >= 0 ? op % W - px : 0, opy = ogre >= 0 ? op / W - py : 0;
-    const float num[32] = {(float)e.hp, (float)e.regen, (float)e.ticks, (float)e.killed, (float)px, (float)py,
-                           (float)nvis, (float)nvis_awake, near >= 0 ? 1.f : 0.f, (float)npx, (float)npy,
-                           near >= 0 ? (float)nh : 0.f, near >= 0 ? (float)na : 0.f, near >= 0 ? (float)nk : 0.f,
-                           known ? 1.f : 0.f, known ? (float)(e.stairs % W - px) : 0.f,
-                           known ? (float)(e.stairs / W - py) : 0.f, e.player == e.stairs ? 1.f : 0.f, (float)nadj,
-                           (float)weakest, rest_ok ? 1.f : 0.f, attack_ok ? 1.f : 0.f, (float)e.floor_seen,
-                           (float)e.blocks, 1.f, ogre >= 0 ? 1.f : 0.f, (float)opx, (float)opy,
-                           ogre >= 0 ? (float)oa : 0.f, ogre >= 0 ? (float)oh : 0.f, 0.f, 0.f};
-    const float den[32] = {(float)c.hp, 100.f, (float)c.limit, 10.f, 80.f, 70.f, 10.f, 10.f, 1.f, 7.f, 7.f, 16.f,
-                           1.f, 4.f, 1.f, 80.f, 70.f, 1.f, 8.f, 16.f, 1.f, 1.f, 1024.f, 2.f, 1.f, 1.f, 7.f, 7.f,
-                           1.f, 30.f, 1.f, 1.f};
-    const float f = num[lane] / den[lane];
+    float4 *stage = reinterpret_cast<float4 *>(s.occ);
+    if (lane == 0) {
+        stage[0] = make_float4((float)e.hp, (float)e.regen, (float)e.ticks, (float)e.killed);
+        stage[1] = make_float4((float)px, (float)py, (float)nvis, (float)nvis_awake);
+        stage[2] = make_float4(near >= 0 ? 1.f : 0.f, (float)npx, (float)npy, near >= 0 ? (float)nh : 0.f);
+        stage[3] = make_float4(near >= 0 ? (float)na : 0.f, near >= 0 ? (float)nk : 0.f, known ? 1.f : 0.f,
+                               known ? (float)(e.stairs % W - px) : 0.f);
+        stage[4] = make_float4(known ? (float)(e.stairs / W - py) : 0.f, e.player == e.stairs ? 1.f : 0.f,
+                               (float)nadj, (float)weakest);
+        stage[5] = make_float4(rest_ok ? 1.f : 0.f, attack_ok ? 1.f : 0.f, (float)e.floor_seen, (float)e.blocks);
+        stage[6] = make_float4(1.f, ogre >= 0 ? 1.f : 0.f, (float)opx, (float)opy);
+        stage[7] = make_float4(ogre >= 0 ? (float)oa : 0.f, ogre >= 0 ? (float)oh : 0.f, 0.f, 0.f);
+    }
+    __syncwarp();
+    const float num = reinterpret_cast<const float *>(s.occ)[lane];
+    const float den = lane == 0 ? (float)c.hp : lane == 2 ? (float)c.limit : __ldg(SCALAR_DEN + lane);
+    const float f = num / den;
     if (obs) obs[1800 + lane] = __float2bfloat16_rn(f);
     if (cobs) {
         reinterpret_cast<__nv_bfloat16 *>(reinterpret_cast<uint8_t *>(s.crow) + COBS_SCALARS)[lane] =
