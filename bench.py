@@ -25,7 +25,7 @@ REPO = pathlib.Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / 'dcss-auto_b200'))
 
 METRIC = 'env decisions/sec (sim+policy, device-timed)'
-ENV_TRAFFIC_BYTES = 563.0e6  # step_kernel DRAM bytes per 65,536-env launch (ncu: 140.4 MB read + 422.6 MB write)
+ENV_TRAFFIC_BYTES = 357.6e6  # step_kernel DRAM bytes per 65,536-env launch (ncu: 139.5 MB read + 218.1 MB write)
 UNIT = 'decisions/s'
 ENVS, HORIZON = 65536, 128
 # Algorithmic bytes per decision of the env step (sim + bf16 observation write):
