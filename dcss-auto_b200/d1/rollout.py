@@ -65,7 +65,9 @@ class DecisionGraph:
     """One decision of a host-driven loop captured once as a CUDA graph:
     copy the actions in from pinned host memory, step the env, run the policy on
     the new observation (two GEMMs + head + masked draw) and copy the outcome
-    rows and the next actions back to pinned host memory. The sampling step is a
+    rows and the next actions back to pinned host memory. The outcome rows are
+    copied on a second stream forked after the env step, so that copy overlaps
+    the policy; the graph joins it before it ends. The sampling step is a
     device counter that the graph advances, so every replay draws fresh
     uniforms. replay() launches it; the caller synchronises before reading the
     host buffers."""
@@ -84,16 +86,21 @@ class DecisionGraph:
         self.value = torch.empty(n, device=dev)
         self.step = torch.full((1,), step, dtype=torch.int64, device=dev)
         lib = library()
+        copy = torch.cuda.Stream(dev)  # the outcome rows go back while the policy runs
 
         def body():
             s = launch_stream(dev)
+            main = torch.cuda.current_stream(dev)
             self.d_act.copy_(self.h_act, non_blocking=True)
             env.step(self.d_act)
+            copy.wait_stream(main)
+            with torch.cuda.stream(copy):
+                self.h_out.copy_(env.out, non_blocking=True)
             policy.act(env.obs, env.legal, seed, self.step, first_env, action=self.next, logp=self.logp,
                        value=self.value)
             check(lib.d1_counter_add(self.step.data_ptr(), 1, s), 'd1_counter_add')
-            self.h_out.copy_(env.out, non_blocking=True)
             self.h_next.copy_(self.next, non_blocking=True)
+            main.wait_stream(copy)
 
         body()  # warm-up: kernel attributes and workspaces exist before capture
         torch.cuda.synchronize(dev)
