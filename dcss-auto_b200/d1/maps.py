@@ -1,4 +1,4 @@
-"""Map files of the reference and their compiler on the GPU (SURVEY next item 1).
+"""Map files of the reference and their compiler on the GPU.
 
 * fixture.bin -- the single-map fixture (writer gpu-d1/scripts/compile_fixture.py:
   75-80, reader learn_env.py:15-40): magic 0x44314750, 8-int header (player, hp,

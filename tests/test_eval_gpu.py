@@ -1,5 +1,5 @@
 """Evaluation harness, greedy heads, frame stack and exact checkpoint/resume on
-the GPU (SURVEY next items 2-4; reference: gpu-d1/scripts/train_clear.py:42-76,
+the GPU (reference: gpu-d1/scripts/train_clear.py:42-76,
 run_ring_ablations.py:231-309, scripts/test_resume.py, vision15-centered-map-v1/
 scripts/frame_stack.py):
 
