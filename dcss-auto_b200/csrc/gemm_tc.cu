@@ -1314,7 +1314,7 @@ int d1_gemm_error(void) {
 namespace d1 {
 namespace tc {
 constexpr int64_t NOALLOC_FLOATS = 4 * 1024 * 1024;
-__device__ __align__(256) float g_noalloc_slabs[NOALLOC_FLOATS];
+static __device__ __align__(256) float g_noalloc_slabs[NOALLOC_FLOATS];
 
 __global__ void reduce_2d_kernel(const float *__restrict__ slabs, int splits, int M, int N, int ldcf,
                                  float *__restrict__ out, int ldo) {
