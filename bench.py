@@ -212,35 +212,33 @@ def run_ours(args, rank, world, local_rank):
     progress('env + policy built; warm-up')
     for k in range(args.warmup):
         step(k)
-    # Kernel-level timing of the env step (events on its launching stream).
-    ev_env = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
-    orig_env_step = env.step
-
-    def timed_env_step(*a, **kw):
-        i = timed_env_step.i
-        ev_env[i][0].record(stream)
-        r = orig_env_step(*a, **kw)
-        ev_env[i][1].record(stream)
-        timed_env_step.i += 1
-        return r
-    timed_env_step.i = 0
     clocks = Clocks(local_rank)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    env.step = timed_env_step
     start.record(stream)
     for k in range(args.warmup, args.warmup + args.steps):
         step(k)
+    roll.join()  # the env ranges' streams
     stop.record(stream)
     torch.cuda.synchronize()
-    env.step = orig_env_step
     clk = clocks.stop()
     ms = start.elapsed_time(stop)
-    env_ms = sum(a.elapsed_time(b) for a, b in ev_env) / args.steps
+    # Kernel-level timing of the env step for the roofline: the rollout's env
+    # ranges overlap the policy on other streams, so the kernel is timed alone
+    # here, whole batch per launch, with events on its launching stream,
+    # continuing the same episodes with the rollout's last actions.
+    n_env = min(16, args.steps)
+    ev_env = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_env)]
+    for i in range(n_env):
+        t_env = (args.warmup + args.steps + i) % T
+        ev_env[i][0].record(stream)
+        env.step(roll.actions[t_env])
+        ev_env[i][1].record(stream)
+    torch.cuda.synchronize()
+    env_ms = sum(a.elapsed_time(b) for a, b in ev_env) / n_env
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -440,6 +438,7 @@ def run_ours(args, rank, world, local_rank):
         'config': {'workload': 'config1 rollout: 65,536 envs/GPU on seeded generated 80x70 D:1 maps, '
                                'obs 1832 bf16, MLP 1832-256-256-13 (random N(0,1/fan_in)), masked sampling',
                    'envs_per_gpu': B, 'horizon': T, 'parallelism': f'dp{world} (env shards)',
+                   'rollout_streams': roll.parts,
                    'l2': 'inputs larger than L2 (240 MB obs slot + 134 MB env state per step)'},
         'roofline': {'kernel': 'd1::spec::step_kernel', 'bound': 'hbm', 'achieved': achieved,
                      'peak': pk['hbm_gbs'], 'unit': 'GB/s', 'frac': achieved / pk['hbm_gbs'],
@@ -458,7 +457,7 @@ def run_ours(args, rank, world, local_rank):
         'config4': c4_line,
         'clocks': clk,
         'e2e': e2e,
-        'gpu_launches': args.steps * 4,
+        'gpu_launches': args.steps * 4 * roll.parts,
     }
     if not args.no_cpu:
         progress('CPU baseline')
@@ -494,7 +493,7 @@ def run_kernels(args):
     B = args.envs
     env = SpecEnv(B, seed=1)
     pol = Policy(seed=0)
-    roll = Rollout(env, pol, 8, seed=1)
+    roll = Rollout(env, pol, 8, seed=1, parts=1)  # one stream: the launch order below is fixed
     roll.collect()
     tr = PPO(pol, roll, minibatch=args.minibatch, epochs=1, graph=False)
     tr.advantages()

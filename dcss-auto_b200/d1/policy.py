@@ -105,11 +105,13 @@ class Policy:
                                            seed, step, first_env, ptr(action), ptr(logp), ptr(value), ptr(logits),
                                            stream), 'd1_gemm_head_sample')
 
-    def act(self, obs, legal, seed, step, first_env=0, action=None, logp=None, value=None, logits=None):
+    def act(self, obs, legal, seed, step, first_env=0, action=None, logp=None, value=None, logits=None, part=0):
         """Forward + sample: two tcgen05 GEMMs, then the head + sampler kernel.
-        Writes into the given buffers (allocated if None)."""
+        Writes into the given buffers (allocated if None). `part` selects the
+        activation buffers, so that parts of a batch can run on different
+        streams at the same time."""
         n = obs.shape[0]
-        _, h2 = self.hidden_layers(obs, h1=self._h1_buffer(n), h2=self._h2_buffer(n))
+        _, h2 = self.hidden_layers(obs, h1=self._h1_buffer(n, part), h2=self._h2_buffer(n, part))
         if action is None:
             action = torch.empty(n, dtype=torch.int64, device=self.device)
         if logp is None:
@@ -134,15 +136,18 @@ class Policy:
         self.fused_head(self._h1(obs), legal, seed, step, first_env, action, logp, value, logits)
         return action, logp, value
 
-    def _h2_buffer(self, n):
-        if getattr(self, '_h2_buf', None) is None or self._h2_buf.shape[0] < n:
-            self._h2_buf = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=self.device)
-        return self._h2_buf[:n]
+    def _buffer(self, kind, n, part):
+        bufs = self.__dict__.setdefault('_act_bufs', {})
+        b = bufs.get((kind, part))
+        if b is None or b.shape[0] < n:
+            b = bufs[(kind, part)] = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=self.device)
+        return b[:n]
 
-    def _h1_buffer(self, n):
-        if getattr(self, '_h1_buf', None) is None or self._h1_buf.shape[0] < n:
-            self._h1_buf = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=self.device)
-        return self._h1_buf[:n]
+    def _h2_buffer(self, n, part=0):
+        return self._buffer('h2', n, part)
+
+    def _h1_buffer(self, n, part=0):
+        return self._buffer('h1', n, part)
 
     def value(self, obs, out=None):
         n = obs.shape[0]

@@ -6,9 +6,9 @@ Every step the policy reads the current one-hot observation (`obs`, one
 writes the next one-hot observation over it, its compact form (320 B per env)
 into history slot `cobs[t+1]`, the legal mask into slot t+1 and its outcome row
 into out[t]. The history is kept compact -- 320 instead of 3,664 bytes per
-sample, 2.7 instead of 31 GB at 65,536 envs x 128 steps -- and the update
-expands the minibatch's rows (d1_ppo_gather_cobs). Nothing is copied between
-kernels.
+sample, 2.7 instead of 31 GB at 65,536 envs x 128 steps -- and the update's
+layer-1 and dW1 GEMMs expand the minibatch's rows into their operand tiles.
+Nothing is copied between kernels.
 """
 import torch
 
@@ -16,7 +16,16 @@ OBS, COBS = 1832, 320
 
 
 class Rollout:
-    def __init__(self, env, policy, horizon, seed=0, sample_seed=None):
+    """parts > 1 splits the batch into that many contiguous env ranges, each
+    stepped (policy, then env) on its own stream: one range's env kernel then
+    overlaps another's policy GEMMs (measured on one B200 at 65,536 envs: 0.373
+    -> 0.342 ms per step with two ranges). The ranges' streams follow the
+    current stream's earlier work at every step and are joined back into it by
+    join(), which roll(), bootstrap() and collect() call; a caller that drives
+    step() itself calls join() before reading the buffers on another stream.
+    Trajectories do not depend on `parts`."""
+
+    def __init__(self, env, policy, horizon, seed=0, sample_seed=None, parts=2):
         self.env, self.policy, self.T = env, policy, horizon
         B, dev = env.batch, env.device
         self.seed = seed
@@ -29,16 +38,43 @@ class Rollout:
         self.values = torch.empty((horizon + 1, B), device=dev)
         self.out = torch.zeros((horizon, B, env.out.shape[1]), device=dev)
         self.global_step = 0
+        parts = max(1, min(parts, B // 4096)) if B >= 8192 else 1
+        edges = [B * i // parts for i in range(parts + 1)]
+        self.ranges = [(edges[i], edges[i + 1]) for i in range(parts)]
+        self.streams = [torch.cuda.Stream(dev) for _ in range(parts)] if parts > 1 else []
         env.reset(seed, obs_out=self.obs, legal_out=self.legal[0], cobs_out=self.cobs[0])
 
+    @property
+    def parts(self):
+        return len(self.ranges)
+
+    def join(self):
+        """Make the current stream wait for the ranges' streams."""
+        main = torch.cuda.current_stream(self.env.device)
+        for s in self.streams:
+            main.wait_stream(s)
+
     def step(self, t):
-        self.policy.act(self.obs, self.legal[t], self.sample_seed, self.global_step, self.env.first_env,
-                        action=self.actions[t], logp=self.logp[t], value=self.values[t])
-        self.env.step(self.actions[t], obs_out=self.obs, legal_out=self.legal[t + 1], out_out=self.out[t],
-                      cobs_out=self.cobs[t + 1])
+        if not self.streams:
+            self.policy.act(self.obs, self.legal[t], self.sample_seed, self.global_step, self.env.first_env,
+                            action=self.actions[t], logp=self.logp[t], value=self.values[t])
+            self.env.step(self.actions[t], obs_out=self.obs, legal_out=self.legal[t + 1], out_out=self.out[t],
+                          cobs_out=self.cobs[t + 1])
+        else:
+            main = torch.cuda.current_stream(self.env.device)
+            for i, (lo, hi) in enumerate(self.ranges):
+                s = self.streams[i]
+                s.wait_stream(main)
+                with torch.cuda.stream(s):
+                    self.policy.act(self.obs[lo:hi], self.legal[t][lo:hi], self.sample_seed, self.global_step,
+                                    self.env.first_env + lo, action=self.actions[t][lo:hi],
+                                    logp=self.logp[t][lo:hi], value=self.values[t][lo:hi], part=i)
+                    self.env.step(self.actions[t], obs_out=self.obs, legal_out=self.legal[t + 1],
+                                  out_out=self.out[t], cobs_out=self.cobs[t + 1], rows=(lo, hi))
         self.global_step += 1
 
     def bootstrap(self):
+        self.join()
         self.policy.value(self.obs, out=self.values[self.T])
 
     def collect(self):
@@ -49,6 +85,7 @@ class Rollout:
     def roll(self):
         """Start the next rollout from the last observation (the one-hot buffer
         already holds it)."""
+        self.join()
         self.cobs[0].copy_(self.cobs[self.T])
         self.legal[0].copy_(self.legal[self.T])
 

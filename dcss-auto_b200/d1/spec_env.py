@@ -137,21 +137,27 @@ class SpecEnv:
                                        self.stream), 'd1_spec_init_ex')
         return obs
 
-    def step(self, actions, active=None, obs_out=None, legal_out=None, out_out=None, cobs_out=None):
+    def step(self, actions, active=None, obs_out=None, legal_out=None, out_out=None, cobs_out=None, rows=None):
         """One semantic decision per env. `obs_out`/`legal_out`/`out_out`/`cobs_out`
-        let the caller point the writes at rollout-buffer slots (no extra copies)."""
+        let the caller point the writes at rollout-buffer slots (no extra copies).
+        rows=(lo, hi) steps only envs lo..hi-1 of the batch (every tensor is still
+        the whole batch's; the launch reads and writes its rows only), so that
+        parts of one batch can run on different streams."""
         assert actions.device == self.device and actions.dtype == torch.int64 and actions.is_contiguous()
+        lo, hi = (0, self.batch) if rows is None else rows
+        assert 0 <= lo <= hi <= self.batch and actions.shape[0] == self.batch
         act = 0
         if active is not None:
             assert active.device == self.device and active.dtype == torch.bool and active.shape == (self.batch,)
-            act = active.data_ptr()
+            act = active[lo:hi].data_ptr()
         obs = self.obs if obs_out is None else obs_out
         legal = self.legal if legal_out is None else legal_out
         out = self.out if out_out is None else out_out
-        check(self.lib.d1_spec_step_ex(self.state.data_ptr(), self.batch, C.byref(self.config), actions.data_ptr(),
-                                       None if obs is None else obs.data_ptr(),
-                                       None if cobs_out is None else cobs_out.data_ptr(), legal.data_ptr(),
-                                       out.data_ptr(), act or None, self.stream), 'd1_spec_step_ex')
+        check(self.lib.d1_spec_step_ex(self.state[lo:hi].data_ptr(), hi - lo, C.byref(self.config),
+                                       actions[lo:hi].data_ptr(), None if obs is None else obs[lo:hi].data_ptr(),
+                                       None if cobs_out is None else cobs_out[lo:hi].data_ptr(),
+                                       legal[lo:hi].data_ptr(), out[lo:hi].data_ptr(), act or None, self.stream),
+              'd1_spec_step_ex')
         return obs, out
 
     def legal_mask(self):

@@ -126,3 +126,24 @@ def test_decision_graph_replays_the_eager_loop(lib):
         assert torch.equal(dg.h_next, a.cpu()), k
         dg.h_act.copy_(dg.h_next)
         act = a.clone()
+
+
+def test_rollout_on_two_streams_equals_one_stream():
+    """Rollout(parts=2) steps two env ranges on their own streams (each range's
+    env kernel overlapping the other's policy GEMMs); every buffer equals the
+    one-stream rollout's bit for bit."""
+    from d1.policy import Policy
+    from d1.rollout import Rollout
+    from d1.spec_env import SpecEnv
+    B, T = 8192, 12
+    one = Rollout(SpecEnv(B, seed=21), Policy(seed=4), T, seed=21, parts=1)
+    two = Rollout(SpecEnv(B, seed=21), Policy(seed=4), T, seed=21, parts=2)
+    assert one.parts == 1 and two.parts == 2
+    for r in (one, two):
+        r.collect()
+        r.roll()
+        r.collect()
+    torch.cuda.synchronize()
+    for name in ('obs', 'cobs', 'legal', 'actions', 'logp', 'values', 'out'):
+        assert torch.equal(getattr(one, name), getattr(two, name)), name
+    assert torch.equal(one.env.state, two.env.state)
