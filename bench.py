@@ -275,7 +275,8 @@ def run_ours(args, rank, world, local_rank):
             dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
         e2e = {'value': B * world * e2e_steps / e2e_s.item(), 'unit': UNIT,
                'h2d_bytes_per_step': B * 8, 'd2h_bytes_per_step': B * (env.out.shape[1] * 4 + 8),
-               'steps': e2e_steps, 'path': 'd1.rollout.DecisionGraph (captured decision, host copies inside)'}
+               'steps': e2e_steps, 'streams': len(dg.ranges),
+               'path': 'd1.rollout.DecisionGraph (captured decision, host copies inside)'}
         del dg
     progress('e2e done')
     from d1 import gemm as G

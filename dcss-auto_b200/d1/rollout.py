@@ -15,6 +15,15 @@ import torch
 OBS, COBS = 1832, 320
 
 
+def env_ranges(batch, parts):
+    """Contiguous env ranges for `parts` streams (one range below 8,192 envs,
+    and ranges of at least 4,096 envs: smaller launches lose more to their
+    tails than the overlap gains)."""
+    parts = max(1, min(parts, batch // 4096)) if batch >= 8192 else 1
+    edges = [batch * i // parts for i in range(parts + 1)]
+    return [(edges[i], edges[i + 1]) for i in range(parts)]
+
+
 class Rollout:
     """parts > 1 splits the batch into that many contiguous env ranges, each
     stepped (policy, then env) on its own stream: one range's env kernel then
@@ -38,10 +47,8 @@ class Rollout:
         self.values = torch.empty((horizon + 1, B), device=dev)
         self.out = torch.zeros((horizon, B, env.out.shape[1]), device=dev)
         self.global_step = 0
-        parts = max(1, min(parts, B // 4096)) if B >= 8192 else 1
-        edges = [B * i // parts for i in range(parts + 1)]
-        self.ranges = [(edges[i], edges[i + 1]) for i in range(parts)]
-        self.streams = [torch.cuda.Stream(dev) for _ in range(parts)] if parts > 1 else []
+        self.ranges = env_ranges(B, parts)
+        self.streams = [torch.cuda.Stream(dev) for _ in self.ranges] if len(self.ranges) > 1 else []
         env.reset(seed, obs_out=self.obs, legal_out=self.legal[0], cobs_out=self.cobs[0])
 
     @property
@@ -102,14 +109,16 @@ class DecisionGraph:
     """One decision of a host-driven loop captured once as a CUDA graph:
     copy the actions in from pinned host memory, step the env, run the policy on
     the new observation (two GEMMs + head + masked draw) and copy the outcome
-    rows and the next actions back to pinned host memory. The outcome rows are
-    copied on a second stream forked after the env step, so that copy overlaps
-    the policy; the graph joins it before it ends. The sampling step is a
-    device counter that the graph advances, so every replay draws fresh
-    uniforms. replay() launches it; the caller synchronises before reading the
-    host buffers."""
+    rows and the next actions back to pinned host memory. As in Rollout, the
+    batch runs as contiguous env ranges on their own streams (the first range's
+    policy overlaps the next range's env kernel), and each range's outcome rows
+    are copied back on a further stream while its policy runs; the graph joins
+    them all before it ends. The sampling step is a device counter that the
+    graph advances after the draws, so every replay draws fresh uniforms.
+    replay() launches it; the caller synchronises before reading the host
+    buffers."""
 
-    def __init__(self, env, policy, seed, first_env=0, step=0):
+    def __init__(self, env, policy, seed, first_env=0, step=0, parts=2):
         import torch
         from ._lib import check, library, launch_stream
         dev, n = env.device, env.batch
@@ -123,21 +132,30 @@ class DecisionGraph:
         self.value = torch.empty(n, device=dev)
         self.step = torch.full((1,), step, dtype=torch.int64, device=dev)
         lib = library()
-        copy = torch.cuda.Stream(dev)  # the outcome rows go back while the policy runs
+        self.ranges = env_ranges(n, parts)
+        split = len(self.ranges) > 1
+        streams = [torch.cuda.Stream(dev) for _ in self.ranges] if split else []
+        copies = [torch.cuda.Stream(dev) for _ in self.ranges]  # outcome rows back while the policy runs
 
         def body():
-            s = launch_stream(dev)
             main = torch.cuda.current_stream(dev)
             self.d_act.copy_(self.h_act, non_blocking=True)
-            env.step(self.d_act)
-            copy.wait_stream(main)
-            with torch.cuda.stream(copy):
-                self.h_out.copy_(env.out, non_blocking=True)
-            policy.act(env.obs, env.legal, seed, self.step, first_env, action=self.next, logp=self.logp,
-                       value=self.value)
-            check(lib.d1_counter_add(self.step.data_ptr(), 1, s), 'd1_counter_add')
-            self.h_next.copy_(self.next, non_blocking=True)
-            main.wait_stream(copy)
+            for i, (lo, hi) in enumerate(self.ranges):
+                st = streams[i] if split else main
+                st.wait_stream(main)
+                with torch.cuda.stream(st):
+                    env.step(self.d_act, rows=(lo, hi))
+                    copies[i].wait_stream(st)
+                    with torch.cuda.stream(copies[i]):
+                        self.h_out[lo:hi].copy_(env.out[lo:hi], non_blocking=True)
+                    policy.act(env.obs[lo:hi], env.legal[lo:hi], seed, self.step, first_env + lo,
+                               action=self.next[lo:hi], logp=self.logp[lo:hi], value=self.value[lo:hi], part=i)
+                    self.h_next[lo:hi].copy_(self.next[lo:hi], non_blocking=True)
+            for i in range(len(self.ranges)):
+                if split:
+                    main.wait_stream(streams[i])
+                main.wait_stream(copies[i])
+            check(lib.d1_counter_add(self.step.data_ptr(), 1, launch_stream(dev)), 'd1_counter_add')
 
         body()  # warm-up: kernel attributes and workspaces exist before capture
         torch.cuda.synchronize(dev)

@@ -100,16 +100,18 @@ def test_fused_layer2_head_matches_the_unfused_path_and_the_oracle(lib, n):
     assert gemm.gemm_error() == 0
 
 
-def test_decision_graph_replays_the_eager_loop(lib):
+@pytest.mark.parametrize('n', [4096, 8192])
+def test_decision_graph_replays_the_eager_loop(lib, n):
     """DecisionGraph (one captured decision with host copies and a device step
-    counter) reproduces the eager host-driven loop exactly."""
+    counter; at 8,192 envs as two env ranges on two streams) reproduces the
+    eager host-driven loop exactly."""
     from d1.policy import Policy
     from d1.rollout import DecisionGraph
     from d1.spec_env import SpecEnv
-    n = 4096
     pol = Policy(seed=4)
     eager, graphed = SpecEnv(n, seed=6), SpecEnv(n, seed=6)
     dg = DecisionGraph(graphed, pol, seed=9, step=0)
+    assert len(dg.ranges) == (1 if n < 8192 else 2)
     # DecisionGraph ran one warm-up decision with zero actions and step 0
     act = torch.zeros(n, dtype=torch.int64, device='cuda')
     eager.step(act)
