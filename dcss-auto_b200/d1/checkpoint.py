@@ -24,6 +24,7 @@ def job_of(trainer):
 
 def state_dict(trainer, generator=None, extra=None):
     r, env, p = trainer.rollout, trainer.rollout.env, trainer.policy
+    r.join()  # the rollout's env-range streams
     return dict(format=FORMAT, job=job_of(trainer), params=p.flat.cpu(), adam_m=trainer.m.cpu(),
                 adam_v=trainer.v.cpu(), adam_step=trainer.step_dev.cpu(), env_state=env.state.cpu(),
                 obs=r.obs.cpu(), cobs=r.cobs[0].cpu(), legal=r.legal[0].cpu(), global_step=r.global_step,

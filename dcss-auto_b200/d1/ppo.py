@@ -162,6 +162,7 @@ class PPO:
     # ------------------------------------------------------------------ GAE
     def advantages(self):
         r = self.rollout
+        r.join()  # a caller may have driven r.step() itself
         out = r.out  # [T, B, OUT]: reward at column 0, done at column 1
         self.stats.zero_()
         check(self.lib.d1_gae(out.data_ptr(), out[:, :, 1].data_ptr(), out.stride(0), out.stride(1),
