@@ -19,6 +19,7 @@
 //
 // Every wait on an mbarrier is bounded: on expiry the kernel records an error
 // code in d1_gemm_error and runs its teardown (TMEM is always freed).
+#include <atomic>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -1328,25 +1329,32 @@ __global__ void reduce_2d_kernel(const float *__restrict__ slabs, int splits, in
 
 // Host-side `g_noalloc_slabs` names a host stand-in, not device memory: the
 // device address is looked up with cudaGetSymbolAddress once per device, with
-// that device current, on the first call made on it.
+// that device current, on the first call made on it (so that first call should
+// come before any stream capture). Concurrent first calls from several host
+// threads may each look it up; they find the same address and publish it
+// through an atomic. The cached address belongs to the device's primary
+// context: after cudaDeviceReset on a device, this entry point must not be
+// called again on that device in the same process.
 static float *noalloc_scratch(int *err) {
-    static float *ptrs[128] = {nullptr};
+    static std::atomic<float *> ptrs[128];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= 128) {
         *err = e != cudaSuccess ? (int)e : D1_ERR_BAD_ARGUMENT;
         return nullptr;
     }
-    if (!ptrs[dev]) {
+    float *cached = ptrs[dev].load(std::memory_order_acquire);
+    if (!cached) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_slabs);
         if (e != cudaSuccess || !p) {
             *err = e != cudaSuccess ? (int)e : D1_ERR_BAD_ARGUMENT;
             return nullptr;
         }
-        ptrs[dev] = static_cast<float *>(p);
+        cached = static_cast<float *>(p);
+        ptrs[dev].store(cached, std::memory_order_release);
     }
-    return ptrs[dev];
+    return cached;
 }
 }  // namespace tc
 }  // namespace d1

@@ -833,7 +833,11 @@ struct StepArgs {
 };
 __device__ double g_step_part[STEP_MAX_BLOCKS];
 __device__ unsigned g_step_ticket, g_peer_ticket;
-__device__ int g_peer_error;
+// g_peer_error: sticky, read and cleared by the host (d1_peer_error).
+// g_peer_abort: this step's verdict, cleared by the step's reduction launch,
+// set by any all-reduce block that gave up waiting; the Adam launch then
+// leaves the parameters, moments and step count untouched.
+__device__ int g_peer_error, g_peer_abort;
 
 struct Remap {
     const float *from;
@@ -897,6 +901,7 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint64_t epoch = a.xbuf ? (uint64_t)(*a.epoch_src + 1) : 0;
     const Remap rm{a.remap_from, a.xbuf ? a.xbuf + (epoch & 1) * a.xstride : nullptr, a.remap_len};
+    if (a.xbuf && blockIdx.x == 0 && threadIdx.x == 0) g_peer_abort = 0;
     double sq = 0.0;
     if (a.njobs > 0) {
         // jobs with many partials: a block per chunk, its 8 warps splitting the partials
@@ -943,7 +948,7 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
         __shared__ unsigned last;
         __syncthreads();
         if (threadIdx.x == 0) {
-            __threadfence();
+            __threadfence_system();
             last = atomicAdd(&g_peer_ticket, 1u) == gridDim.x - 1;
         }
         __syncthreads();
@@ -972,8 +977,9 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
 // first waits (bounded) until each peer has flagged this epoch, then sums a
 // contiguous range of all ranks' exchange buffers in rank order, divides by the
 // world size, writes the flat gradient and its block partial of the sum of
-// squares. A wait that gives up sets g_peer_error (d1_peer_error) and leaves
-// the block's range as it was.
+// squares. A wait that gives up (after wait_limit polls) sets g_peer_error
+// (d1_peer_error) and g_peer_abort, and leaves the block's range as it was;
+// the Adam launch that follows then changes nothing.
 struct PeerArgs {
     const float *xbuf[PEER_MAX];  // each rank's exchange buffer (this rank's is local)
     int64_t xstride;
@@ -982,8 +988,9 @@ struct PeerArgs {
     float *grad;
     int64_t total;
     int world, rank;
+    uint32_t wait_limit;
 };
-constexpr uint32_t PEER_WAIT_LIMIT = 1u << 24;
+constexpr uint32_t PEER_WAIT_LIMIT = 1u << 24;  // default: ~1 s of 64 ns polls
 __global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_constant__ PeerArgs a) {
     __shared__ int ok;
     __shared__ double ws[8];
@@ -997,14 +1004,17 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_consta
                 unsigned long long v;
                 asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.flags + p) : "memory");
                 if (v >= epoch) break;
-                if (it >= PEER_WAIT_LIMIT) {
+                if (it >= a.wait_limit) {
                     good = 0;
                     break;
                 }
                 __nanosleep(64);
             }
         }
-        if (!good) atomicExch(&g_peer_error, 1);
+        if (!good) {
+            atomicExch(&g_peer_error, 1);
+            atomicExch(&g_peer_abort, 1);
+        }
         ok = good;
     }
     __syncthreads();
@@ -1044,10 +1054,12 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_consta
 
 // Adam after grad_reduce_kernel: the global sum of squares is the sum of that
 // launch's block partials, added in block order by every block (so the clip
-// coefficient is the same everywhere), and *step advances on the device.
-__global__ void __launch_bounds__(256) adam_update_kernel(AdamArgs d, int nparts, int64_t *step) {
+// coefficient is the same everywhere), and *step advances on the device. After
+// a peer all-reduce (check_abort) that gave up waiting, nothing is updated.
+__global__ void __launch_bounds__(256) adam_update_kernel(AdamArgs d, int nparts, int64_t *step, int check_abort) {
     __shared__ float sc[3];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (check_abort && *(volatile int *)&g_peer_abort) return;
     const int64_t step0 = *step;
     if (warp == 0) {
         double t = 0.0;
@@ -1195,7 +1207,8 @@ struct PeerSetup {
 
 static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
                        float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
-                       const D1AdamSegment *segs, int nseg, int do_adam, void *stream, const PeerSetup *peer = nullptr) {
+                       const D1AdamSegment *segs, int nseg, int do_adam, void *stream, const PeerSetup *peer = nullptr,
+                       uint32_t wait_limit = 0) {
     using namespace ppo;
     if (njobs < 0 || njobs > STEP_MAX_JOBS || (njobs > 0 && !jobs) || (!do_adam && njobs == 0)) return D1_ERR_BAD_ARGUMENT;
     if (peer && (njobs == 0 || !do_adam || peer->world < 2 || peer->world > PEER_MAX || peer->rank < 0 ||
@@ -1249,6 +1262,7 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
         pa.total = total;
         pa.world = peer->world;
         pa.rank = peer->rank;
+        pa.wait_limit = wait_limit ? wait_limit : PEER_WAIT_LIMIT;
     }
     AdamArgs d;
     if (do_adam) {
@@ -1280,7 +1294,7 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     if (blocks > STEP_MAX_BLOCKS) blocks = STEP_MAX_BLOCKS;
     grad_reduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
     if (peer) peer_allreduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(pa);
-    if (do_adam) adam_update_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d, blocks, step);
+    if (do_adam) adam_update_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d, blocks, step, peer ? 1 : 0);
     return (int)cudaGetLastError();
 }
 
@@ -1294,10 +1308,10 @@ int d1_ppo_step(const D1GradJob *jobs, int njobs, float *param, float *grad, flo
 int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
                      float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
                      const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
-                     int world, int rank, void *stream) {
+                     int world, int rank, unsigned wait_limit, void *stream) {
     const PeerSetup peer{xbufs, flags, xstride, world, rank};
     return step_launch(jobs, njobs, param, grad, m, v, total, lr, beta1, beta2, eps, max_norm, step, segs, nseg, 1,
-                       stream, &peer);
+                       stream, &peer, wait_limit);
 }
 
 // Exchange buffers: plain device allocations shared with the other ranks'

@@ -37,6 +37,7 @@ def load_state_dict(trainer, data, generator=None):
     if data['job'] != job_of(trainer):
         raise ValueError('Resume job does not match checkpoint')
     r, env, p = trainer.rollout, trainer.rollout.env, trainer.policy
+    r.join()  # a range stream still stepping must not race the overwrite below
     p.flat.copy_(data['params'])
     p.refresh()
     trainer.m.copy_(data['adam_m'])

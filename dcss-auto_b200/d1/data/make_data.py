@@ -24,6 +24,7 @@ los_rays.npz
     blockers) where blockers is a 64-bit mask over the quadrant cells (bit y*8+x)
     whose opacity kills the ray.
 """
+import os
 import pathlib
 import struct
 import sys
@@ -74,6 +75,12 @@ def convert_rays(ref: pathlib.Path):
 
 
 if __name__ == '__main__':
-    ref = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference/gpu-d1')
+    # The reference's gpu-d1 folder: the argument, else $DCSS_REFERENCE/gpu-d1.
+    if len(sys.argv) > 1:
+        ref = pathlib.Path(sys.argv[1])
+    elif os.environ.get('DCSS_REFERENCE'):
+        ref = pathlib.Path(os.environ['DCSS_REFERENCE']) / 'gpu-d1'
+    else:
+        sys.exit('usage: make_data.py <reference gpu-d1 folder> (or set DCSS_REFERENCE)')
     convert_fixture(ref)
     print('rays kept:', convert_rays(ref))

@@ -105,13 +105,18 @@ class Policy:
                                            seed, step, first_env, ptr(action), ptr(logp), ptr(value), ptr(logits),
                                            stream), 'd1_gemm_head_sample')
 
-    def act(self, obs, legal, seed, step, first_env=0, action=None, logp=None, value=None, logits=None, part=0):
+    def act(self, obs, legal, seed, step, first_env=0, action=None, logp=None, value=None, logits=None, part=0,
+            h1=None, h2=None):
         """Forward + sample: two tcgen05 GEMMs, then the head + sampler kernel.
         Writes into the given buffers (allocated if None). `part` selects the
-        activation buffers, so that parts of a batch can run on different
-        streams at the same time."""
+        policy's cached activation buffers, so that parts of a batch can run on
+        different streams at the same time; a caller that captures this call in
+        a CUDA graph passes its own h1/h2 ([n, hidden] bf16) instead, because the
+        cached buffers are reallocated when a later call needs more rows."""
         n = obs.shape[0]
-        _, h2 = self.hidden_layers(obs, h1=self._h1_buffer(n, part), h2=self._h2_buffer(n, part))
+        h1 = self._h1_buffer(n, part) if h1 is None else h1
+        h2 = self._h2_buffer(n, part) if h2 is None else h2
+        _, h2 = self.hidden_layers(obs, h1=h1, h2=h2)
         if action is None:
             action = torch.empty(n, dtype=torch.int64, device=self.device)
         if logp is None:

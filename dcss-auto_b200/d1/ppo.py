@@ -40,7 +40,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import check, library, launch_stream
+from ._lib import D1Error, check, library, launch_stream
 from . import gemm as G
 from .policy import HID, NOUT, OBS
 
@@ -61,8 +61,9 @@ class GradJob(C.Structure):
 class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
-                 gae_mode=1, splits=8, group=None, graph=True, peer=True, compact=True):
+                 gae_mode=1, splits=8, group=None, graph=True, peer=True, compact=True, peer_wait_limit=0):
         self.policy, self.rollout = policy, rollout
+        self.peer_wait_limit = peer_wait_limit  # polls per flag wait; 0 = the library default (~1 s)
         self.compact = compact
         self.mb, self.epochs = minibatch, epochs
         self.lr, self.clip, self.vclip, self.vf_coef, self.ent_coef = lr, clip, vclip, vf_coef, ent_coef
@@ -140,7 +141,7 @@ class PPO:
         flag_off = 2 * self.xstride * 4
         base, handle = C.c_void_p(), (C.c_char * lib.d1_peer_handle_bytes())()
         with torch.cuda.device(self.policy.device):
-            check(lib.d1_peer_alloc(flag_off + 8 * 8, C.byref(base), handle), 'd1_peer_alloc')
+            check(lib.d1_peer_alloc(self.peer_bytes(), C.byref(base), handle), 'd1_peer_alloc')
             handles = [None] * world
             dist.all_gather_object(handles, bytes(handle), group=group)
             ptrs = []
@@ -151,7 +152,21 @@ class PPO:
                     q = C.c_void_p()
                     check(lib.d1_peer_open(h, C.byref(q)), 'd1_peer_open')
                     ptrs.append(q.value)
-        self.peer = dict(world=world, rank=rank, base=base.value, ptrs=ptrs,
+        self.peer_attach(world, rank, ptrs)
+        self.peer['base'] = base.value
+
+    def peer_bytes(self):
+        """Size of one rank's exchange buffer: two halves of the flat gradient
+        and one u64 flag per rank (up to 8)."""
+        xstride = (self.grad.numel() + 3) // 4 * 4
+        return 2 * xstride * 4 + 8 * 8
+
+    def peer_attach(self, world, rank, ptrs):
+        """Use the exchange buffers ptrs[p] (rank p's, as mapped here) for the
+        gradient all-reduce of every minibatch."""
+        self.xstride = (self.grad.numel() + 3) // 4 * 4
+        flag_off = 2 * self.xstride * 4
+        self.peer = dict(world=world, rank=rank, base=None, ptrs=list(ptrs),
                          xbufs=(C.c_void_p * world)(*ptrs),
                          flags=(C.c_void_p * world)(*[q + flag_off for q in ptrs]))
 
@@ -211,7 +226,8 @@ class PPO:
             check(lib.d1_ppo_step_peer(jobs, njobs, p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(),
                                        self.v.data_ptr(), g.numel(), self.lr, self.betas[0], self.betas[1], self.eps,
                                        self.max_grad_norm, self.step_dev.data_ptr(), self.segs, len(self.segs),
-                                       pr['xbufs'], pr['flags'], self.xstride, pr['world'], pr['rank'], s),
+                                       pr['xbufs'], pr['flags'], self.xstride, pr['world'], pr['rank'],
+                                       self.peer_wait_limit, s),
                   'd1_ppo_step_peer')
             return self.terms
         if self.group is not None:
@@ -253,6 +269,15 @@ class PPO:
                         self._epoch()
                     torch.cuda.current_stream(dev).wait_stream(side)
                 self.graph.replay()
+        self.check_peer()
+
+    def check_peer(self):
+        """Raise if a gradient exchange since the last check gave up waiting for
+        a peer (that minibatch's step then changed no parameter on this rank, so
+        the ranks' parameters no longer agree). Synchronises the device."""
+        if self.peer is not None and self.lib.d1_peer_error():
+            raise D1Error('peer gradient exchange: a rank did not publish its gradient in time; '
+                          'this rank skipped the optimizer step and training cannot continue')
 
     def release(self):
         """Free the captured graph (before destroying a process group it uses)
@@ -263,11 +288,12 @@ class PPO:
             torch.cuda.synchronize(self.policy.device)
             dist.barrier(group=self.group)
             pr = self.peer
-            for p, q in enumerate(pr['ptrs']):
-                if p != pr['rank']:
-                    self.lib.d1_peer_close(C.c_void_p(q))
-            dist.barrier(group=self.group)
-            self.lib.d1_peer_free(C.c_void_p(pr['base']))
+            if pr['base'] is not None:
+                for p, q in enumerate(pr['ptrs']):
+                    if p != pr['rank']:
+                        self.lib.d1_peer_close(C.c_void_p(q))
+                dist.barrier(group=self.group)
+                self.lib.d1_peer_free(C.c_void_p(pr['base']))
             self.peer = None
 
     def iteration(self, generator=None):

@@ -131,6 +131,11 @@ class DecisionGraph:
         self.logp = torch.empty(n, device=dev)
         self.value = torch.empty(n, device=dev)
         self.step = torch.full((1,), step, dtype=torch.int64, device=dev)
+        # The graph's own activation buffers: the policy's cached ones are
+        # reallocated when a later eager call needs more rows, which would leave
+        # the captured pointers dangling.
+        self.h1 = torch.empty((n, policy.hidden), dtype=torch.bfloat16, device=dev)
+        self.h2 = torch.empty((n, policy.hidden), dtype=torch.bfloat16, device=dev)
         lib = library()
         self.ranges = env_ranges(n, parts)
         split = len(self.ranges) > 1
@@ -149,7 +154,8 @@ class DecisionGraph:
                     with torch.cuda.stream(copies[i]):
                         self.h_out[lo:hi].copy_(env.out[lo:hi], non_blocking=True)
                     policy.act(env.obs[lo:hi], env.legal[lo:hi], seed, self.step, first_env + lo,
-                               action=self.next[lo:hi], logp=self.logp[lo:hi], value=self.value[lo:hi], part=i)
+                               action=self.next[lo:hi], logp=self.logp[lo:hi], value=self.value[lo:hi],
+                               h1=self.h1[lo:hi], h2=self.h2[lo:hi])
                     self.h_next[lo:hi].copy_(self.next[lo:hi], non_blocking=True)
             for i in range(len(self.ranges)):
                 if split:

@@ -443,11 +443,14 @@ int d1_grad_reduce(const D1GradJob *jobs, int njobs, void *stream);
  * (2 * xstride floats, xstride >= total, a multiple of 4) and flag array
  * (world u64) as mapped in this process (d1_peer_open); world <= 8. The two
  * halves make a rank's next write safe: before it, every peer has flagged the
- * epoch in between, which it does only after reading. */
+ * epoch in between, which it does only after reading. Each wait polls a flag
+ * at most wait_limit times (0: 2^24 polls, about a second); a wait that runs
+ * out records d1_peer_error and the step then leaves param, m, v, the bf16
+ * copies and *step unchanged. */
 int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
                      float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
                      const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
-                     int world, int rank, void *stream);
+                     int world, int rank, unsigned wait_limit, void *stream);
 /* Exchange-buffer set-up through CUDA IPC (not on the hot path): allocate
  * `bytes` of zeroed device memory and its handle (d1_peer_handle_bytes()
  * bytes), map another process's buffer from its handle, unmap, free. */
@@ -456,8 +459,9 @@ int d1_peer_alloc(int64_t bytes, void **ptr, void *handle);
 int d1_peer_open(const void *handle, void **ptr);
 int d1_peer_close(void *ptr);
 int d1_peer_free(void *ptr);
-/* Nonzero when a peer all-reduce gave up waiting for a peer (that block's
- * range of the gradient kept its old values); reading clears it. */
+/* Nonzero when a peer all-reduce gave up waiting for a peer since the last
+ * call (that step changed no parameter); reading clears it. Synchronises the
+ * device. */
 int d1_peer_error(void);
 /* Gather x[i, 0..F) = obs[idx[i], 0..F) into rows of pitch ldx; with ones_col,
  * columns F..F+7 of every row are (1, 0, ..., 0), so that a weight-gradient

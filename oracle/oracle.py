@@ -13,6 +13,7 @@ The fixture tables are assembled the way gpu-d1/scripts/learn_env.py:15-40 and
 :66-75 assemble them.
 """
 import ctypes as C
+import os
 import pathlib
 import subprocess
 
@@ -21,6 +22,15 @@ import numpy as np
 HERE = pathlib.Path(__file__).resolve().parent
 REPO = HERE.parent
 DATA = REPO / 'dcss-auto_b200' / 'd1' / 'data'
+
+
+def reference_dir():
+    """The reference's gpu-d1 folder: $DCSS_REFERENCE/gpu-d1, where DCSS_REFERENCE
+    names the reference checkout (default: a folder `reference` beside this
+    repository). Only the build recipes and host-side tests read it; it may be
+    absent, and nothing on a GPU box needs it."""
+    root = os.environ.get('DCSS_REFERENCE')
+    return (pathlib.Path(root) if root else REPO.parent / 'reference') / 'gpu-d1'
 
 V1_OBS, V1_ACTIONS, V1_OUT, V1_COMPACT = 206, 9, 8, 33
 

@@ -83,7 +83,7 @@ def test_ppo_entry_points(lib):
     # peer exchange: 2..8 ranks, a rank inside the world, the stride holds the gradient
     step = lambda world, rank, stride: lib.d1_ppo_step_peer(ok_job, 1, FAKE, FAKE, FAKE, FAKE, 128, 1e-3, 0.9,
                                                             0.999, 1e-5, 0.5, FAKE, None, 0, ptrs, ptrs, stride,
-                                                            world, rank, None)
+                                                            world, rank, 0, None)
     assert step(9, 0, 128) == BAD and step(1, 0, 128) == BAD and step(2, 2, 128) == BAD
     assert step(2, 0, 126) == BAD
     assert lib.d1_peer_alloc(0, C.byref(C.c_void_p()), (C.c_char * 64)()) == BAD

@@ -12,7 +12,7 @@ import pytest
 import oracle
 
 sys.path.insert(0, str(pathlib.Path(__file__).resolve().parents[1] / 'dcss-auto_b200'))
-REF = pathlib.Path('/root/reference/gpu-d1')
+REF = oracle.reference_dir()
 
 
 def synthetic(seed, ncells=40):

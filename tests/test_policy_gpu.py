@@ -112,6 +112,12 @@ def test_decision_graph_replays_the_eager_loop(lib, n):
     eager, graphed = SpecEnv(n, seed=6), SpecEnv(n, seed=6)
     dg = DecisionGraph(graphed, pol, seed=9, step=0)
     assert len(dg.ranges) == (1 if n < 8192 else 2)
+    # An eager call on more rows regrows the policy's cached activation buffers;
+    # the freed blocks are then handed out again. The graph holds its own
+    # buffers, so its replays below are unaffected.
+    big = SpecEnv(2 * n, seed=1)
+    pol.act(big.obs, big.legal, 1, 0)
+    filler = torch.full((8 * n, pol.hidden), 3.0, dtype=torch.bfloat16, device='cuda')
     # DecisionGraph ran one warm-up decision with zero actions and step 0
     act = torch.zeros(n, dtype=torch.int64, device='cuda')
     eager.step(act)
