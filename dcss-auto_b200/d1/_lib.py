@@ -75,6 +75,14 @@ SIGNATURES = {
     'd1_eval_accumulate': [_P, _I, _I, _P, _P, _P, _I, _P],
     'd1_sample_uniform_legal': [_P, _I, _I, _U64, _U64, _I, _P, _P],
     'd1_frame_stack': [_P, _P, _I, _I, _I, _P, _I, _P, _P],
+    'd1_route_state_bytes': [], 'd1_route_obs_size': [], 'd1_route_action_size': [], 'd1_route_out_size': [],
+    'd1_route_config_bytes': [], 'd1_route_compact_size': [],
+    'd1_route_init': [_P, _I, _P, _P, _U64, _P, _P, _P, _P],
+    'd1_route_step': [_P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P],
+    'd1_route_heuristic': [_P, _I, _P, _P, _P, _P],
+    'd1_route_observe': [_P, _I, _P, _P, _P, _P, _P, _P],
+    'd1_route_compact': [_P, _I, _P, _P],
+    'd1_route_memory': [_P, _I, _P, _P, _P],
 }
 
 _LIB = None

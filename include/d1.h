@@ -49,6 +49,7 @@ typedef struct {
  * Same names, argument meaning and error behaviour as the reference exports.
  * ====================================================================== */
 
+#ifndef D1_ROUTE_LIBRARY  /* libd1_route.so exports learn_* with the route task (d1_route.h) */
 /* Bytes of one env's opaque state row (reference: gpu-d1/src/learn.cu:644). */
 int learn_state_bytes(void);
 /* 206 (learn.cu:645). */
@@ -80,6 +81,7 @@ int learn_heuristic(void *state, int n, const D1Config *c, const D1Tables *t, in
  * the host). Returns 0 when all pass, else the number of the failed check. Blocks
  * until the check kernel finishes. */
 int learn_semantic_test(const D1Config *c, const D1Tables *t);
+#endif
 
 /* Extras with no reference counterpart, used by the Python wrapper and tests. */
 /* Canonical compact view of each env (33 x i64: rng.state, rng.inc, episode, hp,
@@ -90,6 +92,80 @@ int learn_compact_state(const void *state, int n, int64_t *rows, void *stream);
  * (replaces the Python BFS of gpu-d1/scripts/learn_env.py:25-39).
  * floor u8[5600], cells i16[ncells] -> distance u16[ncells, 5600] (65535 = unreachable). */
 int learn_distance_table(const uint8_t *floor, const int16_t *cells, int ncells, uint16_t *distance, void *stream);
+
+
+/* ======================================================================
+ * Route-cue task ("route"): the reference's selected fast build of its
+ * headline PPO benchmark -- gpu-d1/src/learn.cu with LEARN_ENEMIES=40,
+ * MULTI_MAP, SLEEP_ON, EXPLORE_REWARD (2 milli per newly seen floor cell),
+ * MARK_WALLS, FRONTIER_RING_MEMORY_WALLS_OBS, KNOWN_FRONTIER,
+ * FRONTIER_ROUTE_CUE_OBS and FAST_FRONTIER (gpu-d1/scripts/
+ * run_ring_ablations.py:141-157; gpu-d1/PERFORMANCE.md:16). 9 actions, up to 40
+ * sleeping monsters, 421 float observations (learn.cu:66-74: 9x9 floor and
+ * monster-HP windows, 40 monster records, the player block, the 11x11
+ * remembered ring, the nearest-frontier pointer through remembered floor and
+ * an 8-way one-hot first step of the route to it), 9 mask and 8 outcome floats.
+ * The exports of libd1_route.so carry the reference's learn_* names with these
+ * semantics (the reference builds one learn.so per variant); libd1.so exports
+ * the same entry points as d1_route_*.
+ * ====================================================================== */
+
+/* Multi-map tables, byte-identical to learn.cu:130-139 with MULTI_MAP (the
+ * layout gpu-d1/scripts/learn_env_ring_multi.py:11-17 fills). Device pointers:
+ * floor u8[n_maps * 5600] (16-byte aligned), cells i16[n_maps * 5600] (map m's
+ * cells at m * 5600, -1 padded), index i16[n_maps * 5600], distance u16[sum of
+ * ncells * 5600] (map m's rows from distance_offsets[m]), map_ncells
+ * i32[n_maps], distance_offsets i32[n_maps]. map_filter: >= 0 plays that map
+ * only, -1 draws a map per episode, -2 gives env i map i % n_maps on the first
+ * episode (learn.cu:626-627). ncells is unused (the reference keeps it). */
+typedef struct {
+    const uint8_t *floor;
+    const int16_t *cells, *index;
+    const uint16_t *distance;
+    int ncells;
+    const int *map_ncells, *distance_offsets;
+    int n_maps, map_filter;
+} D1RouteTables;
+
+/* Row bytes (12,416), 421, 9, 8, sizeof(D1Config), and the compact view's
+ * width (171). Reference: learn.cu:644-648 of this build. */
+int d1_route_state_bytes(void);
+int d1_route_obs_size(void);
+int d1_route_action_size(void);
+int d1_route_out_size(void);
+int d1_route_config_bytes(void);
+int d1_route_compact_size(void);
+/* learn_init of this build (learn.cu:649-660): env i is seeded
+ * PCG(mix(seed + i), i + 1), placed and observed. obs f32[n, 421], mask
+ * f32[n, 9]; legal (optional) receives the mask as u16 bits. */
+int d1_route_init(void *state, int n, const D1Config *c, const D1RouteTables *t, uint64_t seed, float *obs,
+                  float *mask, uint16_t *legal, void *stream);
+/* learn_step / learn_step_active of this build (learn.cu:661-670): one
+ * decision per env (actions i64[n]: 0-7 move/attack, 8 wait), outcomes
+ * out f32[n, 8] = reward, done, clear, kills, hp, ticks, death, timeout, and
+ * auto-reset; limit is the decision deadline (1024 in the reference wrapper).
+ * active (optional, bool[n]) leaves inactive envs and their rows untouched. */
+int d1_route_step(void *state, int n, const D1Config *c, const D1RouteTables *t, const int64_t *actions, int limit,
+                  float *obs, float *mask, float *out, const bool *active, uint16_t *legal, void *stream);
+/* learn_heuristic of this build (learn.cu:599-621, 671-675). */
+int d1_route_heuristic(const void *state, int n, const D1Config *c, const D1RouteTables *t, int64_t *actions,
+                       void *stream);
+/* Extras with no reference counterpart. Observe rows as they are (the
+ * reference's observe(), learn.cu:328-498), e.g. rows built by hand. Row
+ * layout: u64 rng.state, rng.inc, episode; i32 hp, regen, blocks, player,
+ * ticks, killed, map_id, frontier_count at byte 24; i16 pos[40] at 64,
+ * energy[40] at 144, hp[40] at 224; u8 awake[40] at 304; the viewed plane
+ * u32[210] at 352 (row y = words 3y..3y+2, bit x % 32 of word x / 32); the
+ * frontier list i16[5600] at 1216. */
+int d1_route_observe(const void *state, int n, const D1Config *c, const D1RouteTables *t, float *obs, float *mask,
+                     uint16_t *legal, void *stream);
+/* Compact view, i64[n, 171]: rng.state, rng.inc, episode, hp, regen, blocks,
+ * player, ticks, killed, map_id, frontier_count, pos[40], energy[40], hp[40],
+ * awake[40] -- the reference State's fields apart from its three 5600-cell
+ * arrays, which d1_route_memory exports: viewed u32[n, 210] bit planes and the
+ * frontier list i16[n, 5600] (-1 past the count). Either output may be NULL. */
+int d1_route_compact(const void *state, int n, int64_t *rows, void *stream);
+int d1_route_memory(const void *state, int n, uint32_t *viewed, int16_t *frontier, void *stream);
 
 
 /* ======================================================================

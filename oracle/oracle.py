@@ -381,3 +381,173 @@ def sample_uniform_legal(legal, nact, seed, step, first_env=0):
     a = np.empty(legal.shape[0], np.int64)
     lib.oracle_sample_uniform_legal(legal.ctypes.data, nact, legal.shape[0], seed, step, first_env, a.ctypes.data)
     return a
+
+
+# ---------------------------------------------------------------------------
+# route-cue task: the reference's selected fast build of its headline PPO task
+# (gpu-d1/src/learn.cu with the flags of oracle/Makefile ROUTEFLAGS), driven
+# through its own host path (learn_step(..., gpu=0))
+# ---------------------------------------------------------------------------
+ROUTE_OBS, ROUTE_ACTIONS, ROUTE_OUT, ROUTE_ENEMIES, ROUTE_LIMIT = 421, 9, 8, 40, 1024
+# Compact view (int64 per env): rng.state, rng.inc, episode, hp, regen, blocks,
+# player, ticks, killed, map_id, frontier_count, then pos[40], energy[40],
+# hp[40], awake[40].
+ROUTE_COMPACT = 11 + 4 * ROUTE_ENEMIES
+
+
+class RouteTables(C.Structure):
+    """learn.cu:130-139 with MULTI_MAP (the layout learn_env_ring_multi.py:11-17 fills)."""
+    _fields_ = [(k, C.c_void_p) for k in ('floor', 'cells', 'index', 'distance')] + [
+        ('ncells', C.c_int), ('map_ncells', C.c_void_p), ('distance_offsets', C.c_void_p), ('n_maps', C.c_int),
+        ('map_filter', C.c_int)]
+
+
+def route_library():
+    path = HERE / '_ref' / 'learn_route.so'
+    if not path.exists():
+        return None
+    lib = C.CDLL(str(path))
+    p, i = C.c_void_p, C.c_int
+    lib.learn_init.argtypes = [p, i, p, p, C.c_uint64, p, p, p, i]
+    lib.learn_step.argtypes = [p, i, p, p, p, i, p, p, p, p, i]
+    lib.learn_step_active.argtypes = [p, i, p, p, p, i, p, p, p, p, p, i]
+    lib.learn_heuristic.argtypes = [p, i, p, p, p, p, i]
+    return lib
+
+
+def floor_from_bits(bits):
+    """u8 [5600] floor from a row-padded bit plane u32 [210] (3 words per row)."""
+    words = np.asarray(bits, np.uint32).reshape(70, 3)
+    x = np.arange(80)
+    return ((words[:, x // 32] >> (x % 32).astype(np.uint32)) & 1).astype(np.uint8).reshape(-1)
+
+
+def route_map(floor, cells=None):
+    """(floor u8[5600], cells i16[ncells], index i16[5600], distance u16[ncells, 5600])
+    for one map; cells default to every floor cell in index order."""
+    floor = np.ascontiguousarray(floor, np.uint8)
+    if cells is None:
+        cells = np.flatnonzero(floor).astype(np.int16)
+    cells = np.ascontiguousarray(cells, np.int16)
+    index = np.full(5600, -1, np.int16)
+    index[cells] = np.arange(len(cells))
+    distance = np.empty((len(cells), 5600), np.uint16)
+    assert library().oracle_distance_table(floor.ctypes.data, cells.ctypes.data, len(cells),
+                                           distance.ctypes.data) == 0
+    return floor, cells, index, distance
+
+
+def route_corpus(n_maps, spec_config_values, seed=0):
+    """A small corpus in the reference's multi-map layout: map 0 is the fixture
+    (its reachable cells, as learn_env.py:15-40 selects them), maps 1.. are the
+    floors of the spec generator's maps for env ids 0..n_maps-2 under `seed`
+    (the reference's 388-map native corpus is not available)."""
+    _, _, floor, cells, index, distance = fixture()
+    maps = [(floor, cells, index, distance)]
+    if n_maps > 1:
+        gen = OracleSpec(n_maps - 1, spec_config_values, seed=seed)
+        fl, _ = gen.planes()
+        maps += [route_map(floor_from_bits(fl[k])) for k in range(n_maps - 1)]
+    return maps
+
+
+def route_arrays(maps):
+    """Concatenated table arrays as learn_env_ring_multi.py:60-70 builds them:
+    floor u8[n*5600], cells i16[n*5600] (-1 padded per map), index i16[n*5600],
+    distance u16[sum(ncells)*5600], map_ncells i32[n], distance_offsets i32[n]."""
+    floors = np.concatenate([m[0] for m in maps]).astype(np.uint8)
+    cells = np.full((len(maps), 5600), -1, np.int16)
+    for k, m in enumerate(maps):
+        cells[k, :len(m[1])] = m[1]
+    index = np.concatenate([m[2] for m in maps]).astype(np.int16)
+    distance = np.concatenate([m[3].reshape(-1) for m in maps]).astype(np.uint16)
+    ncells = np.array([len(m[1]) for m in maps], np.int32)
+    offsets = np.concatenate(([0], np.cumsum(ncells[:-1]))).astype(np.int32)
+    return dict(floor=floors, cells=cells.reshape(-1), index=index, distance=distance, map_ncells=ncells,
+                distance_offsets=offsets)
+
+
+# Byte offsets in the reference's State for this build (learn.cu:106-129; World is
+# RNG 16 B, hp/regen/blocks/fixture, u64 episode and 13 u64 stats = 144 B).
+_RS = dict(rng=0, hp=16, regen=20, blocks=24, episode=32, player=144, ticks=148, killed=152, map_id=156, pos=160,
+           energy=240, occ=320, mhp=11520, awake=11600, seen=11680, viewed=17280, fcells=22880, fslot=34080,
+           fcount=45280)
+
+
+class ReferenceRoute:
+    """The reference's own route-cue build on the host (gpu=0) over a corpus."""
+
+    def __init__(self, batch, maps, enemies=ROUTE_ENEMIES, seed=0, map_filter=-1):
+        self.lib = route_library()
+        if self.lib is None:
+            raise FileNotFoundError('oracle/_ref/learn_route.so was not built')
+        self.batch, self.enemies, self.limit = batch, enemies, ROUTE_LIMIT
+        values = config_values(enemies)
+        self.config = (C.c_int * len(values))(*values)
+        self.arrays = route_arrays(maps)
+        a = self.arrays
+        self.tables = RouteTables(a['floor'].ctypes.data, a['cells'].ctypes.data, a['index'].ctypes.data,
+                                  a['distance'].ctypes.data, int(a['map_ncells'][0]), a['map_ncells'].ctypes.data,
+                                  a['distance_offsets'].ctypes.data, len(maps), map_filter)
+        assert self.lib.learn_state_bytes() == 45288
+        self.state = np.zeros((batch, self.lib.learn_state_bytes()), np.uint8)
+        self.obs = np.zeros((batch, ROUTE_OBS), np.float32)
+        self.mask = np.zeros((batch, ROUTE_ACTIONS), np.float32)
+        self.out = np.zeros((batch, ROUTE_OUT), np.float32)
+        self.actions = np.zeros(batch, np.int64)
+        self.reset(seed)
+
+    def reset(self, seed):
+        assert self.lib.learn_init(self.state.ctypes.data, self.batch, C.byref(self.config), C.byref(self.tables),
+                                   seed, self.obs.ctypes.data, self.mask.ctypes.data, None, 0) == 0
+        return self.obs
+
+    def step(self, actions, active=None, lo=0, hi=None):
+        """Steps envs [lo, hi) (all by default; slices let a thread pool split the batch)."""
+        hi = self.batch if hi is None else hi
+        actions = np.ascontiguousarray(actions, np.int64)
+        st, ob, mk, ou = (self.state[lo:hi], self.obs[lo:hi], self.mask[lo:hi], self.out[lo:hi])
+        if active is None:
+            self.lib.learn_step(st.ctypes.data, hi - lo, C.byref(self.config), C.byref(self.tables),
+                                actions[lo:hi].ctypes.data, self.limit, ob.ctypes.data, mk.ctypes.data,
+                                ou.ctypes.data, None, 0)
+        else:
+            act = np.ascontiguousarray(active, np.bool_)
+            self.lib.learn_step_active(st.ctypes.data, hi - lo, C.byref(self.config), C.byref(self.tables),
+                                       actions[lo:hi].ctypes.data, self.limit, ob.ctypes.data, mk.ctypes.data,
+                                       ou.ctypes.data, act[lo:hi].ctypes.data, None, 0)
+        return self.obs, self.out
+
+    def heuristic(self):
+        self.lib.learn_heuristic(self.state.ctypes.data, self.batch, C.byref(self.config), C.byref(self.tables),
+                                 self.actions.ctypes.data, None, 0)
+        return self.actions
+
+    def _field(self, name, dtype, count=1):
+        off = _RS[name]
+        size = np.dtype(dtype).itemsize * count
+        return self.state[:, off:off + size].copy().view(dtype).reshape(self.batch, count)
+
+    def compact(self):
+        """The compact view (ROUTE_COMPACT int64 per env) read from the reference's State bytes."""
+        rng = self._field('rng', np.uint64, 2).view(np.int64)
+        i32 = lambda k: self._field(k, np.int32).astype(np.int64)
+        head = [rng[:, :1], rng[:, 1:], self._field('episode', np.uint64).view(np.int64), i32('hp'), i32('regen'),
+                i32('blocks'), i32('player'), i32('ticks'), i32('killed'), i32('map_id'), i32('fcount')]
+        mon = [self._field(k, np.int16, ROUTE_ENEMIES).astype(np.int64) for k in ('pos', 'energy', 'mhp', 'awake')]
+        return np.concatenate(head + mon, axis=1)
+
+    def viewed_bits(self):
+        """The remembered-cell (viewed) plane as u32 [n, 210] row-padded bits."""
+        v = self._field('viewed', np.uint8, 5600).reshape(self.batch, 70, 80).astype(np.uint32)
+        out = np.zeros((self.batch, 70, 3), np.uint32)
+        for x in range(80):
+            out[:, :, x // 32] |= v[:, :, x] << np.uint32(x % 32)
+        return out.reshape(self.batch, 210)
+
+    def frontier(self):
+        """The frontier list, i16 [n, 5600] with entries past the count set to -1."""
+        cells = self._field('fcells', np.int16, 5600).copy()
+        count = self._field('fcount', np.int32)[:, 0]
+        cells[np.arange(5600)[None, :] >= count[:, None]] = -1
+        return cells
