@@ -33,6 +33,11 @@ ENVS, HORIZON = 65536, 128
 # + 3,664 B observation.
 ENV_BYTES_PER_DECISION = 969 + 3664
 POLICY_FLOPS_PER_DECISION = 2 * (1832 * 256 + 256 * 256 + 256 * 13)
+# Route-cue task (the reference's headline build): algorithmic bytes per decision
+# = 2 x (64 B header + 280 B monster table + 840 B remembered plane) state read and
+# written + 700 B bit-packed map + 8 B action + (421 + 9 + 8) x 4 B observation,
+# mask and outcome row. The frontier list (read as far as it is long) is extra.
+ROUTE_BYTES_PER_DECISION = 2 * (64 + 280 + 840) + 700 + 8 + (421 + 9 + 8) * 4
 
 
 _T0 = time.perf_counter()
@@ -63,6 +68,12 @@ def parse():
     ap.add_argument('--c4-envs', type=int, default=131072, help='envs per GPU of the config-4 line')
     ap.add_argument('--c4-horizon', type=int, default=10,
                     help='rollout steps per config-4 iteration (131,072 x 10 x 8 GPUs = 10.5M decisions)')
+    ap.add_argument('--no-ref-tasks', action='store_true',
+                    help="skip the reference-task lines (route-cue and v1 on the GPU beside the reference's own "
+                         'host build)')
+    ap.add_argument('--route-envs', type=int, default=65536, help='envs per GPU of the route-cue line')
+    ap.add_argument('--route-maps', type=int, default=16, help='maps in the route-cue corpus')
+    ap.add_argument('--ref-cpu-envs', type=int, default=8192, help="envs of the reference build's host sample")
     ap.add_argument('--kernels', action='store_true',
                     help='run every hot kernel twice at bench sizes for profiler captures, print nothing else')
     return ap.parse_args()
@@ -125,9 +136,10 @@ def peaks():
 
 
 # ---------------------------------------------------------------- CPU legs
-def cpu_rollout(n_envs, steps, threads):
+def cpu_rollout(n_envs, steps, threads, warmup=1):
     """The oracle's spec env (C, one slice per thread) + a CPU torch policy of the
-    same architecture. Returns decisions/s."""
+    same architecture: `warmup` untimed decisions, then `steps` timed ones.
+    Returns (decisions/s, seconds)."""
     import numpy as np
     import torch
     sys.path.insert(0, str(REPO / 'oracle'))
@@ -157,13 +169,145 @@ def cpu_rollout(n_envs, steps, threads):
             off += e.batch
         list(pool.map(lambda i: envs[i].step(actions[i]), range(len(envs))))
 
-    one_step(0)
+    for s in range(warmup):
+        one_step(s)
     t0 = time.perf_counter()
-    for s in range(steps):
-        one_step(s + 1)
+    for s in range(warmup, warmup + steps):
+        one_step(s)
     dt = time.perf_counter() - t0
     pool.shutdown()
     return n_envs * steps / dt, dt
+
+
+def legal_bits(mask):
+    import numpy as np
+    return ((np.asarray(mask) > 0) * (1 << np.arange(mask.shape[1]))).sum(1).astype(np.uint16)
+
+
+def reference_host_rate(env, warmup, steps, threads, seed=7):
+    """The reference's own learn.cu build (host path, learn_step(..., gpu=0)) over
+    contiguous env slices on `threads` host threads (ctypes drops the GIL), with
+    uniform legal actions from the oracle's sampler; warm-up steps, then `steps`
+    timed steps. Returns (decisions/s, seconds)."""
+    from concurrent.futures import ThreadPoolExecutor
+    sys.path.insert(0, str(REPO / 'oracle'))
+    import oracle
+    n = env.batch
+    per = (n + threads - 1) // threads
+    slices = [(lo, min(n, lo + per)) for lo in range(0, n, per)]
+    pool = ThreadPoolExecutor(len(slices))
+
+    def one(k):
+        a = oracle.sample_uniform_legal(legal_bits(env.mask), env.mask.shape[1], seed, k)
+        list(pool.map(lambda sl: env.step(a, lo=sl[0], hi=sl[1]), slices))
+
+    for k in range(warmup):
+        one(k)
+    t0 = time.perf_counter()
+    for k in range(warmup, warmup + steps):
+        one(k)
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    return n * steps / dt, dt
+
+
+def reference_tasks(args, dev, rank, world, stream):
+    """The reference's own tasks on the GPU beside the reference's own host build
+    of the same task on the host cores: the route-cue task (its headline PPO
+    build, gpu-d1/PERFORMANCE.md:16) on a generated corpus, and the default v1
+    task on the fixture map. A step = uniform legal actions (d1_sample_uniform_legal)
+    + the env step, device-timed like the main line."""
+    import torch
+    import torch.distributed as dist
+    from d1._lib import check, library
+    from d1.learn_env import Env
+    from d1.route_env import RouteEnv, generated_corpus
+    lib = library()
+    pk, pk_kind = peaks()
+    cores = len(os.sched_getaffinity(0))
+    out = {}
+    maps = generated_corpus(args.route_maps, seed=11, device=dev)
+    for name in ('route', 'v1'):
+        n = args.route_envs
+        if name == 'route':
+            env = RouteEnv(n, 40, seed=1, maps=maps, device=dev)
+            legal = env.legal
+        else:
+            env = Env(n, 8, seed=1, device=dev)
+            legal = torch.zeros(n, dtype=torch.int16, device=dev)
+        act = torch.zeros(n, dtype=torch.int64, device=dev)
+        pow2 = (2 ** torch.arange(9, device=dev)).to(torch.float32)
+
+        def step(k):
+            if name == 'v1':  # the v1 wrapper returns a float mask only
+                legal.copy_((env.mask @ pow2).to(torch.int16))
+            check(lib.d1_sample_uniform_legal(legal.data_ptr(), 9, n, 7, k, rank * n, act.data_ptr(),
+                                              stream.cuda_stream), 'd1_sample_uniform_legal')
+            env.step(act)
+
+        for k in range(args.warmup):
+            step(k)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(args.warmup, args.warmup + args.steps):
+            step(k)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        # the env kernel alone, on its launching stream
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(8)]
+        for a, b in kev:
+            a.record(stream)
+            env.step(act)
+            b.record(stream)
+        torch.cuda.synchronize()
+        kms = sum(a.elapsed_time(b) for a, b in kev) / len(kev)
+        line = {'decisions_per_s': n * world * args.steps / (t.item() / 1e3), 'unit': UNIT,
+                'ms_per_step': t.item() / args.steps, 'envs_per_gpu': n, 'window_steps': [args.warmup,
+                                                                                        args.warmup + args.steps],
+                'kernel': 'd1::route::step_kernel' if name == 'route' else 'd1::v1::step_kernel',
+                'kernel_ms': kms}
+        if name == 'route':
+            line['workload'] = ('route-cue task (reference flags of run_ring_ablations.py:141-157): 40 sleeping '
+                                f'monsters, {args.route_maps}-map corpus (fixture + generated), uniform legal actions')
+            ach = ROUTE_BYTES_PER_DECISION * n / (kms / 1e3) / 1e9
+            line['roofline'] = {'bound': 'hbm', 'achieved': ach, 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
+                                'frac': ach / pk['hbm_gbs'], 'peak_kind': pk_kind,
+                                'algorithmic_bytes_per_decision': ROUTE_BYTES_PER_DECISION}
+        else:
+            line['workload'] = 'v1 task (reference default build): fixture map, 8 monsters, uniform legal actions'
+        if rank == 0 and not args.no_cpu:
+            sys.path.insert(0, str(REPO / 'oracle'))
+            import oracle
+            lib_ok = oracle.route_library() if name == 'route' else oracle.reference_library()
+            if lib_ok is None:
+                line['cpu_reference'] = {'unavailable': 'oracle/_ref was not built with the reference sources'}
+            else:
+                m = args.ref_cpu_envs
+                if name == 'route':
+                    ref = oracle.ReferenceRoute(m, oracle.route_corpus(args.route_maps, _spec_default(), seed=11),
+                                                seed=1)
+                else:
+                    ref = oracle.ReferenceV1(m, 8, seed=1)
+                rate, dt = reference_host_rate(ref, args.warmup, args.steps, cores)
+                line['cpu_reference'] = {
+                    'value': rate, 'unit': UNIT, 'cores': cores, 'kind': 'reference',
+                    'sample': f'{m} envs x decisions {args.warmup}-{args.warmup + args.steps} ({dt:.1f} s), '
+                              "the reference's learn.cu host path (oracle/_ref)"}
+                line['gpu_over_cpu_reference'] = line['decisions_per_s'] / rate
+        out[name] = line
+        del env
+    return out
+
+
+def _spec_default():
+    from d1.spec_env import DEFAULT
+    return DEFAULT
 
 
 def run_reference(args, rank, world):
@@ -175,14 +319,15 @@ def run_reference(args, rank, world):
         return
     cores = len(os.sched_getaffinity(0))
     n = min(args.envs, 8192)
-    rate, dt = cpu_rollout(n, max(args.steps // 2, 16), cores)
+    rate, dt = cpu_rollout(n, args.steps, cores, warmup=args.warmup)
     line = {'impl': 'reference', 'metric': METRIC, 'value': rate, 'unit': UNIT, 'n_gpus': args.gpus,
             'steps': args.steps, 'warmup': args.warmup, 'higher_is_better': True, 'scaling': 'weak',
             'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
             'config': {'workload': 'config1 rollout: generated D:1 maps, MLP 1832-256-256-13, host CPU',
                        'envs_sampled': n},
             'cpu_baseline': {'value': rate, 'unit': UNIT, 'cores': cores, 'kind': 'port',
-                             'sample': f'{n} envs x {max(args.steps // 2, 16)} decisions ({dt:.1f} s)'},
+                             'sample': f'{n} envs x decisions {args.warmup}-{args.warmup + args.steps} '
+                                       f'({dt:.1f} s)'},
             'e2e': {'value': rate, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
     print(json.dumps(line), flush=True)
 
@@ -230,15 +375,38 @@ def run_ours(args, rank, world, local_rank):
     # ranges overlap the policy on other streams, so the kernel is timed alone
     # here, whole batch per launch, with events on its launching stream,
     # continuing the same episodes with the rollout's last actions.
-    n_env = min(16, args.steps)
-    ev_env = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_env)]
-    for i in range(n_env):
-        t_env = (args.warmup + args.steps + i) % T
-        ev_env[i][0].record(stream)
-        env.step(roll.actions[t_env])
-        ev_env[i][1].record(stream)
+    def env_kernel_ms(k0):
+        n_env = min(16, args.steps)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_env)]
+        for i in range(n_env):
+            ev[i][0].record(stream)
+            env.step(roll.actions[(k0 + i) % T])
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in ev) / n_env
+
+    env_ms = env_kernel_ms(args.warmup + args.steps)
+    # A later window of the same rollout (episodes under way, many envs past
+    # their first reset); the main window above is the driver's early one.
+    k = args.warmup + args.steps
+    k_late = max(k, 2 * T)
+    while k < k_late:
+        step(k)
+        k += 1
+    late_k = args.steps
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    env_ms = sum(a.elapsed_time(b) for a, b in ev_env) / n_env
+    l0.record(stream)
+    for j in range(late_k):
+        step(k + j)
+    roll.join()
+    l1.record(stream)
+    torch.cuda.synchronize()
+    tl = torch.tensor([l0.elapsed_time(l1)], device=dev)
+    if world > 1:
+        dist.all_reduce(tl, op=dist.ReduceOp.MAX)
+    late_line = {'value': B * world * late_k / (tl.item() / 1e3), 'unit': UNIT, 'window_steps': [k, k + late_k],
+                 'ms_per_step': tl.item() / late_k, 'env_kernel_ms': env_kernel_ms(k + late_k)}
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -428,6 +596,10 @@ def run_ours(args, rank, world, local_rank):
                    'gradient_exchange': exchange4, 'peer_error': int(peer_error4),
                    'finite': bool(torch.isfinite(pol4.flat).all().item())}
         del env4, pol4, roll4, tr4
+    ref_tasks = None
+    if not args.no_ref_tasks:
+        progress('reference tasks (route-cue, v1) beside the reference host build')
+        ref_tasks = reference_tasks(args, dev, rank, world, stream)
     if rank != 0:
         return
     pk, pk_kind = peaks()
@@ -439,6 +611,7 @@ def run_ours(args, rank, world, local_rank):
         'config': {'workload': 'config1 rollout: 65,536 envs/GPU on seeded generated 80x70 D:1 maps, '
                                'obs 1832 bf16, MLP 1832-256-256-13 (random N(0,1/fan_in)), masked sampling',
                    'envs_per_gpu': B, 'horizon': T, 'parallelism': f'dp{world} (env shards)',
+                   'window_steps': [args.warmup, args.warmup + args.steps],
                    'rollout_streams': roll.parts,
                    'l2': 'inputs larger than L2 (240 MB obs slot + 134 MB env state per step)'},
         'roofline': {'kernel': 'd1::spec::step_kernel', 'bound': 'hbm', 'achieved': achieved,
@@ -453,6 +626,8 @@ def run_ours(args, rank, world, local_rank):
                                  'bound': 'tensor', 'achieved': gemm_tflops, 'peak': pk['bf16_tflops'],
                                  'unit': 'TFLOP/s', 'frac': gemm_tflops / pk['bf16_tflops'],
                                  'ms_per_launch': gemm_ms, 'peak_kind': pk_kind + ' burst'},
+        'late_window': late_line,
+        'reference_tasks': ref_tasks,
         'ppo': ppo_line,
         'config3': conv_line,
         'config4': c4_line,
@@ -463,9 +638,10 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_cpu:
         progress('CPU baseline')
         cores = len(os.sched_getaffinity(0))
-        rate, dt = cpu_rollout(8192, 100, cores)
+        rate, dt = cpu_rollout(8192, args.steps, cores, warmup=args.warmup)
         line['cpu_baseline'] = {'value': rate, 'unit': UNIT, 'cores': cores, 'kind': 'port',
-                                'sample': f'8192 envs x 100 decisions of the same workload ({dt:.1f} s)'}
+                                'sample': f'8192 envs x decisions {args.warmup}-{args.warmup + args.steps} of the '
+                                          f'same workload ({dt:.1f} s)'}
     print(json.dumps(line), flush=True)
 
 

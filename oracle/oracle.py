@@ -184,12 +184,14 @@ class ReferenceV1(_Host):
         assert code == 0
         return self.obs
 
-    def step(self, actions, active=None):
+    def step(self, actions, active=None, lo=0, hi=None):
+        """Steps envs [lo, hi) (all by default; slices let a thread pool split the batch)."""
         actions = np.ascontiguousarray(actions, np.int64)
         if active is None:
-            self.lib.learn_step(self.state.ctypes.data, self.batch, C.byref(self.config), C.byref(self.tables),
-                                actions.ctypes.data, self.limit, self.obs.ctypes.data, self.mask.ctypes.data,
-                                self.out.ctypes.data, None, 0)
+            hi = self.batch if hi is None else hi
+            self.lib.learn_step(self.state[lo:hi].ctypes.data, hi - lo, C.byref(self.config), C.byref(self.tables),
+                                actions[lo:hi].ctypes.data, self.limit, self.obs[lo:hi].ctypes.data,
+                                self.mask[lo:hi].ctypes.data, self.out[lo:hi].ctypes.data, None, 0)
         else:
             act = np.ascontiguousarray(active, np.bool_)
             self.lib.learn_step_active(self.state.ctypes.data, self.batch, C.byref(self.config),

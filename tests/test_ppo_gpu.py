@@ -5,8 +5,10 @@
   segmented scan) within 1e-5 relative.
 * One minibatch: loss terms and the flat gradient against torch autograd of the
   same loss with the kernels' bf16 rounding points (activations and the two
-  hidden-layer gradients), tolerance 1e-3 relative on the loss and 2e-3
+  hidden-layer gradients), tolerance 1e-3 relative on the loss and 1e-3
   relative L2 per gradient segment; the optimizer step against torch.optim.Adam.
+* Config 2 sizes (minibatch 16,384 of a 65,536-env rollout): the same bounds on
+  eight optimizer steps in a row.
 """
 import numpy as np
 import pytest
@@ -140,7 +142,8 @@ def test_minibatch_loss_gradient_and_adam_match_torch(mods):
                      ('bh', (13,))]:
         n_el = int(np.prod(shape))
         got = tr.grad[off[k]:off[k] + n_el].view(shape)
-        assert rel(got, grads[k]) < 2e-3, (k, rel(got, grads[k]))
+        print('segment', k, 'relative L2 error', rel(got, grads[k]))
+        assert rel(got, grads[k]) < 1e-3, (k, rel(got, grads[k]))
     # optimizer step = torch.optim.Adam on the same gradient, after grad-norm clipping
     p = before.clone().requires_grad_(True)
     opt = torch.optim.Adam([p], lr=tr.lr, eps=tr.eps, betas=tr.betas)
@@ -224,3 +227,59 @@ def test_compact_update_equals_the_materialised_update(mods):
         assert torch.equal(pa.flat, pb.flat)
     from d1 import gemm
     assert gemm.gemm_error() == 0
+
+
+def test_config2_minibatches_match_torch_over_eight_steps(mods):
+    """BASELINE config 2 sizes: minibatches of 16,384 drawn from a 65,536-env
+    rollout, eight optimizer steps in a row. Every step: loss within 1e-3
+    relative and every gradient segment within 1e-3 relative L2 of torch
+    autograd at the kernels' bf16 rounding points (at the parameters the GPU
+    reached); the step itself equal to clip_grad_norm_(0.5) + torch.optim.Adam
+    fed the same gradient, carried over all eight steps. A torch model trained
+    on its own autograd gradients for the same eight steps stays within 1e-2
+    relative L2 of the GPU's total parameter change."""
+    policy, ppo, rollout, spec_env = mods
+    env = spec_env.SpecEnv(65536, seed=21)
+    pol = policy.Policy(seed=21)
+    roll = rollout.Rollout(env, pol, 8, seed=21)
+    roll.collect()
+    tr = ppo.PPO(pol, roll, minibatch=16384, epochs=1, graph=False)
+    tr.advantages()
+    start = pol.flat.clone()
+    p_adam = start.clone().requires_grad_(True)
+    opt = torch.optim.Adam([p_adam], lr=tr.lr, eps=tr.eps, betas=tr.betas)
+    p_own = start.clone().requires_grad_(True)
+    opt_own = torch.optim.Adam([p_own], lr=tr.lr, eps=tr.eps, betas=tr.betas)
+    g = torch.Generator(device='cuda').manual_seed(5)
+    perm = torch.randperm(tr.total, device='cuda', generator=g)
+    off, n = tr.off, tr.mb
+    shapes = [('w1', (256, 1832)), ('b1', (256,)), ('w2', (256, 256)), ('b2', (256,)), ('wh', (13, 256)),
+              ('bh', (13,))]
+    worst = {}
+    for k in range(8):
+        idx = perm[k * n:(k + 1) * n]
+        loss_ref, _, vf_ref, ent_ref, grads = reference_minibatch(pol, roll, tr, idx)
+        terms = tr.minibatch(idx).clone()
+        torch.cuda.synchronize()
+        loss = terms[0].item() / n + tr.vf_coef * terms[1].item() / n - tr.ent_coef * terms[2].item() / n
+        assert abs(loss - loss_ref) <= 1e-3 * max(1.0, abs(loss_ref)), (k, loss, loss_ref)
+        for name, shape in shapes:
+            got = tr.grad[off[name]:off[name] + int(np.prod(shape))].view(shape)
+            e = rel(got, grads[name])
+            worst[name] = max(worst.get(name, 0.0), e)
+            assert e < 1e-3, (k, name, e)
+        # the optimizer on the GPU's own gradient
+        gg = tr.grad.clone()
+        p_adam.grad = gg
+        torch.nn.utils.clip_grad_norm_([p_adam], tr.max_grad_norm)
+        opt.step()
+        assert torch.allclose(pol.flat, p_adam.detach(), rtol=1e-5, atol=1e-7), k
+        # a torch model on its own autograd gradients (same minibatches)
+        flat = torch.cat([grads[name].reshape(-1) for name, _ in
+                          sorted(shapes, key=lambda s: off[s[0]])])
+        p_own.grad = flat.clone()
+        torch.nn.utils.clip_grad_norm_([p_own], tr.max_grad_norm)
+        opt_own.step()
+    drift = rel(pol.flat - start, p_own.detach() - start)
+    print('worst gradient error per segment', worst, 'update drift vs autograd model', drift)
+    assert drift < 1e-2, drift
