@@ -1035,6 +1035,22 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     store(e, row);
 }
 
+// Observation of rows as they are (rows built or edited by hand): no step.
+__global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
+    observe_kernel(uint8_t *state, int n, D1SpecConfig c, __nv_bfloat16 *obs, uint8_t *cobs, uint16_t *legal) {
+    __shared__ Smem sms[WARPS];
+    const int w = threadIdx.x >> 5, env = blockIdx.x * WARPS + w;
+    if (env >= n) return;
+    Env e;
+    e.lane = threadIdx.x & 31;
+    e.rng.lane = e.lane;
+    e.sm = &sms[w];
+    uint8_t *row = state + (size_t)env * ROW;
+    e.dist = row + OFF_DIST;
+    load(e, row);
+    observe(e, c, obs ? obs + (size_t)env * OBS : nullptr, cobs ? cobs + (size_t)env * COBS : nullptr, legal + env);
+}
+
 // ------------------------------------------------------------------ conv-policy crop
 // Egocentric 63 x 63 crop under D4 element g, one u16 code per pixel (rows of
 // pitch 64, column 63 zero): bits 0-2 the observation's one-hot class, bit 3
@@ -1271,6 +1287,16 @@ int d1_spec_step_ex(void *state, int n, const D1SpecConfig *c, const int64_t *ac
 int d1_spec_step(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, uint16_t *legal,
                  float *out, const bool *active, void *stream) {
     return d1_spec_step_ex(state, n, c, actions, obs_bf16, nullptr, legal, out, active, stream);
+}
+
+int d1_spec_observe(void *state, int n, const D1SpecConfig *c, void *obs_bf16, void *cobs, uint16_t *legal,
+                    void *stream) {
+    if (int err = spec_check(n, c)) return err;
+    if (n == 0) return 0;
+    if (!state || !legal) return D1_ERR_BAD_ARGUMENT;
+    spec::observe_kernel<<<(n + spec::WARPS - 1) / spec::WARPS, spec::WARPS * 32, 0, (cudaStream_t)stream>>>(
+        (uint8_t *)state, n, *c, (__nv_bfloat16 *)obs_bf16, (uint8_t *)cobs, legal);
+    return (int)cudaGetLastError();
 }
 
 int d1_spec_compact(const void *state, int n, int64_t *rows, void *stream) {

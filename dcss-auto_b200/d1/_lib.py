@@ -28,6 +28,7 @@ SIGNATURES = {
     'd1_spec_step_ex': [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P],
     'd1_ppo_gather_cobs': [_P, _P, _I, _P, _I, _I, _P],
     'd1_spec_compact': [_P, _I, _P, _P],
+    'd1_spec_observe': [_P, _I, _P, _P, _P, _P, _P],
     'd1_spec_planes': [_P, _I, _P, _P, _P],
     'd1_policy_head_sample': [_P, _I, _I, _P, _P, _P, _U64, _U64, _I, _P, _P, _P, _P, _P],
     'd1_gemm': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],

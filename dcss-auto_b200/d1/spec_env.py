@@ -160,6 +160,16 @@ class SpecEnv:
               'd1_spec_step_ex')
         return obs, out
 
+    def observe(self, obs_out=None, legal_out=None, cobs_out=None):
+        """Observation and legal bits of the rows as they are (no step)."""
+        obs = self.obs if obs_out is None else obs_out
+        legal = self.legal if legal_out is None else legal_out
+        check(self.lib.d1_spec_observe(self.state.data_ptr(), self.batch, C.byref(self.config),
+                                       None if obs is None else obs.data_ptr(),
+                                       None if cobs_out is None else cobs_out.data_ptr(), legal.data_ptr(),
+                                       self.stream), 'd1_spec_observe')
+        return obs
+
     def legal_mask(self):
         """Legal actions as a float [n, 12] mask (the reference's mask layout)."""
         bits = self.legal.to(torch.int32) & 0xffff

@@ -220,6 +220,16 @@ int d1_spec_init_ex(void *state, int n, const D1SpecConfig *c, uint64_t seed, in
                     void *cobs, uint16_t *legal, void *stream);
 int d1_spec_step_ex(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, void *cobs,
                     uint16_t *legal, float *out, const bool *active, void *stream);
+/* Observation, compact row and legal bits of rows as they are, without a step
+ * (rows built or edited by hand, e.g. for rule tests). No reference counterpart
+ * (the reference's observe() is internal to its step). Row layout: u64 draws
+ * consumed; u32 env, seed lo, seed hi, episode; i32 hp, regen, blocks, player,
+ * ticks, killed, stairs, nmon, floor_seen at byte 24; u16 LOS window rows[15]
+ * at 64 (row dy+7, bit dx+7); i16 pos[16] at 128, energy[16] at 160, hp[16] at
+ * 192; u8 kind[16] at 224, awake[16] at 240; the floor plane u32[210] at 256
+ * and the remembered plane u32[210] at 1096 (row y = words 3y..3y+2). */
+int d1_spec_observe(void *state, int n, const D1SpecConfig *c, void *obs_bf16, void *cobs, uint16_t *legal,
+                    void *stream);
 /* Canonical compact view, 56 x i64 per env: Philox draw count, env id, episode,
  * hp, regen, blocks, player, turns, killed, stairs, monster count, floor seen,
  * then pos[11], energy[11], hp[11], kind*2+awake[11]. */

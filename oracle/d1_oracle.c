@@ -1144,6 +1144,12 @@ int oracle_spec_step(void *states, int n, const D1SpecConfig *c, const int64_t *
     return 0;
 }
 
+int oracle_spec_observe(const void *states, int n, const D1SpecConfig *c, float *obs, uint16_t *legal) {
+    const Spec *s = (const Spec *)states;
+    for (int i = 0; i < n; i++) spec_observe(&s[i], c, obs + (size_t)i * OSPEC_OBS, legal + i);
+    return 0;
+}
+
 int oracle_spec_compact(const void *states, int n, int64_t *rows) {
     const Spec *s = (const Spec *)states;
     for (int i = 0; i < n; i++) {

@@ -78,6 +78,8 @@ int oracle_spec_init(void *states, int n, const D1SpecConfig *c, uint64_t seed, 
                      uint16_t *legal);
 int oracle_spec_step(void *states, int n, const D1SpecConfig *c, const int64_t *actions, float *obs, uint16_t *legal,
                      float *out);
+/* Observation and legal bits of states as they are (no step). */
+int oracle_spec_observe(const void *states, int n, const D1SpecConfig *c, float *obs, uint16_t *legal);
 /* 56 x int64 per env: ctr, env, episode, hp, regen, blocks, player, ticks, killed,
  * stairs, nmon, floor_seen, then pos[11], energy[11], hp[11], kind*2+awake [11].
  */
