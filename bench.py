@@ -657,8 +657,14 @@ def run_kernels(args):
     grad_reduce_kernel, adam_update_kernel), layer 2
     (gemm_kernel), head_sample_kernel, step_kernel, gae_scan_kernel, and the
     config-3 policy on 16,384 envs (crop_kernel, conv_kernel<1..3>, FC
-    gemm_pair_kernel, head gemm_kernel, ar_kernel). A `gemm` regex therefore
-    sees 18 launches in the rollout and 9 per pass."""
+    gemm_pair_kernel, head gemm_kernel, ar_kernel), then GAE over a [128, B]
+    rollout of synthetic rewards and dones in the rollout's plane layout
+    (gae_scan_kernel) and one route-cue env step of B envs on a 16-map
+    corpus (d1::route::step_kernel, after 8 warm-up steps and their heuristic
+    launches). A `gemm` regex therefore sees 18 launches in the rollout and 9
+    per pass; `gae_scan` sees one before the passes (the setup's, T = 8) and
+    two per pass (T = 8, then T = 128); `route.*step` sees 8 before the passes
+    and one per pass."""
     import torch
     from d1 import gemm as G
     from d1.conv_policy import ConvPolicy
@@ -684,6 +690,19 @@ def run_kernels(args):
     env3 = SpecEnv(n3, seed=3, observe=False)
     cp = ConvPolicy(seed=0, chunk=n3)
     buf = cp.buffers(n3)
+    from d1._lib import check, library
+    from d1.route_env import RouteEnv, generated_corpus
+    lib = library()
+    g = torch.Generator(device='cuda').manual_seed(3)
+    gae_out = torch.zeros((128, 10, B), device='cuda')
+    gae_out[:, 0] = torch.randn((128, B), device='cuda', generator=g)
+    gae_out[:, 1] = (torch.rand((128, B), device='cuda', generator=g) < 0.01).float()
+    gae_val = torch.randn((129, B), device='cuda', generator=g)
+    gae_adv, gae_ret = torch.empty((128, B), device='cuda'), torch.empty((128, B), device='cuda')
+    gae_stats = torch.zeros(2, dtype=torch.float64, device='cuda')
+    renv = RouteEnv(B, 40, seed=1, maps=generated_corpus(16, seed=11))
+    for _ in range(8):
+        renv.step(renv.heuristic().clone())
     torch.cuda.synchronize()
     for rep in range(2):
         G.gemm(x, pol.bf16['w1'], bias=pol.params['b1'], relu=True, out=h1)
@@ -693,6 +712,10 @@ def run_kernels(args):
         env.step(act)
         tr.advantages()
         cp.act(env3.state, env3.legal, n3, buf, 1, rep)
+        check(lib.d1_gae(gae_out.data_ptr(), gae_out[:, 1].data_ptr(), gae_out.stride(0), 1, gae_val.data_ptr(),
+                         128, B, 0.999, 0.95, gae_adv.data_ptr(), gae_ret.data_ptr(), gae_stats.data_ptr(), 1,
+                         torch.cuda.current_stream().cuda_stream), 'd1_gae')
+        renv.step(renv.heuristic().clone())
         torch.cuda.synchronize()
 
 

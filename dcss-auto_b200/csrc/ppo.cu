@@ -128,38 +128,51 @@ __global__ void gae_sequential_kernel(GaeArgs a) {
 // w then scans envs w, w+8, ... Rounding differs from the sequential order
 // (tolerance 1e-5 relative).
 constexpr int SCAN_ENVS = 32, SCAN_WARPS = 8;
+// Shared-memory layout of one env's T steps: lane l's run of `per` steps sits
+// at l * (per + 1) (a pad word after every run), and envs are `stride` words
+// apart with stride odd, so the staging stores (32 envs, one step), the run
+// scans (32 lanes, one env) and the final reads are all free of bank conflicts.
+__device__ __forceinline__ int scan_per(int T) { return (T + 31) / 32; }
+__device__ __forceinline__ int scan_stride(int T) {
+    const int per = scan_per(T), s = T + (T + per - 1) / per;
+    return s | 1;
+}
 __global__ void __launch_bounds__(SCAN_WARPS * 32) gae_scan_kernel(GaeArgs a) {
     extern __shared__ float sh[];
-    float *sd = sh;                            // delta   [T][32]
-    float *sc = sd + a.T * SCAN_ENVS;          // c       [T][32]
-    float *sv = sc + a.T * SCAN_ENVS;          // value   [T][32]
+    const int per = scan_per(a.T), stride = scan_stride(a.T);
+    float *sd = sh;                                          // delta [32 envs][stride]
+    uint32_t *sl = reinterpret_cast<uint32_t *>(sd + SCAN_ENVS * stride);  // live bits [stride], bit = env
     const int e0 = blockIdx.x * SCAN_ENVS;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // stage: thread (t-row, env lane) loads reward/done/value and forms delta, c
+    // stage: thread (t-row, env lane) loads reward/done/value and forms delta;
+    // c = gamma * lambda * live is kept as one live bit per (env, step)
+    // (unrolled so that several rows' loads are in flight per thread)
+#pragma unroll 4
     for (int t = warp; t < a.T; t += SCAN_WARPS) {
         const int b = e0 + lane;
-        float d = 0.f, c = 0.f, v = 0.f;
+        float d = 0.f, live = 0.f;
         if (b < a.B) {
             const size_t o = (size_t)t * a.r_step + (size_t)b * a.r_env;
-            const float live = 1.f - a.done[o];
-            v = a.value[(size_t)t * a.B + b];
+            live = 1.f - a.done[o];
+            const float v = a.value[(size_t)t * a.B + b];
             const float nv = a.value[(size_t)(t + 1) * a.B + b];
             d = a.reward[o] + a.gamma * nv * live - v;
-            c = a.gamma_lambda * live;
         }
-        sd[t * SCAN_ENVS + lane] = d;
-        sc[t * SCAN_ENVS + lane] = c;
-        sv[t * SCAN_ENVS + lane] = v;
+        sd[lane * stride + t + t / per] = d;
+        const unsigned lb = __ballot_sync(FULL, live != 0.f);
+        if (lane == 0) sl[t + t / per] = lb;
     }
     __syncthreads();
-    const int per = (a.T + 31) / 32;  // consecutive steps per lane
+    const float gl = a.gamma_lambda;
     for (int env = warp; env < SCAN_ENVS; env += SCAN_WARPS) {
         // lane l owns steps [l*per, l*per + per); compose its run back to front
         const int t0 = lane * per, t1 = min(a.T, t0 + per);
+        float *ed = sd + env * stride + lane * (per + 1) - t0;  // ed[t] for t in the run
+        const uint32_t *el = sl + lane * (per + 1) - t0;
         float D = 0.f, Cc = 1.f;  // identity map
         for (int t = t1 - 1; t >= t0; t--) {
-            const float d = sd[t * SCAN_ENVS + env], c = sc[t * SCAN_ENVS + env];
-            D = d + c * D;
+            const float c = ((el[t] >> env) & 1u) ? gl : 0.f;
+            D = ed[t] + c * D;
             Cc = c * Cc;
         }
         // inclusive suffix scan: after it, (sD, sC) composes the runs of lanes [lane, 31]
@@ -176,18 +189,19 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32) gae_scan_kernel(GaeArgs a) {
         float A = __shfl_down_sync(FULL, sD, 1);
         if (lane == 31) A = 0.f;
         for (int t = t1 - 1; t >= t0; t--) {
-            A = sd[t * SCAN_ENVS + env] + sc[t * SCAN_ENVS + env] * A;
-            sd[t * SCAN_ENVS + env] = A;
+            A = ed[t] + (((el[t] >> env) & 1u) ? gl : 0.f) * A;
+            ed[t] = A;
         }
     }
     __syncthreads();
     double s1 = 0.0, s2 = 0.0;
+#pragma unroll 4
     for (int t = warp; t < a.T; t += SCAN_WARPS) {
         const int b = e0 + lane;
         if (b < a.B) {
-            const float A = sd[t * SCAN_ENVS + lane];
+            const float A = sd[lane * stride + t + t / per];
             a.adv[(size_t)t * a.B + b] = A;
-            a.ret[(size_t)t * a.B + b] = A + sv[t * SCAN_ENVS + lane];
+            a.ret[(size_t)t * a.B + b] = A + a.value[(size_t)t * a.B + b];  // the staging read, from L2
             s1 += A;
             s2 += (double)A * A;
         }
@@ -1365,7 +1379,8 @@ int d1_gae(const float *reward, const float *done, int64_t r_step, int64_t r_env
     if (mode == 0) {
         ppo::gae_sequential_kernel<<<(B + 255) / 256, 256, 0, (cudaStream_t)stream>>>(a);
     } else {
-        const size_t sm = (size_t)3 * T * ppo::SCAN_ENVS * sizeof(float);
+        const int per = (T + 31) / 32, stride = (T + (T + per - 1) / per) | 1;
+        const size_t sm = ((size_t)stride * ppo::SCAN_ENVS + stride) * sizeof(float);
         if (sm > 200 * 1024) return D1_ERR_BAD_ARGUMENT;
         // the kernel also holds a little static shared memory, so opt in to the
         // dynamic size whenever it is near the 48 KB default

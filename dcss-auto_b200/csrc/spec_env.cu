@@ -1017,7 +1017,8 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
 
 __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     step_kernel(uint8_t *state, int n, D1SpecConfig c, RayArgs ra, int extra_layers, const int64_t *actions,
-                __nv_bfloat16 *obs, uint8_t *cobs, uint16_t *legal, float *out, const bool *active) {
+                __nv_bfloat16 *obs, uint8_t *cobs, uint16_t *legal, float *out, int64_t out_env, int64_t out_col,
+                const bool *active) {
     __shared__ Smem sms[WARPS];
     const int w = threadIdx.x >> 5, env = blockIdx.x * WARPS + w;
     if (env >= n) return;
@@ -1030,7 +1031,7 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     e.dist = row + OFF_DIST;
     load(e, row);
     const float o = decision(e, c, ra, extra_layers, (int)actions[env]);
-    if (e.lane < OUT) out[(size_t)env * OUT + e.lane] = o;
+    if (e.lane < OUT) out[env * out_env + e.lane * out_col] = o;
     observe(e, c, obs ? obs + (size_t)env * OBS : nullptr, cobs ? cobs + (size_t)env * COBS : nullptr, legal + env);
     store(e, row);
 }
@@ -1274,14 +1275,21 @@ int d1_spec_crop(const void *state, int n, int g, uint16_t *crop, void *stream) 
     return (int)cudaGetLastError();
 }
 
-int d1_spec_step_ex(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, void *cobs,
-                    uint16_t *legal, float *out, const bool *active, void *stream) {
+int d1_spec_step_strided(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16,
+                         void *cobs, uint16_t *legal, float *out, int64_t out_env, int64_t out_col, const bool *active,
+                         void *stream) {
     if (int err = spec_check(n, c)) return err;
     if (n == 0) return 0;
+    if (out_env < 1 || out_col < 1) return D1_ERR_BAD_ARGUMENT;
     spec::step_kernel<<<(n + spec::WARPS - 1) / spec::WARPS, spec::WARPS * 32, 0, (cudaStream_t)stream>>>(
         (uint8_t *)state, n, *c, g_rays, spec_extra_layers(*c), actions, (__nv_bfloat16 *)obs_bf16, (uint8_t *)cobs,
-        legal, out, active);
+        legal, out, out_env, out_col, active);
     return (int)cudaGetLastError();
+}
+
+int d1_spec_step_ex(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, void *cobs,
+                    uint16_t *legal, float *out, const bool *active, void *stream) {
+    return d1_spec_step_strided(state, n, c, actions, obs_bf16, cobs, legal, out, spec::OUT, 1, active, stream);
 }
 
 int d1_spec_step(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, uint16_t *legal,

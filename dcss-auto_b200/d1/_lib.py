@@ -26,6 +26,7 @@ SIGNATURES = {
     'd1_spec_step': [_P, _I, _P, _P, _P, _P, _P, _P, _P],
     'd1_spec_init_ex': [_P, _I, _P, _U64, _I, _P, _P, _P, _P],
     'd1_spec_step_ex': [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P],
+    'd1_spec_step_strided': [_P, _I, _P, _P, _P, _P, _P, _P, C.c_int64, C.c_int64, _P, _P],
     'd1_ppo_gather_cobs': [_P, _P, _I, _P, _I, _I, _P],
     'd1_spec_compact': [_P, _I, _P, _P],
     'd1_spec_observe': [_P, _I, _P, _P, _P, _P, _P],

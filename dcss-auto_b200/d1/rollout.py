@@ -45,7 +45,10 @@ class Rollout:
         self.actions = torch.empty((horizon, B), dtype=torch.int64, device=dev)
         self.logp = torch.empty((horizon, B), device=dev)
         self.values = torch.empty((horizon + 1, B), device=dev)
-        self.out = torch.zeros((horizon, B, env.out.shape[1]), device=dev)
+        # outcomes stored as planes [T, 10, B] (GAE reads rewards and dones
+        # coalesced); self.out is the [T, B, 10] view of them
+        self.out_planes = torch.zeros((horizon, env.out.shape[1], B), device=dev)
+        self.out = self.out_planes.permute(0, 2, 1)
         self.global_step = 0
         self.ranges = env_ranges(B, parts)
         self.streams = [torch.cuda.Stream(dev) for _ in self.ranges] if len(self.ranges) > 1 else []

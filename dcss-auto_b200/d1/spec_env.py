@@ -153,11 +153,14 @@ class SpecEnv:
         obs = self.obs if obs_out is None else obs_out
         legal = self.legal if legal_out is None else legal_out
         out = self.out if out_out is None else out_out
-        check(self.lib.d1_spec_step_ex(self.state[lo:hi].data_ptr(), hi - lo, C.byref(self.config),
-                                       actions[lo:hi].data_ptr(), None if obs is None else obs[lo:hi].data_ptr(),
-                                       None if cobs_out is None else cobs_out[lo:hi].data_ptr(),
-                                       legal[lo:hi].data_ptr(), out[lo:hi].data_ptr(), act or None, self.stream),
-              'd1_spec_step_ex')
+        assert out.dim() == 2 and out.shape == (self.batch, OUT) and out.dtype == torch.float32
+        # any [B, 10] view: row-major, or a transposed view of a [10, B] plane stack
+        check(self.lib.d1_spec_step_strided(self.state[lo:hi].data_ptr(), hi - lo, C.byref(self.config),
+                                            actions[lo:hi].data_ptr(), None if obs is None else obs[lo:hi].data_ptr(),
+                                            None if cobs_out is None else cobs_out[lo:hi].data_ptr(),
+                                            legal[lo:hi].data_ptr(), out[lo:hi].data_ptr(), out.stride(0),
+                                            out.stride(1), act or None, self.stream),
+              'd1_spec_step_strided')
         return obs, out
 
     def observe(self, obs_out=None, legal_out=None, cobs_out=None):

@@ -220,6 +220,13 @@ int d1_spec_init_ex(void *state, int n, const D1SpecConfig *c, uint64_t seed, in
                     void *cobs, uint16_t *legal, void *stream);
 int d1_spec_step_ex(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, void *cobs,
                     uint16_t *legal, float *out, const bool *active, void *stream);
+/* d1_spec_step_ex with outcome value j of env i at out[i * out_env + j *
+ * out_col] (out_env, out_col >= 1): out_col = B, out_env = 1 stores the outcomes
+ * column by column ([10, B]), so that GAE reads rewards and dones as coalesced
+ * planes. No reference counterpart. */
+int d1_spec_step_strided(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16,
+                         void *cobs, uint16_t *legal, float *out, int64_t out_env, int64_t out_col, const bool *active,
+                         void *stream);
 /* Observation, compact row and legal bits of rows as they are, without a step
  * (rows built or edited by hand, e.g. for rule tests). No reference counterpart
  * (the reference's observe() is internal to its step). Row layout: u64 draws
