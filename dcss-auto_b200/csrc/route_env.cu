@@ -19,13 +19,14 @@
 //     (FAST_FRONTIER), keeping each cell's distance mod 3 in two bit planes --
 //     enough for the route walk-back, whose neighbours differ by at most one.
 //
-// State row (12,416 B per env):
+// State row (13,312 B per env):
 //   0    u64 rng.state   8 u64 rng.inc   16 u64 episode
 //   24   i32 hp, regen, blocks, player, ticks, killed, map_id, frontier_count
 //   56   unused
 //   64   i16 pos[40]   144 i16 energy[40]   224 i16 hp[40]   304 u8 awake[40]
 //   352  u32 viewed[210]  (row y = words 3y..3y+2, bit x%32 of word x/32)
-//   1216 i16 frontier[5600] (entries [0, frontier_count) in list order)
+//   1216 u32 floor[210]   (the episode map's floor, written at reset)
+//   2112 i16 frontier[5600] (entries [0, frontier_count) in list order)
 #include "d1_common.cuh"
 
 namespace d1 {
@@ -35,8 +36,9 @@ constexpr int ENEMIES = 40, OBS = 421, ACTIONS = 9, OUT = 8, COMPACT = 11 + 4 * 
 constexpr int BASE_OBS = 81 * 2 + ENEMIES * 5 + 4;  // 366 (learn.cu:48-49)
 constexpr int EXPLORE_MILLI = 2, DEATH_MILLI = 1000, CLEAR_MILLI = 3000;
 constexpr int PL = 210;
-constexpr int OFF_POS = 64, OFF_ENERGY = 144, OFF_HP = 224, OFF_AWAKE = 304, OFF_VIEWED = 352, OFF_LIST = 1216;
-constexpr int ROW = OFF_LIST + 2 * N;  // 12,416
+constexpr int OFF_POS = 64, OFF_ENERGY = 144, OFF_HP = 224, OFF_AWAKE = 304, OFF_VIEWED = 352, OFF_FLOOR = 1216,
+              OFF_LIST = 2112;
+constexpr int ROW = OFF_LIST + 2 * N;  // 13,312
 constexpr int WARPS = 4;
 
 struct Smem {
@@ -47,6 +49,10 @@ struct Smem {
         } bfs;
         float obs[4 * PL];        // the observation row, staged after the search
         uint32_t keys[11 * 12];   // reveal: sorted refresh keys per region row
+        struct {                  // monster phase, repair search
+            uint32_t inlist[PL];     // cells on its list
+            int16_t cell[24], first[24];  // the list and each entry's first step
+        } nb;
     } u;
     uint32_t nw[11 * 3];  // reveal: newly viewed bits of the region rows
 };
@@ -344,11 +350,11 @@ __device__ void reset(Env &e, const D1Config &c, const D1RouteTables &t, int map
 // rotation and reservoir ties, then the bounded 24-node repair search; the
 // eight neighbour tests run one per lane, the tie walk in rotated order.
 __device__ int choose_move(Env &e, const D1Config &c, const Smem &s, const uint16_t *dist, int p, int lane) {
-    int bd = dist[p], best = -1, ties = 0;
     const int rotation = rng_r(e.rng, 4);
     const int d = lane & 7;
     const int q = neighbor(p, d);
     const bool ok = q >= 0 && bit(s.floor, q) && q != e.player && !bit(s.occ, q);
+    int bd = dist[p], best = -1, ties = 0;
     const int dq = ok ? (int)dist[q] : 0;
     for (int z = 0; z < 8; z++) {
         const int dd = z < 4 ? (z + rotation) % 4 : 4 + (z + rotation) % 4;
@@ -364,29 +370,46 @@ __device__ int choose_move(Env &e, const D1Config &c, const Smem &s, const uint1
         }
     }
     if (best >= 0 || !c.repair) return best;
-    // repair list entry j lives on lane j (cell, first step), length <= 24
-    int cell = lane == 0 ? p : -1, first = -1, len = 1;
+    // Repair search (sim.h:225-252): FIFO over free floor from p, at most 24
+    // nodes on the list, returning the first step of the first cell met (list
+    // order, then compass order) that is closer to the player than p. A head's
+    // 8 neighbours are tested at once: the first closer one in compass order is
+    // the one the serial walk would meet first, and the others join the list in
+    // compass order while there is room. The list and its membership plane live
+    // in shared memory.
+    Smem &sw = const_cast<Smem &>(s);
+    uint32_t *inl = sw.u.nb.inlist;
+    int16_t *lc = sw.u.nb.cell, *lf = sw.u.nb.first;
+    for (int i = lane; i < PL; i += 32) inl[i] = 0u;
+    __syncwarp();
+    if (lane == 0) {
+        lc[0] = (int16_t)p;
+        lf[0] = -1;
+        bit_or(inl, p);
+    }
+    __syncwarp();
     const int dp = dist[p];
+    int len = 1;
     for (int head = 0; head < len; head++) {
-        const int ch = __shfl_sync(FULL, cell, head), fh = __shfl_sync(FULL, first, head);
+        const int ch = lc[head], fh = lf[head];
         const int qn = neighbor(ch, d);
-        const bool okn = qn >= 0 && bit(s.floor, qn) && qn != e.player && !bit(s.occ, qn);
-        const int dqn = okn ? (int)dist[qn] : 0;
-        for (int dd = 0; dd < 8; dd++) {
-            const int qz = __shfl_sync(FULL, qn, dd), dz = __shfl_sync(FULL, dqn, dd);
-            const bool okz = __shfl_sync(FULL, (int)okn, dd);
-            const bool seen = __ballot_sync(FULL, lane < len && cell == qz) != 0;
-            if (!okz || seen) continue;
-            const int step = head == 0 ? qz : fh;
-            if (dz < dp) return step;
-            if (len < 24) {
-                if (lane == len) {
-                    cell = qz;
-                    first = step;
-                }
-                len++;
-            }
+        const bool okn = lane < 8 && qn >= 0 && bit(s.floor, qn) && qn != e.player && !bit(s.occ, qn) && !bit(inl, qn);
+        const int dqn = okn ? (int)dist[qn] : 65535;
+        const unsigned closer = __ballot_sync(FULL, okn && dqn < dp);
+        if (closer) {
+            const int qz = __shfl_sync(FULL, qn, __ffs(closer) - 1);
+            return head == 0 ? qz : fh;
         }
+        const unsigned cand = __ballot_sync(FULL, okn);
+        const int rank = __popc(cand & ((1u << lane) - 1u));
+        __syncwarp();
+        if (okn && len + rank < 24) {
+            lc[len + rank] = (int16_t)qn;
+            lf[len + rank] = (int16_t)(head == 0 ? qn : fh);
+            bit_or(inl, qn);
+        }
+        len = imin(24, len + __popc(cand));
+        __syncwarp();
     }
     return -1;
 }
@@ -682,7 +705,9 @@ __device__ void observe(const Env &e, const D1Config &c, Smem &s, const int16_t 
 }
 
 // ------------------------------------------------------------------ rows
-__device__ void load(const uint8_t *row, Env &e, Smem &s, const D1RouteTables &t, int lane) {
+// from_row: take the floor plane from the row (rows the library wrote), else
+// pack it from the tables (rows built by hand).
+__device__ void load(const uint8_t *row, Env &e, Smem &s, const D1RouteTables &t, int lane, bool from_row) {
     const uint64_t *q = reinterpret_cast<const uint64_t *>(row);
     e.rng.state = q[0];
     e.rng.inc = q[1];
@@ -718,7 +743,13 @@ __device__ void load(const uint8_t *row, Env &e, Smem &s, const D1RouteTables &t
     }
     e.dirty_all = false;
     e.dirty_y0 = -100;
-    load_floor(s, t, e.map_id, lane);  // ends with __syncwarp
+    if (from_row) {
+        const uint32_t *f = reinterpret_cast<const uint32_t *>(row + OFF_FLOOR);
+        for (int i = lane; i < PL; i += 32) s.floor[i] = f[i];
+        __syncwarp();
+    } else {
+        load_floor(s, t, e.map_id, lane);  // ends with __syncwarp
+    }
     if (e.ha > 0) bit_or(s.occ, e.pa);
     if (e.hb > 0) bit_or(s.occ, e.pb);
     const int16_t *list = reinterpret_cast<const int16_t *>(row + OFF_LIST);
@@ -753,7 +784,11 @@ __device__ void store(uint8_t *row, const Env &e, const Smem &s, int lane) {
     }
     uint32_t *v = reinterpret_cast<uint32_t *>(row + OFF_VIEWED);
     if (e.dirty_all) {
-        for (int i = lane; i < PL; i += 32) v[i] = s.viewed[i];
+        uint32_t *f = reinterpret_cast<uint32_t *>(row + OFF_FLOOR);
+        for (int i = lane; i < PL; i += 32) {
+            v[i] = s.viewed[i];
+            f[i] = s.floor[i];
+        }
     } else if (e.dirty_y0 > -100) {
         const int y0 = imax(0, e.dirty_y0), y1 = imin(H - 1, e.dirty_y0 + 8);
         for (int i = y0 * 3 + lane; i < (y1 + 1) * 3; i += 32) v[i] = s.viewed[i];
@@ -795,7 +830,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     uint8_t *row = state + (size_t)env * ROW;
     int16_t *list = reinterpret_cast<int16_t *>(row + OFF_LIST);
     Env e;
-    load(row, e, s, t, lane);
+    load(row, e, s, t, lane, true);
     const float o = transition(e, c, t, s, list, (int)actions[env], limit, lane);
     if (lane < OUT) out[(size_t)env * OUT + lane] = o;
     observe(e, c, s, list, obs + (size_t)env * OBS, mask + (size_t)env * ACTIONS, legal ? legal + env : nullptr,
@@ -812,7 +847,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     Smem &s = sm[w];
     const uint8_t *row = state + (size_t)env * ROW;
     Env e;
-    load(row, e, s, t, lane);
+    load(row, e, s, t, lane, false);
     observe(e, c, s, reinterpret_cast<const int16_t *>(row + OFF_LIST), obs + (size_t)env * OBS,
             mask + (size_t)env * ACTIONS, legal ? legal + env : nullptr, lane);
 }

@@ -591,30 +591,48 @@ __device__ int choose_move(Env &e, int p, int D, int &dq_out) {
         dq_out = bdist;
         return best;
     }
-    int cell = lane == 0 ? p : -1, first = -1, len = 1;
+    // Repair search (sim.h:225-252): FIFO over free floor from p, at most 24
+    // nodes on the list, returning the first step of the first cell met (list
+    // order, then compass order) that is closer to the player than p. A head's
+    // 8 neighbours are tested at once: the first closer one in compass order is
+    // the one the serial walk would meet first, and the others join the list in
+    // compass order while there is room. The list membership plane reuses the
+    // search frontier plane and the list the compact-row staging (both idle
+    // during the monster phase).
+    uint32_t *inl = e.sm->cur;
+    int16_t *lc = reinterpret_cast<int16_t *>(e.sm->crow), *lf = lc + 24;
+    for (int r = lane; r < PL; r += 32) inl[r] = 0u;
+    __syncwarp();
+    if (lane == 0) {
+        lc[0] = (int16_t)p;
+        lf[0] = -1;
+        inl[(p / W) * 3 + (p % W) / 32] |= 1u << ((p % W) & 31);
+    }
+    __syncwarp();
+    int len = 1;
     for (int head = 0; head < len; head++) {
-        const int ch = __shfl_sync(FULL, cell, head), fh = __shfl_sync(FULL, first, head);
+        const int ch = lc[head], fh = lf[head];
         const int qn = neighbor(ch, d);
-        const bool okn = qn >= 0 && floor_at(e, qn) && qn != e.player && !bitp(e.sm->occ, qn);
+        const bool okn = lane < 8 && qn >= 0 && floor_at(e, qn) && qn != e.player && !bitp(e.sm->occ, qn) &&
+                         !bitp(inl, qn);
         const int dqn = okn ? dist_rel(e, qn, D) : 65535;
-        for (int dd = 0; dd < 8; dd++) {
-            const int qz = __shfl_sync(FULL, qn, dd), dz = __shfl_sync(FULL, dqn, dd);
-            const bool okz = __shfl_sync(FULL, (int)okn, dd);
-            const bool seen = __ballot_sync(FULL, lane < len && cell == qz) != 0;
-            if (!okz || seen) continue;
+        const unsigned closer = __ballot_sync(FULL, okn && dqn < D);
+        if (closer) {
+            const int qz = __shfl_sync(FULL, qn, __ffs(closer) - 1);
             const int step = head == 0 ? qz : fh;
-            if (dz < D) {
-                dq_out = dist_rel(e, step, D);
-                return step;
-            }
-            if (len < 24) {
-                if (lane == len) {
-                    cell = qz;
-                    first = step;
-                }
-                len++;
-            }
+            dq_out = dist_rel(e, step, D);
+            return step;
         }
+        const unsigned cand = __ballot_sync(FULL, okn);
+        const int rank = __popc(cand & ((1u << lane) - 1u));
+        __syncwarp();
+        if (okn && len + rank < 24) {
+            lc[len + rank] = (int16_t)qn;
+            lf[len + rank] = (int16_t)(head == 0 ? qn : fh);
+            atomicOr(&inl[(qn / W) * 3 + (qn % W) / 32], 1u << ((qn % W) & 31));
+        }
+        len = imin(24, len + __popc(cand));
+        __syncwarp();
     }
     return -1;
 }

@@ -127,7 +127,7 @@ typedef struct {
     int n_maps, map_filter;
 } D1RouteTables;
 
-/* Row bytes (12,416), 421, 9, 8, sizeof(D1Config), and the compact view's
+/* Row bytes (13,312), 421, 9, 8, sizeof(D1Config), and the compact view's
  * width (171). Reference: learn.cu:644-648 of this build. */
 int d1_route_state_bytes(void);
 int d1_route_obs_size(void);
@@ -156,7 +156,9 @@ int d1_route_heuristic(const void *state, int n, const D1Config *c, const D1Rout
  * ticks, killed, map_id, frontier_count at byte 24; i16 pos[40] at 64,
  * energy[40] at 144, hp[40] at 224; u8 awake[40] at 304; the viewed plane
  * u32[210] at 352 (row y = words 3y..3y+2, bit x % 32 of word x / 32); the
- * frontier list i16[5600] at 1216. */
+ * map's floor plane u32[210] at 1216 (ignored here: the tables' floor is
+ * used; the step reads the row's copy, written at reset); the frontier list
+ * i16[5600] at 2112. */
 int d1_route_observe(const void *state, int n, const D1Config *c, const D1RouteTables *t, float *obs, float *mask,
                      uint16_t *legal, void *stream);
 /* Compact view, i64[n, 171]: rng.state, rng.inc, episode, hp, regen, blocks,

@@ -4,7 +4,7 @@
  * per variant through library(path)) binds it unchanged. Same argument order
  * and meaning as gpu-d1/src/learn.cu:643-676 built with the route flags; the
  * tables argument is the MULTI_MAP struct (D1RouteTables). There is no host
- * path: gpu == 0 returns D1_ERR_NO_HOST_PATH. State rows are opaque, 12,416
+ * path: gpu == 0 returns D1_ERR_NO_HOST_PATH. State rows are opaque, 13,312
  * bytes (the reference's are 45,288). */
 #ifndef D1_ROUTE_H
 #define D1_ROUTE_H

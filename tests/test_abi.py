@@ -66,7 +66,7 @@ def test_route_library_exports_the_reference_names():
     for name in names:
         assert hasattr(route, name), name
     assert (route.learn_obs_size(), route.learn_action_size(), route.learn_out_size(),
-            route.learn_config_bytes(), route.learn_state_bytes()) == (421, 9, 8, 140, 12416)
+            route.learn_config_bytes(), route.learn_state_bytes()) == (421, 9, 8, 140, 13312)
     p, i = C.c_void_p, C.c_int
     route.learn_init.argtypes = [p, i, p, p, C.c_uint64, p, p, p, i]
     cfg = (C.c_int * 35)(*([40] + [0] * 34))
@@ -76,4 +76,4 @@ def test_route_library_exports_the_reference_names():
 def test_route_sizes(lib):
     assert (lib.d1_route_obs_size(), lib.d1_route_action_size(), lib.d1_route_out_size(),
             lib.d1_route_config_bytes(), lib.d1_route_state_bytes(), lib.d1_route_compact_size()) == (
-        421, 9, 8, 140, 12416, 171)
+        421, 9, 8, 140, 13312, 171)

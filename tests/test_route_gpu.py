@@ -140,7 +140,7 @@ def test_route_cue_known_answers():
         viewed[y * W + x] = True
 
     def row(targets):
-        r = np.zeros(12416, np.uint8)
+        r = np.zeros(13312, np.uint8)
         hdr = r[24:56].view(np.int32)
         hdr[:] = [20, 0, 0, player, 0, 0, 0, len(targets)]
         bits = np.zeros((70, 3), np.uint32)
@@ -148,7 +148,7 @@ def test_route_cue_known_answers():
         for x in range(80):
             bits[:, x // 32] |= vv[:, x].astype(np.uint32) << np.uint32(x % 32)
         r[352:352 + 840] = bits.reshape(-1).view(np.uint8)
-        r[1216:1216 + 2 * len(targets)] = np.asarray(targets, np.int16).view(np.uint8)
+        r[2112:2112 + 2 * len(targets)] = np.asarray(targets, np.int16).view(np.uint8)
         return r
 
     cfg_vals = [1, 0, 20] + [0] * 32
