@@ -71,6 +71,8 @@ def parse():
     ap.add_argument('--no-ref-tasks', action='store_true',
                     help="skip the reference-task lines (route-cue and v1 on the GPU beside the reference's own "
                          'host build)')
+    ap.add_argument('--no-ref-gpu', action='store_true',
+                    help="skip timing the reference's own learn.cu GPU build in the reference-task lines")
     ap.add_argument('--route-envs', type=int, default=65536, help='envs per GPU of the route-cue line')
     ap.add_argument('--route-maps', type=int, default=16, help='maps in the route-cue corpus')
     ap.add_argument('--ref-cpu-envs', type=int, default=8192, help="envs of the reference build's host sample")
@@ -281,6 +283,14 @@ def reference_tasks(args, dev, rank, world, stream):
                                 'algorithmic_bytes_per_decision': ROUTE_BYTES_PER_DECISION}
         else:
             line['workload'] = 'v1 task (reference default build): fixture map, 8 monsters, uniform legal actions'
+        if rank == 0 and not args.no_ref_gpu:
+            r = reference_gpu_rate(name, env, args, dev, stream, n)
+            if r is not None:
+                line['reference_gpu_build'] = {
+                    'value': r[0], 'unit': UNIT, 'ms_per_step': r[1],
+                    'what': "the reference's own learn.cu of this task compiled for sm_100a (oracle/_ref), "
+                            'its GPU path on this B200, same tables, envs and steps'}
+                line['over_reference_gpu_build'] = (n / (t.item() / args.steps / 1e3)) / r[0]
         if rank == 0 and not args.no_cpu:
             sys.path.insert(0, str(REPO / 'oracle'))
             import oracle
@@ -303,6 +313,63 @@ def reference_tasks(args, dev, rank, world, stream):
         out[name] = line
         del env
     return out
+
+
+def reference_gpu_rate(name, env, args, dev, stream, n):
+    """The reference's own learn.cu of the task, compiled for sm_100a from the
+    reference sources (oracle/_ref, the route build with its selected
+    LEARN_BLOCK_SIZE=4), run through its own GPU path (learn_step(..., gpu=1))
+    on this B200 with the same tables and uniform legal actions. Returns
+    (decisions/s, ms per step) or None when the build is absent."""
+    import ctypes as C
+    import torch
+    sys.path.insert(0, str(REPO / 'oracle'))
+    import oracle
+    from d1._lib import check, library
+    lib = oracle.route_library() if name == 'route' else oracle.reference_library()
+    if lib is None:
+        return None
+    if name == 'route':
+        a = env.arrays
+        tables = oracle.RouteTables(a[0].data_ptr(), a[1].data_ptr(), a[2].data_ptr(), a[3].data_ptr(),
+                                    env.tables.ncells, a[4].data_ptr(), a[5].data_ptr(), env.n_maps, -1)
+        nobs, limit = 421, 1024
+    else:
+        a = env.arrays
+        tables = oracle.Tables(a[0].data_ptr(), a[1].data_ptr(), a[2].data_ptr(), a[3].data_ptr(), a[1].shape[0])
+        nobs, limit = 206, 256
+    state = torch.zeros((n, lib.learn_state_bytes()), dtype=torch.uint8, device=dev)
+    obs = torch.empty((n, nobs), device=dev)
+    mask = torch.empty((n, 9), device=dev)
+    out = torch.empty((n, 8), device=dev)
+    act = torch.zeros(n, dtype=torch.int64, device=dev)
+    legal = torch.zeros(n, dtype=torch.int16, device=dev)
+    pow2 = (2 ** torch.arange(9, device=dev)).to(torch.float32)
+    s = stream.cuda_stream
+    code = lib.learn_init(state.data_ptr(), n, C.byref(env.config), C.byref(tables), 1, obs.data_ptr(),
+                          mask.data_ptr(), s, 1)
+    if code:
+        return None
+    ulib = library()
+
+    def step(k):
+        legal.copy_((mask @ pow2).to(torch.int16))
+        check(ulib.d1_sample_uniform_legal(legal.data_ptr(), 9, n, 7, k, 0, act.data_ptr(), s),
+              'd1_sample_uniform_legal')
+        lib.learn_step(state.data_ptr(), n, C.byref(env.config), C.byref(tables), act.data_ptr(), limit,
+                       obs.data_ptr(), mask.data_ptr(), out.data_ptr(), s, 1)
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(args.warmup, args.warmup + args.steps):
+        step(k)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    return n / (ms / 1e3), ms
 
 
 def _spec_default():
