@@ -17,11 +17,19 @@ namespace v1 {
 constexpr int ENEMIES = 8, OBS = 206, ACTIONS = 9, OUT = 8, ROW = 128, COMPACT = 33;
 constexpr int WARPS_PER_BLOCK = 8;
 
+// Per-warp shared scratch of the repair search: its list (cell, first step)
+// and a membership bit plane (row y = words 3y..3y+2).
+struct Scratch {
+    uint32_t inlist[PLANE];
+    int16_t cell[24], first[24];
+};
+
 struct State {
     Pcg rng;
     uint64_t episode;
     int hp, regen, blocks, player, ticks, killed;
     int m_pos, m_energy, m_hp;  // this lane's monster (lane < 8), hp 0 beyond count
+    Scratch *sc;
 };
 
 __device__ __forceinline__ D1Kind kind_of(const D1Config &c, int k) {
@@ -127,33 +135,49 @@ __device__ int choose_move(State &s, const D1Config &c, const D1Tables &t, const
             best = qz;
     }
     if (best >= 0 || !c.repair) return best;
-    // Repair search: list entry j lives on lane j (cells/first), length <= 24.
-    int cell = lane == 0 ? p : -1, first = -1, len = 1;
+    // Repair search (sim.h:225-252): FIFO over free floor from p, at most 24
+    // nodes on the list, returning the first step of the first cell met (list
+    // order, then compass order) that is closer to the player than p. A head's
+    // 8 neighbours are tested at once: the first closer one in compass order is
+    // the one the serial walk would meet first, and the others join the list in
+    // compass order while there is room.
+    uint32_t *inl = s.sc->inlist;
+    int16_t *lc = s.sc->cell, *lf = s.sc->first;
+    for (int r = lane; r < PLANE; r += 32) inl[r] = 0u;
+    __syncwarp();
+    if (lane == 0) {
+        lc[0] = (int16_t)p;
+        lf[0] = -1;
+        inl[(p / W) * ROWW + (p % W) / 32] = 1u << ((p % W) & 31);
+    }
+    __syncwarp();
     const int dp = dist[p];
+    int len = 1;
     for (int head = 0; head < len; head++) {
-        int ch = __shfl_sync(FULL, cell, head), fh = __shfl_sync(FULL, first, head);
-        int qn = neighbor(ch, d);
-        bool okn = qn >= 0 && t.floor[qn] && qn != s.player;
+        const int ch = lc[head], fh = lf[head];
+        const int qn = neighbor(ch, d);
+        bool okn = lane < 8 && qn >= 0 && t.floor[qn] && qn != s.player &&
+                   !((inl[(qn / W) * ROWW + (qn % W) / 32] >> ((qn % W) & 31)) & 1u);
         for (int k = 0; k < c.count; k++) {
-            int pk = __shfl_sync(FULL, s.m_pos, k), hk = __shfl_sync(FULL, s.m_hp, k);
+            const int pk = __shfl_sync(FULL, s.m_pos, k), hk = __shfl_sync(FULL, s.m_hp, k);
             if (hk > 0 && pk == qn) okn = false;
         }
-        int dqn = okn ? (int)dist[qn] : 0;
-        for (int dd = 0; dd < 8; dd++) {
-            int qz = __shfl_sync(FULL, qn, dd), dz = __shfl_sync(FULL, dqn, dd);
-            bool okz = __shfl_sync(FULL, (int)okn, dd);
-            bool seen = __ballot_sync(FULL, lane < len && cell == qz) != 0;
-            if (!okz || seen) continue;
-            int step = head == 0 ? qz : fh;
-            if (dz < dp) return step;
-            if (len < 24) {
-                if (lane == len) {
-                    cell = qz;
-                    first = step;
-                }
-                len++;
-            }
+        const int dqn = okn ? (int)dist[qn] : 65535;
+        const unsigned closer = __ballot_sync(FULL, okn && dqn < dp);
+        if (closer) {
+            const int qz = __shfl_sync(FULL, qn, __ffs(closer) - 1);
+            return head == 0 ? qz : fh;
         }
+        const unsigned cand = __ballot_sync(FULL, okn);
+        const int rank = __popc(cand & ((1u << lane) - 1u));
+        __syncwarp();
+        if (okn && len + rank < 24) {
+            lc[len + rank] = (int16_t)qn;
+            lf[len + rank] = (int16_t)(head == 0 ? qn : fh);
+            atomicOr(&inl[(qn / W) * ROWW + (qn % W) / 32], 1u << ((qn % W) & 31));
+        }
+        len = imin(24, len + __popc(cand));
+        __syncwarp();
     }
     return -1;
 }
@@ -354,8 +378,10 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32)
     const int env = blockIdx.x * WARPS_PER_BLOCK + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (env >= n) return;
     if (active && !active[env]) return;
+    __shared__ Scratch scr[WARPS_PER_BLOCK];
     uint8_t *row = state + (size_t)env * ROW;
     State s;
+    s.sc = &scr[threadIdx.x >> 5];
     load(row, lane, s);
     float o = transition(s, c, t, (int)actions[env], limit, lane);
     if (lane < OUT) out[(size_t)env * OUT + lane] = o;
@@ -389,8 +415,10 @@ __global__ void compact_kernel(const uint8_t *state, int n, int64_t *rows) {
 __device__ int g_semantic_status;
 __global__ void semantic_kernel(D1Config c, D1Tables t) {
     const int lane = threadIdx.x & 31;
+    __shared__ Scratch scr;
     c.count = 1;
     State s;
+    s.sc = &scr;
     s.rng.seed(123, 1);
     s.episode = 0;
     s.m_pos = 0;
