@@ -59,6 +59,8 @@ def parse():
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-ppo', action='store_true', help='skip the PPO-update measurement')
     ap.add_argument('--minibatch', type=int, default=16384)
+    ap.add_argument('--exchange', choices=('auto', 'oneshot', 'twophase'), default='auto',
+                    help='peer gradient exchange of the PPO update on several GPUs')
     ap.add_argument('--epochs', type=int, default=4)
     ap.add_argument('--no-cpu', action='store_true')
     ap.add_argument('--no-conv', action='store_true', help='skip the config-3 conv-policy rollout line')
@@ -536,7 +538,7 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_ppo:
         from d1.ppo import PPO
         group = dist.group.WORLD if world > 1 else None
-        trainer = PPO(policy, roll, minibatch=args.minibatch, epochs=args.epochs, group=group)
+        trainer = PPO(policy, roll, minibatch=args.minibatch, epochs=args.epochs, group=group, exchange=args.exchange)
         gen = torch.Generator(device=dev).manual_seed(1234 + rank)
         roll.roll()
         progress('PPO warm-up iteration')
@@ -556,7 +558,10 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         roll.roll()
         peer_error = trainer.lib.d1_peer_error() if trainer.peer is not None else 0
-        exchange = ('peer memory (NVLink)' if trainer.peer is not None else 'NCCL') if world > 1 else None
+        exchange = None
+        if world > 1:
+            exchange = 'NCCL' if trainer.peer is None else (
+                'peer memory (NVLink), two-phase' if trainer.peer['two_phase'] else 'peer memory (NVLink), one-shot')
         trainer.release()  # graph and exchange buffers go before the process group does
         it_ms = torch.tensor([p0.elapsed_time(p3)], device=dev)
         if world > 1:
@@ -632,7 +637,7 @@ def run_ours(args, rank, world, local_rank):
         pol4 = Policy(device=dev, seed=0)
         roll4 = Rollout(env4, pol4, t4, seed=4)
         tr4 = PPO(pol4, roll4, minibatch=args.minibatch, epochs=args.epochs,
-                  group=dist.group.WORLD if world > 1 else None)
+                  group=dist.group.WORLD if world > 1 else None, exchange=args.exchange)
         gen4 = torch.Generator(device=dev).manual_seed(4321 + rank)
         tr4.iteration(gen4)  # warm-up iteration (also captures the update graph)
         if world > 1:
@@ -648,7 +653,10 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         roll4.roll()
         peer_error4 = tr4.lib.d1_peer_error() if tr4.peer is not None else 0
-        exchange4 = ('peer memory (NVLink)' if tr4.peer is not None else 'NCCL') if world > 1 else None
+        exchange4 = None
+        if world > 1:
+            exchange4 = 'NCCL' if tr4.peer is None else (
+                'peer memory (NVLink), two-phase' if tr4.peer['two_phase'] else 'peer memory (NVLink), one-shot')
         tr4.release()
         t_it = torch.tensor([q0.elapsed_time(q2), q0.elapsed_time(q1)], device=dev)
         if world > 1:

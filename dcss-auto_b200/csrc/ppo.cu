@@ -844,6 +844,11 @@ struct StepArgs {
     const int64_t *epoch_src;  // epoch = *epoch_src + 1 (the optimizer's step count)
     unsigned long long *peer_flags[PEER_MAX];
     int world, rank;
+    // two-phase exchange: element e of the flat gradient goes to slot
+    // [half][rank][e - j * slice] of rank j = e / slice's inbox (a peer store)
+    float *inbox[PEER_MAX];
+    int64_t slice;
+    int two_phase;
 };
 __device__ double g_step_part[STEP_MAX_BLOCKS];
 __device__ unsigned g_step_ticket, g_peer_ticket;
@@ -857,9 +862,16 @@ struct Remap {
     const float *from;
     float *to;
     int64_t len;
+    // two-phase: the owners' inboxes, the slice length, this rank's slot offset
+    float *const *inbox;
+    int64_t slice, slot;
 };
 __device__ __forceinline__ float *remap(const Remap &m, float *p) {
-    return (m.to && p >= m.from && p < m.from + m.len) ? m.to + (p - m.from) : p;
+    if (!(m.to && p >= m.from && p < m.from + m.len)) return p;
+    const int64_t off = p - m.from;
+    if (!m.inbox) return m.to + off;
+    const int64_t j = off / m.slice;
+    return m.inbox[j] + m.slot + (off - j * m.slice);
 }
 // Sum of partials p = first, first + step, ... of the chunk's elements (vec of
 // them per lane); returns the lane's first element index.
@@ -914,7 +926,9 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
     __shared__ double ws[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint64_t epoch = a.xbuf ? (uint64_t)(*a.epoch_src + 1) : 0;
-    const Remap rm{a.remap_from, a.xbuf ? a.xbuf + (epoch & 1) * a.xstride : nullptr, a.remap_len};
+    const Remap rm{a.remap_from, a.xbuf ? a.xbuf + (epoch & 1) * a.xstride : nullptr, a.remap_len,
+                   a.two_phase ? a.inbox : nullptr, a.slice,
+                   ((int64_t)(epoch & 1) * a.world + a.rank) * a.slice};
     if (a.xbuf && blockIdx.x == 0 && threadIdx.x == 0) g_peer_abort = 0;
     double sq = 0.0;
     if (a.njobs > 0) {
@@ -1054,6 +1068,128 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_consta
                     a.grad[4 * q + k] = f[k];
                     sq += (double)f[k] * f[k];
                 }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(FULL, sq, o);
+    if (lane == 0) ws[warp] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < 8; w++) t += ws[w];
+        g_step_part[blockIdx.x] = t;
+    }
+}
+
+// Two-phase exchange, for more ranks: each rank owns a slice of the flat
+// gradient. The reduction launch stores every rank's part of slice j straight
+// into rank j's inbox (peer stores) and flags it; then each rank sums its own
+// slice's inbox in rank order, divides by the world size and stores the result
+// into every rank's gather area (peer stores) and flags that; then each rank
+// copies the gathered slices into its flat gradient. Each rank moves 2 (world -
+// 1) / world of the gradient over NVLink instead of reading (world - 1) copies.
+// Buffer of rank p: inbox [2 halves][world][slice] floats, then gather
+// [2][world][slice]; flags: u64 [8] for the first phase, [8] for the second.
+struct Peer2Args {
+    float *xbuf[PEER_MAX];                 // each rank's buffer (this rank's is local)
+    unsigned long long *xflags[PEER_MAX];  // each rank's flag area
+    const int64_t *epoch_src;
+    float *grad;
+    int64_t total, slice;
+    int world, rank;
+    uint32_t wait_limit;
+};
+__device__ unsigned g_peer2_ticket;
+// Bounded wait by thread 0 for flag[p] >= epoch of every other rank; on a
+// timeout records the error and this step's abort. Returns 1 when all arrived.
+__device__ __forceinline__ int wait_peers(const unsigned long long *flag, int world, int rank, uint64_t epoch,
+                                          uint32_t limit) {
+    int good = 1;
+    for (int p = 0; p < world && good; p++) {
+        if (p == rank) continue;
+        for (uint32_t it = 0;; it++) {
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag + p) : "memory");
+            if (v >= epoch) break;
+            if (it >= limit) {
+                good = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (!good) {
+        atomicExch(&g_peer_error, 1);
+        atomicExch(&g_peer_abort, 1);
+    }
+    return good;
+}
+// Every block counts itself in; the last one to finish raises flag[index] =
+// epoch in every other rank's flag area (system-scope release after a system
+// fence), unless a block of this step gave up waiting.
+__device__ __forceinline__ void publish(unsigned long long *const *xflags, int index, int world, int rank,
+                                        uint64_t epoch) {
+    __shared__ unsigned last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(&g_peer2_ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        g_peer2_ticket = 0;
+        __threadfence_system();
+        if (!*(volatile int *)&g_peer_abort)
+            for (int p = 0; p < world; p++)
+                if (p != rank)
+                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(xflags[p] + index), "l"(epoch)
+                                 : "memory");
+    }
+}
+__global__ void __launch_bounds__(256) peer_reduce2_kernel(const __grid_constant__ Peer2Args a) {
+    __shared__ int ok;
+    const uint64_t epoch = (uint64_t)(*a.epoch_src + 1);
+    const int64_t half = (int64_t)(epoch & 1);
+    if (threadIdx.x == 0) ok = wait_peers(a.xflags[a.rank], a.world, a.rank, epoch, a.wait_limit);
+    __syncthreads();
+    // after a timeout nothing is published, so the peers' gathers run out too
+    const float *inbox = a.xbuf[a.rank] + half * a.world * a.slice;
+    const int64_t gather_slot = (2 + half) * a.world * a.slice + (int64_t)a.rank * a.slice;
+    const int64_t n4 = a.slice / 4;
+    const float inv = (float)a.world;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; ok && q < n4;
+         q += (int64_t)gridDim.x * blockDim.x) {
+        float4 t = __ldcv(reinterpret_cast<const float4 *>(inbox) + q);
+        for (int r = 1; r < a.world; r++) {
+            const float4 v = __ldcv(reinterpret_cast<const float4 *>(inbox + (int64_t)r * a.slice) + q);
+            t.x += v.x;
+            t.y += v.y;
+            t.z += v.z;
+            t.w += v.w;
+        }
+        const float4 f = make_float4(__fdiv_rn(t.x, inv), __fdiv_rn(t.y, inv), __fdiv_rn(t.z, inv),
+                                     __fdiv_rn(t.w, inv));
+        for (int j = 0; j < a.world; j++) reinterpret_cast<float4 *>(a.xbuf[j] + gather_slot)[q] = f;
+    }
+    publish(a.xflags, 8 + a.rank, a.world, a.rank, epoch);
+}
+__global__ void __launch_bounds__(256) peer_gather2_kernel(const __grid_constant__ Peer2Args a) {
+    __shared__ int ok;
+    __shared__ double ws[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t epoch = (uint64_t)(*a.epoch_src + 1);
+    const int64_t half = (int64_t)(epoch & 1);
+    if (threadIdx.x == 0) ok = wait_peers(a.xflags[a.rank] + 8, a.world, a.rank, epoch, a.wait_limit);
+    __syncthreads();
+    double sq = 0.0;
+    if (ok) {
+        const float *gather = a.xbuf[a.rank] + (2 + half) * a.world * a.slice;
+        const int64_t per = (a.total + gridDim.x - 1) / gridDim.x;
+        const int64_t e0 = (int64_t)blockIdx.x * per, e1 = e0 + per < a.total ? e0 + per : a.total;
+        for (int64_t e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+            const int64_t j = e / a.slice;
+            const float g = __ldcv(gather + j * a.slice + (e - j * a.slice));
+            a.grad[e] = g;
+            sq += (double)g * g;
         }
     }
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(FULL, sq, o);
@@ -1215,8 +1351,9 @@ int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, v
 struct PeerSetup {
     void *const *xbufs;
     void *const *flags;
-    int64_t xstride;
+    int64_t xstride;  // one-shot: half length; two-phase: slice length
     int world, rank;
+    int two_phase;
 };
 
 static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
@@ -1226,8 +1363,8 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     using namespace ppo;
     if (njobs < 0 || njobs > STEP_MAX_JOBS || (njobs > 0 && !jobs) || (!do_adam && njobs == 0)) return D1_ERR_BAD_ARGUMENT;
     if (peer && (njobs == 0 || !do_adam || peer->world < 2 || peer->world > PEER_MAX || peer->rank < 0 ||
-                 peer->rank >= peer->world || !peer->xbufs || !peer->flags || peer->xstride < total ||
-                 peer->xstride % 4 || !step))
+                 peer->rank >= peer->world || !peer->xbufs || !peer->flags || peer->xstride % 4 || !step ||
+                 (peer->two_phase ? peer->xstride * peer->world < total : peer->xstride < total)))
         return D1_ERR_BAD_ARGUMENT;
     StepArgs a;
     memset(&a, 0, sizeof(a));
@@ -1255,6 +1392,8 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     a.norm = do_adam && !peer;
     PeerArgs pa;
     memset(&pa, 0, sizeof(pa));
+    Peer2Args p2;
+    memset(&p2, 0, sizeof(p2));
     if (peer) {
         a.remap_from = grad;
         a.remap_len = total;
@@ -1277,6 +1416,22 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
         pa.world = peer->world;
         pa.rank = peer->rank;
         pa.wait_limit = wait_limit ? wait_limit : PEER_WAIT_LIMIT;
+        if (peer->two_phase) {
+            a.two_phase = 1;
+            a.slice = peer->xstride;
+            for (int i = 0; i < peer->world; i++) {
+                a.inbox[i] = (float *)peer->xbufs[i];
+                p2.xbuf[i] = (float *)peer->xbufs[i];
+                p2.xflags[i] = (unsigned long long *)peer->flags[i];
+            }
+            p2.epoch_src = step;
+            p2.grad = grad;
+            p2.total = total;
+            p2.slice = peer->xstride;
+            p2.world = peer->world;
+            p2.rank = peer->rank;
+            p2.wait_limit = pa.wait_limit;
+        }
     }
     AdamArgs d;
     if (do_adam) {
@@ -1307,7 +1462,12 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     int blocks = sms * STEP_BLOCKS_PER_SM;
     if (blocks > STEP_MAX_BLOCKS) blocks = STEP_MAX_BLOCKS;
     grad_reduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
-    if (peer) peer_allreduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(pa);
+    if (peer && peer->two_phase) {
+        peer_reduce2_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(p2);
+        peer_gather2_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(p2);
+    } else if (peer) {
+        peer_allreduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(pa);
+    }
     if (do_adam) adam_update_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d, blocks, step, peer ? 1 : 0);
     return (int)cudaGetLastError();
 }
@@ -1323,7 +1483,16 @@ int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad
                      float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
                      const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
                      int world, int rank, unsigned wait_limit, void *stream) {
-    const PeerSetup peer{xbufs, flags, xstride, world, rank};
+    const PeerSetup peer{xbufs, flags, xstride, world, rank, 0};
+    return step_launch(jobs, njobs, param, grad, m, v, total, lr, beta1, beta2, eps, max_norm, step, segs, nseg, 1,
+                       stream, &peer, wait_limit);
+}
+
+int d1_ppo_step_peer2(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                      float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
+                      const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t slice,
+                      int world, int rank, unsigned wait_limit, void *stream) {
+    const PeerSetup peer{xbufs, flags, slice, world, rank, 1};
     return step_launch(jobs, njobs, param, grad, m, v, total, lr, beta1, beta2, eps, max_norm, step, segs, nseg, 1,
                        stream, &peer, wait_limit);
 }

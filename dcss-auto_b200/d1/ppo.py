@@ -61,9 +61,13 @@ class GradJob(C.Structure):
 class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
-                 gae_mode=1, splits=8, group=None, graph=True, peer=True, compact=True, peer_wait_limit=0):
+                 gae_mode=1, splits=8, group=None, graph=True, peer=True, compact=True, peer_wait_limit=0,
+                 exchange='auto'):
         self.policy, self.rollout = policy, rollout
         self.peer_wait_limit = peer_wait_limit  # polls per flag wait; 0 = the library default (~1 s)
+        if exchange not in ('auto', 'oneshot', 'twophase'):
+            raise ValueError("exchange must be 'auto', 'oneshot' or 'twophase'")
+        self.exchange = exchange
         self.compact = compact
         self.mb, self.epochs = minibatch, epochs
         self.lr, self.clip, self.vclip, self.vf_coef, self.ent_coef = lr, clip, vclip, vf_coef, ent_coef
@@ -141,7 +145,7 @@ class PPO:
         flag_off = 2 * self.xstride * 4
         base, handle = C.c_void_p(), (C.c_char * lib.d1_peer_handle_bytes())()
         with torch.cuda.device(self.policy.device):
-            check(lib.d1_peer_alloc(self.peer_bytes(), C.byref(base), handle), 'd1_peer_alloc')
+            check(lib.d1_peer_alloc(self.peer_bytes(world), C.byref(base), handle), 'd1_peer_alloc')
             handles = [None] * world
             dist.all_gather_object(handles, bytes(handle), group=group)
             ptrs = []
@@ -155,18 +159,34 @@ class PPO:
         self.peer_attach(world, rank, ptrs)
         self.peer['base'] = base.value
 
-    def peer_bytes(self):
-        """Size of one rank's exchange buffer: two halves of the flat gradient
-        and one u64 flag per rank (up to 8)."""
-        xstride = (self.grad.numel() + 3) // 4 * 4
-        return 2 * xstride * 4 + 8 * 8
+    def two_phase(self, world):
+        """Whether the peer exchange of `world` ranks is the two-phase one
+        (each rank reduces a slice, then gathers) rather than the one-shot
+        one (each rank reads every peer's whole gradient)."""
+        return self.exchange == 'twophase' or (self.exchange == 'auto' and world >= 4)
+
+    def _peer_layout(self, world):
+        """(stride, flag offset in bytes): one-shot -- two halves of the flat
+        gradient; two-phase -- inbox and gather areas of [2][world][slice]."""
+        P = self.grad.numel()
+        if self.two_phase(world):
+            slice_ = ((P + world - 1) // world + 3) // 4 * 4
+            return slice_, 4 * world * slice_ * 4
+        xstride = (P + 3) // 4 * 4
+        return xstride, 2 * xstride * 4
+
+    def peer_bytes(self, world=None):
+        """Size of one rank's exchange buffer: the gradient areas and 16 u64
+        flags."""
+        import torch.distributed as dist
+        world = world if world is not None else dist.get_world_size(self.group)
+        return self._peer_layout(world)[1] + 16 * 8
 
     def peer_attach(self, world, rank, ptrs):
         """Use the exchange buffers ptrs[p] (rank p's, as mapped here) for the
         gradient all-reduce of every minibatch."""
-        self.xstride = (self.grad.numel() + 3) // 4 * 4
-        flag_off = 2 * self.xstride * 4
-        self.peer = dict(world=world, rank=rank, base=None, ptrs=list(ptrs),
+        self.xstride, flag_off = self._peer_layout(world)
+        self.peer = dict(world=world, rank=rank, base=None, ptrs=list(ptrs), two_phase=self.two_phase(world),
                          xbufs=(C.c_void_p * world)(*ptrs),
                          flags=(C.c_void_p * world)(*[q + flag_off for q in ptrs]))
 
@@ -223,12 +243,12 @@ class PPO:
         jobs, njobs = self.jobs, len(self.jobs)
         if self.peer is not None:
             pr = self.peer
-            check(lib.d1_ppo_step_peer(jobs, njobs, p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(),
-                                       self.v.data_ptr(), g.numel(), self.lr, self.betas[0], self.betas[1], self.eps,
-                                       self.max_grad_norm, self.step_dev.data_ptr(), self.segs, len(self.segs),
-                                       pr['xbufs'], pr['flags'], self.xstride, pr['world'], pr['rank'],
-                                       self.peer_wait_limit, s),
-                  'd1_ppo_step_peer')
+            fn = lib.d1_ppo_step_peer2 if pr['two_phase'] else lib.d1_ppo_step_peer
+            check(fn(jobs, njobs, p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(), self.v.data_ptr(), g.numel(),
+                     self.lr, self.betas[0], self.betas[1], self.eps, self.max_grad_norm, self.step_dev.data_ptr(),
+                     self.segs, len(self.segs), pr['xbufs'], pr['flags'], self.xstride, pr['world'], pr['rank'],
+                     self.peer_wait_limit, s),
+                  'd1_ppo_step_peer2' if pr['two_phase'] else 'd1_ppo_step_peer')
             return self.terms
         if self.group is not None:
             import torch.distributed as dist

@@ -546,6 +546,25 @@ int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad
                      float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
                      const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
                      int world, int rank, unsigned wait_limit, void *stream);
+/* d1_ppo_step_peer with a two-phase exchange, for more ranks: rank j owns
+ * slice j of the flat gradient (`slice` elements, a multiple of 4, slice *
+ * world >= total). (1) The reduction stores this rank's part of every slice j
+ * straight into rank j's inbox, slot [epoch & 1][rank] (peer stores), and
+ * raises flags[p][rank] = epoch on every peer; (2) each rank waits for all of
+ * its inbox's flags, sums its slice over the ranks in rank order, divides by
+ * world and stores the result into slot [epoch & 1][rank] of every rank's
+ * gather area, then raises flags[p][8 + rank]; (3) each rank waits for those
+ * flags and copies the gathered slices into `grad` (and its sums of squares);
+ * (4) Adam. A rank moves 2 (world - 1) / world of the gradient over NVLink
+ * instead of reading (world - 1) whole copies. xbufs[p]: rank p's buffer of
+ * 4 * world * slice floats (inbox [2][world][slice], then gather
+ * [2][world][slice]); flags[p]: its 16 u64 flags. Same bounded waits and
+ * failure behaviour as d1_ppo_step_peer; the same bits as the one-shot and
+ * NCCL exchanges. No reference counterpart. */
+int d1_ppo_step_peer2(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                      float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
+                      const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t slice,
+                      int world, int rank, unsigned wait_limit, void *stream);
 /* Exchange-buffer set-up through CUDA IPC (not on the hot path): allocate
  * `bytes` of zeroed device memory and its handle (d1_peer_handle_bytes()
  * bytes), map another process's buffer from its handle, unmap, free. */

@@ -1,6 +1,6 @@
 """Multi-GPU PPO update with the gradient all-reduce through peer memory
-(d1_ppo_step_peer) against the same update with NCCL's all-reduce
-(peer=False), on 2 GPUs as 2 processes: after every minibatch both give the
+(d1_ppo_step_peer, one-shot; d1_ppo_step_peer2, two-phase) against the same
+update with NCCL's all-reduce (peer=False), on 2 GPUs as 2 processes: after every minibatch both give the
 same parameters bit for bit (the mean of two values is one add and one divide
 either way), and every rank holds the same parameters. Several minibatches in a
 row exercise both halves of the exchange buffer; a captured epoch exercises the
@@ -27,36 +27,41 @@ def _worker(rank, world, port, results):
     try:
         B, T, mb = 512, 16, 2048
 
-        def make(peer, graph):
+        def make(peer, graph, exchange='oneshot'):
             env = spec_env.SpecEnv(B, seed=3, first_env=rank * B, device=f'cuda:{rank}')
             pol = policy.Policy(seed=0, device=f'cuda:{rank}')
             roll = rollout.Rollout(env, pol, T, seed=3)
             roll.collect()
-            tr = ppo.PPO(pol, roll, minibatch=mb, epochs=2, group=dist.group.WORLD, peer=peer, graph=graph)
+            tr = ppo.PPO(pol, roll, minibatch=mb, epochs=2, group=dist.group.WORLD, peer=peer, graph=graph,
+                         exchange=exchange)
             tr.advantages()
             return tr
 
-        a, b = make(True, False), make(False, False)
+        a, b, a2 = make(True, False), make(False, False), make(True, False, 'twophase')
+        assert a2.peer['two_phase'] and not a.peer['two_phase']
         g = torch.Generator(device=f'cuda:{rank}').manual_seed(7)
         same, ranks_agree = True, True
         for k in range(5):
             idx = torch.randperm(a.total, device=f'cuda:{rank}', generator=g)[:mb]
             a.minibatch(idx)
             b.minibatch(idx)
+            a2.minibatch(idx)
             torch.cuda.synchronize()
             same &= torch.equal(a.policy.flat, b.policy.flat) and torch.equal(a.grad, b.grad)
+            same &= torch.equal(a2.policy.flat, b.policy.flat) and torch.equal(a2.grad, b.grad)
             both = [torch.empty_like(a.policy.flat) for _ in range(world)]
             dist.all_gather(both, a.policy.flat)
             ranks_agree &= all(torch.equal(both[0], x) for x in both)
         # a captured epoch (the second update epoch replays a CUDA graph)
-        c, d = make(True, True), make(False, True)
-        gc, gd = torch.Generator(device=f'cuda:{rank}').manual_seed(9), torch.Generator(device=f'cuda:{rank}').manual_seed(9)
-        c.update(gc)
-        d.update(gd)
+        c, d, c2 = make(True, True), make(False, True), make(True, True, 'twophase')
+        gens = [torch.Generator(device=f'cuda:{rank}').manual_seed(9) for _ in range(3)]
+        c.update(gens[0])
+        d.update(gens[1])
+        c2.update(gens[2])
         torch.cuda.synchronize()
-        graphed_same = torch.equal(c.policy.flat, d.policy.flat)
+        graphed_same = torch.equal(c.policy.flat, d.policy.flat) and torch.equal(c2.policy.flat, d.policy.flat)
         err = a.lib.d1_peer_error()
-        for tr in (a, b, c, d):
+        for tr in (a, b, a2, c, d, c2):
             tr.release()
         results[rank] = dict(same=bool(same), ranks_agree=bool(ranks_agree), graphed_same=bool(graphed_same),
                              err=int(err))

@@ -14,7 +14,8 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def test_peer_wait_runs_out_reports_and_changes_nothing():
+@pytest.mark.parametrize('exchange', ['oneshot', 'twophase'])
+def test_peer_wait_runs_out_reports_and_changes_nothing(exchange):
     from d1._lib import D1Error
     from d1.policy import Policy
     from d1.ppo import PPO
@@ -23,9 +24,9 @@ def test_peer_wait_runs_out_reports_and_changes_nothing():
     B, T, mb = 512, 8, 2048
     roll = Rollout(SpecEnv(B, seed=3), Policy(seed=0), T, seed=3)
     roll.collect()
-    tr = PPO(roll.policy, roll, minibatch=mb, epochs=1, graph=False, peer_wait_limit=2000)
+    tr = PPO(roll.policy, roll, minibatch=mb, epochs=1, graph=False, peer_wait_limit=2000, exchange=exchange)
     tr.advantages()
-    nbytes = tr.peer_bytes()
+    nbytes = tr.peer_bytes(world=2)
     bufs = [torch.zeros(nbytes // 4, dtype=torch.int32, device='cuda') for _ in range(2)]
     tr.peer_attach(2, 0, [b.data_ptr() for b in bufs])
     before = [t.clone() for t in (tr.policy.flat, tr.m, tr.v, tr.step_dev, tr.policy.bf16['w1'])]
