@@ -62,7 +62,7 @@ class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
                  gae_mode=1, splits=8, group=None, graph=True, peer=True, compact=True, peer_wait_limit=0,
-                 exchange='auto'):
+                 exchange='auto', splits2=None):
         self.policy, self.rollout = policy, rollout
         self.peer_wait_limit = peer_wait_limit  # polls per flag wait; 0 = the library default (~1 s)
         if exchange not in ('auto', 'oneshot', 'twophase'):
@@ -100,7 +100,7 @@ class PPO:
         self.slab1 = torch.empty((self.s1, HID, self.xw), **f32)
         # dW2 is 256 x 256: its output has only 2 tiles, so it needs 8x the K splits
         # of dW1 (2 x 8 tiles) to put ~128 CTAs to work
-        self.s2 = G.splits_for(mb, splits * 8)
+        self.s2 = G.splits_for(mb, splits * 8 if splits2 is None else splits2)
         self.slab2 = torch.empty((self.s2, HID, HID), **f32)
         self.part_len = self.lib.d1_ppo_loss_part_len()
         batches = (mb + 63) // 64                     # the loss kernel takes 64 rows per pass
