@@ -73,6 +73,9 @@ def parse():
     ap.add_argument('--no-ref-tasks', action='store_true',
                     help="skip the reference-task lines (route-cue and v1 on the GPU beside the reference's own "
                          'host build)')
+    ap.add_argument('--no-route-ppo', action='store_true',
+                    help="skip the route-cue task's PPO pipeline (the reference's benchmark loop) in the "
+                         'reference-task lines')
     ap.add_argument('--no-ref-gpu', action='store_true',
                     help="skip timing the reference's own learn.cu GPU build in the reference-task lines")
     ap.add_argument('--route-envs', type=int, default=65536, help='envs per GPU of the route-cue line')
@@ -312,6 +315,19 @@ def reference_tasks(args, dev, rank, world, stream):
                     'sample': f'{m} envs x decisions {args.warmup}-{args.warmup + args.steps} ({dt:.1f} s), '
                               "the reference's learn.cu host path (oracle/_ref)"}
                 line['gpu_over_cpu_reference'] = line['decisions_per_s'] / rate
+        if name == 'route' and rank == 0 and not args.no_route_ppo:
+            progress("route-cue PPO pipeline (the reference's benchmark loop)")
+            pipe = {'what': "the reference's PPO benchmark loop restated (gpu-d1/scripts/benchmark_pipeline.py): "
+                            'torch fp32 MLP 421-128-128 tanh, T=64 turns, 4 epochs of minibatch 4096; the env '
+                            "under it is ours or the reference's own learn.cu GPU build on this B200; random "
+                            'initialisation (the mature checkpoint is not available)',
+                    'published_rtx5000_decisions_per_s': 153123, 'published_source': 'gpu-d1/PERFORMANCE.md:16'}
+            for worlds in (512, 8192):
+                for kind in ('ours', 'reference'):
+                    r = route_ppo_pipeline(kind, maps, worlds, 64, 4, 2, dev)
+                    if r is not None:
+                        pipe[f'{kind}_{worlds}_worlds'] = r
+            line['ppo_pipeline'] = pipe
         out[name] = line
         del env
     return out
@@ -372,6 +388,120 @@ def reference_gpu_rate(name, env, args, dev, stream, n):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     return n / (ms / 1e3), ms
+
+
+def route_ppo_pipeline(kind, maps, B, T, updates, warmup, dev):
+    """The reference's own PPO benchmark loop for the route-cue task, restated
+    (gpu-d1/scripts/benchmark_pipeline.py; the loop of run_ring_ablations.py:
+    332-372): its MLP policy (421 -> 128 tanh -> 128 tanh, actor 9, critic 1,
+    fp32, TF32 off), T-turn rollouts of B worlds, GAE, 4 epochs of minibatch
+    4096, clip 0.2, 0.25 MSE, entropy 0.01, grad-norm 0.5, Adam 3e-4. `kind`
+    picks the env under it: 'ours' (libd1's route kernel) or 'reference' (the
+    reference's own learn.cu of the task compiled for sm_100a, its GPU path).
+    The mature checkpoint that benchmark starts from is not available, so the
+    policy starts from the reference's initialisation. Returns the median
+    decisions/s over `updates` timed updates."""
+    import ctypes as C
+    import math
+    import torch
+    from torch import nn
+    from torch.distributions import Categorical, Distribution
+    sys.path.insert(0, str(REPO / 'oracle'))
+    import oracle
+    from d1.route_env import RouteEnv
+    Distribution.set_default_validate_args(False)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(0)
+    env = RouteEnv(B, 40, seed=17, maps=maps, device=dev)
+    if kind == 'reference':
+        lib = oracle.route_library()
+        if lib is None:
+            return None
+        a = env.arrays
+        tables = oracle.RouteTables(a[0].data_ptr(), a[1].data_ptr(), a[2].data_ptr(), a[3].data_ptr(),
+                                    env.tables.ncells, a[4].data_ptr(), a[5].data_ptr(), env.n_maps, -1)
+        state = torch.zeros((B, lib.learn_state_bytes()), dtype=torch.uint8, device=dev)
+        obs, mask, out = env.obs.clone(), env.mask.clone(), env.out.clone()
+        s = torch.cuda.current_stream(dev).cuda_stream
+        assert lib.learn_init(state.data_ptr(), B, C.byref(env.config), C.byref(tables), 17, obs.data_ptr(),
+                              mask.data_ptr(), s, 1) == 0
+
+        def step(act):
+            lib.learn_step(state.data_ptr(), B, C.byref(env.config), C.byref(tables), act.data_ptr(), 1024,
+                           obs.data_ptr(), mask.data_ptr(), out.data_ptr(), s, 1)
+            return obs, out
+    else:
+        obs, mask = env.obs, env.mask
+        step = env.step
+
+    class Policy(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.body = nn.Sequential(nn.Linear(421, 128), nn.Tanh(), nn.Linear(128, 128), nn.Tanh())
+            self.actor, self.critic = nn.Linear(128, 9), nn.Linear(128, 1)
+            for layer in self.modules():
+                if isinstance(layer, nn.Linear):
+                    nn.init.orthogonal_(layer.weight, math.sqrt(2))
+                    nn.init.zeros_(layer.bias)
+            nn.init.orthogonal_(self.actor.weight, .01)
+            nn.init.orthogonal_(self.critic.weight, 1)
+
+        def forward(self, o, m):
+            h = self.body(o)
+            return Categorical(logits=self.actor(h).masked_fill(m == 0, -1e9)), self.critic(h).squeeze(-1)
+
+    model = Policy().to(dev)
+    opt = torch.optim.Adam(model.parameters(), lr=3e-4, eps=1e-5)
+    observations = torch.empty((T, B, 421), device=dev)
+    masks = torch.empty((T, B, 9), device=dev)
+    actions = torch.empty((T, B), dtype=torch.int64, device=dev)
+    oldlp, values, rewards, dones, advantages = [torch.empty((T, B), device=dev) for _ in range(5)]
+
+    def update():
+        with torch.no_grad():
+            for t in range(T):
+                observations[t].copy_(obs)
+                masks[t].copy_(mask)
+                dist, v = model(obs, mask)
+                act = dist.sample()
+                actions[t] = act
+                oldlp[t] = dist.log_prob(act)
+                values[t] = v
+                _, o = step(act)
+                rewards[t] = o[:, 0]
+                dones[t] = o[:, 1]
+            _, nextv = model(obs, mask)
+            gae = torch.zeros(B, device=dev)
+            for t in reversed(range(T)):
+                live = 1 - dones[t]
+                delta = rewards[t] + .99 * nextv * live - values[t]
+                gae = delta + .99 * .95 * live * gae
+                advantages[t], nextv = gae, values[t]
+            returns = (advantages + values).flatten()
+            adv = advantages.flatten()
+            adv = (adv - adv.mean()) / (adv.std() + 1e-8)
+        for _ in range(4):
+            for inds in torch.randperm(T * B, device=dev).split(4096):
+                dist, v = model(observations.flatten(0, 1)[inds], masks.flatten(0, 1)[inds])
+                ratio = (dist.log_prob(actions.flatten()[inds]) - oldlp.flatten()[inds]).exp()
+                pg = -torch.minimum(ratio * adv[inds], ratio.clamp(.8, 1.2) * adv[inds]).mean()
+                loss = pg + .25 * (v - returns[inds]).square().mean() - .01 * dist.entropy().mean()
+                if not torch.isfinite(loss).item():
+                    raise RuntimeError('Non-finite PPO loss')
+                opt.zero_grad(set_to_none=True)
+                loss.backward()
+                nn.utils.clip_grad_norm_(model.parameters(), .5)
+                opt.step()
+
+    times = []
+    for i in range(warmup + updates):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        update()
+        torch.cuda.synchronize()
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return T * B / statistics.median(times)
 
 
 def _spec_default():
