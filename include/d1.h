@@ -560,7 +560,9 @@ int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad
  * 4 * world * slice floats (inbox [2][world][slice], then gather
  * [2][world][slice]); flags[p]: its 16 u64 flags. Same bounded waits and
  * failure behaviour as d1_ppo_step_peer; the same bits as the one-shot and
- * NCCL exchanges. No reference counterpart. */
+ * NCCL exchanges. Measured slower than the one-shot exchange on 2 and 8
+ * B200s (the added flag round outweighs the smaller transfer). No reference
+ * counterpart. */
 int d1_ppo_step_peer2(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
                       float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
                       const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t slice,
