@@ -668,11 +668,11 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_ppo:
         from d1.ppo import PPO
         group = dist.group.WORLD if world > 1 else None
-        trainer = PPO(policy, roll, minibatch=args.minibatch, epochs=args.epochs, group=group, exchange=args.exchange)
-        gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+        trainer = PPO(policy, roll, minibatch=args.minibatch, epochs=args.epochs, group=group, exchange=args.exchange,
+                      perm_seed=1234 + rank)
         roll.roll()
         progress('PPO warm-up iteration')
-        trainer.iteration(gen)  # warm-up iteration
+        trainer.iteration()  # warm-up iteration
         progress('PPO timed iteration')
         if world > 1:
             dist.barrier()
@@ -683,7 +683,7 @@ def run_ours(args, rank, world, local_rank):
         p1.record(stream)
         trainer.advantages()
         p2.record(stream)
-        trainer.update(gen)
+        trainer.update()
         p3.record(stream)
         torch.cuda.synchronize()
         roll.roll()
@@ -767,9 +767,8 @@ def run_ours(args, rank, world, local_rank):
         pol4 = Policy(device=dev, seed=0)
         roll4 = Rollout(env4, pol4, t4, seed=4)
         tr4 = PPO(pol4, roll4, minibatch=args.minibatch, epochs=args.epochs,
-                  group=dist.group.WORLD if world > 1 else None, exchange=args.exchange)
-        gen4 = torch.Generator(device=dev).manual_seed(4321 + rank)
-        tr4.iteration(gen4)  # warm-up iteration (also captures the update graph)
+                  group=dist.group.WORLD if world > 1 else None, exchange=args.exchange, perm_seed=4321 + rank)
+        tr4.iteration()  # warm-up iteration (also captures the update graph)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -778,7 +777,7 @@ def run_ours(args, rank, world, local_rank):
         roll4.collect()
         q1.record(stream)
         tr4.advantages()
-        tr4.update(gen4)
+        tr4.update()
         q2.record(stream)
         torch.cuda.synchronize()
         roll4.roll()

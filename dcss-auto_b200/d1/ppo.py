@@ -62,8 +62,9 @@ class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
                  gae_mode=1, splits=8, group=None, graph=True, peer=True, compact=True, peer_wait_limit=0,
-                 exchange='auto', splits2=None):
+                 exchange='auto', splits2=None, perm_seed=0):
         self.policy, self.rollout = policy, rollout
+        self.perm_seed = perm_seed  # key of the epoch permutation (with the device epoch count)
         self.peer_wait_limit = peer_wait_limit  # polls per flag wait; 0 = the library default (~1 s)
         if exchange not in ('auto', 'oneshot', 'twophase'):
             raise ValueError("exchange must be 'auto', 'oneshot' or 'twophase'")
@@ -89,6 +90,8 @@ class PPO:
         self.step_dev = torch.zeros(1, dtype=torch.int64, device=dev)  # Adam step count
         self.use_graph, self.graph = graph, None
         self.perm = torch.empty(self.total, dtype=torch.int64, device=dev)
+        self.perm_epoch = torch.zeros(1, dtype=torch.int64, device=dev)  # epochs drawn by d1_ppo_permute
+        self.graph_perm = None  # whether the captured epoch draws its own permutation
         mb = minibatch
         self.xw = OBS + 8  # X row pitch: the 8-column tail carries the ones column
         self.x = None if compact else torch.empty((mb, self.xw), **bf)
@@ -264,32 +267,54 @@ class PPO:
                               self.step_dev.data_ptr(), self.segs, len(self.segs), s), 'd1_ppo_step')
         return self.terms
 
-    def _epoch(self):
+    def _permute(self):
+        """This epoch's minibatch order: d1_ppo_permute keyed by perm_seed and the
+        device epoch count, which it then advances (both on the stream, so a
+        captured epoch draws a fresh order on every replay)."""
+        s = self.stream
+        check(self.lib.d1_ppo_permute(self.perm.data_ptr(), self.total, self.perm_seed & (2 ** 64 - 1),
+                                      self.perm_epoch.data_ptr(), s), 'd1_ppo_permute')
+        check(self.lib.d1_counter_add(self.perm_epoch.data_ptr(), 1, s), 'd1_counter_add')
+
+    def _epoch(self, own_perm):
+        if own_perm:
+            self._permute()
         for i in range(0, self.total, self.mb):
             self.minibatch(self.perm[i:i + self.mb])
 
     def update(self, generator=None):
         """epochs x (total / mb) minibatch steps over a fresh permutation each epoch.
 
+        The order comes from d1_ppo_permute (a keyed bijection, one pass, no
+        sort) unless a torch generator is given: then it is
+        torch.randperm(total, generator=generator), the reference's own draw
+        (gpu-d1/scripts/run_ring_ablations.py:364), so the minibatches follow
+        the reference's order for the same generator state.
+
         With graph=True the first epoch runs eagerly (it also initialises every
         kernel's attributes) and the second is captured once into a CUDA graph
-        over the static permutation buffer; later epochs replay it, so a whole
-        epoch of ~15 launches per minibatch costs one host call."""
+        (with the permutation when it is d1_ppo_permute's); later epochs replay
+        it, so a whole epoch of ~15 launches per minibatch costs one host call."""
         dev = self.policy.device
+        own = generator is None
+        if self.graph is not None and self.graph_perm != own:
+            self.graph = None  # captured for the other permutation source
         for _ in range(self.epochs):
-            torch.randperm(self.total, device=dev, generator=generator, out=self.perm)
+            if not own:
+                torch.randperm(self.total, device=dev, generator=generator, out=self.perm)
             if not self.use_graph:
-                self._epoch()
+                self._epoch(own)
             elif self.graph is None and not getattr(self, '_warm', False):
-                self._epoch()
+                self._epoch(own)
                 self._warm = True
             else:
                 if self.graph is None:
                     self.graph = torch.cuda.CUDAGraph()
+                    self.graph_perm = own
                     side = torch.cuda.Stream(dev)
                     side.wait_stream(torch.cuda.current_stream(dev))
                     with torch.cuda.stream(side), torch.cuda.graph(self.graph, stream=side):
-                        self._epoch()
+                        self._epoch(own)
                     torch.cuda.current_stream(dev).wait_stream(side)
                 self.graph.replay()
         self.check_peer()

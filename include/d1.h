@@ -461,10 +461,12 @@ int d1_gemm_error(void);
  * `stats` (double[2]) is given, sum(adv) and sum(adv^2) are added to it (the
  * advantage-normalisation statistics; all-reduced across ranks by the caller).
  * mode 0 replays the reference's per-step op order exactly; mode 1 is the
- * warp-level segmented scan over time (within 1e-5 relative). The sums are
- * deterministic (block partials added in block order through a fixed array in
- * the library, so calls on one device must not overlap); with stats, B is at
- * most 16,777,216 (mode 0) or 2,097,152 (mode 1), else D1_ERR_TOO_LARGE. */
+ * segmented scan over time (each thread composes a run of steps in registers,
+ * the runs of an env are combined across the 8 warps of a block; within 1e-5
+ * relative). The sums are deterministic for a given device (block partials
+ * added in block order through a fixed array in the library, so calls on one
+ * device must not overlap); with stats in mode 0, B is at most 16,777,216,
+ * else D1_ERR_TOO_LARGE. */
 int d1_gae(const float *reward, const float *done, int64_t r_step, int64_t r_env, const float *value, int T, int B,
            float gamma, float lambda, float *adv, float *ret, double *stats, int mode, void *stream);
 /* Gather + expand of compact observations (d1_spec_step_ex's cobs rows, 320 B
@@ -495,6 +497,14 @@ int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, v
  * [offset, offset + count) form a [rows, cols] matrix; bf16 receives the same
  * layout and bf16_t (when not NULL) its transpose. */
 typedef struct { int64_t offset, count; int rows, cols; void *bf16, *bf16_t; } D1AdamSegment;
+/* The minibatch order of one epoch: perm[i] (i < n) is a keyed bijection of
+ * [0, n) -- an alternating Feistel network over the smallest power of two >= n
+ * with cycle walking -- keyed by `seed` and the count *epoch read on the device
+ * (advance it with d1_counter_add between epochs, so that a captured epoch draws
+ * a new order on every replay). Replaces the reference's per-epoch
+ * torch.randperm(T*B, device='cuda') (gpu-d1/scripts/run_ring_ablations.py:364)
+ * with one pass and no sort. n <= 2^40. */
+int d1_ppo_permute(int64_t *perm, int64_t n, uint64_t seed, const int64_t *epoch, void *stream);
 /* *counter += delta on the device (the optimizer's step count lives on the
  * device so that a captured CUDA graph of many updates stays correct). */
 int d1_counter_add(int64_t *counter, int64_t delta, void *stream);

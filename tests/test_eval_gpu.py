@@ -161,15 +161,18 @@ def test_frame_stack_matches_the_reference_wrapper(d1mods):
         assert torch.equal(a.obs.view(torch.int16), b.obs.view(torch.int16)), k
 
 
-def test_checkpoint_resume_is_exact(d1mods, tmp_path):
+@pytest.mark.parametrize('torch_order', [False, True])
+def test_checkpoint_resume_is_exact(d1mods, tmp_path, torch_order):
+    """The epoch order from d1_ppo_permute (device epoch count in the
+    checkpoint) or from torch.randperm on a generator (its state saved)."""
     spec_env, policy, rollout, ppo, ckpt = (d1mods[k] for k in ('spec_env', 'policy', 'rollout', 'ppo', 'checkpoint'))
 
     def make():
         env = spec_env.SpecEnv(256, seed=1)
         pol = policy.Policy(seed=0)
         roll = rollout.Rollout(env, pol, 16, seed=1)
-        tr = ppo.PPO(pol, roll, minibatch=1024, epochs=2)
-        return tr, torch.Generator(device='cuda').manual_seed(5)
+        tr = ppo.PPO(pol, roll, minibatch=1024, epochs=2, perm_seed=11)
+        return tr, (torch.Generator(device='cuda').manual_seed(5) if torch_order else None)
 
     full, g_full = make()
     for _ in range(4):
@@ -184,7 +187,8 @@ def test_checkpoint_resume_is_exact(d1mods, tmp_path):
         resumed.iteration(g_res)
     torch.cuda.synchronize()
     a, b = ckpt.state_dict(full, g_full), ckpt.state_dict(resumed, g_res)
-    for key in ('params', 'adam_m', 'adam_v', 'adam_step', 'env_state', 'obs', 'cobs', 'legal', 'generator'):
+    keys = ['params', 'adam_m', 'adam_v', 'adam_step', 'perm_epoch', 'env_state', 'obs', 'cobs', 'legal']
+    for key in keys + (['generator'] if torch_order else []):
         assert torch.equal(a[key], b[key]), key
     assert a['global_step'] == b['global_step']
     # a different job is refused

@@ -62,6 +62,39 @@ def test_gae_modes_against_the_reference_loop(mods):
     assert (ret1 - ref_ret).abs().max().item() <= 1e-5 * max(ret1.abs().max().item(), 1.0)
 
 
+@pytest.mark.parametrize('planes', [True, False])
+@pytest.mark.parametrize('T,B', [(1, 40), (7, 33), (32, 96), (80, 64), (100, 70), (128, 1000), (256, 32), (300, 45),
+                                 (1000, 130)])
+def test_gae_scan_over_horizons_and_ragged_batches(T, B, planes):
+    """d1_gae mode 1 against the reference loop: horizons from 1 to 1,000 (runs
+    of one row to several chunks per warp), env counts that are not a multiple
+    of an env group (odd ones take the one-env-per-lane form), outcome rows in
+    the env's plane layout [T, 10, B] (reward and done rows contiguous over
+    envs: read in pairs) and as [T, B, 10] rows; the statistics against float64
+    sums of the same advantages (1e-6 of the absolute sum)."""
+    from d1._lib import library
+    lib = library()
+    g = torch.Generator(device='cuda').manual_seed(T * 1000 + B)
+    out = torch.zeros((T, 10, B), device='cuda').permute(0, 2, 1) if planes else torch.zeros((T, B, 10), device='cuda')
+    out[:, :, 0] = torch.randn((T, B), device='cuda', generator=g)
+    out[:, :, 1] = (torch.rand((T, B), device='cuda', generator=g) < 0.05).float()
+    values = torch.randn((T + 1, B), device='cuda', generator=g)
+    adv, ret = torch.empty((T, B), device='cuda'), torch.empty((T, B), device='cuda')
+    stats = torch.zeros(2, dtype=torch.float64, device='cuda')
+    assert lib.d1_gae(out.data_ptr(), out[:, :, 1].data_ptr(), out.stride(0), out.stride(1), values.data_ptr(), T, B,
+                      0.999, 0.95, adv.data_ptr(), ret.data_ptr(), stats.data_ptr(), 1, 0) == 0
+    torch.cuda.synchronize()
+    ref_adv, ref_ret = torch_gae(out[:, :, 0], out[:, :, 1], values, 0.999, 0.95)
+    scale = max(ref_adv.abs().max().item(), 1.0)
+    assert (adv - ref_adv).abs().max().item() <= 1e-5 * scale
+    assert (ret - ref_ret).abs().max().item() <= 1e-5 * max(ref_ret.abs().max().item(), 1.0)
+    # each thread adds a chunk of 8 steps in float before the double totals:
+    # error below 8 * 2^-24 of the absolute sum
+    a64 = adv.double()
+    assert abs(stats[0].item() - a64.sum().item()) <= 1e-6 * max(1.0, a64.abs().sum().item())
+    assert abs(stats[1].item() - (a64 * a64).sum().item()) <= 1e-6 * (a64 * a64).sum().item()
+
+
 def bf16_round(x):
     return x.to(torch.bfloat16).to(torch.float32)
 
@@ -283,3 +316,93 @@ def test_config2_minibatches_match_torch_over_eight_steps(mods):
     drift = rel(pol.flat - start, p_own.detach() - start)
     print('worst gradient error per segment', worst, 'update drift vs autograd model', drift)
     assert drift < 1e-2, drift
+
+
+def permute_restated(n, seed, epoch):
+    """numpy restatement of d1_ppo_permute: alternating Feistel rounds (murmur3
+    32-bit finaliser of round key ^ half; round keys from the splitmix64
+    finaliser) over the smallest 2^m >= n, walked into [0, n)."""
+    def h64(z):
+        z = np.asarray(z, dtype=np.uint64)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xbf58476d1ce4e5b9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94d049bb133111eb)
+        return z ^ (z >> np.uint64(31))
+
+    def h32(v):
+        v = np.asarray(v, dtype=np.uint32)
+        v = (v ^ (v >> np.uint32(16))) * np.uint32(0x85ebca6b)
+        v = (v ^ (v >> np.uint32(13))) * np.uint32(0xc2b2ae35)
+        return v ^ (v >> np.uint32(16))
+
+    with np.errstate(over='ignore'):
+        key = h64(np.uint64(seed) ^ h64(np.uint64(epoch) + np.uint64(0x9e3779b97f4a7c15)))
+        rk = [np.uint32(int(h64(key + np.uint64(r))) & 0xFFFFFFFF) for r in range(6)]
+        m = max(0, int(n - 1).bit_length())
+        hb, lb = m // 2, m - m // 2
+        hmask, lmask = np.uint32((1 << hb) - 1), np.uint32((1 << lb) - 1)
+        x = np.arange(n, dtype=np.uint64)
+        todo = np.ones(n, dtype=bool)
+        while todo.any():
+            y = x[todo]
+            hi, lo = (y >> np.uint64(lb)).astype(np.uint32), y.astype(np.uint32) & lmask
+            for r in range(0, 6, 2):
+                hi = hi ^ (h32(rk[r] ^ lo) & hmask)
+                lo = lo ^ (h32(rk[r + 1] ^ hi) & lmask)
+            x[todo] = (hi.astype(np.uint64) << np.uint64(lb)) | lo.astype(np.uint64)
+            todo[todo] = x[todo] >= np.uint64(n)
+        return x.astype(np.int64)
+
+
+@pytest.mark.parametrize('n', [1, 2, 3, 1000, 4097, 65536])
+def test_epoch_permutation_matches_its_restatement(n):
+    from d1._lib import library
+    lib = library()
+    epoch = torch.tensor([7], dtype=torch.int64, device='cuda')
+    perm = torch.empty(n, dtype=torch.int64, device='cuda')
+    assert lib.d1_ppo_permute(perm.data_ptr(), n, 0x1234, epoch.data_ptr(), 0) == 0
+    torch.cuda.synchronize()
+    got = perm.cpu().numpy()
+    assert np.array_equal(np.sort(got), np.arange(n))
+    assert np.array_equal(got, permute_restated(n, 0x1234, 7))
+
+
+def test_epoch_permutation_at_rollout_size_and_across_epochs(mods):
+    """65,536 x 128 samples: every index exactly once, a fresh order for each
+    epoch count, and no visible structure (a minibatch's indices spread over
+    the whole rollout)."""
+    from d1._lib import library
+    lib = library()
+    n, mb = 65536 * 128, 16384
+    epoch = torch.zeros(1, dtype=torch.int64, device='cuda')
+    perms = []
+    for _ in range(2):
+        p = torch.empty(n, dtype=torch.int64, device='cuda')
+        assert lib.d1_ppo_permute(p.data_ptr(), n, 99, epoch.data_ptr(), 0) == 0
+        assert lib.d1_counter_add(epoch.data_ptr(), 1, 0) == 0
+        perms.append(p)
+    torch.cuda.synchronize()
+    assert epoch.item() == 2
+    for p in perms:
+        assert torch.equal(torch.sort(p).values, torch.arange(n, device='cuda'))
+    assert (perms[0] == perms[1]).float().mean().item() < 1e-3
+    first = perms[0][:mb].double()
+    # a uniform draw of 16,384 indices has mean n/2 +- n / sqrt(12 * 16384)
+    assert abs(first.mean().item() - n / 2) < 5 * n / (12 * mb) ** 0.5
+    # the time step (index // B) of consecutive draws is uncorrelated
+    t = (perms[0][:mb] // 65536).double()
+    c = torch.corrcoef(torch.stack([t[:-1], t[1:]]))[0, 1].item()
+    assert abs(c) < 0.05
+
+
+def test_update_draws_its_order_on_the_device(mods):
+    """update() without a generator advances the device epoch count once per
+    epoch, eager and graph-replayed epochs alike."""
+    pol, roll, tr = small_setup(mods, B=512, T=32, mb=4096, seed=4)
+    tr.epochs = 2
+    tr.advantages()
+    tr.update()
+    tr.update()
+    torch.cuda.synchronize()
+    assert tr.perm_epoch.item() == 4
+    assert tr.graph is not None and tr.graph_perm is True
+    assert np.array_equal(tr.perm.cpu().numpy(), permute_restated(tr.total, 0, 3))
