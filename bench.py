@@ -856,19 +856,19 @@ def run_kernels(args):
     gemm_pair_kernel, layer 2 on gemm_kernel, head_sample_kernel), then the same
     two GEMMs + head_sample_kernel for the bootstrap value) and GAE; then per
     pass: rollout layer 1 (gemm_pair_kernel<2, 0>), one PPO minibatch of 16,384
-    (layer 1 from compact rows gemm_pair_kernel<1, 1>; layer 2, dW2 and dh1
-    gemm_kernel; dW1 from compact rows gemm_pair_kernel<1, 2>; loss_mma_kernel,
-    grad_reduce_kernel, adam_update_kernel), layer 2
+    (layer 1 from compact rows gemm_pair_kernel<1, 1>; tail_kernel: layer 2,
+    head, loss, dh2 and dh1; dW2 gemm_kernel; dW1 from compact rows
+    gemm_pair_kernel<1, 2>; grad_reduce_kernel, adam_update_kernel), layer 2
     (gemm_kernel), head_sample_kernel, step_kernel, gae_scan_kernel, and the
     config-3 policy on 16,384 envs (crop_kernel, conv_kernel<1..3>, FC
     gemm_pair_kernel, head gemm_kernel, ar_kernel), then GAE over a [128, B]
     rollout of synthetic rewards and dones in the rollout's plane layout
     (gae_scan_kernel) and one route-cue env step of B envs on a 16-map
     corpus (d1::route::step_kernel, after 8 warm-up steps and their heuristic
-    launches). A `gemm` regex therefore sees 18 launches in the rollout and 9
-    per pass; `gae_scan` sees one before the passes (the setup's, T = 8) and
-    two per pass (T = 8, then T = 128); `route.*step` sees 8 before the passes
-    and one per pass."""
+    launches). A `gemm` regex therefore sees 18 launches in the rollout and 7
+    per pass; `tail_kernel` one per pass; `gae_scan` one before the passes
+    (the setup's, T = 8) and two per pass (T = 8, then T = 128); `route.*step`
+    8 before the passes and one per pass."""
     import torch
     from d1 import gemm as G
     from d1.conv_policy import ConvPolicy

@@ -39,6 +39,9 @@ SIGNATURES = {
     'd1_reduce_slabs': [_P, _I, C.c_int64, _P, _P],
     'd1_counter_add': [_P, C.c_int64, _P],
     'd1_ppo_permute': [_P, C.c_int64, C.c_uint64, _P, _P],
+    'd1_ppo_tail': [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_double, _I, _F, _F, _F, _F, _P, _P, _P, _P],
+    'd1_ppo_tail_blocks': [_I],
+    'd1_ppo_tail_error': [],
     'd1_gemm_splits': [_I, _I],
     'd1_gemm_bkn': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_rows': [_P, _I, _I, _P, _I, _P, _I, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],

@@ -7,11 +7,13 @@ Per minibatch (all device work is libd1 kernels, launched on the current stream)
   layer 1    h1 = relu(X W1^T + b1)                d1_gemm_cobs_a (tcgen05, K = 1832; X's
              rows are the one-hot expansion of the rollout's compact history
              rows cobs[idx], written into the operand tiles in shared memory)
-  layer 2    h2 = relu(h1 W2^T + b2)               d1_gemm
-  loss       head, PPO loss, dlogits/dvalue,       d1_ppo_loss (fused, warp MMAs)
-             dh2 = dhead Wh * relu'(h2), partials of dWh, dbh, db2
+  tail       h2 = relu(h1 W2^T + b2), head, PPO    d1_ppo_tail (one tcgen05 launch: W2 and
+             loss, dlogits/dvalue, dh2 = dhead Wh  an activation tile in shared memory,
+             * relu'(h2), dh1 = (dh2 W2) * relu'(h1),  accumulators in TMEM)
+             partials of dWh, dbh, db2
   dW2        dh2^T h1 (split-K fp32 slabs)         d1_gemm_ex
-  dh1        (dh2 W2) * relu'(h1)                  d1_gemm (mask epilogue)
+  (fused_tail=False: layer 2 by d1_gemm, the loss by d1_ppo_loss on warp MMAs,
+  dh1 by d1_gemm with a mask epilogue -- three launches for the same products)
   dW1, db1   dh1^T [X | 1] (split-K fp32 slabs;    d1_gemm_cobs_b (the B operand expanded
              column 1832 = db1)                    from cobs[idx] the same way)
   step       slab and loss-partial reductions      d1_ppo_step (a reduction
@@ -62,8 +64,9 @@ class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
                  gae_mode=1, splits=8, group=None, graph=True, peer=True, compact=True, peer_wait_limit=0,
-                 exchange='auto', splits2=None, perm_seed=0):
+                 exchange='auto', splits2=None, perm_seed=0, fused_tail=True):
         self.policy, self.rollout = policy, rollout
+        self.fused_tail = fused_tail  # layer 2 + loss + dh1 as one launch (d1_ppo_tail)
         self.perm_seed = perm_seed  # key of the epoch permutation (with the device epoch count)
         self.peer_wait_limit = peer_wait_limit  # polls per flag wait; 0 = the library default (~1 s)
         if exchange not in ('auto', 'oneshot', 'twophase'):
@@ -106,9 +109,12 @@ class PPO:
         self.s2 = G.splits_for(mb, splits * 8 if splits2 is None else splits2)
         self.slab2 = torch.empty((self.s2, HID, HID), **f32)
         self.part_len = self.lib.d1_ppo_loss_part_len()
-        batches = (mb + 63) // 64                     # the loss kernel takes 64 rows per pass
-        per = (batches + 591) // 592                  # passes per block with four blocks per SM
-        self.loss_blocks = (batches + per - 1) // per
+        if fused_tail:
+            self.loss_blocks = self.lib.d1_ppo_tail_blocks(mb)  # one partial per 128 rows
+        else:
+            batches = (mb + 63) // 64                 # the loss kernel takes 64 rows per pass
+            per = (batches + 591) // 592              # passes per block with four blocks per SM
+            self.loss_blocks = (batches + per - 1) // per
         self.part = torch.empty((self.loss_blocks, self.part_len), **f32)
         self.terms = torch.zeros(8, **f32)
         self.history = []
@@ -225,22 +231,33 @@ class PPO:
         cobs = r.cobs[:r.T].reshape(self.total, r.cobs.shape[2])
         if self.compact:
             G.gemm_cobs_a(cobs, p.bf16['w1'], idx=idx, bias=p.params['b1'], relu=True, out=self.h1)
-            G.gemm(self.h1, p.bf16['w2'], bias=p.params['b2'], relu=True, out=self.h2)
         else:
             check(lib.d1_ppo_gather_cobs(cobs.data_ptr(), idx.data_ptr(), mb, self.x.data_ptr(), self.xw, 1, s),
                   'd1_ppo_gather_cobs')
-            p.hidden_layers(self.x[:, :OBS], h1=self.h1, h2=self.h2)
+            G.gemm(self.x[:, :OBS], p.bf16['w1'], bias=p.params['b1'], relu=True, out=self.h1)
         g = self.grad
-        check(lib.d1_ppo_loss(self.h2.data_ptr(), p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(),
-                              idx.data_ptr(), r.legal.data_ptr(), r.actions.data_ptr(), r.logp.data_ptr(),
-                              self.adv.data_ptr(), self.ret.data_ptr(), r.values.data_ptr(), self.stats.data_ptr(),
-                              self.adv_count, mb, self.clip, self.vclip, self.vf_coef, self.ent_coef,
-                              self.dh2.data_ptr(), None, mb, self.part.data_ptr(), self.loss_blocks,
-                              s), 'd1_ppo_loss')
-        # dW2 = dh2^T h1
-        G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
-        # dh1 = (dh2 W2) * relu'(h1)
-        G.gemm(self.dh2, p.bf16['w2t'], mask=self.h1, out=self.dh1)
+        if self.fused_tail:
+            # layer 2, head, loss, dh2 and dh1 in one launch
+            check(lib.d1_ppo_tail(self.h1.data_ptr(), p.bf16['w2'].data_ptr(), p.params['b2'].data_ptr(),
+                                  p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(), idx.data_ptr(),
+                                  r.legal.data_ptr(), r.actions.data_ptr(), r.logp.data_ptr(), self.adv.data_ptr(),
+                                  self.ret.data_ptr(), r.values.data_ptr(), self.stats.data_ptr(), self.adv_count,
+                                  mb, self.clip, self.vclip, self.vf_coef, self.ent_coef, self.dh2.data_ptr(),
+                                  self.dh1.data_ptr(), self.part.data_ptr(), s), 'd1_ppo_tail')
+            # dW2 = dh2^T h1
+            G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
+        else:
+            G.gemm(self.h1, p.bf16['w2'], bias=p.params['b2'], relu=True, out=self.h2)
+            check(lib.d1_ppo_loss(self.h2.data_ptr(), p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(),
+                                  idx.data_ptr(), r.legal.data_ptr(), r.actions.data_ptr(), r.logp.data_ptr(),
+                                  self.adv.data_ptr(), self.ret.data_ptr(), r.values.data_ptr(),
+                                  self.stats.data_ptr(), self.adv_count, mb, self.clip, self.vclip, self.vf_coef,
+                                  self.ent_coef, self.dh2.data_ptr(), None, mb, self.part.data_ptr(),
+                                  self.loss_blocks, s), 'd1_ppo_loss')
+            # dW2 = dh2^T h1
+            G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
+            # dh1 = (dh2 W2) * relu'(h1)
+            G.gemm(self.dh2, p.bf16['w2t'], mask=self.h1, out=self.dh1)
         # dW1 = dh1^T X; X's ones column makes slab column 1832 the column sums of dh1 (db1)
         if self.compact:
             G.gemm_cobs_b(self.dh1, cobs, idx, self.xw, self.slab1, splits=self.s1)

@@ -491,6 +491,26 @@ int d1_ppo_loss(const void *h2, const void *wh, const float *bh, const int64_t *
                 const float *old_value, const double *adv_stats, double adv_count, int n, float clip, float vclip,
                 float vf_coef, float ent_coef, void *dh2, void *dh2t, int ldt, float *part, int blocks,
                 void *stream);
+/* The tail of a minibatch in one tcgen05 launch, from h1 bf16 [n, 256] (the
+ * first hidden layer as stored) to dh1: layer 2 (w2 bf16 [256, 256], b2), the
+ * head (wh bf16 [13, 256], bh), the loss and dhead exactly as d1_ppo_loss
+ * computes them (same rollout arrays, advantage statistics and coefficients),
+ * dh2 = relu'(h2) * (dhead Wh) and dh1 = relu'(h1) * (dh2 W2). Writes dh2 and
+ * dh1 bf16 [n, 256] (16-byte aligned) and d1_ppo_tail_blocks(n) block partials
+ * in d1_ppo_loss's layout (dWh, dbh, db2, loss terms) to `part`. Replaces the
+ * layer-2 GEMM, d1_ppo_loss and the dh1 GEMM of the unfused update (the
+ * reference's update: gpu-d1/scripts/run_ring_ablations.py:363-372). */
+int d1_ppo_tail(const void *h1, const void *w2, const float *b2, const void *wh, const float *bh, const int64_t *idx,
+                const uint16_t *legal, const int64_t *action, const float *old_logp, const float *adv,
+                const float *ret, const float *old_value, const double *adv_stats, double adv_count, int n,
+                float clip, float vclip, float vf_coef, float ent_coef, void *dh2, void *dh1, float *part,
+                void *stream);
+/* Block partials d1_ppo_tail writes for n rows (one per 128 rows). */
+int d1_ppo_tail_blocks(int n);
+/* Nonzero when a d1_ppo_tail launch gave up on a bounded wait (it then skipped
+ * the rest of its work and freed its tensor memory); reading clears it.
+ * Synchronises the device. */
+int d1_ppo_tail_error(void);
 /* out[i] = sum_s slabs[s * count + i] (split-K partial products, deterministic order). */
 int d1_reduce_slabs(const float *slabs, int splits, int64_t count, float *out, void *stream);
 /* A parameter segment whose bf16 compute copy the optimizer refreshes: elements

@@ -406,3 +406,48 @@ def test_update_draws_its_order_on_the_device(mods):
     assert tr.perm_epoch.item() == 4
     assert tr.graph is not None and tr.graph_perm is True
     assert np.array_equal(tr.perm.cpu().numpy(), permute_restated(tr.total, 0, 3))
+
+
+@pytest.mark.parametrize('B,T,mb', [(512, 32, 4096), (100, 10, 500)])
+def test_fused_tail_matches_the_three_launch_path(mods, B, T, mb):
+    """d1_ppo_tail (layer 2, head, loss, dh2, dh1 in one launch) against the
+    layer-2 GEMM + d1_ppo_loss + dh1 GEMM path on the same minibatch, from the
+    same parameters: the flat gradient per segment (1e-3 relative L2), the loss
+    terms (1e-5 relative), dh2 and dh1 (bf16 values computed in another
+    summation order: nearly all equal, the rest within a rounding step). 500
+    rows leave the last 128-row tile ragged."""
+    policy, ppo, rollout, spec_env = mods
+    from d1 import gemm
+    env = spec_env.SpecEnv(B, seed=5)
+    pol = policy.Policy(seed=5)
+    roll = rollout.Rollout(env, pol, T, seed=5)
+    roll.collect()
+    fused = ppo.PPO(pol, roll, minibatch=mb, epochs=1, graph=False)
+    plain = ppo.PPO(pol, roll, minibatch=mb, epochs=1, graph=False, fused_tail=False)
+    assert fused.loss_blocks == (mb + 127) // 128
+    fused.advantages()
+    plain.advantages()
+    g = torch.Generator(device='cuda').manual_seed(3)
+    idx = torch.randperm(fused.total, device='cuda', generator=g)[:mb]
+    start = pol.flat.clone()
+    out = {}
+    for name, tr in (('fused', fused), ('plain', plain)):
+        pol.flat.copy_(start)
+        pol.refresh()
+        terms = tr.minibatch(idx).clone()
+        torch.cuda.synchronize()
+        out[name] = (terms, tr.grad.clone(), tr.dh2.clone(), tr.dh1.clone())
+    assert fused.lib.d1_ppo_tail_error() == 0
+    assert gemm.gemm_error() == 0
+    (tf, gf, d2f, d1f), (tp, gp, d2p, d1p) = out['fused'], out['plain']
+    for k in range(5):
+        assert abs(tf[k].item() - tp[k].item()) <= 1e-5 * max(1.0, abs(tp[k].item())), (k, tf[k].item(), tp[k].item())
+    off = fused.off
+    for name, size in [('w1', 256 * 1832), ('b1', 256), ('w2', 256 * 256), ('b2', 256), ('wh', 13 * 256),
+                       ('bh', 13)]:
+        e = rel(gf[off[name]:off[name] + size], gp[off[name]:off[name] + size])
+        assert e < 1e-3, (name, e)
+    for a, b in ((d2f, d2p), (d1f, d1p)):
+        a, b = a.float(), b.float()
+        assert (a == b).float().mean().item() > 0.99
+        assert (a - b).abs().max().item() <= 2e-2 * b.abs().max().item()
