@@ -64,7 +64,7 @@ class PPO:
     def __init__(self, policy, rollout, minibatch=16384, epochs=4, lr=3e-4, clip=0.2, vclip=0.2, vf_coef=0.5,
                  ent_coef=0.01, max_grad_norm=0.5, gamma=0.999, lam=0.95, adam_eps=1e-5, betas=(0.9, 0.999),
                  gae_mode=1, splits=8, group=None, graph=True, peer=True, compact=True, peer_wait_limit=0,
-                 exchange='auto', splits2=None, perm_seed=0, fused_tail=True):
+                 exchange='auto', splits2=None, perm_seed=0, fused_tail=True, dw2_stream=True):
         self.policy, self.rollout = policy, rollout
         self.fused_tail = fused_tail  # layer 2 + loss + dh1 as one launch (d1_ppo_tail)
         self.perm_seed = perm_seed  # key of the epoch permutation (with the device epoch count)
@@ -104,9 +104,11 @@ class PPO:
         self.dh1 = torch.empty((mb, HID), **bf)
         self.s1 = G.splits_for(mb, splits)
         self.slab1 = torch.empty((self.s1, HID, self.xw), **f32)
-        # dW2 is 256 x 256: its output has only 2 tiles, so it needs 8x the K splits
-        # of dW1 (2 x 8 tiles) to put ~128 CTAs to work
-        self.s2 = G.splits_for(mb, splits * 8 if splits2 is None else splits2)
+        # dW2 is 256 x 256: one 2-SM tile. Alone it needs 8x the K splits of dW1
+        # to put ~128 CTAs to work; on its own stream beside dW1 (whose 64 CTA
+        # pairs leave 20 SMs idle) 8 splits = 16 CTAs run in those gaps.
+        self.side = torch.cuda.Stream(dev) if dw2_stream else None
+        self.s2 = G.splits_for(mb, (splits if dw2_stream else splits * 8) if splits2 is None else splits2)
         self.slab2 = torch.empty((self.s2, HID, HID), **f32)
         self.part_len = self.lib.d1_ppo_loss_part_len()
         if fused_tail:
@@ -244,8 +246,6 @@ class PPO:
                                   self.ret.data_ptr(), r.values.data_ptr(), self.stats.data_ptr(), self.adv_count,
                                   mb, self.clip, self.vclip, self.vf_coef, self.ent_coef, self.dh2.data_ptr(),
                                   self.dh1.data_ptr(), self.part.data_ptr(), s), 'd1_ppo_tail')
-            # dW2 = dh2^T h1
-            G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
         else:
             G.gemm(self.h1, p.bf16['w2'], bias=p.params['b2'], relu=True, out=self.h2)
             check(lib.d1_ppo_loss(self.h2.data_ptr(), p.bf16['wh'].data_ptr(), p.params['bh'].data_ptr(),
@@ -254,15 +254,23 @@ class PPO:
                                   self.stats.data_ptr(), self.adv_count, mb, self.clip, self.vclip, self.vf_coef,
                                   self.ent_coef, self.dh2.data_ptr(), None, mb, self.part.data_ptr(),
                                   self.loss_blocks, s), 'd1_ppo_loss')
-            # dW2 = dh2^T h1
-            G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
             # dh1 = (dh2 W2) * relu'(h1)
             G.gemm(self.dh2, p.bf16['w2t'], mask=self.h1, out=self.dh1)
+        # dW2 = dh2^T h1, beside dW1 when it has its own stream
+        main = torch.cuda.current_stream(p.device)
+        if self.side is not None:
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
+        else:
+            G.gemm_ex(self.dh2, self.h1, a_kn=True, b_kn=True, out_f32=self.slab2, splits=self.s2)
         # dW1 = dh1^T X; X's ones column makes slab column 1832 the column sums of dh1 (db1)
         if self.compact:
             G.gemm_cobs_b(self.dh1, cobs, idx, self.xw, self.slab1, splits=self.s1)
         else:
             G.gemm_ex(self.dh1, self.x, a_kn=True, b_kn=True, out_f32=self.slab1, splits=self.s1)
+        if self.side is not None:
+            main.wait_stream(self.side)
         jobs, njobs = self.jobs, len(self.jobs)
         if self.peer is not None:
             pr = self.peer
