@@ -42,6 +42,8 @@ SIGNATURES = {
     'd1_ppo_tail': [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_double, _I, _F, _F, _F, _F, _P, _P, _P, _P],
     'd1_ppo_tail_blocks': [_I],
     'd1_ppo_tail_error': [],
+    'd1_policy_tail_sample': [_P, _I, _I, _P, _P, _P, _P, _P, C.c_uint64, C.c_uint64, _P, _I, _P, _P, _P, _P, _P],
+    'd1_policy_tail_error': [],
     'd1_gemm_splits': [_I, _I],
     'd1_gemm_bkn': [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _I, _P],
     'd1_gemm_rows': [_P, _I, _I, _P, _I, _P, _I, _I, _P, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P],

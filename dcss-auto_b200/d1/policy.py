@@ -30,8 +30,10 @@ def layout(obs=OBS, hidden=HID):
 
 
 class Policy:
-    def __init__(self, device='cuda', seed=0, obs=OBS, hidden=HID):
+    def __init__(self, device='cuda', seed=0, obs=OBS, hidden=HID, tail=True):
         self.device = resolve_device(device)
+        # act() and value() run layer 2, the head and the draw as one fused kernel
+        self.tail = tail and hidden == HID
         self.obs, self.hidden = obs, hidden
         self.layout, self.size = layout(obs, hidden)
         self.flat = torch.zeros(self.size, device=self.device)
@@ -107,24 +109,43 @@ class Policy:
 
     def act(self, obs, legal, seed, step, first_env=0, action=None, logp=None, value=None, logits=None, part=0,
             h1=None, h2=None):
-        """Forward + sample: two tcgen05 GEMMs, then the head + sampler kernel.
-        Writes into the given buffers (allocated if None). `part` selects the
-        policy's cached activation buffers, so that parts of a batch can run on
+        """Forward + sample: layer 1 on the tcgen05 pair GEMM, then layer 2, the
+        head and the draw in one persistent kernel (d1_policy_tail_sample; with
+        tail=False: the layer-2 GEMM and the head + sampler kernel). Writes into
+        the given buffers (allocated if None). `part` selects the policy's
+        cached activation buffers, so that parts of a batch can run on
         different streams at the same time; a caller that captures this call in
         a CUDA graph passes its own h1/h2 ([n, hidden] bf16) instead, because the
         cached buffers are reallocated when a later call needs more rows."""
         n = obs.shape[0]
         h1 = self._h1_buffer(n, part) if h1 is None else h1
-        h2 = self._h2_buffer(n, part) if h2 is None else h2
-        _, h2 = self.hidden_layers(obs, h1=h1, h2=h2)
         if action is None:
             action = torch.empty(n, dtype=torch.int64, device=self.device)
         if logp is None:
             logp = torch.empty(n, device=self.device)
         if value is None:
             value = torch.empty(n, device=self.device)
-        self.head(h2, legal, seed, step, first_env, action, logp, value, logits)
+        if self.tail:
+            gemm.gemm(obs, self.bf16['w1'], bias=self.params['b1'], relu=True, out=h1)
+            self.tail_sample(h1, legal, seed, step, first_env, action, logp, value, logits)
+        else:
+            h2 = self._h2_buffer(n, part) if h2 is None else h2
+            self.hidden_layers(obs, h1=h1, h2=h2)
+            self.head(h2, legal, seed, step, first_env, action, logp, value, logits)
         return action, logp, value
+
+    def tail_sample(self, h1, legal, seed, step, first_env, action, logp, value, logits=None):
+        """Layer 2 + head + draw from h1 (d1_policy_tail_sample). `step` is an int
+        or an int64 device tensor of one element read when the kernel runs;
+        action None: value (and logits) only."""
+        dev_step = isinstance(step, torch.Tensor)
+        ptr = lambda t: None if t is None else t.data_ptr()
+        check(self.lib.d1_policy_tail_sample(h1.data_ptr(), h1.shape[0], h1.stride(0), self.bf16['w2'].data_ptr(),
+                                             self.params['b2'].data_ptr(), self.bf16['wh'].data_ptr(),
+                                             self.params['bh'].data_ptr(), ptr(legal), seed,
+                                             0 if dev_step else step, step.data_ptr() if dev_step else None,
+                                             first_env, ptr(action), ptr(logp), value.data_ptr(), ptr(logits),
+                                             launch_stream(self.device)), 'd1_policy_tail_sample')
 
     def act_fused(self, obs, legal, seed, step, first_env=0, action=None, logp=None, value=None, logits=None):
         """The same draw with layer 2, the head and the sampler in one GEMM
@@ -155,8 +176,15 @@ class Policy:
         return self._buffer('h1', n, part)
 
     def value(self, obs, out=None):
+        """The value head alone (the rollout's bootstrap), by the same kernels
+        as act() so that both agree bit for bit."""
         n = obs.shape[0]
-        _, h2 = self.hidden_layers(obs, h1=self._h1_buffer(n), h2=self._h2_buffer(n))
         value = torch.empty(n, device=self.device) if out is None else out
+        if self.tail:
+            h1 = self._h1_buffer(n)
+            gemm.gemm(obs, self.bf16['w1'], bias=self.params['b1'], relu=True, out=h1)
+            self.tail_sample(h1, None, 0, 0, 0, None, None, value)
+            return value
+        _, h2 = self.hidden_layers(obs, h1=self._h1_buffer(n), h2=self._h2_buffer(n))
         self.head(h2, None, 0, 0, 0, None, None, value)
         return value

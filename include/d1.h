@@ -276,6 +276,22 @@ int d1_spec_crop(const void *state, int n, int g, uint16_t *crop, void *stream);
 int d1_policy_head_sample(const void *h_bf16, int n, int hidden, const void *wh_bf16, const float *bh,
                           const uint16_t *legal, uint64_t seed, uint64_t step, int first_env, int64_t *action,
                           float *logp, float *value, float *logits, void *stream);
+/* Layer 2, the head and the draw in one persistent tcgen05 launch, from h1
+ * bf16 [n, 256] (row pitch ldh elements, 16-byte aligned) as layer 1 leaves
+ * it: h2 = relu(h1 W2^T + b2) (w2 bf16 [256, 256]), logits and value = h2
+ * Wh^T + bh (wh bf16 [13, 256]), then the masked draw of
+ * d1_policy_head_sample (same Philox counter: first_env + row, seed, step;
+ * the step is *step_dev when step_dev is not NULL, read when the kernel runs).
+ * action NULL: value (and logits) only. Replaces d1_gemm (layer 2) +
+ * d1_policy_head_sample, the reference's policy forward and
+ * Categorical(logits).sample() (gpu-d1/scripts/run_ring_ablations.py:350). */
+int d1_policy_tail_sample(const void *h1, int n, int ldh, const void *w2, const float *b2, const void *wh,
+                          const float *bh, const uint16_t *legal, uint64_t seed, uint64_t step,
+                          const int64_t *step_dev, int first_env, int64_t *action, float *logp, float *value,
+                          float *logits, void *stream);
+/* Nonzero when a d1_policy_tail_sample launch gave up on a bounded wait;
+ * reading clears it. Synchronises the device. */
+int d1_policy_tail_error(void);
 /* As d1_policy_head_sample with the step read from device memory (*step_dev)
  * when the kernel runs, so a captured CUDA graph that also advances the counter
  * (d1_counter_add) draws fresh uniforms on every replay. */

@@ -155,3 +155,36 @@ def test_rollout_on_two_streams_equals_one_stream():
     for name in ('obs', 'cobs', 'legal', 'actions', 'logp', 'values', 'out'):
         assert torch.equal(getattr(one, name), getattr(two, name)), name
     assert torch.equal(one.env.state, two.env.state)
+
+
+@pytest.mark.parametrize('n', [65536, 1000])
+def test_policy_tail_matches_the_unfused_path_and_the_oracle(lib, n):
+    """d1_policy_tail_sample (layer 2, head and draw in one persistent launch)
+    against the layer-2 GEMM + head kernel on the same observations: logits and
+    value within 1e-5 (another summation order), draws exact against the oracle
+    given the kernel's own logits, the same action as the unfused path for
+    nearly every row; the device-step form equals the host-step form, and
+    value() equals act()'s value bit for bit."""
+    from d1.policy import Policy
+    from d1.spec_env import SpecEnv
+    env = SpecEnv(n, seed=2)
+    pol, plain = Policy(seed=3), Policy(seed=3, tail=False)
+    assert pol.tail and not plain.tail
+    lt = torch.empty((n, 12), device='cuda')
+    lu = torch.empty((n, 12), device='cuda')
+    ta, tlp, tv = pol.act(env.obs, env.legal, 11, 5, 7, logits=lt)
+    ua, ulp, uv = plain.act(env.obs, env.legal, 11, 5, 7, logits=lu)
+    torch.cuda.synchronize()
+    assert torch.allclose(lt, lu, rtol=1e-5, atol=1e-5)
+    assert torch.allclose(tv, uv, rtol=1e-5, atol=1e-5)
+    legal = env.legal.cpu().numpy().view(np.uint16)
+    ora, olp = oracle.sample_actions(lt.cpu().numpy(), legal, 11, 5, 7)
+    assert np.array_equal(ta.cpu().numpy(), ora)
+    assert np.allclose(tlp.cpu().numpy(), olp, rtol=1e-5, atol=1e-5)
+    assert (ta == ua).float().mean().item() > 0.999
+    da, dlp, dv = pol.act(env.obs, env.legal, 11, torch.tensor([5], dtype=torch.int64, device='cuda'), 7)
+    vals = pol.value(env.obs)
+    torch.cuda.synchronize()
+    assert torch.equal(da, ta) and torch.equal(dlp, tlp) and torch.equal(dv, tv)
+    assert torch.equal(vals, tv)
+    assert lib.d1_policy_tail_error() == 0
