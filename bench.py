@@ -865,8 +865,10 @@ def run_kernels(args):
     rollout of synthetic rewards and dones in the rollout's plane layout
     (gae_scan_kernel) and one route-cue env step of B envs on a 16-map
     corpus (d1::route::step_kernel, after 8 warm-up steps and their heuristic
-    launches). A `gemm` regex therefore sees 18 launches in the rollout and 7
-    per pass; `tail_kernel` one per pass; `gae_scan` one before the passes
+    launches), and last the fused rollout policy (policy_tail_kernel: layer 2,
+    head and draw from the pass's h1). A `gemm` regex therefore sees 18
+    launches in the rollout and 7 per pass; `tail_kernel` (the PPO tail) one
+    per pass; `policy_tail` one per pass; `gae_scan` one before the passes
     (the setup's, T = 8) and two per pass (T = 8, then T = 128); `route.*step`
     8 before the passes and one per pass."""
     import torch
@@ -879,7 +881,10 @@ def run_kernels(args):
     torch.cuda.set_device(0)
     B = args.envs
     env = SpecEnv(B, seed=1)
-    pol = Policy(seed=0)
+    # the unfused layer 2 + head in the rollout part, so that the launch order
+    # (and the -s offsets of the captures summarised in profiles/) stays fixed;
+    # the fused policy tail runs once at the end of every pass
+    pol = Policy(seed=0, tail=False)
     roll = Rollout(env, pol, 8, seed=1, parts=1)  # one stream: the launch order below is fixed
     roll.collect()
     tr = PPO(pol, roll, minibatch=args.minibatch, epochs=1, graph=False)
@@ -920,6 +925,7 @@ def run_kernels(args):
                          128, B, 0.999, 0.95, gae_adv.data_ptr(), gae_ret.data_ptr(), gae_stats.data_ptr(), 1,
                          torch.cuda.current_stream().cuda_stream), 'd1_gae')
         renv.step(renv.heuristic().clone())
+        pol.tail_sample(h1, env.legal, 1, rep, 0, act, lp, val)
         torch.cuda.synchronize()
 
 
