@@ -59,7 +59,7 @@ def parse():
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-ppo', action='store_true', help='skip the PPO-update measurement')
     ap.add_argument('--minibatch', type=int, default=16384)
-    ap.add_argument('--exchange', choices=('auto', 'oneshot', 'twophase'), default='auto',
+    ap.add_argument('--exchange', choices=('auto', 'oneshot', 'twophase', 'nvls'), default='auto',
                     help='peer gradient exchange of the PPO update on several GPUs')
     ap.add_argument('--epochs', type=int, default=4)
     ap.add_argument('--no-cpu', action='store_true')
@@ -690,8 +690,7 @@ def run_ours(args, rank, world, local_rank):
         peer_error = trainer.lib.d1_peer_error() if trainer.peer is not None else 0
         exchange = None
         if world > 1:
-            exchange = 'NCCL' if trainer.peer is None else (
-                'peer memory (NVLink), two-phase' if trainer.peer['two_phase'] else 'peer memory (NVLink), one-shot')
+            exchange = exchange_label(trainer)
         trainer.release()  # graph and exchange buffers go before the process group does
         it_ms = torch.tensor([p0.elapsed_time(p3)], device=dev)
         if world > 1:
@@ -784,8 +783,7 @@ def run_ours(args, rank, world, local_rank):
         peer_error4 = tr4.lib.d1_peer_error() if tr4.peer is not None else 0
         exchange4 = None
         if world > 1:
-            exchange4 = 'NCCL' if tr4.peer is None else (
-                'peer memory (NVLink), two-phase' if tr4.peer['two_phase'] else 'peer memory (NVLink), one-shot')
+            exchange4 = exchange_label(tr4)
         tr4.release()
         t_it = torch.tensor([q0.elapsed_time(q2), q0.elapsed_time(q1)], device=dev)
         if world > 1:
@@ -847,6 +845,16 @@ def run_ours(args, rank, world, local_rank):
                                 'sample': f'8192 envs x decisions {args.warmup}-{args.warmup + args.steps} of the '
                                           f'same workload ({dt:.1f} s)'}
     print(json.dumps(line), flush=True)
+
+
+def exchange_label(trainer):
+    """How a multi-GPU trainer exchanged its gradients."""
+    pr = trainer.peer
+    if pr is None:
+        return 'NCCL'
+    if pr.get('mc'):
+        return 'peer memory (NVLink), one-shot read through NVLS multicast'
+    return 'peer memory (NVLink), two-phase' if pr['two_phase'] else 'peer memory (NVLink), one-shot'
 
 
 def run_kernels(args):

@@ -1126,12 +1126,15 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
             last = atomicAdd(&g_peer_ticket, 1u) == gridDim.x - 1;
         }
         __syncthreads();
-        if (last && threadIdx.x == 0) {
-            g_peer_ticket = 0;
+        if (last && threadIdx.x < 32) {
+            // one system-scope fence, then lane p raises peer p's flag (a fence
+            // followed by relaxed stores is a release of everything before it)
+            if (threadIdx.x == 0) g_peer_ticket = 0;
             __threadfence_system();
-            for (int p = 0; p < a.world; p++)
-                if (p != a.rank)
-                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.peer_flags[p] + a.rank), "l"(epoch)
+#pragma unroll
+            for (int p = 0; p < PEER_MAX; p++)  // static indices: the flag pointers stay in the parameter space
+                if (p == (int)threadIdx.x && p < a.world && p != a.rank)
+                    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a.peer_flags[p] + a.rank), "l"(epoch)
                                  : "memory");
         }
     }
@@ -1156,6 +1159,10 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant_
 // the Adam launch that follows then changes nothing.
 struct PeerArgs {
     const float *xbuf[PEER_MAX];  // each rank's exchange buffer (this rank's is local)
+    // NVLS: the exchange buffers' multicast address; when set, each block reads
+    // the sum over the ranks with multimem.ld_reduce (the switch adds) instead
+    // of reading every peer's buffer
+    const float *mc;
     int64_t xstride;
     const unsigned long long *flags;  // this rank's flag array, written by the peers
     const int64_t *epoch_src;
@@ -1199,13 +1206,28 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_consta
         const int64_t q0 = (int64_t)blockIdx.x * per, q1 = q0 + per < n4 ? q0 + per : n4;
         const float inv = (float)a.world;
         for (int64_t q = q0 + threadIdx.x; q < q1; q += blockDim.x) {
-            float4 t = __ldcv(reinterpret_cast<const float4 *>(a.xbuf[0] + half) + q);
-            for (int r = 1; r < a.world; r++) {
-                const float4 v = __ldcv(reinterpret_cast<const float4 *>(a.xbuf[r] + half) + q);
-                t.x += v.x;
-                t.y += v.y;
-                t.z += v.z;
-                t.w += v.w;
+            float4 t;
+            if (a.mc) {
+                asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                             : "=f"(t.x), "=f"(t.y), "=f"(t.z), "=f"(t.w)
+                             : "l"(reinterpret_cast<const float4 *>(a.mc + half) + q)
+                             : "memory");
+            } else {
+                // every rank's value is loaded before the first add (one NVLink
+                // round trip, not one per rank); the adds keep rank order
+                float4 v[PEER_MAX];
+#pragma unroll
+                for (int r = 0; r < PEER_MAX; r++)
+                    if (r < a.world) v[r] = __ldcv(reinterpret_cast<const float4 *>(a.xbuf[r] + half) + q);
+                t = v[0];
+#pragma unroll
+                for (int r = 1; r < PEER_MAX; r++)
+                    if (r < a.world) {
+                        t.x += v[r].x;
+                        t.y += v[r].y;
+                        t.z += v[r].z;
+                        t.w += v[r].w;
+                    }
             }
             const float f[4] = {__fdiv_rn(t.x, inv), __fdiv_rn(t.y, inv), __fdiv_rn(t.z, inv), __fdiv_rn(t.w, inv)};
 #pragma unroll
@@ -1505,6 +1527,7 @@ struct PeerSetup {
     int64_t xstride;  // one-shot: half length; two-phase: slice length
     int world, rank;
     int two_phase;
+    const void *mc;   // one-shot over NVLS: the exchange buffers' multicast address
 };
 
 static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
@@ -1560,6 +1583,7 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
             pa.xbuf[i] = (const float *)peer->xbufs[i];
         }
         pa.xstride = peer->xstride;
+        pa.mc = (const float *)peer->mc;
         pa.flags = (const unsigned long long *)peer->flags[peer->rank];
         pa.epoch_src = step;
         pa.grad = grad;
@@ -1635,6 +1659,16 @@ int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad
                      const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
                      int world, int rank, unsigned wait_limit, void *stream) {
     const PeerSetup peer{xbufs, flags, xstride, world, rank, 0};
+    return step_launch(jobs, njobs, param, grad, m, v, total, lr, beta1, beta2, eps, max_norm, step, segs, nseg, 1,
+                       stream, &peer, wait_limit);
+}
+
+int d1_ppo_step_nvls(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                     float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
+                     const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
+                     const void *mc, int world, int rank, unsigned wait_limit, void *stream) {
+    if (!mc || (reinterpret_cast<uintptr_t>(mc) & 15)) return D1_ERR_BAD_ARGUMENT;
+    const PeerSetup peer{xbufs, flags, xstride, world, rank, 0, mc};
     return step_launch(jobs, njobs, param, grad, m, v, total, lr, beta1, beta2, eps, max_norm, step, segs, nseg, 1,
                        stream, &peer, wait_limit);
 }

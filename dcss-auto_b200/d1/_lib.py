@@ -58,6 +58,8 @@ SIGNATURES = {
                          _I, C.c_uint, _P],
     'd1_ppo_step_peer2': [_P, _I, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _P, _P, _I, _P, _P, C.c_int64, _I,
                           _I, C.c_uint, _P],
+    'd1_ppo_step_nvls': [_P, _I, _P, _P, _P, _P, C.c_int64, _F, _F, _F, _F, _F, _P, _P, _I, _P, _P, C.c_int64, _P,
+                         _I, _I, C.c_uint, _P],
     'd1_peer_handle_bytes': [],
     'd1_peer_alloc': [C.c_int64, _P, _P],
     'd1_peer_open': [_P, _P],

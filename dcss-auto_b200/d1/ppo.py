@@ -69,8 +69,8 @@ class PPO:
         self.fused_tail = fused_tail  # layer 2 + loss + dh1 as one launch (d1_ppo_tail)
         self.perm_seed = perm_seed  # key of the epoch permutation (with the device epoch count)
         self.peer_wait_limit = peer_wait_limit  # polls per flag wait; 0 = the library default (~1 s)
-        if exchange not in ('auto', 'oneshot', 'twophase'):
-            raise ValueError("exchange must be 'auto', 'oneshot' or 'twophase'")
+        if exchange not in ('auto', 'oneshot', 'twophase', 'nvls'):
+            raise ValueError("exchange must be 'auto', 'oneshot', 'twophase' or 'nvls'")
         self.exchange = exchange
         self.compact = compact
         self.mb, self.epochs = minibatch, epochs
@@ -151,6 +151,9 @@ class PPO:
         lib, world, rank = self.lib, dist.get_world_size(group), dist.get_rank(group)
         if world > 8:
             raise ValueError('the peer all-reduce supports up to 8 ranks')
+        if self.exchange == 'nvls':
+            self._nvls_setup(group, world, rank)
+            return
         P = self.grad.numel()
         self.xstride = (P + 3) // 4 * 4
         flag_off = 2 * self.xstride * 4
@@ -170,6 +173,26 @@ class PPO:
         self.peer_attach(world, rank, ptrs)
         self.peer['base'] = base.value
 
+    def _nvls_setup(self, group, world, rank):
+        """The exchange buffer as torch symmetric memory bound to an NVLink
+        multicast object: the one-shot layout (two gradient halves, flags),
+        peer pointers for the flags, and the multicast address the all-reduce
+        reads the summed gradient through (multimem.ld_reduce)."""
+        import torch.distributed._symmetric_memory as symm
+        dev = self.policy.device
+        self.exchange_nvls = True
+        nbytes = self.peer_bytes(world)
+        buf = symm.empty((nbytes + 15) // 16 * 4, dtype=torch.float32, device=dev)
+        buf.zero_()
+        torch.cuda.synchronize(dev)
+        hdl = symm.rendezvous(buf, group)
+        mc = int(getattr(hdl, 'multicast_ptr', 0) or 0)
+        if not mc:
+            raise D1Error('exchange="nvls": this system gives the exchange buffer no NVLink multicast address')
+        self.peer_attach(world, rank, [int(p) for p in hdl.buffer_ptrs])
+        self.peer['mc'] = mc
+        self.peer['symm'] = (buf, hdl)  # keeps the mapping alive
+
     def two_phase(self, world):
         """Whether the peer exchange of `world` ranks is the two-phase one
         (each rank reduces a slice, then gathers) rather than the one-shot
@@ -177,7 +200,7 @@ class PPO:
         one-shot exchange: measured on 8 B200s, a minibatch took 0.194 ms with
         it and 0.199 ms with the two-phase one (2 GPUs: 0.153 and 0.168 ms);
         the extra flag round costs more than the smaller transfer saves."""
-        return self.exchange == 'twophase'
+        return self.exchange == 'twophase' and not getattr(self, 'exchange_nvls', False)
 
     def _peer_layout(self, world):
         """(stride, flag offset in bytes): one-shot -- two halves of the flat
@@ -272,6 +295,14 @@ class PPO:
         if self.side is not None:
             main.wait_stream(self.side)
         jobs, njobs = self.jobs, len(self.jobs)
+        if self.peer is not None and self.peer.get('mc'):
+            pr = self.peer
+            check(lib.d1_ppo_step_nvls(jobs, njobs, p.flat.data_ptr(), g.data_ptr(), self.m.data_ptr(),
+                                       self.v.data_ptr(), g.numel(), self.lr, self.betas[0], self.betas[1], self.eps,
+                                       self.max_grad_norm, self.step_dev.data_ptr(), self.segs, len(self.segs),
+                                       pr['xbufs'], pr['flags'], self.xstride, C.c_void_p(pr['mc']), pr['world'],
+                                       pr['rank'], self.peer_wait_limit, s), 'd1_ppo_step_nvls')
+            return self.terms
         if self.peer is not None:
             pr = self.peer
             fn = lib.d1_ppo_step_peer2 if pr['two_phase'] else lib.d1_ppo_step_peer

@@ -592,6 +592,16 @@ int d1_ppo_step_peer(const D1GradJob *jobs, int njobs, float *param, float *grad
                      float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
                      const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
                      int world, int rank, unsigned wait_limit, void *stream);
+/* d1_ppo_step_peer over NVLink SHARP (NVLS): the exchange buffers are bound to
+ * one multicast object whose address is `mc` (the same offset maps every
+ * rank's buffer), and after the bounded flag waits each block reads its range
+ * of the summed gradient with multimem.ld_reduce -- the NVSwitch adds the
+ * ranks' values -- instead of reading the N - 1 peer buffers. Publishing,
+ * flags, the skip-on-timeout rule and Adam are those of d1_ppo_step_peer. */
+int d1_ppo_step_nvls(const D1GradJob *jobs, int njobs, float *param, float *grad, float *m, float *v, int64_t total,
+                     float lr, float beta1, float beta2, float eps, float max_norm, int64_t *step,
+                     const D1AdamSegment *segs, int nseg, void *const *xbufs, void *const *flags, int64_t xstride,
+                     const void *mc, int world, int rank, unsigned wait_limit, void *stream);
 /* d1_ppo_step_peer with a two-phase exchange, for more ranks: rank j owns
  * slice j of the flat gradient (`slice` elements, a multiple of 4, slice *
  * world >= total). (1) The reduction stores this rank's part of every slice j
