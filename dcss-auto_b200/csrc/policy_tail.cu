@@ -189,6 +189,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         int i = 0;
         for (int t = blockIdx.x; t < a.tiles; t += gridDim.x, i++) {
             const uint32_t par = (uint32_t)i & 1u;
+            const int grow = t * ROWS + row;
+            // this row's legal mask, loaded now so its latency hides behind layer 2
+            const uint32_t bits = (half == 0 && grow < a.n && a.legal) ? (uint32_t)a.legal[grow] : 0xfffu;
             // h2 = relu(acc + b2) as bf16 into the tile
             ok = mbar_wait(bar_acc, par, WAIT_LIMIT) && !*abort_s;
             if (ok) {
@@ -222,7 +225,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 uint32_t v[16];
                 D1X_TMEM_LD16(tmem + lanes + D_HEAD, v);
                 tmem_wait_ld();
-                const int grow = t * ROWS + row;
                 if (grow < a.n) {
                     float l[NOUT];
 #pragma unroll
@@ -235,8 +237,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (a.action) {
                         int act;
                         float lp;
-                        sample_masked(l, a.legal ? (uint32_t)a.legal[grow] : 0xfffu, (uint32_t)(a.first_env + grow),
-                                      a.seed, step, false, act, lp);
+                        sample_masked(l, bits, (uint32_t)(a.first_env + grow), a.seed, step, false, act, lp);
                         a.action[grow] = act;
                         if (a.logp) a.logp[grow] = lp;
                     }
