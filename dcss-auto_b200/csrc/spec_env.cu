@@ -684,14 +684,19 @@ __device__ int adjacent_attack(const Env &e) {
     return key == 0xffffffffu ? -1 : (int)(key & 7u);
 }
 
+// saw_awake (tracked only when `watch`, i.e. inside a rest macro): an awake
+// monster was in view at some point of the turn -- after the player's move, after
+// any monster's action, or at its end; the rest macro's interrupt signal
+// (semantic-actions-v1 learn.cu:680-681,708,729,819).
 struct Prim {
     float reward;
-    bool done, descended, death, timeout;
+    bool done, descended, death, timeout, saw_awake;
 };
 
 // One physical turn (learn.cu:505-598 with the sleep/explore/stairs variants).
-__device__ Prim primitive(Env &e, const D1SpecConfig &c, const RayArgs &ra, int extra_layers, int d) {
+__device__ Prim primitive(Env &e, const D1SpecConfig &c, const RayArgs &ra, int extra_layers, int d, bool watch) {
     Prim r;
+    r.saw_awake = false;
     int reward_milli = -1;
     e.blocks = 0;
     e.regen += c.regen;
@@ -724,6 +729,7 @@ __device__ Prim primitive(Env &e, const D1SpecConfig &c, const RayArgs &ra, int 
     }
     const bool descended = d == PRIM_DESCEND && e.player == e.stairs && e.hp > 0;
     reward_milli += c.explore_milli * reveal(e);
+    if (watch) r.saw_awake = visible_awake(e);
     if (!descended) {
         const bool alive = e.lane < e.nmon && e.m_hp > 0;
         if (alive && !e.m_awake && cheb(e.m_pos, e.player) <= 6 && visible(e, e.m_pos)) {
@@ -743,6 +749,7 @@ __device__ Prim primitive(Env &e, const D1SpecConfig &c, const RayArgs &ra, int 
             const int id = scan_ready(e.m_energy, e.lane, e.nmon);
             if (id < 0) break;
             act(e, c, id);
+            if (watch && __any_sync(FULL, e.lane == id && e.m_awake && visible(e, e.m_pos))) r.saw_awake = true;
         }
     }
     e.ticks++;
@@ -754,11 +761,13 @@ __device__ Prim primitive(Env &e, const D1SpecConfig &c, const RayArgs &ra, int 
     r.descended = descended;
     r.death = death;
     r.timeout = timeout;
+    if (watch && !r.saw_awake) r.saw_awake = visible_awake(e);
     return r;
 }
 
 // Semantic decision: 0-7 move/attack, 8 wait, 9 rest (repeat waits until full
-// HP, an awake monster in view, or the end), 10 attack the weakest visible
+// HP, an awake monster in view during a turn, or the end; semantic-actions-v1
+// learn.cu:803-826), 10 attack the weakest visible
 // adjacent monster, 11 descend. Illegal actions cost one wait turn.
 // Returns out[lane] for lane < OUT.
 __device__ float decision(Env &e, const D1SpecConfig &c, const RayArgs &ra, int extra_layers, int a) {
@@ -782,11 +791,11 @@ __device__ float decision(Env &e, const D1SpecConfig &c, const RayArgs &ra, int 
             else invalid = true;
         } else
             invalid = true;
-        r = primitive(e, c, ra, extra_layers, d);
+        r = primitive(e, c, ra, extra_layers, d, a == 9);
         elapsed++;
         total += r.reward;
         if (r.done || invalid || a != 9) break;
-        if (e.hp >= c.hp || visible_awake(e)) break;
+        if (r.saw_awake || e.hp >= c.hp) break;
     }
     float o = 0.f;
     switch (e.lane) {

@@ -920,7 +920,10 @@ static int spec_scan(const Spec *s) {
 }
 
 enum { PRIM_WAIT = 8, PRIM_DESCEND = 9 };
-typedef struct { float reward; int done, descended, death, timeout; } Prim;
+/* saw_awake: an awake monster was in view at some point of the turn -- after the
+ * player's move, after any monster's action, or at its end (the interrupt signal
+ * of the reference's rest macro, semantic-actions-v1 learn.cu:680-681,708,729,819). */
+typedef struct { float reward; int done, descended, death, timeout, saw_awake; } Prim;
 
 /* One physical turn: learn.cu:505-598 with the sleep/exploration variants of
  * semantic-actions-v1 learn.cu:638-730 and the stairs clear of d1-stairs-v2. */
@@ -956,6 +959,7 @@ static Prim spec_primitive(Spec *s, const D1SpecConfig *c, int d) {
     }
     int descended = d == PRIM_DESCEND && s->player == s->stairs && s->hp > 0;
     reward_milli += c->explore_milli * spec_reveal(s);
+    r.saw_awake = s_visible_awake(s);
     if (!descended) {
         for (int i = 0; i < s->nmon; i++)
             if (s->mhp[i] > 0 && !s->awake[i] && cheb(s->pos[i], s->player) <= 6 && s_visible(s, s->pos[i])) {
@@ -971,6 +975,7 @@ static Prim spec_primitive(Spec *s, const D1SpecConfig *c, int d) {
             int id = spec_scan(s);
             if (id < 0) break;
             spec_act(s, c, dist, id);
+            if (s->awake[id] && s_visible(s, s->pos[id])) r.saw_awake = 1;
         }
     }
     s->ticks++;
@@ -982,13 +987,15 @@ static Prim spec_primitive(Spec *s, const D1SpecConfig *c, int d) {
     r.descended = descended;
     r.death = death;
     r.timeout = timeout;
+    r.saw_awake |= s_visible_awake(s);
     return r;
 }
 
 /* Actions: 0-7 move/attack N,E,S,W,NE,SE,SW,NW; 8 wait; 9 rest; 10 attack the
  * weakest visible adjacent monster; 11 descend. An action that is not legal
  * becomes one wait turn and is flagged invalid. REST repeats wait turns until HP
- * is full, an awake monster is in view, or the episode ends. */
+ * is full, an awake monster was in view during a turn, or the episode ends
+ * (semantic-actions-v1 learn.cu:803-826). */
 static void spec_decision(Spec *s, const D1SpecConfig *c, int a, float *out) {
     float total = 0.f;
     int elapsed = 0, invalid = 0;
@@ -1013,7 +1020,7 @@ static void spec_decision(Spec *s, const D1SpecConfig *c, int a, float *out) {
         elapsed++;
         total += r.reward;
         if (r.done || invalid || a != 9) break;
-        if (s->hp >= c->hp || s_visible_awake(s)) break;
+        if (r.saw_awake || s->hp >= c->hp) break;
     }
     out[0] = total;
     out[1] = (float)r.done;
@@ -1149,6 +1156,10 @@ int oracle_spec_observe(const void *states, int n, const D1SpecConfig *c, float 
     for (int i = 0; i < n; i++) spec_observe(&s[i], c, obs + (size_t)i * OSPEC_OBS, legal + i);
     return 0;
 }
+
+/* Rule hook for tests: the direction attack-nearest would strike from this
+ * state (-1 when no visible monster is adjacent). */
+int oracle_spec_attack_dir(const void *state) { return s_adjacent_attack((const Spec *)state); }
 
 int oracle_spec_compact(const void *states, int n, int64_t *rows) {
     const Spec *s = (const Spec *)states;

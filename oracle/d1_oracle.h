@@ -83,6 +83,7 @@ int oracle_spec_observe(const void *states, int n, const D1SpecConfig *c, float 
 /* 56 x int64 per env: ctr, env, episode, hp, regen, blocks, player, ticks, killed,
  * stairs, nmon, floor_seen, then pos[11], energy[11], hp[11], kind*2+awake [11].
  */
+int oracle_spec_attack_dir(const void *state);
 int oracle_spec_compact(const void *states, int n, int64_t *rows);
 /* Copies the floor and remembered (viewed) bit planes, u32[n, 210] each. */
 int oracle_spec_planes(const void *states, int n, uint32_t *floor, uint32_t *viewed);

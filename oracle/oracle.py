@@ -553,3 +553,107 @@ class ReferenceRoute:
         count = self._field('fcount', np.int32)[:, 0]
         cells[np.arange(5600)[None, :] >= count[:, None]] = -1
         return cells
+
+
+# ------------------------------------------------------------------ semantic-actions build
+class SemanticTables(C.Structure):
+    """semantic-actions-v1 learn.cu:141-151 (MULTI_MAP, with the LOS table)."""
+    _fields_ = [(k, C.c_void_p) for k in ('floor', 'cells', 'index', 'distance')] + [
+        ('ncells', C.c_int), ('map_ncells', C.c_void_p), ('distance_offsets', C.c_void_p), ('n_maps', C.c_int),
+        ('map_filter', C.c_int), ('los', C.c_void_p)]
+
+
+# semantic_harness.cu's field numbers for sem_offset
+SEM_FIELDS = ('hp', 'regen', 'player', 'ticks', 'killed', 'pos', 'energy', 'mhp', 'awake', 'occ', 'viewed', 'seen',
+              'floor_seen', 'enemy_slot')
+# The build's five actions (semantic-actions-v1 learn.cu:800)
+SEM_ATTACK, SEM_EXPLORE, SEM_ENGAGE, SEM_WAIT, SEM_REST = range(5)
+
+
+def semantic_library():
+    """The reference's semantic-actions build driven by oracle/semantic_harness.cu
+    (host code), or None when it was not built here."""
+    path = HERE / '_ref' / 'semantic_rules.so'
+    if not path.exists():
+        return None
+    lib = C.CDLL(str(path))
+    p, i = C.c_void_p, C.c_int
+    lib.sem_empty.argtypes = [p, p, p, i, i, i, C.c_uint64]
+    lib.sem_put.argtypes = [p, p, p, i, i, i, i]
+    lib.sem_transition.argtypes = [p, p, p, i, i, p]
+    lib.sem_observe.argtypes = [p, p, p, p, p]
+    lib.sem_adjacent_attack.argtypes = [p, p, p]
+    lib.sem_visible_awake.argtypes = [p, p, p]
+    lib.sem_in_view.argtypes = [p, p, i]
+    lib.sem_detects.argtypes = [p, p, i]
+    return lib
+
+
+class SemanticReference:
+    """One hand-built env of the reference's semantic-actions build on the fixture
+    map (map 0 of a one-map corpus, its native LOS table), on the host.
+
+    `spec` is a spec-task config dict (d1.spec_env.DEFAULT's keys): the player's
+    HP, defence and regeneration and kinds 0-3 are copied into the build's Config
+    (sim.h:64-67; count = the build's REQUIRED regular monsters, as its reset
+    asserts without ogres), so both tasks play the same numbers. Monster slot `id` has kind c.kinds[id % 6]; slots from
+    sem_required() on are the build's ogres, which these cases never use."""
+
+    def __init__(self, spec):
+        lib = semantic_library()
+        if lib is None:
+            raise RuntimeError('oracle/_ref/semantic_rules.so is not built (make -C oracle ref)')
+        self.lib = lib
+        z = np.load(DATA / 'fixture_1057.npz')
+        floor, native_los = z['floor'], z['native_los']
+        _, _, _, cells, index, distance = fixture()
+        arrays = route_arrays([(floor, cells, index, distance)])
+        arrays['los'] = np.ascontiguousarray(native_los, np.uint32).reshape(-1)
+        self.arrays = arrays
+        self.tables = SemanticTables(*(arrays[k].ctypes.data for k in ('floor', 'cells', 'index', 'distance')),
+                                     len(cells), arrays['map_ncells'].ctypes.data,
+                                     arrays['distance_offsets'].ctypes.data, 1, 0, arrays['los'].ctypes.data)
+        kinds = list(spec['kinds'][:4]) + list(spec['kinds'][:2])
+        values = [lib.sem_required(), 0, spec['hp'], spec['ac100'], spec['ev100'], spec['sh100'],
+                  spec['shield_limit'], spec['regen'], 1, *spec['gdr'], *[v for k in kinds for v in k]]
+        self.config = (C.c_int * len(values))(*values)
+        self.state = np.zeros(lib.sem_state_bytes(), np.uint8)
+        self.obs = np.zeros(lib.sem_obs_size(), np.float32)
+        self.mask = np.zeros(lib.sem_action_size(), np.float32)
+        self.out = np.zeros(lib.sem_out_size(), np.float32)
+        self.off = {k: lib.sem_offset(i) for i, k in enumerate(SEM_FIELDS)}
+        self.floor = floor
+
+    def _args(self):
+        return self.state.ctypes.data, C.byref(self.config), C.byref(self.tables)
+
+    def empty(self, player, hp, ticks=0, seed=0):
+        self.lib.sem_empty(*self._args(), player, hp, ticks, seed)
+
+    def put(self, slot, pos, hp, awake):
+        self.lib.sem_put(*self._args(), slot, pos, hp, int(awake))
+
+    def step(self, action, limit=2048):
+        self.lib.sem_transition(*self._args(), action, limit, self.out.ctypes.data)
+        return self.out.copy()
+
+    def observe(self):
+        self.lib.sem_observe(*self._args(), self.obs.ctypes.data, self.mask.ctypes.data)
+        return self.mask.copy()
+
+    def attack_dir(self):
+        return self.lib.sem_adjacent_attack(*self._args())
+
+    def visible_awake(self):
+        return bool(self.lib.sem_visible_awake(*self._args()))
+
+    def detects(self, origin):
+        return bool(self.lib.sem_detects(self.state.ctypes.data, C.byref(self.tables), origin))
+
+    def field(self, name, index=None, dtype=np.int32):
+        o = self.off[name]
+        if name in ('pos', 'energy', 'mhp', 'awake', 'occ', 'enemy_slot'):
+            dtype, o = np.int16, o + 2 * (index or 0)
+        elif name in ('viewed', 'seen'):
+            dtype, o = np.uint8, o + (index or 0)
+        return int(self.state[o:o + np.dtype(dtype).itemsize].view(dtype)[0])

@@ -25,12 +25,15 @@ def plane(bits_u8):
     return out.reshape(-1)
 
 
-def build(player=(40, 35), hp=3, ticks=0, mons=(), room=(25, 25, 60, 45), stairs=(30, 30), env=0, seed=5):
-    """mons: (x, y, hp, kind, awake) tuples."""
-    floor = np.zeros((H, W), np.uint8)
-    x0, y0, x1, y1 = room
-    floor[y0:y1 + 1, x0:x1 + 1] = 1
-    floor = floor.reshape(-1)
+def build(player=(40, 35), hp=3, ticks=0, mons=(), room=(25, 25, 60, 45), stairs=(30, 30), env=0, seed=5,
+          floor=None):
+    """mons: (x, y, hp, kind, awake) tuples. `floor` (u8[5600]) replaces the
+    rectangular room when given."""
+    if floor is None:
+        floor = np.zeros((H, W), np.uint8)
+        x0, y0, x1, y1 = room
+        floor[y0:y1 + 1, x0:x1 + 1] = 1
+    floor = np.ascontiguousarray(floor, np.uint8).reshape(-1)
     p = player[1] * W + player[0]
     los = oracle.los_mask(floor, p)  # 17x17, bit (dy+8)*17 + dx+8
     vis = np.zeros(15, np.uint32)
