@@ -581,6 +581,7 @@ def semantic_library():
     lib.sem_empty.argtypes = [p, p, p, i, i, i, C.c_uint64]
     lib.sem_put.argtypes = [p, p, p, i, i, i, i]
     lib.sem_transition.argtypes = [p, p, p, i, i, p]
+    lib.sem_primitive.argtypes = [p, p, p, i, i, p]
     lib.sem_observe.argtypes = [p, p, p, p, p]
     lib.sem_adjacent_attack.argtypes = [p, p, p]
     lib.sem_visible_awake.argtypes = [p, p, p]
@@ -636,6 +637,14 @@ class SemanticReference:
     def step(self, action, limit=2048):
         self.lib.sem_transition(*self._args(), action, limit, self.out.ctypes.data)
         return self.out.copy()
+
+    def primitive(self, d, limit=2048):
+        self.lib.sem_primitive(*self._args(), d, limit, self.out.ctypes.data)
+        return self.out.copy()
+
+    def viewed(self):
+        o = self.off['viewed']
+        return self.state[o:o + 5600].copy()
 
     def observe(self):
         self.lib.sem_observe(*self._args(), self.obs.ctypes.data, self.mask.ctypes.data)

@@ -87,6 +87,11 @@ void sem_transition(State *s, const Config *c, const Tables *t, int action, int 
     transition(*s, *c, *t, action, limit, out);
 }
 
+// One physical turn with primitive d (0-7 a step or bump in compass order, 8 a wait).
+void sem_primitive(State *s, const Config *c, const Tables *t, int d, int limit, float *out) {
+    primitive_transition(*s, *c, *t, d, limit, out);
+}
+
 void sem_observe(State *s, const Config *c, const Tables *t, float *obs, float *mask) {
     observe(*s, *c, *t, obs, mask);
 }

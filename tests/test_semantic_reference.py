@@ -328,3 +328,51 @@ def test_invalid_actions_cost_one_wait_like_reference(backend):
         assert o[38] or actions[i] == ATTACK  # the reference flags an invalid rest
         assert g[9] == 1 and g[8] == 1 == o[26], i
         assert g[4] == o[4] and g[5] == o[5] and np.float32(g[0]) == np.float32(o[0]), i
+
+
+@pytest.mark.parametrize('backend', BACKENDS)
+def test_steps_and_reveal_match_reference(backend):
+    """The one-turn primitive of a lone player (learn.cu:638-700): a step onto floor
+    or a bump into a wall, then the LOS-gated 15x15 reveal (learn.cu:296-331) --
+    every in-view cell remembered, every newly seen floor cell paying the explore
+    reward. 64 players walk 150 random compass steps from random fixture cells;
+    each turn's reward, the position, HP, clock and seen-floor count must agree,
+    and at the end the remembered plane cell for cell."""
+    ref = reference()
+    rng = np.random.default_rng(7)
+    floor = fixture_floor()
+    cells = [int(p) for p in np.flatnonzero(floor)]
+    n, T = 64, 150
+    starts = [cells[rng.integers(len(cells))] for _ in range(n)]
+    hps = [int(rng.integers(1, 16)) for _ in range(n)]
+    moves = rng.integers(0, 8, (T, n))
+    want_out = np.zeros((T, n, 4), np.float64)
+    want_viewed = np.zeros((n, N), np.uint8)
+    for i in range(n):
+        ref.empty(starts[i], hps[i])
+        for t in range(T):
+            o = ref.primitive(int(moves[t, i]), LIMIT)
+            want_out[t, i] = (o[0], ref.field('player'), o[4], ref.field('floor_seen'))
+            assert o[5] == t + 1
+        want_viewed[i] = ref.viewed()
+    ours = Ours(backend, [spec_case(starts[i], hps[i], []) for i in range(n)])
+    moved = 0
+    for t in range(T):
+        out = ours.step(moves[t])
+        if backend == 'oracle':
+            rows = ours.env.compact()
+        else:
+            rows = ours.env.compact().cpu().numpy()
+        got = np.stack([out[:, 0], rows[:, 6], out[:, 4], rows[:, 11]], axis=1)
+        assert np.array_equal(out[:, 5], np.full(n, t + 1)), t
+        for i in range(n):
+            assert np.float32(got[i, 0]) == np.float32(want_out[t, i, 0]), (t, i)
+            assert tuple(got[i, 1:]) == tuple(want_out[t, i, 1:]), (t, i)
+        moved += int((want_out[t, :, 0] > 0).sum())
+    if backend == 'oracle':
+        _, viewed = ours.env.planes()
+    else:
+        viewed = ours.env.planes()[1].cpu().numpy().view(np.uint32)
+    for i in range(n):
+        assert np.array_equal(oracle.floor_from_bits(viewed[i]), want_viewed[i]), i
+    assert moved > 200  # turns that revealed new floor
