@@ -26,9 +26,10 @@ def plane(bits_u8):
 
 
 def build(player=(40, 35), hp=3, ticks=0, mons=(), room=(25, 25, 60, 45), stairs=(30, 30), env=0, seed=5,
-          floor=None):
+          floor=None, energy=None):
     """mons: (x, y, hp, kind, awake) tuples. `floor` (u8[5600]) replaces the
-    rectangular room when given."""
+    rectangular room when given; `energy` (one value per monster) replaces the
+    default -30000."""
     if floor is None:
         floor = np.zeros((H, W), np.uint8)
         x0, y0, x1, y1 = room
@@ -46,6 +47,7 @@ def build(player=(40, 35), hp=3, ticks=0, mons=(), room=(25, 25, 60, 45), stairs
                 viewed[(player[1] + dy) * W + player[0] + dx] = 1
     return dict(env=env, seed=seed, hp=hp, ticks=ticks, player=p, stairs=stairs[1] * W + stairs[0],
                 nmon=len(mons), floor_seen=int((viewed & floor).sum()), mons=list(mons),
+                energy=list(energy) if energy is not None else [-30000] * len(mons),
                 floor=plane(floor), viewed=plane(viewed), vis=vis)
 
 
@@ -58,7 +60,7 @@ def gpu_row(c):
     r[64:64 + 30].view(np.uint16)[:] = c['vis'].astype(np.uint16)
     m = r[128:224].view(np.int16)
     for i, (x, y, mh, kind, awake) in enumerate(c['mons']):
-        m[i], m[16 + i], m[32 + i] = y * W + x, -30000, mh
+        m[i], m[16 + i], m[32 + i] = y * W + x, c['energy'][i], mh
         r[224 + i], r[240 + i] = kind, awake
     r[256:256 + 840] = c['floor'].view(np.uint8)
     r[1096:1096 + 840] = c['viewed'].view(np.uint8)
@@ -73,7 +75,7 @@ def oracle_row(c):
                                  c['floor_seen']]
     pos, en, mh = r[60:82].view(np.int16), r[82:104].view(np.int16), r[104:126].view(np.int16)
     for i, (x, y, hp, kind, awake) in enumerate(c['mons']):
-        pos[i], en[i], mh[i] = y * W + x, -30000, hp
+        pos[i], en[i], mh[i] = y * W + x, c['energy'][i], hp
         r[126 + i], r[137 + i] = kind, awake
     r[148:148 + 840] = c['floor'].view(np.uint8)
     r[988:988 + 840] = c['viewed'].view(np.uint8)
