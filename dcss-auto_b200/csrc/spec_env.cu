@@ -729,7 +729,9 @@ __device__ Prim primitive(Env &e, const D1SpecConfig &c, const RayArgs &ra, int 
     }
     const bool descended = d == PRIM_DESCEND && e.player == e.stairs && e.hp > 0;
     reward_milli += c.explore_milli * reveal(e);
-    if (watch) r.saw_awake = visible_awake(e);
+    // (The interrupt rule's first check, an awake monster in view right after
+    // the player's move, is always false inside a rest: the player does not
+    // move, and the previous turn ended -- or the rest began -- with none.)
     if (!descended) {
         const bool alive = e.lane < e.nmon && e.m_hp > 0;
         if (alive && !e.m_awake && cheb(e.m_pos, e.player) <= 6 && visible(e, e.m_pos)) {
@@ -796,6 +798,30 @@ __device__ float decision(Env &e, const D1SpecConfig &c, const RayArgs &ra, int 
         total += r.reward;
         if (r.done || invalid || a != 9) break;
         if (r.saw_awake || e.hp >= c.hp) break;
+        // A rest turn with no living monster awake leaves a fixed point behind:
+        // the player stands still (nothing new in view), every sleeping monster
+        // keeps failing the same wake test, and none holds the energy to act.
+        // Each further turn therefore changes only regeneration, HP and the
+        // clock, and pays one wait (-1 milli); those turns run here as scalar
+        // arithmetic, bit-identical to running them as primitives.
+        if (!__any_sync(FULL, e.lane < e.nmon && e.m_hp > 0 && e.m_awake)) {
+            for (;;) {
+                e.blocks = 0;
+                e.regen += c.regen;
+                while (e.regen >= 100) {
+                    e.hp = imin(c.hp, e.hp + 1);
+                    e.regen -= 100;
+                }
+                e.ticks++;
+                r.timeout = e.ticks >= c.limit;
+                r.done = r.timeout;
+                r.reward = 0.001f * (float)(-1);
+                elapsed++;
+                total += r.reward;
+                if (r.done || e.hp >= c.hp) break;
+            }
+            break;
+        }
     }
     float o = 0.f;
     switch (e.lane) {
