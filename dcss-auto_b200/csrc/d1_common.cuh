@@ -77,6 +77,27 @@ template <class G> __device__ __forceinline__ int rng_r(G &g, int bound) {
     }
     return (int)(m >> 32);
 }
+// The pursuit step's tie walk (gpu-d1/src/sim.h:213-222) without the walk. The
+// reference visits the directions in the order (z + rotation) % 4 for z < 4,
+// then 4 + (z + rotation) % 4, keeping a free neighbour that is closer to the
+// player than the mover. Distances of neighbouring cells differ by at most one,
+// so the cells it can keep are exactly those one step closer (bit d of `cand`
+// for direction d): the first of them in walk order, each later one replacing
+// it when its draw r(2), r(3), ... comes up 0. The same draws in the same order;
+// returns the kept direction (cand != 0).
+template <class G> __device__ __forceinline__ int walk_pick(G &g, unsigned cand, int rotation) {
+    const unsigned lo = cand & 0xfu, hi = (cand >> 4) & 0xfu;
+    const unsigned walk = (((lo >> rotation) | (lo << (4 - rotation))) & 0xfu) |
+                          ((((hi >> rotation) | (hi << (4 - rotation))) & 0xfu) << 4);
+    int pick = __ffs(walk) - 1;
+    unsigned later = walk & (walk - 1);
+    for (int t = 2; later; t++) {
+        const int z = __ffs(later) - 1;
+        later &= later - 1;
+        if (rng_r(g, t) == 0) pick = z;
+    }
+    return pick < 4 ? (pick + rotation) % 4 : 4 + (pick - 4 + rotation) % 4;
+}
 template <class G> __device__ __forceinline__ int rng_avg(G &g, int n) {
     int a = rng_r(g, n);
     return (a + rng_r(g, n + 1)) / 2;

@@ -109,10 +109,10 @@ __device__ void reset(State &s, const D1Config &c, const D1Tables &t, int lane) 
 }
 
 // gpu-d1/src/sim.h:207-253: distance-field step with random rotation, reservoir
-// ties and the bounded 24-node repair search. The eight neighbour tests run one
-// per lane; the tie-breaking walk stays in the reference's rotated order.
+// ties (walk_pick) and the bounded 24-node repair search. The eight neighbour
+// tests run one per lane.
 __device__ int choose_move(State &s, const D1Config &c, const D1Tables &t, const uint16_t *dist, int p, int lane) {
-    int bd = dist[p], best = -1, ties = 0;
+    const int bd = dist[p];
     int rotation = rng_r(s.rng, 4);
     const int d = lane & 7;
     int q = neighbor(p, d);
@@ -121,20 +121,9 @@ __device__ int choose_move(State &s, const D1Config &c, const D1Tables &t, const
         int pk = __shfl_sync(FULL, s.m_pos, k), hk = __shfl_sync(FULL, s.m_hp, k);
         if (hk > 0 && pk == q) ok = false;
     }
-    int dq = ok ? (int)dist[q] : 0;
-    for (int z = 0; z < 8; z++) {
-        int dd = z < 4 ? (z + rotation) % 4 : 4 + (z + rotation) % 4;
-        bool okz = __shfl_sync(FULL, (int)ok, dd);
-        int dz = __shfl_sync(FULL, dq, dd), qz = __shfl_sync(FULL, q, dd);
-        if (!okz) continue;
-        if (dz < bd) {
-            bd = dz;
-            best = qz;
-            ties = 1;
-        } else if (dz == bd && best >= 0 && rng_r(s.rng, ++ties) == 0)
-            best = qz;
-    }
-    if (best >= 0 || !c.repair) return best;
+    const unsigned cand = __ballot_sync(FULL, lane < 8 && ok && (int)dist[q] < bd);
+    if (cand) return __shfl_sync(FULL, q, walk_pick(s.rng, cand, rotation));
+    if (!c.repair) return -1;
     // Repair search (sim.h:225-252): FIFO over free floor from p, at most 24
     // nodes on the list, returning the first step of the first cell met (list
     // order, then compass order) that is closer to the player than p. A head's

@@ -347,29 +347,17 @@ __device__ void reset(Env &e, const D1Config &c, const D1RouteTables &t, int map
 }
 
 // sim.h:207-253 over the occupancy plane: distance-field step with random
-// rotation and reservoir ties, then the bounded 24-node repair search; the
-// eight neighbour tests run one per lane, the tie walk in rotated order.
+// rotation and reservoir ties (walk_pick), then the bounded 24-node repair
+// search; the eight neighbour tests run one per lane.
 __device__ int choose_move(Env &e, const D1Config &c, const Smem &s, const uint16_t *dist, int p, int lane) {
     const int rotation = rng_r(e.rng, 4);
     const int d = lane & 7;
     const int q = neighbor(p, d);
     const bool ok = q >= 0 && bit(s.floor, q) && q != e.player && !bit(s.occ, q);
-    int bd = dist[p], best = -1, ties = 0;
-    const int dq = ok ? (int)dist[q] : 0;
-    for (int z = 0; z < 8; z++) {
-        const int dd = z < 4 ? (z + rotation) % 4 : 4 + (z + rotation) % 4;
-        const bool okz = __shfl_sync(FULL, (int)ok, dd);
-        const int dz = __shfl_sync(FULL, dq, dd), qz = __shfl_sync(FULL, q, dd);
-        if (!okz) continue;
-        if (dz < bd) {
-            bd = dz;
-            best = qz;
-            ties = 1;
-        } else if (dz == bd && best >= 0 && rng_r(e.rng, ++ties) == 0) {
-            best = qz;
-        }
-    }
-    if (best >= 0 || !c.repair) return best;
+    const int bd = dist[p];
+    const unsigned cand = __ballot_sync(FULL, lane < 8 && ok && (int)dist[q] < bd);
+    if (cand) return __shfl_sync(FULL, q, walk_pick(e.rng, cand, rotation));
+    if (!c.repair) return -1;
     // Repair search (sim.h:225-252): FIFO over free floor from p, at most 24
     // nodes on the list, returning the first step of the first cell met (list
     // order, then compass order) that is closer to the player than p. A head's

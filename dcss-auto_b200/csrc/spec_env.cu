@@ -571,25 +571,13 @@ __device__ int choose_move(Env &e, int p, int D, int &dq_out) {
     const int q = neighbor(p, d);
     const bool okq = q >= 0 && floor_at(e, q) && q != e.player && !bitp(e.sm->occ, q);
     const int dq = okq ? dist_rel(e, q, D) : 0;
-    int best = -1, bd = D, bdist = D, ties = 0;
-    for (int z = 0; z < 8; z++) {
-        const int dd = z < 4 ? (z + rotation) % 4 : 4 + (z + rotation) % 4;
-        const bool okz = __shfl_sync(FULL, (int)okq, dd);
-        const int dz = __shfl_sync(FULL, dq, dd), qz = __shfl_sync(FULL, q, dd);
-        if (!okz) continue;
-        if (dz < bd) {
-            bd = dz;
-            best = qz;
-            bdist = dz;
-            ties = 1;
-        } else if (dz == bd && best >= 0 && rng_r(e.rng, ++ties) == 0) {
-            best = qz;
-            bdist = dz;
-        }
-    }
-    if (best >= 0) {
-        dq_out = bdist;
-        return best;
+    // the rotated tie walk of sim.h:213-222 (walk_pick): a free neighbour's
+    // distance is D - 1, D or D + 1, so the candidates are those at D - 1
+    const unsigned cand = __ballot_sync(FULL, lane < 8 && okq && dq < D);
+    if (cand) {
+        const int dir = walk_pick(e.rng, cand, rotation);
+        dq_out = __shfl_sync(FULL, dq, dir);
+        return __shfl_sync(FULL, q, dir);
     }
     // Repair search (sim.h:225-252): FIFO over free floor from p, at most 24
     // nodes on the list, returning the first step of the first cell met (list
