@@ -98,6 +98,21 @@ template <class G> __device__ __forceinline__ int walk_pick(G &g, unsigned cand,
     }
     return pick < 4 ? (pick + rotation) % 4 : 4 + (pick - 4 + rotation) % 4;
 }
+// Directions d (bit d, compass order) in which p's neighbour holds a live
+// monster, for lane-distributed monsters: each monster lane marks its own
+// direction from p, and one OR-reduction collects them.
+__device__ __forceinline__ unsigned occupied_dirs(int p, int pos, bool live) {
+    unsigned bit = 0;
+    if (live) {
+        const int dx = pos % W - p % W, dy = pos / W - p / W;
+        if (dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1 && (dx | dy)) {
+            const int dir = dy == -1 ? (dx == 0 ? 0 : dx == 1 ? 4 : 7)
+                                     : dy == 0 ? (dx == 1 ? 1 : 3) : (dx == 0 ? 2 : dx == 1 ? 5 : 6);
+            bit = 1u << dir;
+        }
+    }
+    return __reduce_or_sync(FULL, bit);
+}
 template <class G> __device__ __forceinline__ int rng_avg(G &g, int n) {
     int a = rng_r(g, n);
     return (a + rng_r(g, n + 1)) / 2;

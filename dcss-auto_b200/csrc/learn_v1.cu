@@ -116,11 +116,8 @@ __device__ int choose_move(State &s, const D1Config &c, const D1Tables &t, const
     int rotation = rng_r(s.rng, 4);
     const int d = lane & 7;
     int q = neighbor(p, d);
-    bool ok = q >= 0 && t.floor[q] && q != s.player;
-    for (int k = 0; k < c.count; k++) {
-        int pk = __shfl_sync(FULL, s.m_pos, k), hk = __shfl_sync(FULL, s.m_hp, k);
-        if (hk > 0 && pk == q) ok = false;
-    }
+    const unsigned occd = occupied_dirs(p, s.m_pos, lane < c.count && s.m_hp > 0);  // all lanes
+    const bool ok = q >= 0 && t.floor[q] && q != s.player && !((occd >> d) & 1u);
     const unsigned cand = __ballot_sync(FULL, lane < 8 && ok && (int)dist[q] < bd);
     if (cand) return __shfl_sync(FULL, q, walk_pick(s.rng, cand, rotation));
     if (!c.repair) return -1;
@@ -145,12 +142,9 @@ __device__ int choose_move(State &s, const D1Config &c, const D1Tables &t, const
     for (int head = 0; head < len; head++) {
         const int ch = lc[head], fh = lf[head];
         const int qn = neighbor(ch, d);
-        bool okn = lane < 8 && qn >= 0 && t.floor[qn] && qn != s.player &&
-                   !((inl[(qn / W) * ROWW + (qn % W) / 32] >> ((qn % W) & 31)) & 1u);
-        for (int k = 0; k < c.count; k++) {
-            const int pk = __shfl_sync(FULL, s.m_pos, k), hk = __shfl_sync(FULL, s.m_hp, k);
-            if (hk > 0 && pk == qn) okn = false;
-        }
+        const unsigned occd = occupied_dirs(ch, s.m_pos, lane < c.count && s.m_hp > 0);
+        const bool okn = lane < 8 && qn >= 0 && t.floor[qn] && qn != s.player &&
+                         !((inl[(qn / W) * ROWW + (qn % W) / 32] >> ((qn % W) & 31)) & 1u) && !((occd >> d) & 1u);
         const int dqn = okn ? (int)dist[qn] : 65535;
         const unsigned closer = __ballot_sync(FULL, okn && dqn < dp);
         if (closer) {
