@@ -26,6 +26,7 @@
 #include <stdint.h>
 
 #include "../../include/d1.h"
+#include "d1_pdl.cuh"
 #include "d1_sampler.cuh"
 
 
@@ -684,6 +685,7 @@ __global__ void __launch_bounds__(THREADS + (XM ? 32 * X_EXPANDERS : 0), 1)
     cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // the previous kernel's outputs (operands, the weights) are complete from here on
 
     if (warp == 0 && lane == 0) {
         // ---- producer (both CTAs): this CTA's A rows and B half, signalling the leader
@@ -1244,17 +1246,21 @@ static int pair_launch(const void *a, int lda, const void *b, int ldb, int M, in
     const int tiles = tiles_m * tiles_n * splits;
     const int clusters = tiles < sms / 2 ? tiles : sms / 2;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // launch and prologue may overlap the end of the stream's previous kernel
+    // (the kernel's pdl_wait precedes its first global access)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(THREADS + (xm ? 32 * X_EXPANDERS : 0));
     cfg.dynamicSmemBytes = (sub == 2 ? P2_SMEM_BYTES : P_SMEM_BYTES) + (xm ? X_SMEM_BYTES : 0);
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     void (*kern)(const CUtensorMap, const CUtensorMap, Params, int, int, int) =
         sub == 2 ? (xm == 1 ? gemm_pair_kernel<2, 1> : xm == 2 ? gemm_pair_kernel<2, 2> : gemm_pair_kernel<2, 0>)
                  : (xm == 1 ? gemm_pair_kernel<1, 1> : xm == 2 ? gemm_pair_kernel<1, 2> : gemm_pair_kernel<1, 0>);

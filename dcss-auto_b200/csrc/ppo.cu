@@ -9,6 +9,7 @@
 #include <string.h>
 
 #include "d1_common.cuh"
+#include "d1_pdl.cuh"
 
 namespace d1 {
 namespace ppo {
@@ -1068,6 +1069,7 @@ __device__ __forceinline__ double chunk_store(const StepJob &jb, int64_t e, floa
 }
 
 __global__ void __launch_bounds__(256) grad_reduce_kernel(const __grid_constant__ StepArgs a) {
+    pdl_wait();  // before any global access: the slabs come from the previous kernels
     __shared__ float4 ps[8][32];
     __shared__ double ws[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1375,6 +1377,7 @@ __global__ void __launch_bounds__(256) peer_gather2_kernel(const __grid_constant
 // coefficient is the same everywhere), and *step advances on the device. After
 // a peer all-reduce (check_abort) that gave up waiting, nothing is updated.
 __global__ void __launch_bounds__(256) adam_update_kernel(AdamArgs d, int nparts, int64_t *step, int check_abort) {
+    pdl_wait();  // before any global access: the gradient and its norm partials come from the previous kernel
     __shared__ float sc[3];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (check_abort && *(volatile int *)&g_peer_abort) return;
@@ -1636,14 +1639,21 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
     int blocks = sms * STEP_BLOCKS_PER_SM;
     if (blocks > STEP_MAX_BLOCKS) blocks = STEP_MAX_BLOCKS;
-    grad_reduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
+    // the reduction and Adam launch with programmatic overlap of the previous
+    // kernel's end (both pdl_wait first); the peer exchange kernels launch plainly
+    cudaLaunchAttribute attr;
+    const cudaLaunchConfig_t cfg = pdl_config(dim3(blocks), dim3(256), 0, (cudaStream_t)stream, &attr);
+    if (cudaError_t e = cudaLaunchKernelEx(&cfg, grad_reduce_kernel, a)) return (int)e;
     if (peer && peer->two_phase) {
         peer_reduce2_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(p2);
         peer_gather2_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(p2);
     } else if (peer) {
         peer_allreduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(pa);
     }
-    if (do_adam) adam_update_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d, blocks, step, peer ? 1 : 0);
+    if (do_adam) {
+        const int abort_check = peer ? 1 : 0;
+        if (cudaError_t e = cudaLaunchKernelEx(&cfg, adam_update_kernel, d, blocks, step, abort_check)) return (int)e;
+    }
     return (int)cudaGetLastError();
 }
 

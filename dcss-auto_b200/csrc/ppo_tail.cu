@@ -38,6 +38,7 @@
 #include <stdint.h>
 
 #include "../../include/d1.h"
+#include "d1_pdl.cuh"
 #include "tc_ptx.cuh"
 
 namespace d1 {
@@ -92,6 +93,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 __global__ void __launch_bounds__(THREADS, 1)
     tail_kernel(const __grid_constant__ CUtensorMap map_h1, const __grid_constant__ CUtensorMap map_w2,
                 const __grid_constant__ CUtensorMap map_dh2, const __grid_constant__ CUtensorMap map_dh1, Args a) {
+    d1::pdl_wait();  // before any global access: h1 and the weights come from the previous kernels
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t base = smem_u32(sm);
@@ -558,8 +560,10 @@ int d1_ppo_tail(const void *h1, const void *w2, const float *b2, const void *wh,
     }
     Args a{(const __nv_bfloat16 *)wh, b2, bh, idx, legal, action, old_logp, adv, ret, old_value, adv_stats,
            adv_count, n, clip, vclip, vf_coef, ent_coef, part};
-    tail_kernel<<<(n + ROWS - 1) / ROWS, THREADS, SMEM, (cudaStream_t)stream>>>(mh, mw, md2, md1, a);
-    return (int)cudaGetLastError();
+    cudaLaunchAttribute attr;
+    const cudaLaunchConfig_t cfg = d1::pdl_config(dim3((n + ROWS - 1) / ROWS), dim3(THREADS), SMEM,
+                                                  (cudaStream_t)stream, &attr);
+    return (int)cudaLaunchKernelEx(&cfg, tail_kernel, mh, mw, md2, md1, a);
 }
 
 int d1_ppo_tail_blocks(int n) { return n <= 0 ? 0 : (n + d1::tail::ROWS - 1) / d1::tail::ROWS; }
