@@ -28,6 +28,7 @@
 #include <stdint.h>
 
 #include "../../include/d1.h"
+#include "d1_pdl.cuh"
 #include "d1_sampler.cuh"
 #include "tc_ptx.cuh"
 
@@ -72,6 +73,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 
 __global__ void __launch_bounds__(THREADS, 1)
     policy_tail_kernel(const __grid_constant__ CUtensorMap map_h1, const __grid_constant__ CUtensorMap map_w2, Args a) {
+    d1::pdl_wait();  // before any global access: h1 comes from the previous kernel
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t base = smem_u32(sm);
@@ -310,8 +312,10 @@ int d1_policy_tail_sample(const void *h1, int n, int ldh, const void *w2, const 
     const int tiles = (n + ROWS - 1) / ROWS;
     Args a{(const __nv_bfloat16 *)wh, b2, bh, legal, seed, step, step_dev, first_env, n, tiles, action, logp, value,
            logits};
-    policy_tail_kernel<<<tiles < sms ? tiles : sms, THREADS, SMEM, (cudaStream_t)stream>>>(mh, mw, a);
-    return (int)cudaGetLastError();
+    cudaLaunchAttribute attr;
+    const cudaLaunchConfig_t cfg =
+        d1::pdl_config(dim3(tiles < sms ? tiles : sms), dim3(THREADS), SMEM, (cudaStream_t)stream, &attr);
+    return (int)cudaLaunchKernelEx(&cfg, policy_tail_kernel, mh, mw, a);
 }
 
 int d1_policy_tail_error(void) {

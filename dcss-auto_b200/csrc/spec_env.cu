@@ -24,6 +24,7 @@
 #include <cuda_bf16.h>
 
 #include "d1_common.cuh"
+#include "d1_pdl.cuh"
 
 namespace d1 {
 namespace spec {
@@ -1060,6 +1061,7 @@ __global__ void __launch_bounds__(WARPS * 32, MIN_BLOCKS)
     step_kernel(uint8_t *state, int n, D1SpecConfig c, RayArgs ra, int extra_layers, const int64_t *actions,
                 __nv_bfloat16 *obs, uint8_t *cobs, uint16_t *legal, float *out, int64_t out_env, int64_t out_col,
                 const bool *active) {
+    pdl_wait();  // before any global access: the actions come from the previous kernel
     __shared__ Smem sms[WARPS];
     const int w = threadIdx.x >> 5, env = blockIdx.x * WARPS + w;
     if (env >= n) return;
@@ -1322,10 +1324,12 @@ int d1_spec_step_strided(void *state, int n, const D1SpecConfig *c, const int64_
     if (int err = spec_check(n, c)) return err;
     if (n == 0) return 0;
     if (out_env < 1 || out_col < 1) return D1_ERR_BAD_ARGUMENT;
-    spec::step_kernel<<<(n + spec::WARPS - 1) / spec::WARPS, spec::WARPS * 32, 0, (cudaStream_t)stream>>>(
-        (uint8_t *)state, n, *c, g_rays, spec_extra_layers(*c), actions, (__nv_bfloat16 *)obs_bf16, (uint8_t *)cobs,
-        legal, out, out_env, out_col, active);
-    return (int)cudaGetLastError();
+    cudaLaunchAttribute attr;
+    const cudaLaunchConfig_t cfg = pdl_config(dim3((n + spec::WARPS - 1) / spec::WARPS), dim3(spec::WARPS * 32), 0,
+                                              (cudaStream_t)stream, &attr);
+    return (int)cudaLaunchKernelEx(&cfg, spec::step_kernel, (uint8_t *)state, n, *c, g_rays, spec_extra_layers(*c),
+                                   actions, (__nv_bfloat16 *)obs_bf16, (uint8_t *)cobs, legal, out, out_env, out_col,
+                                   active);
 }
 
 int d1_spec_step_ex(void *state, int n, const D1SpecConfig *c, const int64_t *actions, void *obs_bf16, void *cobs,
