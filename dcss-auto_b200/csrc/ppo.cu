@@ -1175,6 +1175,7 @@ struct PeerArgs {
 };
 constexpr uint32_t PEER_WAIT_LIMIT = 1u << 24;  // default: ~1 s of 64 ns polls
 __global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_constant__ PeerArgs a) {
+    pdl_wait();  // before any global access: this rank's reduced gradient comes from the previous kernel
     __shared__ int ok;
     __shared__ double ws[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1316,6 +1317,7 @@ __device__ __forceinline__ void publish(unsigned long long *const *xflags, int i
     }
 }
 __global__ void __launch_bounds__(256) peer_reduce2_kernel(const __grid_constant__ Peer2Args a) {
+    pdl_wait();  // before any global access: this rank's reduced gradient comes from the previous kernel
     __shared__ int ok;
     const uint64_t epoch = (uint64_t)(*a.epoch_src + 1);
     const int64_t half = (int64_t)(epoch & 1);
@@ -1343,6 +1345,7 @@ __global__ void __launch_bounds__(256) peer_reduce2_kernel(const __grid_constant
     publish(a.xflags, 8 + a.rank, a.world, a.rank, epoch);
 }
 __global__ void __launch_bounds__(256) peer_gather2_kernel(const __grid_constant__ Peer2Args a) {
+    pdl_wait();  // before any global access: this rank's reduced gradient comes from the previous kernel
     __shared__ int ok;
     __shared__ double ws[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1639,16 +1642,16 @@ static int step_launch(const D1GradJob *jobs, int njobs, float *param, float *gr
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
     int blocks = sms * STEP_BLOCKS_PER_SM;
     if (blocks > STEP_MAX_BLOCKS) blocks = STEP_MAX_BLOCKS;
-    // the reduction and Adam launch with programmatic overlap of the previous
-    // kernel's end (both pdl_wait first); the peer exchange kernels launch plainly
+    // the reduction, the peer exchange and Adam launch with programmatic
+    // overlap of the previous kernel's end (each pdl_wait first)
     cudaLaunchAttribute attr;
     const cudaLaunchConfig_t cfg = pdl_config(dim3(blocks), dim3(256), 0, (cudaStream_t)stream, &attr);
     if (cudaError_t e = cudaLaunchKernelEx(&cfg, grad_reduce_kernel, a)) return (int)e;
     if (peer && peer->two_phase) {
-        peer_reduce2_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(p2);
-        peer_gather2_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(p2);
+        if (cudaError_t e = cudaLaunchKernelEx(&cfg, peer_reduce2_kernel, p2)) return (int)e;
+        if (cudaError_t e = cudaLaunchKernelEx(&cfg, peer_gather2_kernel, p2)) return (int)e;
     } else if (peer) {
-        peer_allreduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(pa);
+        if (cudaError_t e = cudaLaunchKernelEx(&cfg, peer_allreduce_kernel, pa)) return (int)e;
     }
     if (do_adam) {
         const int abort_check = peer ? 1 : 0;
