@@ -32,9 +32,19 @@ class Rollout:
     current stream's earlier work at every step and are joined back into it by
     join(), which roll(), bootstrap() and collect() call; a caller that drives
     step() itself calls join() before reading the buffers on another stream.
-    Trajectories do not depend on `parts`."""
+    Trajectories do not depend on `parts`.
 
-    def __init__(self, env, policy, horizon, seed=0, sample_seed=None, parts=2):
+    graphs=True: collect() runs its first rollout eagerly, then captures the
+    whole rollout (every slot's policy and env launches on the ranges' streams,
+    with the same fork/join structure, so consecutive steps still overlap as
+    they do eagerly) as one CUDA graph, and later collect() calls replay it: one
+    launch per rollout from the host instead of a dozen per step, the same
+    kernels and the same trajectories. Slot t reads its sampling step from
+    element t of a device array that collect() fills with global_step + t. The
+    graph reads the policy's weights and the env rows in place, so training
+    between rollouts is seen; step() outside collect() stays eager."""
+
+    def __init__(self, env, policy, horizon, seed=0, sample_seed=None, parts=2, graphs=False):
         self.env, self.policy, self.T = env, policy, horizon
         B, dev = env.batch, env.device
         self.seed = seed
@@ -52,6 +62,8 @@ class Rollout:
         self.global_step = 0
         self.ranges = env_ranges(B, parts)
         self.streams = [torch.cuda.Stream(dev) for _ in self.ranges] if len(self.ranges) > 1 else []
+        self.graphs = graphs
+        self._graph = None
         env.reset(seed, obs_out=self.obs, legal_out=self.legal[0], cobs_out=self.cobs[0])
 
     @property
@@ -64,10 +76,14 @@ class Rollout:
         for s in self.streams:
             main.wait_stream(s)
 
-    def step(self, t):
+    def step(self, t, step=None, h1=None, h2=None):
+        """Slot t's policy and env step. `step` (the sampling step: an int, or an
+        int64 device tensor of one element) defaults to global_step; h1 and h2
+        give the policy's activation rows (the graphs pass their own)."""
+        step = self.global_step if step is None else step
         if not self.streams:
-            self.policy.act(self.obs, self.legal[t], self.sample_seed, self.global_step, self.env.first_env,
-                            action=self.actions[t], logp=self.logp[t], value=self.values[t])
+            self.policy.act(self.obs, self.legal[t], self.sample_seed, step, self.env.first_env,
+                            action=self.actions[t], logp=self.logp[t], value=self.values[t], h1=h1, h2=h2)
             self.env.step(self.actions[t], obs_out=self.obs, legal_out=self.legal[t + 1], out_out=self.out[t],
                           cobs_out=self.cobs[t + 1])
         else:
@@ -76,9 +92,10 @@ class Rollout:
                 s = self.streams[i]
                 s.wait_stream(main)
                 with torch.cuda.stream(s):
-                    self.policy.act(self.obs[lo:hi], self.legal[t][lo:hi], self.sample_seed, self.global_step,
+                    self.policy.act(self.obs[lo:hi], self.legal[t][lo:hi], self.sample_seed, step,
                                     self.env.first_env + lo, action=self.actions[t][lo:hi],
-                                    logp=self.logp[t][lo:hi], value=self.values[t][lo:hi], part=i)
+                                    logp=self.logp[t][lo:hi], value=self.values[t][lo:hi], part=i,
+                                    h1=None if h1 is None else h1[lo:hi], h2=None if h2 is None else h2[lo:hi])
                     self.env.step(self.actions[t], obs_out=self.obs, legal_out=self.legal[t + 1],
                                   out_out=self.out[t], cobs_out=self.cobs[t + 1], rows=(lo, hi))
         self.global_step += 1
@@ -88,9 +105,38 @@ class Rollout:
         self.policy.value(self.obs, out=self.values[self.T])
 
     def collect(self):
-        for t in range(self.T):
-            self.step(t)
+        if self.graphs and self._graph is not None:
+            torch.add(self._slots, self.global_step, out=self._steps)
+            self._graph.replay()
+            self.global_step += self.T
+        else:
+            for t in range(self.T):
+                self.step(t)
+            if self.graphs:
+                self._capture()
         self.bootstrap()
+
+    def _capture(self):
+        """The whole rollout as one graph (the first, eager rollout has set up
+        every kernel's attributes); capturing runs nothing."""
+        dev = self.env.device
+        self._slots = torch.arange(self.T, dtype=torch.int64, device=dev)
+        self._steps = torch.empty(self.T, dtype=torch.int64, device=dev)
+        # the graph's own activation rows: the policy's cached ones may be
+        # reallocated by a later eager call with more rows
+        self._h1 = torch.empty((self.env.batch, self.policy.hidden), dtype=torch.bfloat16, device=dev)
+        self._h2 = torch.empty_like(self._h1)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+            for t in range(self.T):
+                self.step(t, step=self._steps[t:t + 1], h1=self._h1, h2=self._h2)
+            self.join()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.global_step -= self.T
+        self._graph = g
 
     def roll(self):
         """Start the next rollout from the last observation (the one-hot buffer

@@ -157,6 +157,34 @@ def test_rollout_on_two_streams_equals_one_stream():
     assert torch.equal(one.env.state, two.env.state)
 
 
+@pytest.mark.parametrize('parts', [1, 2])
+def test_graphed_collection_equals_eager_collection(parts):
+    """Rollout(graphs=True): the first collect() runs eagerly and captures the
+    rollout as one graph; the later ones replay it. Over three rollouts, with the
+    policy's weights changed in place between them (as a PPO update does), every
+    buffer, the env rows and the sampling step equal the eager rollout's bit
+    for bit."""
+    from d1.policy import Policy
+    from d1.rollout import Rollout
+    from d1.spec_env import SpecEnv
+    B, T = 8192, 6
+    eager = Rollout(SpecEnv(B, seed=23), Policy(seed=5), T, seed=23, parts=parts)
+    graph = Rollout(SpecEnv(B, seed=23), Policy(seed=5), T, seed=23, parts=parts, graphs=True)
+    for k in range(3):
+        for r in (eager, graph):
+            r.collect()
+            r.roll()
+            with torch.no_grad():  # a stand-in for an update: new weights, same buffers
+                r.policy.params['w1'].mul_(0.9)
+                r.policy.refresh()
+        torch.cuda.synchronize()
+        for name in ('obs', 'cobs', 'legal', 'actions', 'logp', 'values', 'out'):
+            assert torch.equal(getattr(eager, name), getattr(graph, name)), (k, name)
+        assert torch.equal(eager.env.state, graph.env.state), k
+        assert eager.global_step == graph.global_step == (k + 1) * T
+    assert graph._graph is not None
+
+
 @pytest.mark.parametrize('n', [65536, 1000])
 def test_policy_tail_matches_the_unfused_path_and_the_oracle(lib, n):
     """d1_policy_tail_sample (layer 2, head and draw in one persistent launch)
