@@ -376,3 +376,79 @@ def test_steps_and_reveal_match_reference(backend):
     for i in range(n):
         assert np.array_equal(oracle.floor_from_bits(viewed[i]), want_viewed[i]), i
     assert moved > 200  # turns that revealed new floor
+
+
+def test_window_channels_match_reference_observation():
+    """The spec task's one-hot window (oracle_spec_observe) against the same
+    information in the semantic build's observation (learn.cu:451-479): for
+    every cell of the 15x15 window, unknown / remembered wall / remembered floor
+    out of view / visible floor equal the build's memory value (0, -1, 1) and
+    its in-view plane, and a visible monster shows as asleep or awake exactly
+    where the build shows its hp and its slot's sleep flag. 48 players walk 60
+    random steps from random fixture cells (memory built by the reveal both
+    tasks share), then up to 10 monsters are placed within seven tiles."""
+    ref = reference()
+    rng = np.random.default_rng(9)
+    floor = fixture_floor()
+    cells = [int(p) for p in np.flatnonzero(floor)]
+    n, T = 48, 60
+    starts = [cells[rng.integers(len(cells))] for _ in range(n)]
+    moves = rng.integers(0, 8, (T, n))
+    ours = Ours('oracle', [spec_case(starts[i], 15, []) for i in range(n)])
+    for t in range(T):
+        ours.step(moves[t])
+    rows = ours.env.compact()
+    env = ours.env
+    checked = {0: 0, 1: 0, 2: 0, 3: 0, 5: 0, 6: 0}
+    for i in range(n):
+        ref.empty(starts[i], 15)
+        for t in range(T):
+            ref.primitive(int(moves[t, i]), LIMIT)
+        p = ref.field('player')
+        assert p == rows[i, 6]
+        px, py = p % W, p // W
+        near = [q for q in cells if 1 <= cheb(p, q) <= 7 and q != rows[i, 9]]
+        spots = [near[j] for j in rng.permutation(len(near))[:int(rng.integers(0, 11))]]
+        kinds = kinds_for(rng, len(spots))
+        mons = [(q, int(rng.integers(1, 9)), k, int(rng.random() < 0.5)) for q, k in zip(spots, kinds)]
+        used, slots = {}, []
+        for q, hp, k, awake in mons:
+            j = used.get(k, 0)
+            used[k] = j + 1
+            ref.put(k + 6 * j, q, hp, awake)
+            slots.append(k + 6 * j)
+        row = env.state[i]  # the oracle's row layout (tests/spec_cases.oracle_row)
+        row[24 + 4 * 7:24 + 4 * 8].view(np.int32)[0] = len(mons)
+        for m, (q, hp, k, awake) in enumerate(mons):
+            row[60 + 2 * m:62 + 2 * m].view(np.int16)[0] = q
+            row[82 + 2 * m:84 + 2 * m].view(np.int16)[0] = -30000
+            row[104 + 2 * m:106 + 2 * m].view(np.int16)[0] = hp
+            row[126 + m], row[137 + m] = k, awake
+        env.lib.oracle_spec_observe(row.ctypes.data, 1, C.byref(env.config), env.obs[i].ctypes.data,
+                                    env.legal[i:i + 1].ctypes.data)
+        ref.observe()
+        o = ref.obs
+        mon_at = {q: (hp, awake, s) for (q, hp, k, awake), s in zip(mons, slots)}
+        for dy in range(-7, 8):
+            for dx in range(-7, 8):
+                j = (dy + 7) * 15 + dx + 7
+                x, y = px + dx, py + dy
+                q = y * W + x
+                if not (0 <= x < W and 0 <= y < 70) or q == rows[i, 9]:
+                    continue
+                ch = int(np.argmax(env.obs[i, 8 * j:8 * j + 8]))
+                mem, vis, mhp = o[j], o[733 + j], o[225 + j]
+                if mhp > 0:
+                    hp, awake, s = mon_at[q]
+                    slot = ref.field('enemy_slot', s)  # the sleep flag sits at the monster's discovery slot
+                    assert mhp == np.float32(hp / 16.0) and o[959 + slot] == (-1.0 if awake else 1.0), (i, q)
+                    want = 6 if awake else 5
+                elif mem == 0:
+                    want = 0
+                elif mem == -1:
+                    want = 1
+                else:
+                    want = 3 if vis else 2
+                assert ch == want, (i, dx, dy, ch, mem, vis, mhp)
+                checked[want] += 1
+    assert min(checked[c] for c in (0, 1, 2, 3)) > 400 and min(checked[5], checked[6]) > 15, checked
