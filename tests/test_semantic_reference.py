@@ -452,3 +452,31 @@ def test_window_channels_match_reference_observation():
                 assert ch == want, (i, dx, dy, ch, mem, vis, mhp)
                 checked[want] += 1
     assert min(checked[c] for c in (0, 1, 2, 3)) > 400 and min(checked[5], checked[6]) > 15, checked
+
+
+@pytest.mark.parametrize('backend', BACKENDS)
+def test_death_ends_the_episode_with_the_penalty_like_reference(backend):
+    """gpu-d1/src/test_combat_ablations.cu:17-21 on both tasks: a player at -100
+    HP who waits dies that turn -- done and death set, not a timeout, the
+    reward one wait minus the death penalty (the semantic build's DEATH_MILLI
+    4000, the spec config set to the same), HP reported as 0 -- and the episode
+    resets."""
+    ref = reference()
+    rng = np.random.default_rng(10)
+    floor = fixture_floor()
+    cells = [int(p) for p in np.flatnonzero(floor)]
+    cases, want = [], []
+    for k in range(40):
+        p = cells[rng.integers(len(cells))]
+        ticks = int(rng.integers(0, 1000))
+        reference_state(ref, p, -100, [], ticks)
+        o = ref.step(oracle.SEM_WAIT, LIMIT)
+        assert o[1] == 1 and o[6] == 1 and o[7] == 0 and o[4] == 0
+        assert ref.field('hp') == config()['hp'] and ref.field('ticks') == 0  # reset
+        want.append(o)
+        cases.append(spec_case(p, -100, [], ticks))
+    out = Ours(backend, cases).step([WAIT] * len(cases))
+    for i, o in enumerate(want):
+        g = out[i]
+        assert g[1] == 1 and g[6] == 1 and g[7] == 0 and g[4] == 0, i
+        assert np.float32(g[0]) == np.float32(o[0]), (i, g[0], o[0])
